@@ -1,0 +1,149 @@
+/*
+ * swiftlet_cuda.h — C ABI of the B200 (sm_100a) decode backend for
+ * Qwen3-Next / Qwen3.5-MoE hybrid models.
+ *
+ * This is the drop-in boundary for Swiftlet's GPU backend. Each entry point
+ * names the Swiftlet interface it replaces (paths inside the Swiftlet tree).
+ * Every function returns 0 (SWL_OK) or a negative SWL_ERR_* status; the
+ * message of the last failure on the calling thread is swl_last_error().
+ *
+ * Threading: calls on one model are serialised by the caller, as with
+ * QwenMetalModel (SwiftletSession.swift:139-169 serialises under genLock).
+ * Device state is keyed per swl_state, so several sequences can be
+ * interleaved on one model.
+ */
+#ifndef SWIFTLET_CUDA_H
+#define SWIFTLET_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct swl_model swl_model;
+typedef struct swl_state swl_state;
+
+enum {
+  SWL_OK = 0,
+  SWL_ERR_INVALID = -1,     /* bad argument (null handle, token out of range, ...) */
+  SWL_ERR_IO = -2,          /* missing or unreadable file */
+  SWL_ERR_FORMAT = -3,      /* malformed config / safetensors / .qpack */
+  SWL_ERR_CUDA = -4,        /* CUDA runtime failure */
+  SWL_ERR_OOM = -5,         /* device allocation failed */
+  SWL_ERR_UNSUPPORTED = -6, /* valid but unsupported format (e.g. 2-bit) */
+  SWL_ERR_CAPACITY = -7     /* context or pool capacity exceeded */
+};
+
+/* Model configuration: the fields of QwenConfig (QwenConfig.swift:10-50). */
+typedef struct swl_config {
+  int32_t hidden_size, num_hidden_layers, num_attention_heads, num_key_value_heads, head_dim;
+  int32_t vocab_size, full_attention_interval;
+  int32_t linear_num_value_heads, linear_num_key_heads, linear_key_head_dim, linear_value_head_dim;
+  int32_t linear_conv_kernel_dim;
+  int32_t num_experts, num_experts_per_tok, moe_intermediate_size, shared_expert_intermediate_size;
+  int32_t norm_topk_prob, tie_word_embeddings;
+  int32_t split_delta_layout; /* 1: qwen3_5 in_proj_qkv/z/b/a; 0: qwen3_next in_proj_qkvz/ba */
+  int32_t rotary_dims;
+  double rope_theta, partial_rotary_factor, rms_norm_eps;
+} swl_config;
+
+/* Expert pool statistics (ExpertCache.swift:11,21-22,40-41). The pool is
+ * HBM-resident: every expert of every layer is uploaded once at open
+ * (counted as misses); each routed expert use during decode is a hit. */
+typedef struct swl_pool_info {
+  int64_t expert_stride;   /* bytes per expert blob (ExpertCache.stride) */
+  int64_t slot_count;      /* ExpertCache.slotCount */
+  int64_t allocated_slots; /* ExpertCache.allocatedSlots */
+  int64_t hits, misses;    /* ExpertCache.hits / .misses */
+  int64_t resident_bytes;  /* HBM held by the pool */
+} swl_pool_info;
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* swl_last_error(void);
+
+/* Replaces QwenMetalModel.init(modelDir:cacheBudgetGB:) (QwenMetalModel.swift:104).
+ * `dir` is an mlx-lm checkpoint directory, a .qpack container
+ * (Qpack.swift:3-16) or a synthetic checkpoint (config.json with a
+ * "synthetic" block). pool_gb caps the HBM expert pool; <= 0 means no cap.
+ * A pool that does not fit the cap fails with SWL_ERR_CAPACITY. */
+int swl_model_open(const char* dir, double pool_gb, int device, swl_model** out);
+
+/* Releases every device buffer of the model. States must be freed first. */
+int swl_model_close(swl_model* model);
+
+/* InferenceModel.config (TextGenerator.swift:5). */
+int swl_model_config(const swl_model* model, swl_config* out);
+
+/* Replaces QwenCPUModel.DecodeState() (QwenCPUModel.swift:183-193): a fresh
+ * sequence at position 0 with room for max_ctx tokens of KV cache. */
+int swl_state_new(swl_model* model, int32_t max_ctx, swl_state** out);
+int swl_state_free(swl_state* state);
+/* DecodeState.position (QwenCPUModel.swift:185). */
+int32_t swl_state_position(const swl_state* state);
+
+/* Replaces InferenceModel.step(_:state:) (TextGenerator.swift:7;
+ * QwenMetalModel.swift:359-366): consumes n >= 1 tokens, advances the
+ * state's position by n and writes the LAST position's logits (vocab_size
+ * floats, host memory) to logits_out. */
+int swl_step(swl_model* model, swl_state* state, const int32_t* tokens, int32_t n, float* logits_out);
+
+/* Batched form: sequence i consumes counts[i] tokens (concatenated in
+ * `tokens`); logits_out receives nseq rows of vocab_size floats. */
+int swl_step_batch(swl_model* model, swl_state** states, const int32_t* tokens, const int32_t* counts, int32_t nseq,
+                   float* logits_out);
+
+/* Same as swl_step with device-resident tokens and logits (either logits
+ * pointer may be NULL); `greedy_out` (device, may be NULL) receives the
+ * argmax of the last logits (first index on ties, as TextGenerator.swift:90). */
+int swl_step_device(swl_model* model, swl_state* state, const int32_t* d_tokens, int32_t n, float* d_logits,
+                    int32_t* d_greedy_out);
+
+/* ExpertCache counters (ExpertCache.swift:21-22,40-41). */
+int swl_pool_stats(const swl_model* model, swl_pool_info* out);
+
+/* Replaces QwenMetalModel.shrinkCache(toGB:) (QwenMetalModel.swift:324). The
+ * HBM pool holds the full expert set; a budget below it returns
+ * SWL_ERR_CAPACITY and leaves the pool untouched. */
+int swl_pool_resize(swl_model* model, double gb);
+
+/* Runs all work of `model` on this CUDA stream (cudaStream_t); NULL selects
+ * the model's own stream. Graphs are re-captured on the new stream. */
+int swl_set_stream(swl_model* model, void* cuda_stream);
+
+/* ---- inspection entry points used by the parity tests ------------------ */
+
+/* Dequantised rows [r0, r1) of a linear module (Checkpoint.moduleWeightSlice,
+ * Checkpoint.swift:148-155), as host f32. */
+int swl_debug_dequant(swl_model* model, const char* module, int64_t r0, int64_t r1, float* out);
+/* Raw device bytes of elements [e0, e1) of a stored tensor (packed words,
+ * scales, biases or expert sections; plain tensors are held as f32). */
+int swl_debug_tensor_bytes(swl_model* model, const char* name, int64_t e0, int64_t e1, void* out, int64_t out_bytes);
+/* One decoder layer for one token at the state's position (the state
+ * advances only through swl_step): h_in/h_out are host [hidden_size];
+ * pick_ids/pick_w (host, may be NULL) receive the layer's top-k routing. */
+int swl_debug_layer(swl_model* model, swl_state* state, int32_t layer, const float* h_in, float* h_out,
+                    int32_t* pick_ids, float* pick_w);
+/* Delta-rule state of a DeltaNet layer ([nv][dv][dk] f32, host). */
+int swl_debug_delta_state(swl_model* model, swl_state* state, int32_t layer, float* out);
+
+/* Expert-GEMV sweep for the roofline measurement: `iters` passes over all
+ * layers of the fused routed+shared expert kernels (gate/up + SiLU, then
+ * down + combine), using the routing left by the last step, timed with CUDA
+ * events on the model's stream. Outputs the elapsed milliseconds, the
+ * algorithmic bytes one layer's pair of launches must read (K routed + 1
+ * shared expert: packed words, scales, biases) and the kernel launch count.
+ * Needs one prior swl_step; modifies only model scratch. */
+int swl_bench_expert_sweep(swl_model* model, int32_t iters, float* ms_out, double* bytes_per_layer,
+                           int32_t* launches_out);
+
+/* Model-free kernels on host buffers, for kernel-level parity tests:
+ * y = W x for one MLX-affine matrix (sdtype 0 f32, 1 bf16, 2 f16) ... */
+int swl_kernel_gemv_affine(const uint32_t* packed, const void* scales, const void* biases, int sdtype, int out_dim,
+                           int in_dim, int group, int bits, const float* x, float* y);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SWIFTLET_CUDA_H */

@@ -40,7 +40,7 @@ def lib():
         L.orc_open.argtypes = [C.c_char_p, I]
         L.orc_close.argtypes = [P]
         L.orc_config_int.argtypes = [P, C.c_char_p]
-        L.orc_forward.argtypes = [P, ip, I, fp, fp, fp, fp, ip]
+        L.orc_forward.argtypes = [P, ip, I, fp, fp, fp, fp, ip, ip]
         L.orc_layer_forward.argtypes = [P, fp, I, I, P, fp]
         L.orc_moe_forward.argtypes = [P, I, fp, I, fp, ip, fp, fp]
         L.orc_mixer_forward.argtypes = [P, I, fp, I, P, fp]
@@ -136,9 +136,11 @@ class OracleModel:
         emb = np.zeros((n, self.D), np.float32)
         fin = np.zeros((n, self.D), np.float32)
         greedy = np.zeros(n, np.int32)
+        picks = np.zeros((self.L, n, self.K), np.int32)
         _check(lib().orc_forward(self._h, _i(t), n, _f(logits), _f(layers) if layers is not None else None,
-                                 _f(emb), _f(fin), _i(greedy)))
-        return {"logits": logits, "layers": layers, "embed": emb, "final_norm": fin, "greedy": greedy.tolist()}
+                                 _f(emb), _f(fin), _i(greedy), _i(picks)))
+        return {"logits": logits, "layers": layers, "embed": emb, "final_norm": fin, "greedy": greedy.tolist(),
+                "picks": picks}
 
     def layer_forward(self, h, layer: int, state: DecodeState | None = None) -> np.ndarray:
         h = np.ascontiguousarray(h, dtype=np.float32).reshape(-1, self.D)

@@ -693,6 +693,7 @@ struct Model {
   std::map<int, std::shared_ptr<LayerW>> all;
   std::pair<int, std::shared_ptr<LayerW>> cache{-1, nullptr};
   std::mutex mu;
+  vector<vector<Pick>>* pickLog = nullptr;   // when set, moeForward appends each row's picks
 
   explicit Model(const string& dir) {
     string text;
@@ -965,6 +966,7 @@ struct Model {
     int D = cfg.hiddenSize, inter = cfg.moeIntermediateSize, sInter = cfg.sharedExpertIntermediateSize;
     vector<vector<Pick>> picksPerRow = route(x, S, w, probsOut);
     if (picksOut) *picksOut = picksPerRow;
+    if (pickLog) pickLog->insert(pickLog->end(), picksPerRow.begin(), picksPerRow.end());
     std::map<int, std::array<vector<float>, 3>> ew;                                   // batch union (:524-535)
     for (auto& picks : picksPerRow)
       for (auto& pk : picks)
@@ -1075,9 +1077,11 @@ int orc_config_int(void* mp, const char* key) {
 
 // Whole-sequence forward (QwenCPUModel.forward :205-233). Any output may be NULL.
 int orc_forward(void* mp, const int32_t* tokens, int n, float* logits, float* layers, float* embed_out,
-                float* final_norm, int32_t* greedy) {
+                float* final_norm, int32_t* greedy, int32_t* picks) {
   ORC_TRY({
     Model& m = *(Model*)mp; int D = m.cfg.hiddenSize, V = m.cfg.vocabSize;
+    vector<vector<Pick>> log;
+    m.pickLog = picks ? &log : nullptr;
     vector<int> toks(tokens, tokens + n);
     DecodeState st;
     vector<float> h = m.embedRows(toks);
@@ -1088,6 +1092,12 @@ int orc_forward(void* mp, const int32_t* tokens, int n, float* logits, float* la
     }
     rmsNorm(h.data(), n, D, m.finalNorm.data(), (float)m.cfg.rmsNormEps);
     if (final_norm) memcpy(final_norm, h.data(), h.size() * 4);
+    m.pickLog = nullptr;
+    if (picks) {   // [layers][n][K] in layer order
+      int K = m.cfg.numExpertsPerTok;
+      for (size_t r = 0; r < log.size(); ++r)
+        for (int k = 0; k < K; ++k) picks[r * K + k] = log[r][k].id;
+    }
     vector<float> lg = linear(h, n, D, m.lmHead, V);
     if (logits) memcpy(logits, lg.data(), lg.size() * 4);
     if (greedy)

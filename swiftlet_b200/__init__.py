@@ -1,0 +1,363 @@
+"""swiftlet_b200 — B200 (sm_100a) decode backend for Qwen3-Next / Qwen3.5-MoE.
+
+Python mirror of Swiftlet's model API over the C ABI in
+``include/swiftlet_cuda.h`` (``libswiftlet_cuda.so``, built in-tree):
+
+* ``QwenCUDAModel(model_dir, cache_budget_gb=0)`` — QwenMetalModel
+  (Sources/SwiftletCore/QwenMetalModel.swift:104) with ``config``,
+  ``model_dir``, ``step(tokens, state)``, ``expert_cache`` and
+  ``shrink_cache(to_gb)``.
+* ``DecodeState`` — QwenCPUModel.DecodeState (QwenCPUModel.swift:183).
+* ``TextGenerator`` — greedy generation loop (TextGenerator.swift:19-98).
+
+There is no CPU fallback: without the CUDA library or a GPU every call
+raises ``SwiftletError``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import json
+import os
+import weakref
+from dataclasses import dataclass
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libswiftlet_cuda.so")
+
+SWL_OK = 0
+SWL_ERR_INVALID = -1
+SWL_ERR_IO = -2
+SWL_ERR_FORMAT = -3
+SWL_ERR_CUDA = -4
+SWL_ERR_OOM = -5
+SWL_ERR_UNSUPPORTED = -6
+SWL_ERR_CAPACITY = -7
+
+
+class SwiftletError(RuntimeError):
+    def __init__(self, code: int, message: str):
+        super().__init__(f"[{code}] {message}")
+        self.code = code
+
+
+class swl_config(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in (
+        "hidden_size", "num_hidden_layers", "num_attention_heads", "num_key_value_heads", "head_dim",
+        "vocab_size", "full_attention_interval", "linear_num_value_heads", "linear_num_key_heads",
+        "linear_key_head_dim", "linear_value_head_dim", "linear_conv_kernel_dim", "num_experts",
+        "num_experts_per_tok", "moe_intermediate_size", "shared_expert_intermediate_size", "norm_topk_prob",
+        "tie_word_embeddings", "split_delta_layout", "rotary_dims")] + [
+        ("rope_theta", C.c_double), ("partial_rotary_factor", C.c_double), ("rms_norm_eps", C.c_double)]
+
+
+class swl_pool_info(C.Structure):
+    _fields_ = [(n, C.c_int64) for n in (
+        "expert_stride", "slot_count", "allocated_slots", "hits", "misses", "resident_bytes")]
+
+
+# Every entry point of include/swiftlet_cuda.h with its ctypes signature.
+_P, _I, _I64, _D = C.c_void_p, C.c_int, C.c_int64, C.c_double
+_SIGNATURES = {
+    "swl_last_error": (C.c_char_p, []),
+    "swl_model_open": (_I, [C.c_char_p, _D, _I, C.POINTER(_P)]),
+    "swl_model_close": (_I, [_P]),
+    "swl_model_config": (_I, [_P, C.POINTER(swl_config)]),
+    "swl_state_new": (_I, [_P, C.c_int32, C.POINTER(_P)]),
+    "swl_state_free": (_I, [_P]),
+    "swl_state_position": (C.c_int32, [_P]),
+    "swl_step": (_I, [_P, _P, _P, C.c_int32, _P]),
+    "swl_step_batch": (_I, [_P, _P, _P, _P, C.c_int32, _P]),
+    "swl_step_device": (_I, [_P, _P, _P, C.c_int32, _P, _P]),
+    "swl_pool_stats": (_I, [_P, C.POINTER(swl_pool_info)]),
+    "swl_pool_resize": (_I, [_P, _D]),
+    "swl_set_stream": (_I, [_P, _P]),
+    "swl_debug_dequant": (_I, [_P, C.c_char_p, _I64, _I64, _P]),
+    "swl_debug_tensor_bytes": (_I, [_P, C.c_char_p, _I64, _I64, _P, _I64]),
+    "swl_debug_layer": (_I, [_P, _P, C.c_int32, _P, _P, _P, _P]),
+    "swl_debug_delta_state": (_I, [_P, _P, C.c_int32, _P]),
+    "swl_bench_expert_sweep": (_I, [_P, C.c_int32, _P, _P, _P]),
+    "swl_kernel_gemv_affine": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
+}
+
+_lib = None
+
+
+def library_path() -> str:
+    return LIB_PATH
+
+
+def lib():
+    """Loads libswiftlet_cuda.so (building it first when sources are newer)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            from . import build as _build
+            _build.build()
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _check(rc: int) -> None:
+    if rc != SWL_OK:
+        raise SwiftletError(rc, lib().swl_last_error().decode(errors="replace"))
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+@dataclass
+class QwenConfig:
+    """Fields of QwenConfig (Sources/SwiftletCore/QwenConfig.swift:10-50)."""
+    hidden_size: int
+    num_hidden_layers: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    head_dim: int
+    vocab_size: int
+    full_attention_interval: int
+    linear_num_value_heads: int
+    linear_num_key_heads: int
+    linear_key_head_dim: int
+    linear_value_head_dim: int
+    linear_conv_kernel_dim: int
+    num_experts: int
+    num_experts_per_tok: int
+    moe_intermediate_size: int
+    shared_expert_intermediate_size: int
+    norm_topk_prob: bool
+    tie_word_embeddings: bool
+    split_delta_layout: bool
+    rotary_dims: int
+    rope_theta: float
+    partial_rotary_factor: float
+    rms_norm_eps: float
+
+    def is_linear_layer(self, i: int) -> bool:
+        """QwenConfig.isLinearLayer (QwenConfig.swift:108-110)."""
+        return (i + 1) % self.full_attention_interval != 0
+
+    @property
+    def key_dim(self) -> int:
+        return self.linear_num_key_heads * self.linear_key_head_dim
+
+    @property
+    def value_dim(self) -> int:
+        return self.linear_num_value_heads * self.linear_value_head_dim
+
+
+@dataclass
+class ExpertCacheStats:
+    """ExpertCache counters (ExpertCache.swift:11,21-22,40-41)."""
+    stride: int
+    slot_count: int
+    allocated_slots: int
+    hits: int
+    misses: int
+    resident_bytes: int
+
+
+class DecodeState:
+    """Per-sequence device state (QwenCPUModel.DecodeState). Created by
+    ``QwenCUDAModel.new_state`` or lazily on the first ``step``."""
+
+    def __init__(self, max_ctx: int = 4096):
+        self.max_ctx = int(max_ctx)
+        self._h = None
+        self._model = None
+
+    def _bind(self, model: "QwenCUDAModel") -> int:
+        if self._h is None:
+            h = C.c_void_p()
+            _check(lib().swl_state_new(model._h, self.max_ctx, C.byref(h)))
+            self._h = h.value
+            self._model = model
+            model._states.append(weakref.ref(self))
+        elif self._model is not model:
+            raise SwiftletError(SWL_ERR_INVALID, "state belongs to another model")
+        return self._h
+
+    @property
+    def position(self) -> int:
+        return 0 if self._h is None else lib().swl_state_position(self._h)
+
+    def free(self) -> None:
+        if self._h is not None:
+            lib().swl_state_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+class QwenCUDAModel:
+    """Drop-in for QwenMetalModel: ``step(tokens, state) -> logits``."""
+
+    def __init__(self, model_dir: str, cache_budget_gb: float = 0.0, device: int = 0):
+        h = C.c_void_p()
+        _check(lib().swl_model_open(os.fsencode(model_dir), float(cache_budget_gb), int(device), C.byref(h)))
+        self._h = h.value
+        self.model_dir = model_dir
+        cfg = swl_config()
+        _check(lib().swl_model_config(self._h, C.byref(cfg)))
+        vals = {name: getattr(cfg, name) for name, _ in swl_config._fields_}
+        for b in ("norm_topk_prob", "tie_word_embeddings", "split_delta_layout"):
+            vals[b] = bool(vals[b])
+        self.config = QwenConfig(**vals)
+        self._states: list = []
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            for ref in self._states:   # device states must go before the model
+                st = ref()
+                if st is not None:
+                    st.free()
+            lib().swl_model_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def new_state(self, max_ctx: int = 4096) -> DecodeState:
+        s = DecodeState(max_ctx)
+        s._bind(self)
+        return s
+
+    def step(self, tokens, state: DecodeState) -> np.ndarray:
+        """InferenceModel.step (TextGenerator.swift:7): consumes the tokens,
+        advances ``state.position`` and returns the last position's logits."""
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32).reshape(-1))
+        out = np.empty(self.config.vocab_size, np.float32)
+        _check(lib().swl_step(self._h, state._bind(self), _ptr(t), len(t), _ptr(out)))
+        return out
+
+    def step_batch(self, token_lists, states) -> np.ndarray:
+        counts = np.array([len(t) for t in token_lists], np.int32)
+        flat = np.ascontiguousarray(np.concatenate([np.asarray(t, np.int32).reshape(-1) for t in token_lists]))
+        handles = (C.c_void_p * len(states))(*[s._bind(self) for s in states])
+        out = np.empty((len(states), self.config.vocab_size), np.float32)
+        _check(lib().swl_step_batch(self._h, handles, _ptr(flat), _ptr(counts), len(states), _ptr(out)))
+        return out
+
+    def step_device(self, d_tokens: int, n: int, state: DecodeState, d_logits: int = 0, d_greedy: int = 0) -> None:
+        """Device-pointer form (tokens/logits already in HBM)."""
+        _check(lib().swl_step_device(self._h, state._bind(self), C.c_void_p(d_tokens), int(n),
+                                     C.c_void_p(d_logits or None), C.c_void_p(d_greedy or None)))
+
+    def set_stream(self, cuda_stream: int | None) -> None:
+        _check(lib().swl_set_stream(self._h, C.c_void_p(cuda_stream or None)))
+
+    @property
+    def expert_cache(self) -> ExpertCacheStats:
+        p = swl_pool_info()
+        _check(lib().swl_pool_stats(self._h, C.byref(p)))
+        return ExpertCacheStats(p.expert_stride, p.slot_count, p.allocated_slots, p.hits, p.misses, p.resident_bytes)
+
+    def shrink_cache(self, to_gb: float) -> None:
+        """QwenMetalModel.shrinkCache(toGB:) (QwenMetalModel.swift:324)."""
+        _check(lib().swl_pool_resize(self._h, float(to_gb)))
+
+    # -- inspection (parity tests) -------------------------------------
+    def debug_dequant(self, module: str, r0: int, r1: int, cols: int) -> np.ndarray:
+        out = np.empty((r1 - r0, cols), np.float32)
+        _check(lib().swl_debug_dequant(self._h, module.encode(), r0, r1, _ptr(out)))
+        return out
+
+    def debug_tensor_bytes(self, name: str, e0: int, e1: int, elem_bytes: int) -> bytes:
+        buf = C.create_string_buffer(max(1, (e1 - e0) * elem_bytes))
+        _check(lib().swl_debug_tensor_bytes(self._h, name.encode(), e0, e1, buf, (e1 - e0) * elem_bytes))
+        return buf.raw[: (e1 - e0) * elem_bytes]
+
+    def debug_layer(self, state: DecodeState, layer: int, h):
+        h = np.ascontiguousarray(h, dtype=np.float32).reshape(-1)
+        out = np.empty_like(h)
+        k = self.config.num_experts_per_tok
+        ids = np.empty(k, np.int32)
+        w = np.empty(k, np.float32)
+        _check(lib().swl_debug_layer(self._h, state._bind(self), layer, _ptr(h), _ptr(out), _ptr(ids), _ptr(w)))
+        return out, ids, w
+
+    def bench_expert_sweep(self, iters: int):
+        """(elapsed ms, algorithmic bytes per layer, launches) of `iters` expert sweeps."""
+        ms = C.c_float()
+        b = C.c_double()
+        n = C.c_int32()
+        _check(lib().swl_bench_expert_sweep(self._h, int(iters), C.byref(ms), C.byref(b), C.byref(n)))
+        return ms.value, b.value, n.value
+
+    def debug_delta_state(self, state: DecodeState, layer: int) -> np.ndarray:
+        c = self.config
+        out = np.empty((c.linear_num_value_heads, c.linear_value_head_dim, c.linear_key_head_dim), np.float32)
+        _check(lib().swl_debug_delta_state(self._h, state._bind(self), layer, _ptr(out)))
+        return out
+
+
+def gemv_affine(packed, scales, biases, out_dim: int, in_dim: int, group: int, bits: int, x) -> np.ndarray:
+    """One MLX-affine GEMV on the GPU (the fast kernel of the decode path)."""
+    packed = np.ascontiguousarray(packed, dtype=np.uint32)
+    sd = {np.dtype(np.float32): 0, np.dtype(np.uint16): 1, np.dtype(np.float16): 2}[np.asarray(scales).dtype]
+    scales = np.ascontiguousarray(scales)
+    biases = np.ascontiguousarray(biases)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(out_dim, np.float32)
+    _check(lib().swl_kernel_gemv_affine(_ptr(packed), _ptr(scales), _ptr(biases), sd, out_dim, in_dim, group, bits,
+                                        _ptr(x), _ptr(y)))
+    return y
+
+
+class TextGenerator:
+    """Engine-agnostic greedy loop (TextGenerator.swift:19-98)."""
+
+    def __init__(self, model):
+        self.model = model
+        self.eos_tokens = self.eos_token_ids(model.model_dir)
+
+    @staticmethod
+    def eos_token_ids(model_dir: str) -> set[int]:
+        """EOS ids from generation_config.json / config.json (TextGenerator.swift:29-38)."""
+        eos: set[int] = set()
+        for name in ("generation_config.json", "config.json"):
+            p = os.path.join(model_dir, name)
+            try:
+                obj = json.load(open(p))
+            except (OSError, ValueError):
+                continue
+            v = obj.get("eos_token_id")
+            if isinstance(v, int):
+                eos.add(v)
+            elif isinstance(v, list):
+                eos.update(x for x in v if isinstance(x, int))
+        return eos
+
+    def generate(self, prompt_ids, max_new: int, on_token=lambda t: True, state: DecodeState | None = None) -> dict:
+        """Greedy decode; EOS stops generation and is not reported."""
+        import time
+        state = state if state is not None else DecodeState()
+        stats = {"prompt_tokens": len(prompt_ids), "generated_tokens": 0}
+        t0 = time.perf_counter()
+        logits = self.model.step(list(prompt_ids), state)
+        stats["prefill_seconds"] = time.perf_counter() - t0
+        t1 = time.perf_counter()
+        for _ in range(max_new):
+            best = int(np.argmax(logits))   # first maximal index, as the reference's `>` scan
+            if best in self.eos_tokens:
+                break
+            stats["generated_tokens"] += 1
+            if not on_token(best):
+                break
+            logits = self.model.step([best], state)
+        stats["decode_seconds"] = time.perf_counter() - t1
+        return stats

@@ -1,0 +1,140 @@
+// Launch interface of the decode-path kernels (sm_100a).
+#pragma once
+
+#include "common.h"
+
+namespace swl {
+
+// Per-sequence device state, reached through one indirection so that a
+// captured CUDA graph serves every sequence: the host copies the sequence's
+// descriptor into the model's "current" slot before replaying.
+struct StateDev {
+  int* pos;         // tokens already processed (RoPE offset, ring slot)
+  float** conv;     // [layers] conv ring [conv_k][conv_dim] (slot = pos % conv_k), DeltaNet layers
+  float** dstate;   // [layers] delta state [nv][dv][dk]
+  float** kc;       // [layers] K cache [max_ctx][kv_heads][head_dim], attention layers
+  float** vc;       // [layers] V cache
+  int max_ctx;
+};
+
+// Input transform applied by a GEMV prologue while staging x in shared memory.
+enum Prologue : int {
+  PRO_COPY = 0,      // x as given
+  PRO_RMSNORM = 1,   // rmsnorm(x) * w (eps)
+  PRO_GATEDNORM = 2, // per head: rmsnorm(y) * w * silu(z) (DeltaNet output gate)
+};
+enum Epilogue : int {
+  EPI_STORE = 0,     // y[row] = acc
+  EPI_RESIDUAL = 1,  // y[row] += acc
+};
+
+struct GemvSeg {
+  QLin lin;
+  float* y;
+};
+
+struct GemvArgs {
+  GemvSeg seg[4];
+  int nseg = 0;
+  int in = 0;
+  int prologue = PRO_COPY;
+  int epilogue = EPI_STORE;
+  const float* x = nullptr;     // input vector [in] (PRO_GATEDNORM: y)
+  const float* aux = nullptr;   // norm weight (RMSNORM) / z vector (GATEDNORM)
+  const float* aux2 = nullptr;  // GATEDNORM: per-dim norm weight [head_dim]
+  int head_dim = 0;             // GATEDNORM head size
+  float eps = 1e-6f;
+  float* x_out = nullptr;       // block 0 stores the prepared x here (optional)
+  int* argmax_out = nullptr;    // optional fused greedy argmax over segment 0 rows
+  float* argmax_val = nullptr;  // scratch [gridDim] values for argmax
+  int* argmax_idx = nullptr;    // scratch [gridDim] indices
+  unsigned* counter = nullptr;  // last-block counter for argmax
+};
+
+struct RouterArgs {
+  QLin gate;        // [E, D]
+  QLin sgate;       // shared_expert_gate [1, D]
+  const float* h;   // residual stream
+  const float* norm_w;
+  float eps;
+  float* x_out;     // normalised input for the experts [D]
+  float* logits;    // scratch [E + 1]
+  int* pick_ids;    // [K]
+  float* pick_w;    // [K] combine weights (renormalised when norm_topk)
+  float* shared_scale;  // sigmoid(shared gate logit)
+  unsigned* counter;
+  int topk;
+  int norm_topk;
+};
+
+struct MoeArgs {
+  ExpertProj g, u, d;          // routed experts of this layer (pool addressing)
+  QLin sg, su, sd;             // shared expert
+  const float* x;              // [D] normalised
+  const int* pick_ids;
+  const float* pick_w;
+  const float* shared_scale;
+  float* hmid;                 // [(K+1) * max_inter]
+  int hmid_stride;
+  int topk;
+  float* h;                    // residual stream (down + combine adds here)
+  const StateDev* advance_sd;  // when set: ++*advance_sd->pos and ++*advance_cursor after the layer
+  int* advance_cursor;
+};
+
+struct DeltaArgs {
+  const float* proj;       // in-projection outputs of this token
+  int split;               // 1: [qkv | z | b | a]; 0: qwen3_next interleaved qkvz then ba
+  int nk, nv, dk, dv, conv_k, conv_dim;
+  const float* conv_w;     // [conv_dim][conv_k]
+  const float* a_log;      // [nv]
+  const float* dt_bias;    // [nv]
+  const StateDev* sd;
+  int layer;
+  int rows_per_block;      // dv rows per block
+  float* y;                // [nv*dv] raw recurrence output
+  float* z;                // [nv*dv] gate input, de-interleaved
+};
+
+struct AttnArgs {
+  const float* qout;       // [H * 2 * hd] (per head: q | gate)
+  const float* knew;       // [Hkv * hd]
+  const float* vnew;       // [Hkv * hd]
+  const float* qn;         // q_norm weight [hd]
+  const float* kn;         // k_norm weight [hd]
+  float eps;
+  float rope_theta;
+  int rot;
+  int H, Hkv, hd;
+  int nchunks;
+  int chunk_cap;           // max positions per chunk (smem sizing)
+  const StateDev* sd;
+  int layer;
+  float* part;             // [Hkv][nchunks][G][hd + 2]
+  unsigned* counters;      // [Hkv]
+  float* out;              // [H * hd] gated attention output
+};
+
+struct EmbedArgs {
+  QLin table;
+  const int* tokens;
+  const int* cursor;
+  float* h;
+  int vocab;
+  int* err;
+};
+
+// All launches go to `stream`; `pdl` enables programmatic dependent launch.
+void launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl);
+void launch_router(const RouterArgs& a, int experts, cudaStream_t stream, bool pdl);
+void launch_moe_gateup(const MoeArgs& a, cudaStream_t stream, bool pdl);
+void launch_moe_down(const MoeArgs& a, cudaStream_t stream, bool pdl);
+void launch_delta(const DeltaArgs& a, cudaStream_t stream, bool pdl);
+void launch_attn(const AttnArgs& a, cudaStream_t stream, bool pdl);
+void launch_embed(const EmbedArgs& a, int hidden, cudaStream_t stream, bool pdl);
+// Debug/test helper: dequantise rows [r0, r1) of a module to f32.
+void launch_dequant(const QLin& l, int64_t r0, int64_t r1, float* out, cudaStream_t stream);
+
+int sm_count();
+
+}  // namespace swl

@@ -1,0 +1,26 @@
+// Kernel launch helper: cudaLaunchKernelEx with optional programmatic
+// dependent launch; the launch status is checked directly (never through
+// cudaGetLastError, which can hold an older, unrelated error).
+#pragma once
+
+#include "common.h"
+
+namespace swl {
+
+template <typename Kern, typename... Args>
+void launch(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  if (smem > 48 * 1024) SWL_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  SWL_CUDA(cudaLaunchKernelEx(&cfg, k, args...));
+}
+
+}  // namespace swl

@@ -1,0 +1,1076 @@
+// Model runtime: weight upload into HBM (dense arena + fixed-stride expert
+// pool), per-sequence device state, the decode step as a CUDA graph, and
+// the C ABI of include/swiftlet_cuda.h.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <functional>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/swiftlet_cuda.h"
+#include "common.h"
+#include "host_io.h"
+#include "kernels.h"
+#include "synth.h"
+
+namespace swl {
+
+static thread_local std::string g_error;
+
+static float bf16f(uint16_t u) { uint32_t v = uint32_t(u) << 16; float f; memcpy(&f, &v, 4); return f; }
+static float f16f(uint16_t h) {
+  uint32_t s = (h >> 15) & 1, e = (h >> 10) & 31, m = h & 1023, o;
+  if (e == 0) {
+    if (m == 0) o = s << 31;
+    else { int k = -1; do { m <<= 1; ++k; } while (!(m & 1024)); m &= 1023; o = (s << 31) | uint32_t(127 - 15 - k) << 23 | (m << 13); }
+  } else if (e == 31) o = (s << 31) | 0x7F800000u | (m << 13);
+  else o = (s << 31) | (e + 112) << 23 | (m << 13);
+  float f; memcpy(&f, &o, 4); return f;
+}
+static bool env_flag(const char* k) { const char* v = getenv(k); return v && *v && strcmp(v, "0") != 0; }
+
+struct Section {
+  std::string name, dtype;  // "gate_proj.weight", ...
+  std::vector<int64_t> shape;
+  int64_t offset = 0, size = 0;
+};
+
+struct LayerDev {
+  bool delta = false;
+  QLin in_lin[4];
+  float* in_y[4] = {nullptr, nullptr, nullptr, nullptr};
+  int n_in = 0;
+  QLin out_lin;
+  float *in_norm = nullptr, *post_norm = nullptr;
+  float *conv_w = nullptr, *a_log = nullptr, *dt_bias = nullptr, *dnorm = nullptr;
+  float *qn = nullptr, *kn = nullptr;
+  QLin router, sgate, sh_g, sh_u, sh_d;
+  ExpertProj eg, eu, ed;
+  uint8_t* pool = nullptr;
+};
+
+struct StoredTensor {
+  uint8_t* ptr = nullptr;  // dense: tensor start; expert section: pool of the layer + section offset
+  TensorMeta meta;
+  int64_t expert_stride = 0;  // > 0: stacked expert tensor living in the pool
+  int64_t per_expert = 0;     // elements per expert
+  bool as_f32 = false;        // plain tensor converted to f32 on the device
+};
+
+struct Model;
+
+struct State {
+  Model* model = nullptr;
+  int max_ctx = 0;
+  int pos = 0;
+  uint8_t* mem = nullptr;
+  StateDev* desc = nullptr;  // device copy of the descriptor
+  float** ptr_arrays = nullptr;
+  std::vector<float*> conv, dstate, kc, vc;
+  int* d_pos = nullptr;
+};
+
+struct Model {
+  std::string dir;
+  ModelConfig cfg;
+  QuantTable qt;
+  int device = 0;
+  enum Mode { FILES, QPACK, SYNTH } mode = FILES;
+  uint64_t seed = 0;
+  float wstd = 0.02f;
+  bool syn_scale_bf16 = true, syn_plain_bf16 = true;
+  std::unique_ptr<CheckpointFiles> ck;
+  QpackLayout qlay;
+  std::vector<Section> sections;
+  int64_t stride = 0;
+  double pool_cap_gb = 0;
+
+  cudaStream_t own = nullptr, stream = nullptr;
+  std::vector<void*> allocs;
+  uint8_t* dense = nullptr;
+  size_t dense_size = 0, dense_used = 0;
+  bool planning = true;
+  uint8_t* pool = nullptr;
+  size_t pool_size = 0;
+  std::map<std::string, StoredTensor> stored;
+
+  std::vector<LayerDev> L;
+  QLin embed, lm_head;
+  float* final_norm = nullptr;
+
+  // scratch (one token in flight)
+  float *h = nullptr, *proj = nullptr, *yv = nullptr, *zv = nullptr, *att = nullptr, *xmoe = nullptr;
+  float *rlogits = nullptr, *pick_w = nullptr, *sscale = nullptr, *hmid = nullptr, *part = nullptr, *logits = nullptr;
+  float* amax_v = nullptr;
+  int *pick_ids = nullptr, *tokens = nullptr, *cursor = nullptr, *err = nullptr, *amax_i = nullptr, *greedy = nullptr;
+  unsigned *ctr_router = nullptr, *ctr_attn = nullptr, *ctr_amax = nullptr;
+  StateDev* cur = nullptr;
+  int hmid_stride = 0, max_tokens = 0, attn_chunks = 32, chunk_cap = 0, max_ctx_cap = 0;
+  int64_t hits = 0, misses = 0;
+
+  cudaGraphExec_t g_body = nullptr, g_head = nullptr, g_head_amax = nullptr;
+  bool stepped = false;
+  bool use_graph = true, use_pdl = true;
+  float* h_logits = nullptr;
+  int* h_tokens = nullptr;
+  int h_tokens_cap = 0;
+
+  ~Model();
+  void open(const std::string& d, double pool_gb, int dev);
+  void* dmalloc(size_t n) {
+    void* p = nullptr;
+    SWL_CUDA(cudaMalloc(&p, n));
+    allocs.push_back(p);
+    return p;
+  }
+  uint8_t* take(size_t n) {
+    size_t off = (dense_used + 255) & ~size_t(255);
+    dense_used = off + n;
+    return planning ? nullptr : dense + off;
+  }
+  void build_weights();
+  QLin module(const std::string& path, int out, int in);
+  float* plain(const std::string& name, int64_t n, int role);
+  void plan_sections();
+  ExpertProj expert_proj(uint8_t* pool_l, const std::string& proj, int out, int in);
+  void upload_experts();
+  void alloc_scratch();
+  void enqueue_layer(int l, cudaStream_t st, bool advance);
+  void enqueue_body(cudaStream_t st);
+  void enqueue_head(cudaStream_t st, bool amax);
+  void drop_graphs();
+  void ensure_graphs();
+  void ensure_tokens(int n);
+  void run(State* s, int n, bool amax);
+};
+
+Model::~Model() {
+  drop_graphs();
+  if (stream) cudaStreamSynchronize(stream);
+  for (void* p : allocs) cudaFree(p);
+  if (h_logits) cudaFreeHost(h_logits);
+  if (h_tokens) cudaFreeHost(h_tokens);
+  if (own) cudaStreamDestroy(own);
+}
+
+void Model::drop_graphs() {
+  if (g_body) cudaGraphExecDestroy(g_body);
+  if (g_head) cudaGraphExecDestroy(g_head);
+  if (g_head_amax) cudaGraphExecDestroy(g_head_amax);
+  g_body = g_head = g_head_amax = nullptr;
+}
+
+// Quantised or plain linear module `path` with logical shape [out, in]
+// (Checkpoint.isQuantized / quantSpec, Checkpoint.swift:122-133).
+QLin Model::module(const std::string& path, int out, int in) {
+  QLin q;
+  q.out = out; q.in = in;
+  bool quant = mode == SYNTH ? true : ck->has(path + ".scales");
+  if (quant) {
+    int bits = 0, gs = 0;
+    if (!qt.lookup(path, bits, gs)) throw Error(ERR_FORMAT, "missing tensor " + path + ".scales spec");
+    if (bits != 4 && bits != 8) throw Error(ERR_UNSUPPORTED, "unsupported bits " + std::to_string(bits) + " for " + path);
+    if (gs <= 0 || in % gs || gs % (bits == 4 ? 32 : 16)) throw Error(ERR_UNSUPPORTED, "unsupported group size for " + path);
+    const int pw = 32 / bits;
+    q.bits = bits; q.gs = gs;
+    q.row_bytes = int64_t(in) * bits / 8;
+    q.srow = in / gs;
+    std::string sdt = mode == SYNTH ? (syn_scale_bf16 ? "BF16" : "F32") : ck->meta(path + ".scales").dtype;
+    q.dt = dtype_code(sdt);
+    const int64_t sb = dtype_size(sdt);
+    if (mode != SYNTH) {
+      TensorMeta wm = ck->meta(path + ".weight");
+      if (wm.dtype != "U32" || wm.numel() != int64_t(out) * in / pw || ck->meta(path + ".scales").numel() != int64_t(out) * q.srow)
+        throw Error(ERR_FORMAT, "bad shape for quantised module " + path);
+    }
+    uint8_t* w = take(size_t(out) * q.row_bytes);
+    uint8_t* s = take(size_t(out) * q.srow * sb);
+    uint8_t* b = take(size_t(out) * q.srow * sb);
+    if (!planning) {
+      q.w = w; q.s = s; q.b = b;
+      const int64_t nw = int64_t(out) * in / pw, ns = int64_t(out) * q.srow;
+      if (mode == SYNTH) {
+        synth_words(w, path + ".weight", seed, nw, 0, 0, stream);
+        synth_affine(s, b, path, seed, bits, wstd, syn_scale_bf16, ns, 0, 0, stream);
+      } else {
+        size_t n;
+        SWL_CUDA(cudaMemcpy(w, ck->data(path + ".weight", &n), size_t(nw) * 4, cudaMemcpyHostToDevice));
+        SWL_CUDA(cudaMemcpy(s, ck->data(path + ".scales", &n), size_t(ns) * sb, cudaMemcpyHostToDevice));
+        SWL_CUDA(cudaMemcpy(b, ck->data(path + ".biases", &n), size_t(ns) * sb, cudaMemcpyHostToDevice));
+      }
+      TensorMeta mw; mw.dtype = "U32"; mw.shape = {out, in / pw};
+      TensorMeta ms; ms.dtype = sdt; ms.shape = {out, q.srow};
+      stored[path + ".weight"] = {w, mw};
+      stored[path + ".scales"] = {s, ms};
+      stored[path + ".biases"] = {b, ms};
+    }
+  } else {
+    TensorMeta wm = ck->meta(path + ".weight");
+    if (wm.numel() != int64_t(out) * in) throw Error(ERR_FORMAT, "bad shape for module " + path);
+    q.bits = 0;
+    q.dt = dtype_code(wm.dtype);
+    q.row_bytes = int64_t(in) * dtype_size(wm.dtype);
+    if (q.row_bytes % 16) throw Error(ERR_UNSUPPORTED, "row of " + path + " is not a multiple of 16 bytes");
+    uint8_t* w = take(size_t(out) * q.row_bytes);
+    if (!planning) {
+      q.w = w;
+      size_t n;
+      SWL_CUDA(cudaMemcpy(w, ck->data(path + ".weight", &n), size_t(out) * q.row_bytes, cudaMemcpyHostToDevice));
+      stored[path + ".weight"] = {w, wm};
+    }
+  }
+  if (q.row_bytes % 16) throw Error(ERR_UNSUPPORTED, "row of " + path + " is not a multiple of 16 bytes");
+  return q;
+}
+
+// Plain tensor (norm weights, conv, A_log, dt_bias) held as f32.
+float* Model::plain(const std::string& name, int64_t n, int role) {
+  uint8_t* p = take(size_t(n) * 4);
+  if (planning) return nullptr;
+  float* d = reinterpret_cast<float*>(p);
+  if (mode == SYNTH) {
+    synth_plain(d, name, seed, role, wstd, syn_plain_bf16, n, stream);
+  } else {
+    TensorMeta m = ck->meta(name);
+    if (m.numel() != n) throw Error(ERR_FORMAT, "bad shape for " + name);
+    size_t nb;
+    const uint8_t* src = ck->data(name, &nb);
+    std::vector<float> host(n);
+    for (int64_t i = 0; i < n; ++i) {
+      if (m.dtype == "F32") memcpy(&host[i], src + 4 * i, 4);
+      else {
+        uint16_t u; memcpy(&u, src + 2 * i, 2);
+        host[i] = m.dtype == "BF16" ? bf16f(u) : m.dtype == "F16" ? f16f(u) : throw Error(ERR_UNSUPPORTED, "dtype " + m.dtype);
+      }
+    }
+    SWL_CUDA(cudaMemcpy(d, host.data(), size_t(n) * 4, cudaMemcpyHostToDevice));
+  }
+  StoredTensor t; t.ptr = p; t.meta.dtype = "F32"; t.meta.shape = {n}; t.as_f32 = true;
+  stored[name] = t;
+  return d;
+}
+
+// Blob sections of one expert: gate/up/down x weight/scales/biases in that
+// order, 16 KiB-aligned stride (QpackRepacker.repack, Qpack.swift:64-93).
+void Model::plan_sections() {
+  sections.clear();
+  if (mode == QPACK) {
+    for (auto& s : qlay.sections) sections.push_back({s.name, s.dtype, s.shape, s.offset, s.size});
+    stride = qlay.stride;
+    if (qlay.expert_count != cfg.experts || qlay.layer_count != cfg.layers)
+      throw Error(ERR_FORMAT, "qpack layout does not match config.json");
+    return;
+  }
+  int64_t off = 0;
+  for (const char* proj : {"gate_proj", "up_proj", "down_proj"}) {
+    for (const char* part : {"weight", "scales", "biases"}) {
+      Section s;
+      s.name = std::string(proj) + "." + part;
+      std::string full = "model.layers.0.mlp.switch_mlp." + s.name;
+      const bool down = std::string(proj) == "down_proj";
+      const int out = down ? cfg.hidden : cfg.moe_inter, in = down ? cfg.moe_inter : cfg.hidden;
+      if (mode == SYNTH) {
+        int bits, gs;
+        if (!qt.lookup("model.layers.0.mlp.switch_mlp." + std::string(proj), bits, gs))
+          throw Error(ERR_FORMAT, "synthetic checkpoint without quantization block");
+        if (std::string(part) == "weight") { s.dtype = "U32"; s.shape = {out, in * bits / 32}; }
+        else { s.dtype = syn_scale_bf16 ? "BF16" : "F32"; s.shape = {out, in / gs}; }
+      } else {
+        if (!ck->has(full)) continue;
+        TensorMeta m = ck->meta(full);
+        if (m.shape.empty() || m.shape[0] != cfg.experts) throw Error(ERR_FORMAT, "bad expert tensor " + full);
+        s.dtype = m.dtype;
+        s.shape.assign(m.shape.begin() + 1, m.shape.end());
+      }
+      int64_t n = 1;
+      for (auto d : s.shape) n *= d;
+      s.size = n * dtype_size(s.dtype);
+      s.offset = off;
+      off += s.size;
+      sections.push_back(s);
+    }
+  }
+  stride = (off + 16383) / 16384 * 16384;
+}
+
+static const Section* find_section(const std::vector<Section>& v, const std::string& n) {
+  for (auto& s : v) if (s.name == n) return &s;
+  return nullptr;
+}
+
+// Geometry of one projection inside the blob; bits and group size follow
+// from the section shapes and the logical in-dim.
+ExpertProj Model::expert_proj(uint8_t* pool_l, const std::string& proj, int out, int in) {
+  const Section* w = find_section(sections, proj + ".weight");
+  if (!w) throw Error(ERR_FORMAT, "expert section missing: " + proj + ".weight");
+  const Section* s = find_section(sections, proj + ".scales");
+  const Section* b = find_section(sections, proj + ".biases");
+  ExpertProj e;
+  QLin& q = e.lin;
+  q.out = out; q.in = in;
+  if (w->shape.size() != 2 || w->shape[0] != out) throw Error(ERR_FORMAT, "bad expert section shape: " + proj);
+  if (w->dtype == "U32") {
+    if (!s || !b) throw Error(ERR_FORMAT, "quantised expert without scales/biases: " + proj);
+    const int64_t cols = w->shape[1];
+    if ((cols * 32) % in) throw Error(ERR_FORMAT, "expert section width does not match in-dim: " + proj);
+    q.bits = int(cols * 32 / in);
+    if (q.bits != 4 && q.bits != 8) throw Error(ERR_UNSUPPORTED, "unsupported expert bits");
+    if (s->shape.size() != 2 || s->shape[1] <= 0 || in % s->shape[1]) throw Error(ERR_FORMAT, "bad expert scales: " + proj);
+    q.gs = int(in / s->shape[1]);
+    if (q.gs % (q.bits == 4 ? 32 : 16)) throw Error(ERR_UNSUPPORTED, "unsupported expert group size");
+    q.srow = s->shape[1];
+    q.dt = dtype_code(s->dtype);
+    q.row_bytes = int64_t(in) * q.bits / 8;
+    q.w = pool_l + w->offset; q.s = pool_l + s->offset; q.b = pool_l + b->offset;
+  } else {
+    q.bits = 0;
+    q.dt = dtype_code(w->dtype);
+    q.row_bytes = int64_t(in) * dtype_size(w->dtype);
+    q.w = pool_l + w->offset;
+  }
+  if (q.row_bytes % 16 || (w->offset % 16)) throw Error(ERR_UNSUPPORTED, "expert rows are not 16-byte aligned: " + proj);
+  e.wstride = e.sstride = e.bstride = stride;
+  return e;
+}
+
+void Model::upload_experts() {
+  const int64_t E = cfg.experts, per_layer = E * stride;
+  if (mode == SYNTH) {
+    for (int l = 0; l < cfg.layers; ++l) {
+      uint8_t* pl = pool + int64_t(l) * per_layer;
+      for (const char* proj : {"gate_proj", "up_proj", "down_proj"}) {
+        std::string base = "model.layers." + std::to_string(l) + ".mlp.switch_mlp." + proj;
+        const Section* w = find_section(sections, std::string(proj) + ".weight");
+        const Section* s = find_section(sections, std::string(proj) + ".scales");
+        const Section* b = find_section(sections, std::string(proj) + ".biases");
+        int bits, gs;
+        qt.lookup(base, bits, gs);
+        synth_words(pl + w->offset, base + ".weight", seed, E * (w->size / 4), w->size / 4, stride, stream);
+        const int64_t eb = syn_scale_bf16 ? 2 : 4;
+        synth_affine(pl + s->offset, pl + b->offset, base, seed, bits, wstd, syn_scale_bf16, E * (s->size / eb), s->size / eb, stride, stream);
+      }
+    }
+    SWL_CUDA(cudaStreamSynchronize(stream));
+  } else if (mode == QPACK) {
+    std::vector<uint8_t> buf(size_t(per_layer));
+    for (int l = 0; l < cfg.layers; ++l) {
+      char name[64];
+      snprintf(name, sizeof name, "/packed_experts/layer_%02d.bin", l);
+      MappedFile f(dir + name);
+      if (int64_t(f.size) < per_layer) throw Error(ERR_FORMAT, std::string("short read: ") + name);
+      SWL_CUDA(cudaMemcpy(pool + int64_t(l) * per_layer, f.base, size_t(per_layer), cudaMemcpyHostToDevice));
+    }
+  } else {
+    std::vector<uint8_t> blob(size_t(per_layer), 0);
+    for (int l = 0; l < cfg.layers; ++l) {
+      for (auto& s : sections) {
+        size_t nb;
+        const uint8_t* src = ck->data("model.layers." + std::to_string(l) + ".mlp.switch_mlp." + s.name, &nb);
+        if (int64_t(nb) != E * s.size) throw Error(ERR_FORMAT, "expert tensor size mismatch: " + s.name);
+        for (int64_t e = 0; e < E; ++e) memcpy(blob.data() + e * stride + s.offset, src + e * s.size, size_t(s.size));
+      }
+      SWL_CUDA(cudaMemcpy(pool + int64_t(l) * per_layer, blob.data(), size_t(per_layer), cudaMemcpyHostToDevice));
+    }
+  }
+  misses += int64_t(cfg.layers) * E;
+  // register stacked names for inspection
+  for (int l = 0; l < cfg.layers; ++l)
+    for (auto& s : sections) {
+      StoredTensor t;
+      t.ptr = pool + int64_t(l) * per_layer + s.offset;
+      t.meta.dtype = s.dtype;
+      t.meta.shape = s.shape;
+      t.meta.shape.insert(t.meta.shape.begin(), E);
+      t.expert_stride = stride;
+      t.per_expert = s.size / dtype_size(s.dtype);
+      stored["model.layers." + std::to_string(l) + ".mlp.switch_mlp." + s.name] = t;
+    }
+}
+
+void Model::build_weights() {
+  const ModelConfig& c = cfg;
+  const int D = c.hidden;
+  L.assign(c.layers, LayerDev());
+  embed = module("model.embed_tokens", c.vocab, D);
+  lm_head = c.tie_embed ? embed : module("lm_head", c.vocab, D);
+  final_norm = plain("model.norm.weight", D, SYN_NORM);
+  for (int i = 0; i < c.layers; ++i) {
+    LayerDev& ld = L[i];
+    std::string p = "model.layers." + std::to_string(i) + ".";
+    ld.in_norm = plain(p + "input_layernorm.weight", D, SYN_NORM);
+    ld.post_norm = plain(p + "post_attention_layernorm.weight", D, SYN_NORM);
+    if (c.is_linear(i)) {
+      ld.delta = true;
+      ld.a_log = plain(p + "linear_attn.A_log", c.nv, SYN_ALOG);
+      ld.dt_bias = plain(p + "linear_attn.dt_bias", c.nv, SYN_DTBIAS);
+      ld.conv_w = plain(p + "linear_attn.conv1d.weight", int64_t(c.conv_dim()) * c.conv_k, SYN_CONV);
+      ld.dnorm = plain(p + "linear_attn.norm.weight", c.dv, SYN_NORM);
+      ld.out_lin = module(p + "linear_attn.out_proj", D, c.value_dim());
+      if (c.split_layout) {
+        ld.in_lin[0] = module(p + "linear_attn.in_proj_qkv", c.conv_dim(), D);
+        ld.in_lin[1] = module(p + "linear_attn.in_proj_z", c.value_dim(), D);
+        ld.in_lin[2] = module(p + "linear_attn.in_proj_b", c.nv, D);
+        ld.in_lin[3] = module(p + "linear_attn.in_proj_a", c.nv, D);
+        ld.n_in = 4;
+      } else {
+        ld.in_lin[0] = module(p + "linear_attn.in_proj_qkvz", 2 * c.key_dim() + 2 * c.value_dim(), D);
+        ld.in_lin[1] = module(p + "linear_attn.in_proj_ba", 2 * c.nv, D);
+        ld.n_in = 2;
+      }
+    } else {
+      const int H = c.heads, KVH = c.kv_heads, hd = c.head_dim;
+      ld.in_lin[0] = module(p + "self_attn.q_proj", 2 * H * hd, D);
+      ld.in_lin[1] = module(p + "self_attn.k_proj", KVH * hd, D);
+      ld.in_lin[2] = module(p + "self_attn.v_proj", KVH * hd, D);
+      ld.n_in = 3;
+      ld.out_lin = module(p + "self_attn.o_proj", D, H * hd);
+      ld.qn = plain(p + "self_attn.q_norm.weight", hd, SYN_NORM);
+      ld.kn = plain(p + "self_attn.k_norm.weight", hd, SYN_NORM);
+    }
+    ld.router = module(p + "mlp.gate", c.experts, D);
+    ld.sgate = module(p + "mlp.shared_expert_gate", 1, D);
+    ld.sh_g = module(p + "mlp.shared_expert.gate_proj", c.shared_inter, D);
+    ld.sh_u = module(p + "mlp.shared_expert.up_proj", c.shared_inter, D);
+    ld.sh_d = module(p + "mlp.shared_expert.down_proj", D, c.shared_inter);
+  }
+}
+
+void Model::alloc_scratch() {
+  const ModelConfig& c = cfg;
+  const int D = c.hidden, H = c.heads, KVH = c.kv_heads, hd = c.head_dim, G = H / KVH;
+  size_t projn = std::max<size_t>({size_t(c.conv_dim() + c.value_dim() + 2 * c.nv),
+                                   size_t(2 * c.key_dim() + 2 * c.value_dim() + 2 * c.nv),
+                                   size_t(2 * H * hd + 2 * KVH * hd)});
+  hmid_stride = (std::max(c.moe_inter, c.shared_inter) + 31) / 32 * 32;
+  auto f = [&](size_t n) { return reinterpret_cast<float*>(dmalloc(std::max<size_t>(n, 1) * 4)); };
+  h = f(D); proj = f(projn); yv = f(c.value_dim()); zv = f(c.value_dim()); att = f(size_t(H) * hd); xmoe = f(D);
+  rlogits = f(c.experts + 1); pick_w = f(c.topk); sscale = f(1);
+  hmid = f(size_t(c.topk + 1) * hmid_stride);
+  part = f(size_t(KVH) * attn_chunks * G * (hd + 2));
+  logits = f(c.vocab);
+  amax_v = f(1024);
+  pick_ids = reinterpret_cast<int*>(dmalloc(size_t(std::max(c.topk, 1)) * 4));
+  cursor = reinterpret_cast<int*>(dmalloc(4));
+  err = reinterpret_cast<int*>(dmalloc(4));
+  amax_i = reinterpret_cast<int*>(dmalloc(1024 * 4));
+  greedy = reinterpret_cast<int*>(dmalloc(4));
+  ctr_router = reinterpret_cast<unsigned*>(dmalloc(4));
+  ctr_attn = reinterpret_cast<unsigned*>(dmalloc(size_t(KVH) * 4));
+  ctr_amax = reinterpret_cast<unsigned*>(dmalloc(4));
+  cur = reinterpret_cast<StateDev*>(dmalloc(sizeof(StateDev)));
+  SWL_CUDA(cudaMemset(ctr_router, 0, 4));
+  SWL_CUDA(cudaMemset(ctr_attn, 0, size_t(KVH) * 4));
+  SWL_CUDA(cudaMemset(ctr_amax, 0, 4));
+  SWL_CUDA(cudaMemset(err, 0, 4));
+  {
+    std::vector<int> ids(std::max(c.topk, 1));
+    for (size_t i = 0; i < ids.size(); ++i) ids[i] = int(i % c.experts);
+    SWL_CUDA(cudaMemcpy(pick_ids, ids.data(), ids.size() * 4, cudaMemcpyHostToDevice));
+  }
+  SWL_CUDA(cudaMallocHost(&h_logits, size_t(c.vocab) * 4));
+  ensure_tokens(4096);
+  // GEMV segment outputs
+  for (auto& ld : L) {
+    if (ld.delta) {
+      if (c.split_layout) {
+        ld.in_y[0] = proj;
+        ld.in_y[1] = proj + c.conv_dim();
+        ld.in_y[2] = proj + c.conv_dim() + c.value_dim();
+        ld.in_y[3] = proj + c.conv_dim() + c.value_dim() + c.nv;
+      } else {
+        ld.in_y[0] = proj;
+        ld.in_y[1] = proj + 2 * c.key_dim() + 2 * c.value_dim();
+      }
+    } else {
+      ld.in_y[0] = proj;
+      ld.in_y[1] = proj + 2 * H * hd;
+      ld.in_y[2] = proj + 2 * H * hd + KVH * hd;
+    }
+  }
+}
+
+void Model::ensure_tokens(int n) {
+  if (n <= max_tokens) return;
+  int cap = std::max(n, 2 * max_tokens);
+  tokens = reinterpret_cast<int*>(dmalloc(size_t(cap) * 4));
+  if (h_tokens) cudaFreeHost(h_tokens);
+  SWL_CUDA(cudaMallocHost(&h_tokens, size_t(cap) * 4));
+  max_tokens = cap;
+  drop_graphs();  // the token buffer address is baked into the body graph
+}
+
+void Model::open(const std::string& d, double pool_gb, int dev) {
+  dir = d;
+  device = dev;
+  pool_cap_gb = pool_gb;
+  use_graph = !env_flag("SWL_NO_GRAPH");
+  use_pdl = !env_flag("SWL_NO_PDL");
+  Json top = Json::parse(read_text_file(dir + "/config.json"));
+  cfg.parse(top);
+  qt.parse(top);
+  if (cfg.heads % cfg.kv_heads || cfg.nv % cfg.nk || cfg.topk > cfg.experts || cfg.topk > 64 || cfg.topk < 1)
+    throw Error(ERR_UNSUPPORTED, "unsupported head or expert geometry");
+  if (cfg.dk > 1024 || cfg.head_dim > 1024 || cfg.dv % std::min(cfg.dv, 32)) throw Error(ERR_UNSUPPORTED, "unsupported head dims");
+  if (const Json* sy = top.find("synthetic")) {
+    mode = SYNTH;
+    if (const Json* v = sy->find("seed")) seed = uint64_t(v->num);
+    if (const Json* v = sy->find("weight_std")) wstd = float(v->num);
+    if (const Json* v = sy->find("scale_dtype")) syn_scale_bf16 = v->str != "f32";
+    if (const Json* v = sy->find("plain_dtype")) syn_plain_bf16 = v->str != "f32";
+    if (!qt.has_default) throw Error(ERR_FORMAT, "synthetic checkpoint needs a quantization block");
+  } else {
+    ck.reset(new CheckpointFiles(dir));
+    if (path_exists(dir + "/packed_experts/layout.json")) { mode = QPACK; qlay.load(dir); }
+  }
+  SWL_CUDA(cudaSetDevice(dev));
+  SWL_CUDA(cudaStreamCreateWithFlags(&own, cudaStreamNonBlocking));
+  stream = own;
+  const char* mc = getenv("SWL_MAX_CTX");
+  max_ctx_cap = mc ? std::max(16, atoi(mc)) : 32768;
+  chunk_cap = (max_ctx_cap + attn_chunks - 1) / attn_chunks;
+  plan_sections();
+  pool_size = size_t(cfg.layers) * cfg.experts * stride;
+  if (pool_gb > 0 && double(pool_size) > pool_gb * 1073741824.0)
+    throw Error(ERR_CAPACITY, "expert pool needs " + std::to_string(double(pool_size) / 1073741824.0) +
+                                  " GB of HBM, above the budget; the HBM-resident pool does not stream experts");
+  // pass 1: plan the dense arena, pass 2: allocate and fill
+  planning = true; dense_used = 0;
+  build_weights();
+  dense_size = dense_used;
+  dense = reinterpret_cast<uint8_t*>(dmalloc(dense_size));
+  pool = reinterpret_cast<uint8_t*>(dmalloc(pool_size));
+  planning = false; dense_used = 0;
+  build_weights();
+  for (int l = 0; l < cfg.layers; ++l) {
+    LayerDev& ld = L[l];
+    ld.pool = pool + size_t(l) * cfg.experts * stride;
+    ld.eg = expert_proj(ld.pool, "gate_proj", cfg.moe_inter, cfg.hidden);
+    ld.eu = expert_proj(ld.pool, "up_proj", cfg.moe_inter, cfg.hidden);
+    ld.ed = expert_proj(ld.pool, "down_proj", cfg.hidden, cfg.moe_inter);
+  }
+  upload_experts();
+  alloc_scratch();
+  SWL_CUDA(cudaStreamSynchronize(stream));
+  ck.reset();  // weights are resident; drop the file mappings
+}
+
+void Model::enqueue_layer(int l, cudaStream_t st, bool advance) {
+  const ModelConfig& c = cfg;
+  const LayerDev& ld = L[l];
+  const bool pdl = use_pdl;
+  GemvArgs g;
+  for (int s = 0; s < ld.n_in; ++s) { g.seg[s].lin = ld.in_lin[s]; g.seg[s].y = ld.in_y[s]; }
+  g.nseg = ld.n_in; g.in = c.hidden; g.prologue = PRO_RMSNORM; g.epilogue = EPI_STORE;
+  g.x = h; g.aux = ld.in_norm; g.eps = float(c.eps);
+  launch_gemv(g, st, pdl);
+  if (ld.delta) {
+    DeltaArgs d;
+    d.proj = proj; d.split = c.split_layout; d.nk = c.nk; d.nv = c.nv; d.dk = c.dk; d.dv = c.dv;
+    d.conv_k = c.conv_k; d.conv_dim = c.conv_dim(); d.conv_w = ld.conv_w; d.a_log = ld.a_log; d.dt_bias = ld.dt_bias;
+    d.sd = cur; d.layer = l; d.rows_per_block = std::min(c.dv, 32); d.y = yv; d.z = zv;
+    launch_delta(d, st, pdl);
+    GemvArgs o;
+    o.seg[0].lin = ld.out_lin; o.seg[0].y = h; o.nseg = 1; o.in = c.value_dim();
+    o.prologue = PRO_GATEDNORM; o.epilogue = EPI_RESIDUAL; o.x = yv; o.aux = zv; o.aux2 = ld.dnorm;
+    o.head_dim = c.dv; o.eps = float(c.eps);
+    launch_gemv(o, st, pdl);
+  } else {
+    AttnArgs a;
+    a.qout = ld.in_y[0]; a.knew = ld.in_y[1]; a.vnew = ld.in_y[2]; a.qn = ld.qn; a.kn = ld.kn;
+    a.eps = float(c.eps); a.rope_theta = float(c.rope_theta); a.rot = c.rot_dims();
+    a.H = c.heads; a.Hkv = c.kv_heads; a.hd = c.head_dim; a.nchunks = attn_chunks; a.chunk_cap = chunk_cap;
+    a.sd = cur; a.layer = l; a.part = part; a.counters = ctr_attn; a.out = att;
+    launch_attn(a, st, pdl);
+    GemvArgs o;
+    o.seg[0].lin = ld.out_lin; o.seg[0].y = h; o.nseg = 1; o.in = c.heads * c.head_dim;
+    o.prologue = PRO_COPY; o.epilogue = EPI_RESIDUAL; o.x = att;
+    launch_gemv(o, st, pdl);
+  }
+  RouterArgs r;
+  r.gate = ld.router; r.sgate = ld.sgate; r.h = h; r.norm_w = ld.post_norm; r.eps = float(c.eps);
+  r.x_out = xmoe; r.logits = rlogits; r.pick_ids = pick_ids; r.pick_w = pick_w; r.shared_scale = sscale;
+  r.counter = ctr_router; r.topk = c.topk; r.norm_topk = c.norm_topk;
+  launch_router(r, c.experts, st, pdl);
+  MoeArgs m;
+  m.g = ld.eg; m.u = ld.eu; m.d = ld.ed; m.sg = ld.sh_g; m.su = ld.sh_u; m.sd = ld.sh_d;
+  m.x = xmoe; m.pick_ids = pick_ids; m.pick_w = pick_w; m.shared_scale = sscale;
+  m.hmid = hmid; m.hmid_stride = hmid_stride; m.topk = c.topk; m.h = h;
+  m.advance_sd = advance ? cur : nullptr; m.advance_cursor = cursor;
+  launch_moe_gateup(m, st, pdl);
+  launch_moe_down(m, st, pdl);
+}
+
+void Model::enqueue_body(cudaStream_t st) {
+  EmbedArgs e;
+  e.table = embed; e.tokens = tokens; e.cursor = cursor; e.h = h; e.vocab = cfg.vocab; e.err = err;
+  launch_embed(e, cfg.hidden, st, use_pdl);
+  for (int l = 0; l < cfg.layers; ++l) enqueue_layer(l, st, l == cfg.layers - 1);
+}
+
+void Model::enqueue_head(cudaStream_t st, bool amax) {
+  GemvArgs g;
+  g.seg[0].lin = lm_head; g.seg[0].y = logits; g.nseg = 1; g.in = cfg.hidden;
+  g.prologue = PRO_RMSNORM; g.epilogue = EPI_STORE; g.x = h; g.aux = final_norm; g.eps = float(cfg.eps);
+  if (amax) { g.argmax_out = greedy; g.argmax_val = amax_v; g.argmax_idx = amax_i; g.counter = ctr_amax; }
+  launch_gemv(g, st, use_pdl);
+}
+
+static cudaGraphExec_t capture(cudaStream_t st, const std::function<void()>& body) {
+  cudaGraph_t graph = nullptr;
+  SWL_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  try {
+    body();
+  } catch (...) {
+    cudaStreamEndCapture(st, &graph);
+    if (graph) cudaGraphDestroy(graph);
+    throw;
+  }
+  SWL_CUDA(cudaStreamEndCapture(st, &graph));
+  cudaGraphExec_t exec = nullptr;
+  cudaError_t e = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  SWL_CUDA(e);
+  return exec;
+}
+
+void Model::ensure_graphs() {
+  if (!use_graph || (g_body && g_head && g_head_amax)) return;
+  drop_graphs();
+  g_body = capture(stream, [&] { enqueue_body(stream); });
+  g_head = capture(stream, [&] { enqueue_head(stream, false); });
+  g_head_amax = capture(stream, [&] { enqueue_head(stream, true); });
+}
+
+// Runs n tokens already placed in `tokens` for state s.
+void Model::run(State* s, int n, bool amax) {
+  if (n < 1) throw Error(ERR_INVALID, "step needs at least one token");
+  if (s->pos + n > s->max_ctx) throw Error(ERR_CAPACITY, "context capacity exceeded (max_ctx " + std::to_string(s->max_ctx) + ")");
+  ensure_graphs();
+  SWL_CUDA(cudaMemsetAsync(cursor, 0, 4, stream));
+  SWL_CUDA(cudaMemcpyAsync(cur, s->desc, sizeof(StateDev), cudaMemcpyDeviceToDevice, stream));
+  for (int i = 0; i < n; ++i) {
+    if (use_graph) SWL_CUDA(cudaGraphLaunch(g_body, stream));
+    else enqueue_body(stream);
+  }
+  if (use_graph) SWL_CUDA(cudaGraphLaunch(amax ? g_head_amax : g_head, stream));
+  else enqueue_head(stream, amax);
+  s->pos += n;
+  stepped = true;
+  hits += int64_t(n) * cfg.topk * cfg.layers;
+}
+
+static State* new_state(Model* m, int max_ctx) {
+  if (max_ctx < 1) throw Error(ERR_INVALID, "max_ctx must be positive");
+  if (max_ctx > m->max_ctx_cap)
+    throw Error(ERR_CAPACITY, "max_ctx above the model's context cap " + std::to_string(m->max_ctx_cap) + " (SWL_MAX_CTX)");
+  const ModelConfig& c = m->cfg;
+  std::unique_ptr<State> s(new State());
+  s->model = m;
+  s->max_ctx = max_ctx;
+  const size_t conv_n = size_t(c.conv_k) * c.conv_dim(), dstate_n = size_t(c.nv) * c.dv * c.dk;
+  const size_t kv_n = size_t(max_ctx) * c.kv_heads * c.head_dim;
+  size_t total = 256;
+  for (int l = 0; l < c.layers; ++l) total += c.is_linear(l) ? (conv_n + dstate_n) * 4 + 512 : 2 * kv_n * 4 + 512;
+  total += 4 * size_t(c.layers) * sizeof(float*) + sizeof(StateDev) + 512;
+  SWL_CUDA(cudaMalloc(&s->mem, total));
+  size_t off = 0;
+  auto take = [&](size_t n) { off = (off + 255) & ~size_t(255); uint8_t* p = s->mem + off; off += n; return p; };
+  s->d_pos = reinterpret_cast<int*>(take(4));
+  s->conv.assign(c.layers, nullptr); s->dstate.assign(c.layers, nullptr);
+  s->kc.assign(c.layers, nullptr); s->vc.assign(c.layers, nullptr);
+  for (int l = 0; l < c.layers; ++l) {
+    if (c.is_linear(l)) {
+      s->conv[l] = reinterpret_cast<float*>(take(conv_n * 4));
+      s->dstate[l] = reinterpret_cast<float*>(take(dstate_n * 4));
+    } else {
+      s->kc[l] = reinterpret_cast<float*>(take(kv_n * 4));
+      s->vc[l] = reinterpret_cast<float*>(take(kv_n * 4));
+    }
+  }
+  float** arrays = reinterpret_cast<float**>(take(4 * size_t(c.layers) * sizeof(float*)));
+  s->desc = reinterpret_cast<StateDev*>(take(sizeof(StateDev)));
+  // zero the recurrent state (a fresh sequence: conv tail and delta state are 0)
+  SWL_CUDA(cudaMemsetAsync(s->mem, 0, total, m->stream));
+  std::vector<float*> host(4 * size_t(c.layers));
+  for (int l = 0; l < c.layers; ++l) {
+    host[l] = s->conv[l]; host[c.layers + l] = s->dstate[l];
+    host[2 * c.layers + l] = s->kc[l]; host[3 * c.layers + l] = s->vc[l];
+  }
+  SWL_CUDA(cudaMemcpyAsync(arrays, host.data(), host.size() * sizeof(float*), cudaMemcpyHostToDevice, m->stream));
+  StateDev sd;
+  sd.pos = s->d_pos; sd.conv = arrays; sd.dstate = arrays + c.layers; sd.kc = arrays + 2 * c.layers; sd.vc = arrays + 3 * c.layers;
+  sd.max_ctx = max_ctx;
+  SWL_CUDA(cudaMemcpyAsync(s->desc, &sd, sizeof sd, cudaMemcpyHostToDevice, m->stream));
+  SWL_CUDA(cudaStreamSynchronize(m->stream));
+  return s.release();
+}
+
+static int fail(const Error& e) { g_error = e.what(); return e.code; }
+
+}  // namespace swl
+
+using namespace swl;
+
+struct swl_model { Model m; };
+struct swl_state { State s; };
+
+// A failed call in a destructor path (or in another library sharing the
+// context) leaves a non-sticky "last error" behind; drop it at entry so it
+// can never be attributed to this call.
+static void clear_stale_error() {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess && getenv("SWL_DEBUG")) fprintf(stderr, "[swiftlet] stale CUDA error at API entry: %s\n", cudaGetErrorString(e));
+}
+
+#define API_BEGIN \
+  try {           \
+    clear_stale_error();
+#define API_END                                                  \
+  }                                                              \
+  catch (const swl::Error& e) { return fail(e); }                \
+  catch (const std::exception& e) { g_error = e.what(); return SWL_ERR_INVALID; } \
+  return SWL_OK;
+
+extern "C" {
+
+const char* swl_last_error(void) { return g_error.c_str(); }
+
+int swl_model_open(const char* dir, double pool_gb, int device, swl_model** out) {
+  API_BEGIN
+  if (!dir || !out) throw Error(ERR_INVALID, "null argument");
+  *out = nullptr;
+  std::unique_ptr<swl_model> m(new swl_model());
+  m->m.open(dir, pool_gb, device);
+  *out = m.release();
+  API_END
+}
+
+int swl_model_close(swl_model* model) {
+  API_BEGIN
+  if (!model) throw Error(ERR_INVALID, "null model");
+  cudaSetDevice(model->m.device);
+  delete model;
+  API_END
+}
+
+int swl_model_config(const swl_model* model, swl_config* o) {
+  API_BEGIN
+  if (!model || !o) throw Error(ERR_INVALID, "null argument");
+  const ModelConfig& c = model->m.cfg;
+  o->hidden_size = c.hidden; o->num_hidden_layers = c.layers; o->num_attention_heads = c.heads;
+  o->num_key_value_heads = c.kv_heads; o->head_dim = c.head_dim; o->vocab_size = c.vocab;
+  o->full_attention_interval = c.full_attn_interval; o->linear_num_value_heads = c.nv; o->linear_num_key_heads = c.nk;
+  o->linear_key_head_dim = c.dk; o->linear_value_head_dim = c.dv; o->linear_conv_kernel_dim = c.conv_k;
+  o->num_experts = c.experts; o->num_experts_per_tok = c.topk; o->moe_intermediate_size = c.moe_inter;
+  o->shared_expert_intermediate_size = c.shared_inter; o->norm_topk_prob = c.norm_topk; o->tie_word_embeddings = c.tie_embed;
+  o->split_delta_layout = c.split_layout; o->rotary_dims = c.rot_dims();
+  o->rope_theta = c.rope_theta; o->partial_rotary_factor = c.partial_rotary; o->rms_norm_eps = c.eps;
+  API_END
+}
+
+int swl_state_new(swl_model* model, int32_t max_ctx, swl_state** out) {
+  API_BEGIN
+  if (!model || !out) throw Error(ERR_INVALID, "null argument");
+  SWL_CUDA(cudaSetDevice(model->m.device));
+  State* s = new_state(&model->m, max_ctx);
+  swl_state* w = new swl_state();
+  w->s = *s;
+  delete s;
+  *out = w;
+  API_END
+}
+
+int swl_state_free(swl_state* state) {
+  API_BEGIN
+  if (!state) throw Error(ERR_INVALID, "null state");
+  cudaSetDevice(state->s.model->device);
+  cudaStreamSynchronize(state->s.model->stream);
+  cudaFree(state->s.mem);
+  delete state;
+  API_END
+}
+
+int32_t swl_state_position(const swl_state* state) { return state ? state->s.pos : -1; }
+
+static void check_tokens(const Model& m, const int32_t* t, int n) {
+  if (!t || n < 1) throw Error(ERR_INVALID, "step needs at least one token");
+  for (int i = 0; i < n; ++i)
+    if (t[i] < 0 || t[i] >= m.cfg.vocab) throw Error(ERR_INVALID, "token id " + std::to_string(t[i]) + " out of range");
+}
+
+int swl_step(swl_model* model, swl_state* state, const int32_t* tokens, int32_t n, float* logits_out) {
+  API_BEGIN
+  if (!model || !state || !logits_out) throw Error(ERR_INVALID, "null argument");
+  Model& m = model->m;
+  if (state->s.model != &m) throw Error(ERR_INVALID, "state belongs to another model");
+  SWL_CUDA(cudaSetDevice(m.device));
+  check_tokens(m, tokens, n);
+  m.ensure_tokens(n);
+  memcpy(m.h_tokens, tokens, size_t(n) * 4);
+  SWL_CUDA(cudaMemcpyAsync(m.tokens, m.h_tokens, size_t(n) * 4, cudaMemcpyHostToDevice, m.stream));
+  m.run(&state->s, n, false);
+  SWL_CUDA(cudaMemcpyAsync(m.h_logits, m.logits, size_t(m.cfg.vocab) * 4, cudaMemcpyDeviceToHost, m.stream));
+  SWL_CUDA(cudaStreamSynchronize(m.stream));
+  memcpy(logits_out, m.h_logits, size_t(m.cfg.vocab) * 4);
+  API_END
+}
+
+int swl_step_batch(swl_model* model, swl_state** states, const int32_t* tokens, const int32_t* counts, int32_t nseq,
+                   float* logits_out) {
+  API_BEGIN
+  if (!model || !states || !tokens || !counts || !logits_out || nseq < 1) throw Error(ERR_INVALID, "null argument");
+  int64_t off = 0;
+  for (int i = 0; i < nseq; ++i) {
+    int rc = swl_step(model, states[i], tokens + off, counts[i], logits_out + int64_t(i) * model->m.cfg.vocab);
+    if (rc) return rc;
+    off += counts[i];
+  }
+  API_END
+}
+
+int swl_step_device(swl_model* model, swl_state* state, const int32_t* d_tokens, int32_t n, float* d_logits,
+                    int32_t* d_greedy) {
+  API_BEGIN
+  if (!model || !state || !d_tokens) throw Error(ERR_INVALID, "null argument");
+  Model& m = model->m;
+  if (state->s.model != &m) throw Error(ERR_INVALID, "state belongs to another model");
+  SWL_CUDA(cudaSetDevice(m.device));
+  m.ensure_tokens(n);
+  SWL_CUDA(cudaMemcpyAsync(m.tokens, d_tokens, size_t(n) * 4, cudaMemcpyDeviceToDevice, m.stream));
+  m.run(&state->s, n, d_greedy != nullptr);
+  if (d_logits) SWL_CUDA(cudaMemcpyAsync(d_logits, m.logits, size_t(m.cfg.vocab) * 4, cudaMemcpyDeviceToDevice, m.stream));
+  if (d_greedy) SWL_CUDA(cudaMemcpyAsync(d_greedy, m.greedy, 4, cudaMemcpyDeviceToDevice, m.stream));
+  API_END
+}
+
+int swl_pool_stats(const swl_model* model, swl_pool_info* o) {
+  API_BEGIN
+  if (!model || !o) throw Error(ERR_INVALID, "null argument");
+  const Model& m = model->m;
+  o->expert_stride = m.stride;
+  o->slot_count = int64_t(m.cfg.layers) * m.cfg.experts;
+  o->allocated_slots = o->slot_count;
+  o->hits = m.hits;
+  o->misses = m.misses;
+  o->resident_bytes = int64_t(m.pool_size);
+  API_END
+}
+
+int swl_pool_resize(swl_model* model, double gb) {
+  API_BEGIN
+  if (!model) throw Error(ERR_INVALID, "null model");
+  if (gb > 0 && double(model->m.pool_size) > gb * 1073741824.0)
+    throw Error(ERR_CAPACITY, "the HBM-resident expert pool holds every expert; it cannot shrink below " +
+                                  std::to_string(double(model->m.pool_size) / 1073741824.0) + " GB");
+  API_END
+}
+
+int swl_set_stream(swl_model* model, void* st) {
+  API_BEGIN
+  if (!model) throw Error(ERR_INVALID, "null model");
+  Model& m = model->m;
+  SWL_CUDA(cudaSetDevice(m.device));
+  SWL_CUDA(cudaStreamSynchronize(m.stream));
+  m.drop_graphs();
+  m.stream = st ? reinterpret_cast<cudaStream_t>(st) : m.own;
+  API_END
+}
+
+int swl_debug_dequant(swl_model* model, const char* module, int64_t r0, int64_t r1, float* out) {
+  API_BEGIN
+  if (!model || !module || !out) throw Error(ERR_INVALID, "null argument");
+  Model& m = model->m;
+  SWL_CUDA(cudaSetDevice(m.device));
+  std::string p = module;
+  // find the QLin of the module among the loaded ones
+  QLin q;
+  bool found = false;
+  auto chk = [&](const QLin& l, const std::string& name) { if (!found && name == p) { q = l; found = true; } };
+  chk(m.embed, "model.embed_tokens");
+  chk(m.lm_head, m.cfg.tie_embed ? "model.embed_tokens" : "lm_head");
+  for (int l = 0; l < m.cfg.layers && !found; ++l) {
+    const LayerDev& ld = m.L[l];
+    std::string pre = "model.layers." + std::to_string(l) + ".";
+    chk(ld.router, pre + "mlp.gate");
+    chk(ld.sgate, pre + "mlp.shared_expert_gate");
+    chk(ld.sh_g, pre + "mlp.shared_expert.gate_proj");
+    chk(ld.sh_u, pre + "mlp.shared_expert.up_proj");
+    chk(ld.sh_d, pre + "mlp.shared_expert.down_proj");
+    chk(ld.out_lin, pre + (ld.delta ? "linear_attn.out_proj" : "self_attn.o_proj"));
+    const char* dn[4] = {"linear_attn.in_proj_qkv", "linear_attn.in_proj_z", "linear_attn.in_proj_b", "linear_attn.in_proj_a"};
+    const char* fn[2] = {"linear_attn.in_proj_qkvz", "linear_attn.in_proj_ba"};
+    const char* an[3] = {"self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"};
+    for (int s = 0; s < ld.n_in; ++s)
+      chk(ld.in_lin[s], pre + (ld.delta ? (m.cfg.split_layout ? dn[s] : fn[s]) : an[s]));
+    // stacked experts: rows [r0, r1) of the [E*out, in] view
+    for (auto pr : {std::make_pair("gate_proj", &ld.eg), std::make_pair("up_proj", &ld.eu), std::make_pair("down_proj", &ld.ed)}) {
+      if (found || p != pre + "mlp.switch_mlp." + pr.first) continue;
+      const ExpertProj& ep = *pr.second;
+      const int rows = ep.lin.out;
+      std::vector<float> buf;
+      float* dbuf = nullptr;
+      SWL_CUDA(cudaMalloc(&dbuf, size_t(r1 - r0) * ep.lin.in * 4));
+      for (int64_t r = r0; r < r1;) {
+        const int e = int(r / rows);
+        const int64_t lr0 = r % rows, lr1 = std::min<int64_t>(rows, lr0 + (r1 - r));
+        QLin el = ep.lin;
+        el.w += int64_t(e) * ep.wstride; el.s += int64_t(e) * ep.sstride; el.b += int64_t(e) * ep.bstride;
+        launch_dequant(el, lr0, lr1, dbuf + (r - r0) * ep.lin.in, m.stream);
+        r += lr1 - lr0;
+      }
+      SWL_CUDA(cudaStreamSynchronize(m.stream));
+      cudaError_t e = cudaMemcpy(out, dbuf, size_t(r1 - r0) * ep.lin.in * 4, cudaMemcpyDeviceToHost);
+      cudaFree(dbuf);
+      SWL_CUDA(e);
+      return SWL_OK;
+    }
+  }
+  if (!found) throw Error(ERR_INVALID, "unknown module " + p);
+  if (r0 < 0 || r1 > q.out || r0 >= r1) throw Error(ERR_INVALID, "row range out of bounds");
+  float* dbuf = nullptr;
+  SWL_CUDA(cudaMalloc(&dbuf, size_t(r1 - r0) * q.in * 4));
+  launch_dequant(q, r0, r1, dbuf, m.stream);
+  SWL_CUDA(cudaStreamSynchronize(m.stream));
+  cudaError_t e = cudaMemcpy(out, dbuf, size_t(r1 - r0) * q.in * 4, cudaMemcpyDeviceToHost);
+  cudaFree(dbuf);
+  SWL_CUDA(e);
+  API_END
+}
+
+int swl_debug_tensor_bytes(swl_model* model, const char* name, int64_t e0, int64_t e1, void* out, int64_t out_bytes) {
+  API_BEGIN
+  if (!model || !name || !out) throw Error(ERR_INVALID, "null argument");
+  Model& m = model->m;
+  SWL_CUDA(cudaSetDevice(m.device));
+  auto it = m.stored.find(name);
+  if (it == m.stored.end()) throw Error(ERR_INVALID, std::string("unknown tensor ") + name);
+  const StoredTensor& t = it->second;
+  const int64_t eb = dtype_size(t.meta.dtype);
+  if (e0 < 0 || e1 > t.meta.numel() || e0 > e1 || (e1 - e0) * eb > out_bytes) throw Error(ERR_INVALID, "element range out of bounds");
+  uint8_t* o = reinterpret_cast<uint8_t*>(out);
+  SWL_CUDA(cudaStreamSynchronize(m.stream));
+  if (t.expert_stride == 0) {
+    SWL_CUDA(cudaMemcpy(o, t.ptr + e0 * eb, size_t((e1 - e0) * eb), cudaMemcpyDeviceToHost));
+  } else {
+    for (int64_t e = e0; e < e1;) {
+      const int64_t ex = e / t.per_expert, w = e % t.per_expert, n = std::min(t.per_expert - w, e1 - e);
+      SWL_CUDA(cudaMemcpy(o + (e - e0) * eb, t.ptr + ex * t.expert_stride + w * eb, size_t(n * eb), cudaMemcpyDeviceToHost));
+      e += n;
+    }
+  }
+  API_END
+}
+
+int swl_debug_layer(swl_model* model, swl_state* state, int32_t layer, const float* h_in, float* h_out, int32_t* ids,
+                    float* w) {
+  API_BEGIN
+  if (!model || !state || !h_in || !h_out) throw Error(ERR_INVALID, "null argument");
+  Model& m = model->m;
+  if (layer < 0 || layer >= m.cfg.layers) throw Error(ERR_INVALID, "layer out of range");
+  SWL_CUDA(cudaSetDevice(m.device));
+  SWL_CUDA(cudaMemcpyAsync(m.h, h_in, size_t(m.cfg.hidden) * 4, cudaMemcpyHostToDevice, m.stream));
+  SWL_CUDA(cudaMemcpyAsync(m.cur, state->s.desc, sizeof(StateDev), cudaMemcpyDeviceToDevice, m.stream));
+  m.enqueue_layer(layer, m.stream, false);
+  SWL_CUDA(cudaMemcpyAsync(h_out, m.h, size_t(m.cfg.hidden) * 4, cudaMemcpyDeviceToHost, m.stream));
+  if (ids) SWL_CUDA(cudaMemcpyAsync(ids, m.pick_ids, size_t(m.cfg.topk) * 4, cudaMemcpyDeviceToHost, m.stream));
+  if (w) SWL_CUDA(cudaMemcpyAsync(w, m.pick_w, size_t(m.cfg.topk) * 4, cudaMemcpyDeviceToHost, m.stream));
+  SWL_CUDA(cudaStreamSynchronize(m.stream));
+  API_END
+}
+
+int swl_debug_delta_state(swl_model* model, swl_state* state, int32_t layer, float* out) {
+  API_BEGIN
+  if (!model || !state || !out) throw Error(ERR_INVALID, "null argument");
+  Model& m = model->m;
+  if (layer < 0 || layer >= m.cfg.layers || !m.cfg.is_linear(layer)) throw Error(ERR_INVALID, "not a DeltaNet layer");
+  SWL_CUDA(cudaSetDevice(m.device));
+  SWL_CUDA(cudaStreamSynchronize(m.stream));
+  SWL_CUDA(cudaMemcpy(out, state->s.dstate[layer], size_t(m.cfg.nv) * m.cfg.dv * m.cfg.dk * 4, cudaMemcpyDeviceToHost));
+  API_END
+}
+
+static int64_t qlin_bytes(const QLin& q) {
+  const int64_t sb = q.bits ? int64_t(q.srow) * (q.dt == DT_F32 ? 4 : 2) * 2 : 0;
+  return int64_t(q.out) * (q.row_bytes + sb);
+}
+
+int swl_bench_expert_sweep(swl_model* model, int32_t iters, float* ms_out, double* bytes_per_layer, int32_t* launches) {
+  API_BEGIN
+  if (!model || !ms_out || iters < 1) throw Error(ERR_INVALID, "bad argument");
+  Model& m = model->m;
+  if (!m.stepped) throw Error(ERR_INVALID, "run one step before the expert sweep");
+  SWL_CUDA(cudaSetDevice(m.device));
+  cudaEvent_t e0, e1;
+  SWL_CUDA(cudaEventCreate(&e0));
+  SWL_CUDA(cudaEventCreate(&e1));
+  SWL_CUDA(cudaEventRecord(e0, m.stream));
+  for (int it = 0; it < iters; ++it)
+    for (int l = 0; l < m.cfg.layers; ++l) {
+      const LayerDev& ld = m.L[l];
+      MoeArgs a;
+      a.g = ld.eg; a.u = ld.eu; a.d = ld.ed; a.sg = ld.sh_g; a.su = ld.sh_u; a.sd = ld.sh_d;
+      a.x = m.xmoe; a.pick_ids = m.pick_ids; a.pick_w = m.pick_w; a.shared_scale = m.sscale;
+      a.hmid = m.hmid; a.hmid_stride = m.hmid_stride; a.topk = m.cfg.topk; a.h = m.h;
+      a.advance_sd = nullptr; a.advance_cursor = nullptr;
+      launch_moe_gateup(a, m.stream, m.use_pdl);
+      launch_moe_down(a, m.stream, m.use_pdl);
+    }
+  SWL_CUDA(cudaEventRecord(e1, m.stream));
+  SWL_CUDA(cudaEventSynchronize(e1));
+  SWL_CUDA(cudaEventElapsedTime(ms_out, e0, e1));
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  const LayerDev& l0 = m.L[0];
+  if (bytes_per_layer)
+    *bytes_per_layer = double(m.cfg.topk) * double(qlin_bytes(l0.eg.lin) + qlin_bytes(l0.eu.lin) + qlin_bytes(l0.ed.lin)) +
+                       double(qlin_bytes(l0.sh_g) + qlin_bytes(l0.sh_u) + qlin_bytes(l0.sh_d));
+  if (launches) *launches = 2 * iters * m.cfg.layers;
+  API_END
+}
+
+int swl_kernel_gemv_affine(const uint32_t* packed, const void* scales, const void* biases, int sdtype, int out_dim,
+                           int in_dim, int group, int bits, const float* x, float* y) {
+  API_BEGIN
+  if (!packed || !scales || !biases || !x || !y) throw Error(ERR_INVALID, "null argument");
+  if (bits != 4 && bits != 8) throw Error(ERR_UNSUPPORTED, "bits must be 4 or 8");
+  if (group <= 0 || in_dim % group || group % (bits == 4 ? 32 : 16) || sdtype < 0 || sdtype > 2)
+    throw Error(ERR_UNSUPPORTED, "unsupported group size or scale dtype");
+  const int64_t wbytes = int64_t(out_dim) * in_dim * bits / 8, ns = int64_t(out_dim) * (in_dim / group);
+  const int64_t sb = sdtype == 0 ? 4 : 2;
+  std::vector<void*> bufs;
+  auto dm = [&](size_t n) { void* p = nullptr; SWL_CUDA(cudaMalloc(&p, std::max<size_t>(n, 16))); bufs.push_back(p); return p; };
+  try {
+    uint8_t* dw = (uint8_t*)dm(wbytes);
+    uint8_t* ds = (uint8_t*)dm(ns * sb);
+    uint8_t* db = (uint8_t*)dm(ns * sb);
+    float* dx = (float*)dm(size_t(in_dim) * 4);
+    float* dy = (float*)dm(size_t(out_dim) * 4);
+    SWL_CUDA(cudaMemcpy(dw, packed, wbytes, cudaMemcpyHostToDevice));
+    SWL_CUDA(cudaMemcpy(ds, scales, ns * sb, cudaMemcpyHostToDevice));
+    SWL_CUDA(cudaMemcpy(db, biases, ns * sb, cudaMemcpyHostToDevice));
+    SWL_CUDA(cudaMemcpy(dx, x, size_t(in_dim) * 4, cudaMemcpyHostToDevice));
+    GemvArgs g;
+    QLin& q = g.seg[0].lin;
+    q.w = dw; q.s = ds; q.b = db; q.out = out_dim; q.in = in_dim; q.bits = bits; q.gs = group; q.dt = sdtype;
+    q.row_bytes = int64_t(in_dim) * bits / 8; q.srow = in_dim / group;
+    if (q.row_bytes % 16) throw Error(ERR_UNSUPPORTED, "row must be a multiple of 16 bytes");
+    g.seg[0].y = dy; g.nseg = 1; g.in = in_dim; g.x = dx;
+    launch_gemv(g, 0, false);
+    SWL_CUDA(cudaDeviceSynchronize());
+    SWL_CUDA(cudaMemcpy(y, dy, size_t(out_dim) * 4, cudaMemcpyDeviceToHost));
+  } catch (...) {
+    for (void* p : bufs) cudaFree(p);
+    throw;
+  }
+  for (void* p : bufs) cudaFree(p);
+  API_END
+}
+
+}  // extern "C"
