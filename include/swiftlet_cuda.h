@@ -137,6 +137,14 @@ int swl_debug_delta_state(swl_model* model, swl_state* state, int32_t layer, flo
 int swl_bench_expert_sweep(swl_model* model, int32_t iters, float* ms_out, double* bytes_per_layer,
                            int32_t* launches_out);
 
+/* Kernel timeline: with SWL_TRACE=<records> set when the model was opened,
+ * every CTA of every decode kernel appends {tag, block, start, after the
+ * dependency wait, end} (ns, %globaltimer); tag = kind + 16 * (layer + 1)
+ * with kind 1 embed, 2 in-projection, 3 DeltaNet/attention, 4 out-projection,
+ * 5 router, 6 expert gate/up, 7 expert down, 8 lm_head. Writes the records
+ * as CSV to `path` and clears the buffer. */
+int swl_trace_dump(swl_model* model, const char* path);
+
 /* Model-free kernels on host buffers, for kernel-level parity tests:
  * y = W x for one MLX-affine matrix (sdtype 0 f32, 1 bf16, 2 f16) ... */
 int swl_kernel_gemv_affine(const uint32_t* packed, const void* scales, const void* biases, int sdtype, int out_dim,

@@ -78,6 +78,7 @@ _SIGNATURES = {
     "swl_debug_layer": (_I, [_P, _P, C.c_int32, _P, _P, _P, _P]),
     "swl_debug_delta_state": (_I, [_P, _P, C.c_int32, _P]),
     "swl_bench_expert_sweep": (_I, [_P, C.c_int32, _P, _P, _P]),
+    "swl_trace_dump": (_I, [_P, C.c_char_p]),
     "swl_kernel_gemv_affine": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
 }
 
@@ -297,6 +298,10 @@ class QwenCUDAModel:
         n = C.c_int32()
         _check(lib().swl_bench_expert_sweep(self._h, int(iters), C.byref(ms), C.byref(b), C.byref(n)))
         return ms.value, b.value, n.value
+
+    def trace_dump(self, path: str) -> None:
+        """Writes the per-block kernel timeline (needs SWL_TRACE at open)."""
+        _check(lib().swl_trace_dump(self._h, path.encode()))
 
     def debug_delta_state(self, state: DecodeState, layer: int) -> np.ndarray:
         c = self.config

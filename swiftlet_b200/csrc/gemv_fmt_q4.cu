@@ -1,0 +1,8 @@
+// Instantiates the weight-streaming kernels for one family of weight formats.
+#include "gemv_impl.cuh"
+
+namespace swl {
+SWL_INSTANTIATE_FORMAT(4, DT_BF16)
+SWL_INSTANTIATE_FORMAT(4, DT_F32)
+SWL_INSTANTIATE_FORMAT(4, DT_F16)
+}  // namespace swl

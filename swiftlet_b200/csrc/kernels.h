@@ -12,9 +12,18 @@ struct StateDev {
   int* pos;         // tokens already processed (RoPE offset, ring slot)
   float** conv;     // [layers] conv ring [conv_k][conv_dim] (slot = pos % conv_k), DeltaNet layers
   float** dstate;   // [layers] delta state [nv][dv][dk]
-  float** kc;       // [layers] K cache [max_ctx][kv_heads][head_dim], attention layers
+  float** kc;       // [layers] K cache [kv_heads][max_ctx][head_dim], attention layers
   float** vc;       // [layers] V cache
   int max_ctx;
+};
+
+// Optional per-block timeline (SWL_TRACE): each CTA appends one record of
+// {kernel tag, block, start ns, after-dependency-wait ns, end ns}.
+struct Trace {
+  unsigned long long* buf = nullptr;  // [cap][5]
+  unsigned* count = nullptr;
+  unsigned cap = 0;
+  unsigned tag = 0;
 };
 
 // Input transform applied by a GEMV prologue while staging x in shared memory.
@@ -49,6 +58,7 @@ struct GemvArgs {
   float* argmax_val = nullptr;  // scratch [gridDim] values for argmax
   int* argmax_idx = nullptr;    // scratch [gridDim] indices
   unsigned* counter = nullptr;  // last-block counter for argmax
+  Trace trace;
 };
 
 struct RouterArgs {
@@ -65,6 +75,10 @@ struct RouterArgs {
   unsigned* counter;
   int topk;
   int norm_topk;
+  const uint8_t* pool;        // expert blobs of this layer (L2 prefetch of the picks), may be null
+  int64_t pool_stride;
+  uint32_t prefetch_bytes;    // bytes per expert to prefetch (multiple of 16)
+  Trace trace;
 };
 
 struct MoeArgs {
@@ -80,6 +94,7 @@ struct MoeArgs {
   float* h;                    // residual stream (down + combine adds here)
   const StateDev* advance_sd;  // when set: ++*advance_sd->pos and ++*advance_cursor after the layer
   int* advance_cursor;
+  Trace trace;
 };
 
 struct DeltaArgs {
@@ -94,6 +109,7 @@ struct DeltaArgs {
   int rows_per_block;      // dv rows per block
   float* y;                // [nv*dv] raw recurrence output
   float* z;                // [nv*dv] gate input, de-interleaved
+  Trace trace;
 };
 
 struct AttnArgs {
@@ -106,13 +122,14 @@ struct AttnArgs {
   float rope_theta;
   int rot;
   int H, Hkv, hd;
-  int nchunks;
+  int nchunks;             // grid.y: context chunks per kv head
   int chunk_cap;           // max positions per chunk (smem sizing)
   const StateDev* sd;
   int layer;
   float* part;             // [Hkv][nchunks][G][hd + 2]
   unsigned* counters;      // [Hkv]
   float* out;              // [H * hd] gated attention output
+  Trace trace;
 };
 
 struct EmbedArgs {
@@ -122,6 +139,7 @@ struct EmbedArgs {
   float* h;
   int vocab;
   int* err;
+  Trace trace;
 };
 
 // All launches go to `stream`; `pdl` enables programmatic dependent launch.

@@ -67,7 +67,7 @@ struct StoredTensor {
 struct Model;
 
 struct State {
-  Model* model = nullptr;
+  Model* model = nullptr;  // null once the model was closed first
   int max_ctx = 0;
   int pos = 0;
   uint8_t* mem = nullptr;
@@ -112,7 +112,8 @@ struct Model {
   int *pick_ids = nullptr, *tokens = nullptr, *cursor = nullptr, *err = nullptr, *amax_i = nullptr, *greedy = nullptr;
   unsigned *ctr_router = nullptr, *ctr_attn = nullptr, *ctr_amax = nullptr;
   StateDev* cur = nullptr;
-  int hmid_stride = 0, max_tokens = 0, attn_chunks = 32, chunk_cap = 0, max_ctx_cap = 0;
+  int hmid_stride = 0, max_tokens = 0, attn_chunks = 64, chunk_cap = 0, max_ctx_cap = 0;
+  int64_t payload = 0;  // bytes of one expert blob before the stride padding
   int64_t hits = 0, misses = 0;
 
   cudaGraphExec_t g_body = nullptr, g_head = nullptr, g_head_amax = nullptr;
@@ -121,6 +122,9 @@ struct Model {
   float* h_logits = nullptr;
   int* h_tokens = nullptr;
   int h_tokens_cap = 0;
+  std::vector<State*> live;  // states created on this model and not yet freed
+  Trace trace;               // SWL_TRACE=<records>: per-block kernel timeline
+  Trace tagged(unsigned tag) const { Trace t = trace; t.tag = tag; return t; }
 
   ~Model();
   void open(const std::string& d, double pool_gb, int dev);
@@ -154,6 +158,11 @@ struct Model {
 Model::~Model() {
   drop_graphs();
   if (stream) cudaStreamSynchronize(stream);
+  for (State* s : live) {  // a caller that frees states after the model only releases the handle
+    cudaFree(s->mem);
+    s->mem = nullptr;
+    s->model = nullptr;
+  }
   for (void* p : allocs) cudaFree(p);
   if (h_logits) cudaFreeHost(h_logits);
   if (h_tokens) cudaFreeHost(h_tokens);
@@ -342,6 +351,8 @@ ExpertProj Model::expert_proj(uint8_t* pool_l, const std::string& proj, int out,
 
 void Model::upload_experts() {
   const int64_t E = cfg.experts, per_layer = E * stride;
+  payload = 0;
+  for (auto& s : sections) payload = std::max(payload, s.offset + s.size);
   if (mode == SYNTH) {
     for (int l = 0; l < cfg.layers; ++l) {
       uint8_t* pl = pool + int64_t(l) * per_layer;
@@ -532,9 +543,18 @@ void Model::open(const std::string& d, double pool_gb, int dev) {
   SWL_CUDA(cudaSetDevice(dev));
   SWL_CUDA(cudaStreamCreateWithFlags(&own, cudaStreamNonBlocking));
   stream = own;
+  if (const char* tr = getenv("SWL_TRACE")) {
+    const long cap = atol(tr);
+    if (cap > 0) {
+      trace.cap = unsigned(cap);
+      trace.buf = reinterpret_cast<unsigned long long*>(dmalloc(size_t(cap) * 5 * 8));
+      trace.count = reinterpret_cast<unsigned*>(dmalloc(4));
+      SWL_CUDA(cudaMemset(trace.count, 0, 4));
+    }
+  }
   const char* mc = getenv("SWL_MAX_CTX");
   max_ctx_cap = mc ? std::max(16, atoi(mc)) : 32768;
-  chunk_cap = (max_ctx_cap + attn_chunks - 1) / attn_chunks;
+  chunk_cap = std::max((max_ctx_cap + attn_chunks - 1) / attn_chunks, attn_chunks);
   plan_sections();
   pool_size = size_t(cfg.layers) * cfg.experts * stride;
   if (pool_gb > 0 && double(pool_size) > pool_gb * 1073741824.0)
@@ -569,17 +589,21 @@ void Model::enqueue_layer(int l, cudaStream_t st, bool advance) {
   for (int s = 0; s < ld.n_in; ++s) { g.seg[s].lin = ld.in_lin[s]; g.seg[s].y = ld.in_y[s]; }
   g.nseg = ld.n_in; g.in = c.hidden; g.prologue = PRO_RMSNORM; g.epilogue = EPI_STORE;
   g.x = h; g.aux = ld.in_norm; g.eps = float(c.eps);
+  const unsigned lt = 16u * unsigned(l + 1);
+  g.trace = tagged(lt + 2);
   launch_gemv(g, st, pdl);
   if (ld.delta) {
     DeltaArgs d;
     d.proj = proj; d.split = c.split_layout; d.nk = c.nk; d.nv = c.nv; d.dk = c.dk; d.dv = c.dv;
     d.conv_k = c.conv_k; d.conv_dim = c.conv_dim(); d.conv_w = ld.conv_w; d.a_log = ld.a_log; d.dt_bias = ld.dt_bias;
     d.sd = cur; d.layer = l; d.rows_per_block = std::min(c.dv, 32); d.y = yv; d.z = zv;
+    d.trace = tagged(lt + 3);
     launch_delta(d, st, pdl);
     GemvArgs o;
     o.seg[0].lin = ld.out_lin; o.seg[0].y = h; o.nseg = 1; o.in = c.value_dim();
     o.prologue = PRO_GATEDNORM; o.epilogue = EPI_RESIDUAL; o.x = yv; o.aux = zv; o.aux2 = ld.dnorm;
     o.head_dim = c.dv; o.eps = float(c.eps);
+    o.trace = tagged(lt + 4);
     launch_gemv(o, st, pdl);
   } else {
     AttnArgs a;
@@ -587,29 +611,36 @@ void Model::enqueue_layer(int l, cudaStream_t st, bool advance) {
     a.eps = float(c.eps); a.rope_theta = float(c.rope_theta); a.rot = c.rot_dims();
     a.H = c.heads; a.Hkv = c.kv_heads; a.hd = c.head_dim; a.nchunks = attn_chunks; a.chunk_cap = chunk_cap;
     a.sd = cur; a.layer = l; a.part = part; a.counters = ctr_attn; a.out = att;
+    a.trace = tagged(lt + 3);
     launch_attn(a, st, pdl);
     GemvArgs o;
     o.seg[0].lin = ld.out_lin; o.seg[0].y = h; o.nseg = 1; o.in = c.heads * c.head_dim;
     o.prologue = PRO_COPY; o.epilogue = EPI_RESIDUAL; o.x = att;
+    o.trace = tagged(lt + 4);
     launch_gemv(o, st, pdl);
   }
   RouterArgs r;
   r.gate = ld.router; r.sgate = ld.sgate; r.h = h; r.norm_w = ld.post_norm; r.eps = float(c.eps);
   r.x_out = xmoe; r.logits = rlogits; r.pick_ids = pick_ids; r.pick_w = pick_w; r.shared_scale = sscale;
   r.counter = ctr_router; r.topk = c.topk; r.norm_topk = c.norm_topk;
+  r.pool = nullptr; r.pool_stride = stride; r.prefetch_bytes = 0;
+  r.trace = tagged(lt + 5);
   launch_router(r, c.experts, st, pdl);
   MoeArgs m;
   m.g = ld.eg; m.u = ld.eu; m.d = ld.ed; m.sg = ld.sh_g; m.su = ld.sh_u; m.sd = ld.sh_d;
   m.x = xmoe; m.pick_ids = pick_ids; m.pick_w = pick_w; m.shared_scale = sscale;
   m.hmid = hmid; m.hmid_stride = hmid_stride; m.topk = c.topk; m.h = h;
   m.advance_sd = advance ? cur : nullptr; m.advance_cursor = cursor;
+  m.trace = tagged(lt + 6);
   launch_moe_gateup(m, st, pdl);
+  m.trace = tagged(lt + 7);
   launch_moe_down(m, st, pdl);
 }
 
 void Model::enqueue_body(cudaStream_t st) {
   EmbedArgs e;
   e.table = embed; e.tokens = tokens; e.cursor = cursor; e.h = h; e.vocab = cfg.vocab; e.err = err;
+  e.trace = tagged(1);
   launch_embed(e, cfg.hidden, st, use_pdl);
   for (int l = 0; l < cfg.layers; ++l) enqueue_layer(l, st, l == cfg.layers - 1);
 }
@@ -619,6 +650,7 @@ void Model::enqueue_head(cudaStream_t st, bool amax) {
   g.seg[0].lin = lm_head; g.seg[0].y = logits; g.nseg = 1; g.in = cfg.hidden;
   g.prologue = PRO_RMSNORM; g.epilogue = EPI_STORE; g.x = h; g.aux = final_norm; g.eps = float(cfg.eps);
   if (amax) { g.argmax_out = greedy; g.argmax_val = amax_v; g.argmax_idx = amax_i; g.counter = ctr_amax; }
+  g.trace = tagged(8);
   launch_gemv(g, st, use_pdl);
 }
 
@@ -721,6 +753,7 @@ using namespace swl;
 struct swl_model { Model m; };
 struct swl_state { State s; };
 
+
 // A failed call in a destructor path (or in another library sharing the
 // context) leaves a non-sticky "last error" behind; drop it at entry so it
 // can never be attributed to this call.
@@ -783,6 +816,7 @@ int swl_state_new(swl_model* model, int32_t max_ctx, swl_state** out) {
   swl_state* w = new swl_state();
   w->s = *s;
   delete s;
+  model->m.live.push_back(&w->s);
   *out = w;
   API_END
 }
@@ -790,9 +824,12 @@ int swl_state_new(swl_model* model, int32_t max_ctx, swl_state** out) {
 int swl_state_free(swl_state* state) {
   API_BEGIN
   if (!state) throw Error(ERR_INVALID, "null state");
-  cudaSetDevice(state->s.model->device);
-  cudaStreamSynchronize(state->s.model->stream);
-  cudaFree(state->s.mem);
+  if (Model* m = state->s.model) {
+    cudaSetDevice(m->device);
+    cudaStreamSynchronize(m->stream);
+    cudaFree(state->s.mem);
+    m->live.erase(std::remove(m->live.begin(), m->live.end(), &state->s), m->live.end());
+  }
   delete state;
   API_END
 }
@@ -1032,6 +1069,28 @@ int swl_bench_expert_sweep(swl_model* model, int32_t iters, float* ms_out, doubl
     *bytes_per_layer = double(m.cfg.topk) * double(qlin_bytes(l0.eg.lin) + qlin_bytes(l0.eu.lin) + qlin_bytes(l0.ed.lin)) +
                        double(qlin_bytes(l0.sh_g) + qlin_bytes(l0.sh_u) + qlin_bytes(l0.sh_d));
   if (launches) *launches = 2 * iters * m.cfg.layers;
+  API_END
+}
+
+int swl_trace_dump(swl_model* model, const char* path) {
+  API_BEGIN
+  if (!model || !path) throw Error(ERR_INVALID, "null argument");
+  Model& m = model->m;
+  if (!m.trace.buf) throw Error(ERR_INVALID, "tracing is off (set SWL_TRACE=<records> before opening the model)");
+  SWL_CUDA(cudaSetDevice(m.device));
+  SWL_CUDA(cudaStreamSynchronize(m.stream));
+  unsigned n = 0;
+  SWL_CUDA(cudaMemcpy(&n, m.trace.count, 4, cudaMemcpyDeviceToHost));
+  n = std::min(n, m.trace.cap);
+  std::vector<unsigned long long> buf(size_t(n) * 5);
+  if (n) SWL_CUDA(cudaMemcpy(buf.data(), m.trace.buf, buf.size() * 8, cudaMemcpyDeviceToHost));
+  FILE* f = fopen(path, "w");
+  if (!f) throw Error(ERR_IO, std::string("cannot write ") + path);
+  fprintf(f, "tag,block,start_ns,waited_ns,end_ns\n");
+  for (unsigned i = 0; i < n; ++i)
+    fprintf(f, "%llu,%llu,%llu,%llu,%llu\n", buf[5 * i], buf[5 * i + 1], buf[5 * i + 2], buf[5 * i + 3], buf[5 * i + 4]);
+  fclose(f);
+  SWL_CUDA(cudaMemset(m.trace.count, 0, 4));
   API_END
 }
 
