@@ -149,6 +149,13 @@ int swl_trace_dump(swl_model* model, const char* path);
  * y = W x for one MLX-affine matrix (sdtype 0 f32, 1 bf16, 2 f16) ... */
 int swl_kernel_gemv_affine(const uint32_t* packed, const void* scales, const void* biases, int sdtype, int out_dim,
                            int in_dim, int group, int bits, const float* x, float* y);
+/* ... and one expert's SwiGLU, y = down(silu(gate x) * (up x))
+ * (QwenCPUModel.swift:552-555), through the fused expert kernels; gate/up are
+ * [inter, hidden], down [hidden, inter], all with the same bits/group/sdtype. */
+int swl_kernel_expert_swiglu(const uint32_t* gate_w, const void* gate_s, const void* gate_b, const uint32_t* up_w,
+                             const void* up_s, const void* up_b, const uint32_t* down_w, const void* down_s,
+                             const void* down_b, int sdtype, int bits, int group, int hidden, int inter, const float* x,
+                             float* y);
 
 #ifdef __cplusplus
 }

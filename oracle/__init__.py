@@ -56,6 +56,7 @@ def lib():
         L.orc_set_threads.argtypes = [I]
         L.orc_gemv_affine.argtypes = [C.POINTER(C.c_uint32), P, P, I, I, I, I, I, fp, fp]
         L.orc_gated_delta.argtypes = [fp, fp, fp, fp, fp, fp, fp, I, I, I, I, I]
+        L.orc_expert_swiglu.argtypes = [P] * 9 + [I, I, I, I, I, fp, fp]
         _lib = L
     return _lib
 
@@ -204,6 +205,16 @@ def gemv_affine(packed, scales, biases, out_dim, in_dim, group, bits, x):
     y = np.zeros(out_dim, np.float32)
     lib().orc_gemv_affine(packed.ctypes.data_as(C.POINTER(C.c_uint32)), scales.ctypes.data, biases.ctypes.data, sd,
                           out_dim, in_dim, group, bits, _f(x), _f(y))
+    return y
+
+
+def expert_swiglu(gate, up, down, D, I, group, bits, x):
+    """y = down(silu(gate x) * up x) for one MLX-affine expert; each matrix is (packed, scales, biases)."""
+    arrs = [np.ascontiguousarray(a) for m in (gate, up, down) for a in m]
+    sd = {np.dtype(np.float32): 0, np.dtype(np.uint16): 1, np.dtype(np.float16): 2}[arrs[1].dtype]
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.zeros(D, np.float32)
+    lib().orc_expert_swiglu(*[a.ctypes.data for a in arrs], sd, bits, group, D, I, _f(x), _f(y))
     return y
 
 

@@ -1235,6 +1235,18 @@ int orc_gemv_affine(const uint32_t* packed, const void* scales, const void* bias
   return 0;
 }
 
+// One expert's SwiGLU, y = down (silu(gate x) * (up x)), on MLX-affine
+// matrices (QwenCPUModel.swift:552-555). gate/up [I, D], down [D, I].
+int orc_expert_swiglu(const uint32_t* gw, const void* gs_, const void* gb, const uint32_t* uw, const void* us,
+                      const void* ub, const uint32_t* dw, const void* ds, const void* db, int sdtype, int bits,
+                      int group, int D, int I, const float* x, float* y) {
+  std::vector<float> g(I), u(I);
+  orc_gemv_affine(gw, gs_, gb, sdtype, I, D, group, bits, x, g.data());
+  orc_gemv_affine(uw, us, ub, sdtype, I, D, group, bits, x, u.data());
+  for (int i = 0; i < I; ++i) g[i] = siluf_(g[i]) * u[i];
+  return orc_gemv_affine(dw, ds, db, sdtype, D, I, group, bits, g.data(), y);
+}
+
 // Gated delta rule over T steps (MetalKernelTests.swift:194-220; gated_delta.py ops path).
 // q,k [T,Hk,Dk], v [T,Hv,Dv], g,beta [T,Hv], state [Hv,Dv,Dk] in/out, y [T,Hv,Dv].
 int orc_gated_delta(const float* q, const float* k, const float* v, const float* g, const float* beta, float* state,

@@ -80,6 +80,7 @@ _SIGNATURES = {
     "swl_bench_expert_sweep": (_I, [_P, C.c_int32, _P, _P, _P]),
     "swl_trace_dump": (_I, [_P, C.c_char_p]),
     "swl_kernel_gemv_affine": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
+    "swl_kernel_expert_swiglu": (_I, [_P] * 9 + [_I, _I, _I, _I, _I, _P, _P]),
 }
 
 _lib = None
@@ -320,6 +321,16 @@ def gemv_affine(packed, scales, biases, out_dim: int, in_dim: int, group: int, b
     y = np.empty(out_dim, np.float32)
     _check(lib().swl_kernel_gemv_affine(_ptr(packed), _ptr(scales), _ptr(biases), sd, out_dim, in_dim, group, bits,
                                         _ptr(x), _ptr(y)))
+    return y
+
+
+def expert_swiglu(gate, up, down, hidden: int, inter: int, group: int, bits: int, x) -> np.ndarray:
+    """One expert's SwiGLU on the GPU; each matrix is (packed uint32, scales, biases)."""
+    arrs = [np.ascontiguousarray(a) for m in (gate, up, down) for a in m]
+    sd = {np.dtype(np.float32): 0, np.dtype(np.uint16): 1, np.dtype(np.float16): 2}[arrs[1].dtype]
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.empty(hidden, np.float32)
+    _check(lib().swl_kernel_expert_swiglu(*[_ptr(a) for a in arrs], sd, bits, group, hidden, inter, _ptr(x), _ptr(y)))
     return y
 
 

@@ -1094,6 +1094,68 @@ int swl_trace_dump(swl_model* model, const char* path) {
   API_END
 }
 
+// Device-side MLX-affine matrix from host buffers (helper of the kernel-level entry points).
+static QLin upload_affine(std::vector<void*>& bufs, const void* w, const void* sc, const void* bi, int sdtype, int bits,
+                          int group, int out, int in) {
+  auto dm = [&](size_t n) { void* p = nullptr; SWL_CUDA(cudaMalloc(&p, std::max<size_t>(n, 16))); bufs.push_back(p); return p; };
+  QLin q;
+  q.out = out; q.in = in; q.bits = bits; q.gs = group; q.dt = sdtype;
+  q.row_bytes = int64_t(in) * bits / 8; q.srow = in / group;
+  const int64_t sb = sdtype == 0 ? 4 : 2, ns = int64_t(out) * q.srow;
+  uint8_t* dw = (uint8_t*)dm(size_t(out) * q.row_bytes);
+  uint8_t* ds = (uint8_t*)dm(size_t(ns * sb));
+  uint8_t* db = (uint8_t*)dm(size_t(ns * sb));
+  SWL_CUDA(cudaMemcpy(dw, w, size_t(out) * q.row_bytes, cudaMemcpyHostToDevice));
+  SWL_CUDA(cudaMemcpy(ds, sc, size_t(ns * sb), cudaMemcpyHostToDevice));
+  SWL_CUDA(cudaMemcpy(db, bi, size_t(ns * sb), cudaMemcpyHostToDevice));
+  q.w = dw; q.s = ds; q.b = db;
+  return q;
+}
+
+int swl_kernel_expert_swiglu(const uint32_t* gate_w, const void* gate_s, const void* gate_b, const uint32_t* up_w,
+                             const void* up_s, const void* up_b, const uint32_t* down_w, const void* down_s,
+                             const void* down_b, int sdtype, int bits, int group, int hidden, int inter, const float* x,
+                             float* y) {
+  API_BEGIN
+  if (!gate_w || !up_w || !down_w || !x || !y) throw Error(ERR_INVALID, "null argument");
+  if (bits != 4 && bits != 8) throw Error(ERR_UNSUPPORTED, "bits must be 4 or 8");
+  if (group <= 0 || hidden % group || inter % group || group % (bits == 4 ? 32 : 16) || sdtype < 0 || sdtype > 2)
+    throw Error(ERR_UNSUPPORTED, "unsupported group size or scale dtype");
+  std::vector<void*> bufs;
+  try {
+    MoeArgs m;
+    m.sg = upload_affine(bufs, gate_w, gate_s, gate_b, sdtype, bits, group, inter, hidden);
+    m.su = upload_affine(bufs, up_w, up_s, up_b, sdtype, bits, group, inter, hidden);
+    m.sd = upload_affine(bufs, down_w, down_s, down_b, sdtype, bits, group, hidden, inter);
+    if (m.sg.row_bytes % 16 || m.sd.row_bytes % 16) throw Error(ERR_UNSUPPORTED, "rows must be multiples of 16 bytes");
+    m.g.lin = m.sg; m.u.lin = m.su; m.d.lin = m.sd;  // geometry only: no routed experts
+    m.topk = 0;
+    m.hmid_stride = (inter + 31) / 32 * 32;
+    float* scratch = nullptr;
+    SWL_CUDA(cudaMalloc(&scratch, size_t(m.hmid_stride + 4) * 4));
+    bufs.push_back(scratch);
+    float* dx = nullptr;
+    float* dy = nullptr;
+    SWL_CUDA(cudaMalloc(&dx, size_t(hidden) * 4)); bufs.push_back(dx);
+    SWL_CUDA(cudaMalloc(&dy, size_t(hidden) * 4)); bufs.push_back(dy);
+    const float one = 1.f;
+    SWL_CUDA(cudaMemcpy(scratch + m.hmid_stride, &one, 4, cudaMemcpyHostToDevice));
+    SWL_CUDA(cudaMemcpy(dx, x, size_t(hidden) * 4, cudaMemcpyHostToDevice));
+    SWL_CUDA(cudaMemset(dy, 0, size_t(hidden) * 4));
+    m.x = dx; m.h = dy; m.hmid = scratch; m.shared_scale = scratch + m.hmid_stride;
+    m.pick_ids = nullptr; m.pick_w = nullptr; m.advance_sd = nullptr; m.advance_cursor = nullptr;
+    launch_moe_gateup(m, 0, false);
+    launch_moe_down(m, 0, false);
+    SWL_CUDA(cudaDeviceSynchronize());
+    SWL_CUDA(cudaMemcpy(y, dy, size_t(hidden) * 4, cudaMemcpyDeviceToHost));
+  } catch (...) {
+    for (void* p : bufs) cudaFree(p);
+    throw;
+  }
+  for (void* p : bufs) cudaFree(p);
+  API_END
+}
+
 int swl_kernel_gemv_affine(const uint32_t* packed, const void* scales, const void* biases, int sdtype, int out_dim,
                            int in_dim, int group, int bits, const float* x, float* y) {
   API_BEGIN

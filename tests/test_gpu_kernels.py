@@ -41,3 +41,26 @@ def test_gemv_matches_oracle_on_decode_shapes(bits, out, inn, group):
     y = swl.gemv_affine(packed, scales, biases, out, inn, group, bits, x)
     scale = np.abs(ref).max() + 1e-6
     assert np.abs(y - ref).max() / scale < 1e-5
+
+
+def random_affine(rng, out, inn, group, bits, sdtype="bf16"):
+    per = 32 // bits
+    packed = rng.integers(0, 2**32, size=out * inn // per, dtype=np.uint64).astype(np.uint32)
+    s = np.abs(rng.normal(0, 0.01, out * inn // group)).astype(np.float32)
+    b = rng.normal(0, 0.01, out * inn // group).astype(np.float32)
+    if sdtype == "bf16":
+        s, b = _bf16(s), _bf16(b)
+    return packed, s, b
+
+
+@pytest.mark.parametrize("bits,hidden,inter,group,sdtype", [(4, 2048, 512, 64, "bf16"), (8, 2048, 512, 64, "bf16"),
+                                                            (4, 64, 32, 32, "f32"), (4, 1024, 256, 128, "bf16")])
+def test_expert_swiglu_matches_oracle(bits, hidden, inter, group, sdtype):
+    rng = np.random.default_rng(hidden + inter + bits)
+    gate = random_affine(rng, inter, hidden, group, bits, sdtype)
+    up = random_affine(rng, inter, hidden, group, bits, sdtype)
+    down = random_affine(rng, hidden, inter, group, bits, sdtype)
+    x = rng.normal(0, 1, hidden).astype(np.float32)
+    ref = oracle.expert_swiglu(gate, up, down, hidden, inter, group, bits, x)
+    y = swl.expert_swiglu(gate, up, down, hidden, inter, group, bits, x)
+    assert np.abs(y - ref).max() / (np.abs(ref).max() + 1e-6) < 1e-5
