@@ -157,6 +157,35 @@ int swl_kernel_expert_swiglu(const uint32_t* gate_w, const void* gate_s, const v
                              const void* down_b, int sdtype, int bits, int group, int hidden, int inter, const float* x,
                              float* y);
 
+/* ---- allocation-free entry point (no counterpart in the reference) ----- */
+
+/* A device-resident MLX-affine matrix: uint32 words packed low bits first,
+ * [rows][cols * bits / 32] (16-byte aligned rows and pointer), and one scale
+ * and one bias per `group` inputs, [rows][cols / group]. */
+typedef struct swl_affine_matrix {
+  const void* weight;
+  const void* scales;
+  const void* biases;
+  int32_t rows, cols, bits, group;
+  int32_t scale_dtype; /* 0 f32, 1 bf16, 2 f16 */
+} swl_affine_matrix;
+
+/* One expert's SwiGLU, y = down(silu(gate x) * (up x)), with device-resident
+ * x [hidden] (16-byte aligned) and y [hidden], that allocates no device
+ * memory: for callers that cannot call cudaMalloc (a host runtime that owns
+ * all device memory in its own arena, a plugin that must not grow the
+ * process's device footprint). No counterpart in the reference.
+ * The intermediate vector lives in one library-wide __device__ array that
+ * holds at most 16384 values (moe_intermediate_size); a larger expert fails
+ * with SWL_ERR_CAPACITY. Every GPU that loads the library keeps that array
+ * (64 KiB) until exit, and every call shares it: calls that overlap on the
+ * GPU (different streams without ordering) race on it. Work is queued on
+ * `stream` (a cudaStream_t; NULL = legacy default stream) and not waited
+ * for. The first call on a device looks up the array's device address
+ * (host-side set-up); make that first call before any stream capture. */
+int swl_expert_swiglu_noalloc(const swl_affine_matrix* gate, const swl_affine_matrix* up,
+                              const swl_affine_matrix* down, const float* x, float* y, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

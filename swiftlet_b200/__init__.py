@@ -52,6 +52,12 @@ class swl_config(C.Structure):
         ("rope_theta", C.c_double), ("partial_rotary_factor", C.c_double), ("rms_norm_eps", C.c_double)]
 
 
+class swl_affine_matrix(C.Structure):
+    """A device-resident MLX-affine matrix (see include/swiftlet_cuda.h)."""
+    _fields_ = [("weight", C.c_void_p), ("scales", C.c_void_p), ("biases", C.c_void_p), ("rows", C.c_int32),
+                ("cols", C.c_int32), ("bits", C.c_int32), ("group", C.c_int32), ("scale_dtype", C.c_int32)]
+
+
 class swl_pool_info(C.Structure):
     _fields_ = [(n, C.c_int64) for n in (
         "expert_stride", "slot_count", "allocated_slots", "hits", "misses", "resident_bytes")]
@@ -81,6 +87,7 @@ _SIGNATURES = {
     "swl_trace_dump": (_I, [_P, C.c_char_p]),
     "swl_kernel_gemv_affine": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
     "swl_kernel_expert_swiglu": (_I, [_P] * 9 + [_I, _I, _I, _I, _I, _P, _P]),
+    "swl_expert_swiglu_noalloc": (_I, [C.POINTER(swl_affine_matrix)] * 3 + [_P, _P, _P]),
 }
 
 _lib = None
@@ -332,6 +339,13 @@ def expert_swiglu(gate, up, down, hidden: int, inter: int, group: int, bits: int
     y = np.empty(hidden, np.float32)
     _check(lib().swl_kernel_expert_swiglu(*[_ptr(a) for a in arrs], sd, bits, group, hidden, inter, _ptr(x), _ptr(y)))
     return y
+
+
+def expert_swiglu_noalloc(gate: swl_affine_matrix, up: swl_affine_matrix, down: swl_affine_matrix, d_x: int,
+                          d_y: int, stream: int | None = None) -> None:
+    """Allocation-free expert SwiGLU on device buffers (queued on `stream`, not waited for)."""
+    _check(lib().swl_expert_swiglu_noalloc(C.byref(gate), C.byref(up), C.byref(down), C.c_void_p(d_x),
+                                           C.c_void_p(d_y), C.c_void_p(stream or None)))
 
 
 class TextGenerator:

@@ -30,6 +30,9 @@ struct Error : std::runtime_error {
   Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
 };
 
+// Message returned by swl_last_error() on the calling thread.
+void set_last_error(const std::string& message);
+
 #define SWL_CUDA(x)                                                                              \
   do {                                                                                           \
     cudaError_t e_ = (x);                                                                        \

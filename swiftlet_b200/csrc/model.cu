@@ -23,6 +23,7 @@
 namespace swl {
 
 static thread_local std::string g_error;
+void set_last_error(const std::string& message) { g_error = message; }
 
 static float bf16f(uint16_t u) { uint32_t v = uint32_t(u) << 16; float f; memcpy(&f, &v, 4); return f; }
 static float f16f(uint16_t h) {
