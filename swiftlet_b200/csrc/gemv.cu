@@ -5,8 +5,10 @@
 // every CTA is resident at once and the next kernel (programmatic dependent
 // launch) can start on the rest of each SM.
 #include <algorithm>
+#include <cstdlib>
 
 #include "kernels.h"
+#include "slice.h"
 
 namespace swl {
 
@@ -28,6 +30,18 @@ template <int B, int D>
 void gateup_fmt(const MoeArgs&, int, int, int, int, int, int, int, int, size_t, cudaStream_t, bool);
 template <int B, int D>
 void down_fmt(const MoeArgs&, int, int, int, int, int, int, size_t, cudaStream_t, bool);
+template <int B, int D>
+void sgemv_fmt(const GemvArgs&, const SliceTab&, const RouterTail&, int, int, size_t, cudaStream_t, bool);
+template <int B, int D>
+void sgateup_fmt(const MoeArgs&, const SliceTab&, int, size_t, cudaStream_t, bool);
+template <int B, int D>
+void sdown_fmt(const MoeArgs&, const SliceTab&, int, size_t, cudaStream_t, bool);
+template <int B, int D>
+void igemv_fmt(const GemvArgs&, const SliceTab&, const RouterTail&, int, size_t, cudaStream_t, bool);
+template <int B, int D>
+void igateup_fmt(const MoeArgs&, const SliceTab&, int, size_t, cudaStream_t, bool);
+template <int B, int D>
+void idown_fmt(const MoeArgs&, const SliceTab&, int, size_t, cudaStream_t, bool);
 
 constexpr int GT = 128;
 static constexpr int kBlocksPerSm = 2;
@@ -96,6 +110,18 @@ static int grid_for(int tasks, int spw) {
     else throw Error(ERR_UNSUPPORTED, "unsupported weight format");      \
   } while (0)
 
+#define SWL_DISPATCH_IMMA(BITS_, DT_, CALL)                              \
+  do {                                                                   \
+    const int b_ = (BITS_), d_ = (DT_);                                  \
+    if (b_ == 4 && d_ == DT_BF16) CALL(4, DT_BF16);                      \
+    else if (b_ == 4 && d_ == DT_F32) CALL(4, DT_F32);                   \
+    else if (b_ == 4 && d_ == DT_F16) CALL(4, DT_F16);                   \
+    else if (b_ == 8 && d_ == DT_BF16) CALL(8, DT_BF16);                 \
+    else if (b_ == 8 && d_ == DT_F32) CALL(8, DT_F32);                   \
+    else if (b_ == 8 && d_ == DT_F16) CALL(8, DT_F16);                   \
+    else throw Error(ERR_UNSUPPORTED, "unsupported weight format");      \
+  } while (0)
+
 static SegTab make_tab(const QLin* lins, float* const* ys, int n, int R) {
   SegTab T = {};
   T.nseg = n;
@@ -106,6 +132,263 @@ static SegTab make_tab(const QLin* lins, float* const* ys, int n, int R) {
     T.task0[s + 1] = T.task0[s] + (s < n ? (l.out + R - 1) / R : 0);
   }
   return T;
+}
+
+// ------------------------------------------------------ slice planning --
+// Shared memory per slice CTA: at most about half an SM, so that the CTA of
+// the next kernel (programmatic dependent launch) fits beside it and copies
+// its weights while this one runs.
+static constexpr size_t kSliceSmem = 110 * 1024;
+
+static bool slice_enabled() {
+  static const int on = std::getenv("SWL_LEGACY_GEMV") ? 0 : 1;  // diagnostics: the register-streaming kernels
+  return on != 0;
+}
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+static int scale_bytes(int dt) { return dt == DT_F32 ? 4 : 2; }
+
+// Formats and layouts the slice kernels take: 16-byte aligned rows, scale rows
+// and base pointers (bulk copies), inputs of at most 4096 values (staging
+// registers), power-of-two groups.
+static bool slice_fmt_ok(const QLin& l) {
+  if (l.bits != 0 && l.bits != 4 && l.bits != 8) return false;
+  if (l.row_bytes % 16 || !aligned16(l.w) || l.in > 4096 || l.in % 32) return false;
+  if (l.bits) {
+    if ((l.srow * scale_bytes(l.dt)) % 16 || !aligned16(l.s) || !aligned16(l.b)) return false;
+    if (l.gs <= 0 || (l.gs & (l.gs - 1))) return false;
+  }
+  return true;
+}
+static int row_total(const QLin& l) {
+  return int(l.row_bytes) + (l.bits ? 2 * int(l.srow) * scale_bytes(l.dt) : 0);
+}
+// Lanes per row, K windows and rows per tile for R rows per sub-warp.
+static void slice_geom(const QLin& l, int R, SliceTab& T) {
+  const int cpl = 64 / wpc_of(l.bits, l.dt), nch = int(l.row_bytes >> 4);
+  int lpr = 1;
+  while (lpr < 32 && lpr * cpl < nch) lpr <<= 1;
+  T.LPR = lpr;
+  T.W = std::max(1, (nch + 32 * cpl - 1) / (32 * cpl));
+  T.TR = (SL_CW / T.W) * (32 / lpr) * R;
+  T.rb = int(l.row_bytes);
+  T.srow = l.bits ? int(l.srow) : 0;
+  T.gs_shift = gs_shift_of(l);
+}
+// Lays out [ring | xs | cs | red | part | raw | barriers]; returns the bytes.
+static size_t slice_layout(SliceTab& T, int xs_f, int cs_f, int part_f, int raw_f) {
+  auto al = [](size_t v, size_t a) { return (v + a - 1) / a * a; };
+  size_t off = size_t(T.S) * T.slot;
+  off = al(off, 16); T.off_xs = int(off); off += size_t(xs_f) * 4;
+  off = al(off, 16); T.off_cs = int(off); off += size_t(cs_f) * 4;
+  off = al(off, 16); T.off_red = int(off); off += SL_RED * 4;
+  off = al(off, 16); T.off_part = int(off); off += size_t(part_f) * 4;
+  off = al(off, 16); T.off_raw = int(off); off += size_t(raw_f) * 4;
+  off = al(off, 8); T.off_bar = int(off); off += size_t(2 * T.S) * 8;
+  return off;
+}
+// Ring slots: as many tiles as the CTA has, within the shared-memory budget.
+static bool slice_ring(SliceTab& T, int max_tiles, int xs_f, int cs_f, int part_f, int raw_f, size_t& smem) {
+  T.S = 0;
+  const size_t stage = slice_layout(T, xs_f, cs_f, part_f, raw_f);
+  if (stage + size_t(T.slot) + 16 > kSliceSmem) return false;
+  const int fit = int((kSliceSmem - stage - 16) / (size_t(T.slot) + 16));
+  T.S = std::max(1, std::min({max_tiles, fit, 32}));
+  smem = slice_layout(T, xs_f, cs_f, part_f, raw_f);
+  return smem <= kSliceSmem;
+}
+
+// Dense GEMV over up to four same-format segments; R = rows per sub-warp and tile.
+static bool plan_dense(const QLin* lins, float* const* ys, int nseg, int in, int prologue, int head_dim,
+                       const float* x, const float* aux, const float* aux2, const float* x_out, int* status,
+                       SliceTab& T, int& R, int& grid, size_t& smem) {
+  if (!slice_enabled()) return false;
+  const QLin& l0 = lins[0];
+  for (int s = 0; s < nseg; ++s) if (!slice_fmt_ok(lins[s]) || lins[s].in != in) return false;
+  if (prologue == PRO_GATEDNORM && (head_dim <= 0 || head_dim % 32)) return false;
+  if (!aligned16(x) || !aligned16(aux) || !aligned16(aux2) || !aligned16(x_out)) return false;
+  T = SliceTab{};
+  slice_geom(l0, 1, T);
+  R = T.LPR >= 4 ? 4 : 1;
+  slice_geom(l0, R, T);
+  T.nseg = nseg;
+  T.cum[0] = 0;
+  for (int s = 0; s < 4; ++s) {
+    const int k = s < nseg ? s : 0;
+    T.w[s] = lins[k].w; T.s[s] = lins[k].s; T.b[s] = lins[k].b; T.y[s] = ys[k];
+    T.cum[s + 1] = T.cum[s] + (s < nseg ? lins[s].out : 0);
+  }
+  T.total = T.cum[nseg];
+  if (T.total <= 0) return false;
+  T.rpc = std::max((T.total + sm_count() - 1) / sm_count(), T.TR);
+  grid = (T.total + T.rpc - 1) / T.rpc;
+  T.slot = T.TR * row_total(l0);
+  const int max_tiles = (T.rpc + T.TR - 1) / T.TR + nseg - 1;
+  const int wpc = wpc_of(l0.bits, l0.dt);
+  T.status = status;
+  return slice_ring(T, max_tiles, in, in / wpc + 4, T.W > 1 ? T.W * T.rpc : 0, in, smem);
+}
+
+// ------------------------------------------- integer tensor-core planning --
+// 4/8-bit weights with groups of >= 32 take the mma.sync (u8 x s8) kernels of
+// imma_impl.cuh; slots hold rows at a 16-byte padded pitch.
+static bool imma_enabled() {
+  static const int on = std::getenv("SWL_NO_IMMA") ? 0 : 1;  // diagnostics: the f32 slice kernels
+  return on != 0;
+}
+static bool imma_fmt_ok(const QLin& l) {
+  return slice_fmt_ok(l) && (l.bits == 4 || l.bits == 8) && l.gs >= 32 && l.gs <= 128 && (l.in / l.gs) % 4 == 0;
+}
+// Warps per tile (K split) for a CTA of `tiles` tiles and `ngroups`
+// quantisation groups per row: the fewest rounds of tile work, counting a
+// split tile as 1 / KS of a tile plus a small cost for the combine.
+static int choose_ks(int tiles, int ngroups) {
+  int best = 0;
+  double best_cost = 1e30;
+  for (int ks : {1, 2, 4}) {
+    if (ngroups % (4 * ks)) continue;  // whole steps of four groups per warp
+    const int groups = SL_CW / ks;
+    const double cost = double((tiles + groups - 1) / groups) * (1.0 / ks + (ks > 1 ? 0.08 : 0.0));
+    if (cost < best_cost - 1e-9) { best_cost = cost; best = ks; }
+  }
+  return best;
+}
+static int imma_rows_bytes(const QLin& l, int rows) {
+  return rows * (int(l.row_bytes) + 16 + 2 * int(l.srow) * scale_bytes(l.dt));
+}
+
+static bool plan_idense(const QLin* lins, float* const* ys, int nseg, int in, int prologue, int head_dim,
+                        const float* x, const float* aux, const float* aux2, const float* x_out, int* status,
+                        SliceTab& T, int& grid, size_t& smem) {
+  if (!slice_enabled() || !imma_enabled()) return false;
+  const QLin& l0 = lins[0];
+  for (int s = 0; s < nseg; ++s) if (!imma_fmt_ok(lins[s]) || lins[s].in != in) return false;
+  if (prologue == PRO_GATEDNORM && (head_dim <= 0 || head_dim % 32)) return false;
+  if (!aligned16(x) || !aligned16(aux) || !aligned16(aux2) || !aligned16(x_out)) return false;
+  T = SliceTab{};
+  T.rb = int(l0.row_bytes);
+  T.srow = int(l0.srow);
+  T.gs_shift = gs_shift_of(l0);
+  T.TR = 16;
+  T.nseg = nseg;
+  T.cum[0] = 0;
+  for (int s = 0; s < 4; ++s) {
+    const int k = s < nseg ? s : 0;
+    T.w[s] = lins[k].w; T.s[s] = lins[k].s; T.b[s] = lins[k].b; T.y[s] = ys[k];
+    T.cum[s + 1] = T.cum[s] + (s < nseg ? lins[s].out : 0);
+  }
+  T.total = T.cum[nseg];
+  if (T.total <= 0) return false;
+  T.rpc = std::max((T.total + sm_count() - 1) / sm_count(), 16);
+  grid = (T.total + T.rpc - 1) / T.rpc;
+  T.slot = imma_rows_bytes(l0, 16);
+  const int max_tiles = (T.rpc + 15) / 16 + nseg - 1;
+  T.W = choose_ks((T.rpc + 15) / 16, in >> T.gs_shift);
+  if (!T.W) return false;
+  T.status = status;
+  // xs: B table (3 bytes per input), cs: group sums, part: K-split partials,
+  // raw: the staged input
+  // cs: group sums then group digit scales
+  return slice_ring(T, max_tiles, 3 * in / 4, 2 * (((in >> T.gs_shift) + 3) & ~3) + 4, 2 * SL_CW * 16, in, smem);
+}
+
+static bool expert_strides_ok(const ExpertProj& p) {
+  return p.wstride % 16 == 0 && p.sstride % 16 == 0 && p.bstride % 16 == 0;
+}
+
+// Gate/up: CTA b takes a share of the shared expert's rows and of the routed rows.
+static bool plan_gateup(const MoeArgs& m, SliceTab& T, int& grid, size_t& smem) {
+  if (!slice_enabled()) return false;
+  const QLin& g = m.g.lin;
+  if (!slice_fmt_ok(g) || !slice_fmt_ok(m.u.lin) || !slice_fmt_ok(m.sg) || !slice_fmt_ok(m.su)) return false;
+  if (!expert_strides_ok(m.g) || !expert_strides_ok(m.u) || m.su.out != m.sg.out || m.sg.in != g.in) return false;
+  if (!aligned16(m.x)) return false;
+  T = SliceTab{};
+  slice_geom(g, 2, T);  // two gate/up row pairs per sub-warp and tile
+  if (T.W != 1 || T.LPR < 4) return false;
+  const int sh = m.sg.out, nq = m.topk * g.out, n = sm_count();
+  T.sh_rpc = std::max(1, (sh + n - 1) / n);
+  T.rt_rpc = nq > 0 ? std::max(1, (nq + n - 1) / n) : 0;
+  grid = std::max(1, std::max((sh + T.sh_rpc - 1) / T.sh_rpc, nq > 0 ? (nq + T.rt_rpc - 1) / T.rt_rpc : 0));
+  T.slot = 2 * T.TR * row_total(g);
+  const int max_tiles = (T.sh_rpc + T.TR - 1) / T.TR +
+                        (nq > 0 ? (T.rt_rpc + T.TR - 1) / T.TR + (T.rt_rpc + g.out - 1) / g.out + 1 : 0);
+  T.status = m.status;
+  const int wpc = wpc_of(g.bits, g.dt);
+  return slice_ring(T, max_tiles, g.in, g.in / wpc + 4, 0, g.in, smem);
+}
+
+static bool plan_igateup(const MoeArgs& m, SliceTab& T, int& grid, size_t& smem) {
+  if (!slice_enabled() || !imma_enabled()) return false;
+  const QLin& g = m.g.lin;
+  if (!imma_fmt_ok(g) || !imma_fmt_ok(m.u.lin) || !imma_fmt_ok(m.sg) || !imma_fmt_ok(m.su)) return false;
+  if (!expert_strides_ok(m.g) || !expert_strides_ok(m.u) || m.su.out != m.sg.out || m.sg.in != g.in) return false;
+  if (!aligned16(m.x) || g.in > 4096) return false;
+  T = SliceTab{};
+  T.rb = int(g.row_bytes);
+  T.srow = int(g.srow);
+  T.gs_shift = gs_shift_of(g);
+  T.TR = 8;
+  const int sh = m.sg.out, nq = m.topk * g.out, n = sm_count();
+  T.sh_rpc = std::max(1, (sh + n - 1) / n);
+  T.rt_rpc = nq > 0 ? std::max(1, (nq + n - 1) / n) : 0;
+  grid = std::max(1, std::max((sh + T.sh_rpc - 1) / T.sh_rpc, nq > 0 ? (nq + T.rt_rpc - 1) / T.rt_rpc : 0));
+  T.slot = 2 * imma_rows_bytes(g, 8);
+  const int max_tiles = (T.sh_rpc + 7) / 8 + (nq > 0 ? (T.rt_rpc + 7) / 8 + (T.rt_rpc + g.out - 1) / g.out + 1 : 0);
+  T.W = choose_ks((T.sh_rpc + 7) / 8 + (T.rt_rpc + 7) / 8, g.in >> T.gs_shift);
+  if (!T.W) return false;
+  T.status = m.status;
+  return slice_ring(T, max_tiles, 3 * g.in / 4, 2 * (((g.in >> T.gs_shift) + 3) & ~3) + 4, 2 * SL_CW * 16, g.in,
+                    smem);
+}
+
+static bool plan_idown(const MoeArgs& m, SliceTab& T, int& grid, size_t& smem) {
+  if (!slice_enabled() || !imma_enabled()) return false;
+  const QLin& d = m.d.lin;
+  if (!imma_fmt_ok(d) || !imma_fmt_ok(m.sd) || !expert_strides_ok(m.d)) return false;
+  if (m.topk + 1 > 16 || !aligned16(m.hmid) || m.hmid_stride % 4 || m.sd.in != d.in) return false;
+  T = SliceTab{};
+  T.rb = int(d.row_bytes);
+  T.srow = int(d.srow);
+  T.gs_shift = gs_shift_of(d);
+  const int D = d.out, K1 = m.topk + 1;
+  T.total = D;
+  T.rpc = std::min(16, (D + sm_count() - 1) / sm_count());
+  T.TR = T.rpc;
+  grid = (D + T.rpc - 1) / T.rpc;
+  T.slot = imma_rows_bytes(d, 16);
+  T.status = m.status;
+  const int nkb = d.in >> 5;
+  return slice_ring(T, K1, K1 * nkb * 24, 2 * ((K1 * (d.in >> T.gs_shift) + 3) & ~3) + 4, K1 * T.rpc,
+                    K1 * m.hmid_stride, smem);
+}
+
+bool moe_routes_from_logits(const MoeArgs& m, int experts) {
+  SliceTab T;
+  int grid = 0;
+  size_t smem = 0;
+  return experts <= 512 && m.topk <= 16 && plan_igateup(m, T, grid, smem) && plan_idown(m, T, grid, smem);
+}
+
+// Down: CTA b takes output rows [b*rpc, (b+1)*rpc) of every picked expert.
+static bool plan_down(const MoeArgs& m, SliceTab& T, int& grid, size_t& smem) {
+  if (!slice_enabled()) return false;
+  const QLin& d = m.d.lin;
+  if (!slice_fmt_ok(d) || !slice_fmt_ok(m.sd) || !expert_strides_ok(m.d)) return false;
+  if (m.topk + 1 > 16 || !aligned16(m.hmid) || m.hmid_stride % 4 || m.sd.in != d.in) return false;
+  T = SliceTab{};
+  slice_geom(d, 1, T);
+  if (T.W != 1 || T.LPR < 4) return false;
+  const int D = d.out, K1 = m.topk + 1, wpc = wpc_of(d.bits, d.dt);
+  T.total = D;
+  T.rpc = (D + sm_count() - 1) / sm_count();
+  if (T.rpc > 64) return false;
+  grid = (D + T.rpc - 1) / T.rpc;
+  T.TR = T.rpc;  // one tile per expert: the CTA's rows
+  T.slot = T.TR * row_total(d);
+  const int max_tiles = K1;
+  T.status = m.status;
+  return slice_ring(T, max_tiles, K1 * m.hmid_stride, K1 * (m.hmid_stride / wpc + 4), K1 * T.rpc, K1 * m.hmid_stride,
+                    smem);
 }
 
 void launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl) {
@@ -122,6 +405,27 @@ void launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl) {
   QLin lins[4];
   float* ys[4];
   for (int s = 0; s < a.nseg; ++s) { lins[s] = a.seg[s].lin; ys[s] = a.seg[s].y; }
+  {
+    SliceTab ST;
+    int sgrid = 0, sR = 1;
+    size_t ssmem = 0;
+    if (plan_idense(lins, ys, a.nseg, a.in, a.prologue, a.head_dim, a.x, a.aux, a.aux2, a.x_out, a.status, ST,
+                    sgrid, ssmem)) {
+      const RouterTail none;
+#define CALL(B, D) igemv_fmt<B, D>(a, ST, none, sgrid, ssmem, st, pdl)
+      SWL_DISPATCH_IMMA(l0.bits, l0.dt, CALL);
+#undef CALL
+      return;
+    }
+    if (plan_dense(lins, ys, a.nseg, a.in, a.prologue, a.head_dim, a.x, a.aux, a.aux2, a.x_out, a.status, ST, sR,
+                   sgrid, ssmem)) {
+      const RouterTail none;
+#define CALL(B, D) sgemv_fmt<B, D>(a, ST, none, sR, sgrid, ssmem, st, pdl)
+      SWL_DISPATCH_FMT(l0.bits, l0.dt, CALL);
+#undef CALL
+      return;
+    }
+  }
   const SegTab T = make_tab(lins, ys, a.nseg, R);
   int grid = grid_for(T.task0[a.nseg], spw);
   if (a.argmax_out) grid = std::min(grid, 1024);
@@ -140,10 +444,38 @@ void launch_router(const RouterArgs& r, int E, cudaStream_t st, bool pdl) {
       r.gate.srow != r.sgate.srow)
     throw Error(ERR_UNSUPPORTED, "router and shared-expert gate differ in format");
   if (r.topk > 64) throw Error(ERR_UNSUPPORTED, "top-k above 64");
-  const int LPR = lanes_per_row(r.gate.row_bytes), spw = 32 / LPR;
-  const int CPL = cpl_of(r.gate, LPR), nslab = slabs_of(r.gate.row_bytes, LPR, CPL);
   const QLin lins[2] = {r.gate, r.sgate};
   float* const ys[2] = {r.logits, r.logits + E};
+  {
+    SliceTab ST;
+    int sgrid = 0, sR = 1;
+    size_t ssmem = 0;
+    const bool imma = E <= r.gate.in && plan_idense(lins, ys, 2, r.gate.in, PRO_RMSNORM, 0, r.h, r.norm_w, nullptr,
+                                                    r.x_out, r.status, ST, sgrid, ssmem);
+    if (imma || (E <= r.gate.in && plan_dense(lins, ys, 2, r.gate.in, PRO_RMSNORM, 0, r.h, r.norm_w, nullptr, r.x_out,
+                                              r.status, ST, sR, sgrid, ssmem))) {
+      GemvArgs a;
+      a.seg[0].lin = r.gate; a.seg[0].y = r.logits; a.seg[1].lin = r.sgate; a.seg[1].y = r.logits + E;
+      a.nseg = 2; a.in = r.gate.in; a.prologue = PRO_RMSNORM; a.epilogue = EPI_STORE;
+      a.x = r.h; a.aux = r.norm_w; a.eps = r.eps; a.x_out = r.x_out; a.status = r.status; a.trace = r.trace;
+      RouterTail rt;
+      if (!r.skip_topk) rt.logits = r.logits;
+      rt.E = E; rt.topk = r.topk; rt.norm_topk = r.norm_topk;
+      rt.pick_ids = r.pick_ids; rt.pick_w = r.pick_w; rt.shared_scale = r.shared_scale; rt.counter = r.counter;
+      if (imma) {
+#define CALL(B, D) igemv_fmt<B, D>(a, ST, rt, sgrid, ssmem, st, pdl)
+        SWL_DISPATCH_IMMA(r.gate.bits, r.gate.dt, CALL);
+#undef CALL
+      } else {
+#define CALL(B, D) sgemv_fmt<B, D>(a, ST, rt, sR, sgrid, ssmem, st, pdl)
+        SWL_DISPATCH_FMT(r.gate.bits, r.gate.dt, CALL);
+#undef CALL
+      }
+      return;
+    }
+  }
+  const int LPR = lanes_per_row(r.gate.row_bytes), spw = 32 / LPR;
+  const int CPL = cpl_of(r.gate, LPR), nslab = slabs_of(r.gate.row_bytes, LPR, CPL);
   const SegTab T = make_tab(lins, ys, 2, 1);
   const int grid = grid_for(T.task0[2], spw);
   const int wpc = wpc_of(r.gate.bits, r.gate.dt);
@@ -159,6 +491,23 @@ void launch_moe_gateup(const MoeArgs& m, cudaStream_t st, bool pdl) {
   if (m.sg.bits != g.bits || m.sg.dt != g.dt || m.sg.row_bytes != g.row_bytes || m.u.lin.row_bytes != g.row_bytes ||
       m.su.row_bytes != g.row_bytes || m.sg.srow != g.srow)
     throw Error(ERR_UNSUPPORTED, "shared and routed experts differ in format");
+  {
+    SliceTab ST;
+    int sgrid = 0;
+    size_t ssmem = 0;
+    if (plan_igateup(m, ST, sgrid, ssmem)) {
+#define CALL(B, D) igateup_fmt<B, D>(m, ST, sgrid, ssmem, st, pdl)
+      SWL_DISPATCH_IMMA(g.bits, g.dt, CALL);
+#undef CALL
+      return;
+    }
+    if (plan_gateup(m, ST, sgrid, ssmem)) {
+#define CALL(B, D) sgateup_fmt<B, D>(m, ST, sgrid, ssmem, st, pdl)
+      SWL_DISPATCH_FMT(g.bits, g.dt, CALL);
+#undef CALL
+      return;
+    }
+  }
   const int LPR = lanes_per_row(g.row_bytes), spw = 32 / LPR;
   const int CPL = cpl_of(g, LPR), nslab = slabs_of(g.row_bytes, LPR, CPL);
   const int R = pick_r(g, (m.topk + 1) * g.out, spw, CPL >= 4 ? 1 : 2);
@@ -177,6 +526,23 @@ void launch_moe_down(const MoeArgs& m, cudaStream_t st, bool pdl) {
   if (m.sd.bits != d.bits || m.sd.dt != d.dt || m.sd.row_bytes != d.row_bytes || m.sd.srow != d.srow)
     throw Error(ERR_UNSUPPORTED, "shared and routed experts differ in format");
   if (m.topk + 1 > 16) throw Error(ERR_UNSUPPORTED, "more than 15 routed experts per token");
+  {
+    SliceTab ST;
+    int sgrid = 0;
+    size_t ssmem = 0;
+    if (plan_idown(m, ST, sgrid, ssmem)) {
+#define CALL(B, D_) idown_fmt<B, D_>(m, ST, sgrid, ssmem, st, pdl)
+      SWL_DISPATCH_IMMA(d.bits, d.dt, CALL);
+#undef CALL
+      return;
+    }
+    if (plan_down(m, ST, sgrid, ssmem)) {
+#define CALL(B, D_) sdown_fmt<B, D_>(m, ST, sgrid, ssmem, st, pdl)
+      SWL_DISPATCH_FMT(d.bits, d.dt, CALL);
+#undef CALL
+      return;
+    }
+  }
   const int LPR = lanes_per_row(d.row_bytes), spw = 32 / LPR;
   const int nslab = int(((d.row_bytes >> 4) + LPR - 1) / LPR);
   const int D = d.out;

@@ -112,7 +112,8 @@ __device__ __forceinline__ void stage_gemv_x(const GemvArgs& a, float* xs, float
     });
   } else if (a.prologue == PRO_GATEDNORM) {
     // DeltaNet output gate (QwenCPUModel.swift:490-493): per v-head RMSNorm
-    // with weight, times silu(z). Head scales first (one warp per head).
+    // with weight, times silu(z) (aux holds silu(z), computed by the DeltaNet
+    // kernel). Head scales first (one warp per head).
     float* hscale = red + 32;
     const int hd = a.head_dim, nh = in / hd, w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
     for (int h = w; h < nh; h += nw) {
@@ -124,7 +125,7 @@ __device__ __forceinline__ void stage_gemv_x(const GemvArgs& a, float* xs, float
     __syncthreads();
     stage_vec<BITS, DT>(in, xs, cs, [&](int k) {
       const int h = k / hd;
-      const float v = (a.x[k] * (hscale[h] * raw3[k - h * hd])) * silu_ref(raw2[k]);
+      const float v = (a.x[k] * (hscale[h] * raw3[k - h * hd])) * raw2[k];
       if (xo) xo[k] = v;
       return v;
     });

@@ -1,0 +1,746 @@
+// Integer tensor-core weight streaming for 4- and 8-bit MLX-affine weights
+// (B = 1 decode): mma.sync m16n8k32 with unsigned 8-bit weight codes (A) and
+// signed 8-bit activation digits (B), int32 accumulation per quantisation
+// group, then the group's scale and bias in f32.
+//
+// Activations: per quantisation group g, with inv = 127 / max_g|x| and
+// xs = x * inv, three base-254 digits d0 = rint(xs), d1 = rint((xs - d0) *
+// 254), d2 = rint(((xs - d0) * 254 - d1) * 254) (each in [-127, 127]) give
+// x = (d0 + d1/254 + d2/254^2) / inv to within 0.5 / 254^2 / inv =
+// 6.1e-8 * max_g|x|, i.e. f32-level accuracy. Digit n is column n of B (columns 3..7 are zero), so one MMA
+// yields sum(q * d_n) for n = 0, 1, 2 of 16 rows at once. A group (>= 32
+// weights) fits an int32 exactly (64 * 255 * 127 < 2^24), so it is converted
+// once per group: acc_n += scale_g / inv_g * float(D_n). Finally
+//   y = acc_0 + (acc_1 + acc_2 / 254) / 254 + sum_g bias_g * sum(x_g).
+//
+// Fragment mapping (m16n8k32, A row-major, B column-major): lane T holds
+// A rows T/4 and T/4 + 8, k-slots 4t..4t+3 (a0/a1) and 16+4t..16+4t+3 (a2/a3)
+// with t = T % 4. For 4-bit weights lane t reads word t (8 codes) of the
+// 16-byte block: low nibbles (codes 0, 2, 4, 6) go to the first slot set, high
+// nibbles (1, 3, 5, 7) to the second; for 8-bit weights words t and 4 + t of
+// the 32-byte block. The B table stores each lane's digits in the same k
+// order, so the permutation cancels in the dot product.
+#pragma once
+
+#include "slice_impl.cuh"
+
+namespace swl {
+
+// D += A * B on the integer tensor cores (16x8x32, u8 x s8 -> s32).
+__device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], uint2 b) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b.x), "r"(b.y));
+}
+
+__device__ __forceinline__ int clamp127(float v) { return max(-127, min(127, int(v))); }
+
+// Exact int -> float for |d| < 2^22 on the full-rate pipes: the bits of
+// 1.5 * 2^23 + d read as a float are 12582912 + d (one group's MMA sum is at
+// most 128 * 255 * 127 < 2^22 in magnitude).
+__device__ __forceinline__ float i2f_small(int d) { return __int_as_float(d + 0x4B400000) - 12582912.f; }
+
+// The three digits of xs (|xs| <= 127) packed as signed bytes at byte `pos`.
+// Adding 1.5 * 2^23 rounds to an integer (round to nearest even, as rintf)
+// whose low byte, read from the float's bits, is the digit's two's-complement
+// byte (|digit| <= 127 by construction).
+__device__ __forceinline__ void put_digits(float xs, int pos, uint32_t (&b)[3]) {
+  constexpr float M = 12582912.f;
+  const float a0 = xs + M;
+  const float r1 = (xs - (a0 - M)) * 254.f;
+  const float a1 = r1 + M;
+  const float r2 = (r1 - (a1 - M)) * 254.f;
+  const float a2 = r2 + M;
+  const int sh = 8 * pos;
+  b[0] |= (__float_as_uint(a0) & 0xFFu) << sh;
+  b[1] |= (__float_as_uint(a1) & 0xFFu) << sh;
+  b[2] |= (__float_as_uint(a2) & 0xFFu) << sh;
+}
+
+__device__ __forceinline__ float absmax4(const float4 v) {
+  return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+}
+__device__ __forceinline__ bool finite4(const float4 v) {
+  return isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w);
+}
+
+// Digit scale of a group from its largest magnitude m (infinite when a value
+// is not finite): inv = 127 / m; rs = 1 / inv, or NaN so that non-finite
+// inputs give non-finite outputs, or 0 for an all-zero group.
+__device__ __forceinline__ void digit_scale(float m, float& inv, float& rs) {
+  inv = (m > 0.f && m < INFINITY) ? 127.f / m : 0.f;
+  rs = inv > 0.f ? 1.f / inv : (m == INFINITY ? __int_as_float(0x7fc00000) : 0.f);
+}
+
+// The 8 values of B-table entry (kb, t) in k order of the fragment: 4-bit
+// weights pair codes 8t..8t+7 of the block (even codes -> first slot set),
+// 8-bit weights words t and 4 + t.
+template <int BITS>
+__device__ __forceinline__ void entry_values(const float* x, int kb, int t, float (&v)[8]) {
+  const float4* p4 = reinterpret_cast<const float4*>(x);
+  float4 lo, hi;
+  if constexpr (BITS == 4) {
+    lo = p4[(32 * kb + 8 * t) >> 2];
+    hi = p4[((32 * kb + 8 * t) >> 2) + 1];
+  } else {
+    lo = p4[(32 * kb + 4 * t) >> 2];
+    hi = p4[(32 * kb + 16 + 4 * t) >> 2];
+  }
+  v[0] = lo.x; v[1] = lo.y; v[2] = lo.z; v[3] = lo.w;
+  v[4] = hi.x; v[5] = hi.y; v[6] = hi.z; v[7] = hi.w;
+}
+template <int BITS>
+__device__ __forceinline__ void entry_store(const float (&v)[8], float inv, uint2* slot_t) {
+  uint32_t b0[3] = {0u, 0u, 0u}, b1[3] = {0u, 0u, 0u};
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if constexpr (BITS == 4) {
+      if (j & 1) put_digits(v[j] * inv, j >> 1, b1);
+      else put_digits(v[j] * inv, j >> 1, b0);
+    } else {
+      if (j < 4) put_digits(v[j] * inv, j, b0);
+      else put_digits(v[j] * inv, j - 4, b1);
+    }
+  }
+#pragma unroll
+  for (int n = 0; n < 3; ++n) slot_t[4 * n] = make_uint2(b0[n], b1[n]);
+}
+
+// Digit staging of `nvec` vectors of n values each (vector v at x + v *
+// stride, shared memory) by the consumer threads: quad (g, t) of four
+// consecutive threads covers group g (KPG 32-value blocks): its largest
+// magnitude and sum (two shuffle rounds), the group's reconstruction scale
+// grs[g] and sum gsum[g], and B-table entries (kb, t) of its blocks. The
+// vectors' groups, tables and sums are laid out back to back.
+template <int BITS, int KPG>
+__device__ __forceinline__ void stage_digits(const float* x, int stride, int nvec, int n, uint2* bt, float* gsum,
+                                             float* grs) {
+  const int tid = threadIdx.x, t = tid & 3;
+  const int gpv = n / (32 * KPG), items = nvec * gpv * 4;
+  for (int base = 0; base < items; base += SL_NT) {
+    const int it = base + tid;
+    const bool ok = it < items;
+    const int G = ok ? it >> 2 : 0, vec = G / gpv, g = G - vec * gpv;
+    const float* xv = x + vec * stride;
+    float v[KPG][8];
+    float m = 0.f, sum = 0.f;
+    bool fin = true;
+#pragma unroll
+    for (int kk = 0; kk < KPG; ++kk) {
+      entry_values<BITS>(xv, g * KPG + kk, t, v[kk]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        m = fmaxf(m, fabsf(v[kk][j]));
+        fin = fin && isfinite(v[kk][j]);
+        sum += v[kk][j];
+      }
+    }
+    if (!fin) m = INFINITY;
+#pragma unroll
+    for (int o = 1; o < 4; o <<= 1) {
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    }
+    float inv, rs;
+    digit_scale(m, inv, rs);
+    if (ok) {
+      uint2* btv = bt + size_t(vec) * (n >> 5) * 12;
+#pragma unroll
+      for (int kk = 0; kk < KPG; ++kk) entry_store<BITS>(v[kk], inv, btv + (g * KPG + kk) * 12 + t);
+      if (t == 0) {
+        gsum[G] = sum;
+        grs[G] = rs;
+      }
+    }
+  }
+}
+template <int BITS>
+__device__ __forceinline__ void stage_digits_any(int kpg, const float* x, int stride, int nvec, int n, uint2* bt,
+                                                 float* gsum, float* grs) {
+  if (kpg == 2) stage_digits<BITS, 2>(x, stride, nvec, n, bt, gsum, grs);
+  else if (kpg == 1) stage_digits<BITS, 1>(x, stride, nvec, n, bt, gsum, grs);
+  else stage_digits<BITS, 4>(x, stride, nvec, n, bt, gsum, grs);
+}
+
+// Order-preserving unsigned key of a float (larger float, larger key).
+__device__ __forceinline__ unsigned f_key(float f) {
+  const unsigned u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float key_f(unsigned k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// Routing by one warp from the router's E + 1 logits (E <= 512, K <= 32):
+// softmax weights over E, top-K, combine weights renormalised when norm_topk,
+// and sigmoid of the shared-expert gate logit (QwenCPUModel.swift:506-521,
+// 546-550; routerPicks QwenMetalModel.swift:875-892). The top-K is taken on
+// the logits, whose order the softmax preserves, with ties to the lower
+// expert id (the reference's insertion scan with a strict `>`): each round is
+// one warp max of order-preserving keys and one warp min over the ids that
+// hold it. Only the K picked probabilities are divided out. ids / w / sh are
+// shared memory.
+__device__ __forceinline__ void warp_route(const float* lg, int E, int K, int norm_topk, int* ids, float* w,
+                                           float* sh) {
+  constexpr int PL = 16;
+  const int lane = threadIdx.x & 31;
+  float lv[PL];
+  unsigned key[PL];
+#pragma unroll
+  for (int i = 0; i < PL; ++i) {
+    const int e = i * 32 + lane;
+    lv[i] = e < E ? __ldcg(lg + e) : 0.f;
+    key[i] = e < E ? f_key(lv[i]) : 0u;
+  }
+  const float shared_logit = __ldcg(lg + E);
+  // this lane's best (first index wins among equal keys)
+  auto local_best = [&](unsigned& bk, int& bi) {
+    bk = 0u;
+    bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < PL; ++i)
+      if (key[i] > bk) { bk = key[i]; bi = i * 32 + lane; }
+  };
+  unsigned bk;
+  int bi;
+  local_best(bk, bi);
+  float mine = 0.f;  // lane k: the logit of pick k
+  float top = 0.f;   // the largest logit (softmax shift)
+  for (int k = 0; k < K; ++k) {
+    const unsigned mx = __reduce_max_sync(0xffffffffu, bk);
+    int id = int(__reduce_min_sync(0xffffffffu, bk == mx ? unsigned(bi) : 0x7fffffffu));
+    if (id >= E) id = 0;  // fewer valid logits than K: keep indices in range
+    const float val = key_f(mx);
+    if (k == 0) top = val;
+    if (lane == k) mine = val;
+    if (lane == 0) ids[k] = id;
+    if ((id & 31) == lane) {
+#pragma unroll
+      for (int i = 0; i < PL; ++i)
+        if (i * 32 + lane == id) key[i] = 0u;
+      local_best(bk, bi);
+    }
+  }
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < PL; ++i)
+    if (i * 32 + lane < E) sum += expf(lv[i] - top);
+  sum = warp_sum(sum);
+  const float p = lane < K ? expf(mine - top) / sum : 0.f;
+  if (lane < K) w[lane] = p;
+  __syncwarp();
+  if (lane == 0) {
+    float score_sum = 0.f;
+    for (int k = 0; k < K; ++k) score_sum += w[k];
+    if (norm_topk)
+      for (int k = 0; k < K; ++k) w[k] = w[k] / score_sum;
+    *sh = sigmoid_ref(shared_logit);
+  }
+  __syncwarp();
+}
+
+// Four consecutive scale (or bias) entries g..g+3 of a row in shared memory
+// (g % 4 == 0; the row is 8-byte aligned for 16-bit and 16-byte aligned for
+// f32 entries).
+template <int DT>
+__device__ __forceinline__ float4 sm_scalar4(const uint8_t* p, int g) {
+  if constexpr (DT == DT_F32) {
+    return *reinterpret_cast<const float4*>(p + 4 * g);
+  } else {
+    const uint2 u = *reinterpret_cast<const uint2*>(p + 2 * g);
+    if constexpr (DT == DT_BF16)
+      return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u), __uint_as_float(u.y << 16),
+                         __uint_as_float(u.y & 0xFFFF0000u));
+    else
+      return make_float4(f16_bits_to_f32(uint16_t(u.x & 0xFFFF)), f16_bits_to_f32(uint16_t(u.x >> 16)),
+                         f16_bits_to_f32(uint16_t(u.y & 0xFFFF)), f16_bits_to_f32(uint16_t(u.y >> 16)));
+  }
+}
+__device__ __forceinline__ float f4_at(const float4 v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+
+// One 16-row tile against staged digits over quantisation groups
+// [g_begin, g_end) ((g_end - g_begin) % 4 == 0, KPG 32-weight blocks per
+// group): rows r0 = T/4 and r1 = T/4 + 8 of the tile, whose weights start at
+// w0 / w1 (row pitch already applied) and whose scale / bias rows start at
+// s0, s1 / b0, b1. Four groups run per step with independent accumulators
+// (all their fragment loads issued first), so the MMA chains overlap. Lane
+// t == 0 of each quad returns the two rows' partial results (others return
+// garbage); partials over disjoint group ranges add up to the full result.
+template <int BITS, int DT, int KPG>
+__device__ __forceinline__ void imma_rows(const uint8_t* w0, const uint8_t* w1, const uint8_t* s0, const uint8_t* s1,
+                                          const uint8_t* b0, const uint8_t* b1, const uint2* bt, const float* gsum,
+                                          const float* grs, int g_begin, int g_end, float& y0, float& y1) {
+  constexpr int KBB = BITS == 4 ? 16 : 32;  // bytes of one 32-weight block in a row
+  constexpr int NB = 4 * KPG;               // blocks per step
+  const int lane = threadIdx.x & 31, t = lane & 3;
+  const uint8_t* p0 = w0 + 4 * t;
+  const uint8_t* p1 = w1 + 4 * t;
+  const bool blane = lane < 12;
+  float f[4] = {0.f, 0.f, 0.f, 0.f};
+  float ba0 = 0.f, ba1 = 0.f;
+  for (int g = g_begin; g < g_end; g += 4) {
+    const int kb0 = g * KPG;
+    uint2 b[NB];
+    uint32_t u0[NB], u1[NB], v0[NB], v1[NB];
+#pragma unroll
+    for (int j = 0; j < NB; ++j) {
+      b[j] = blane ? bt[(kb0 + j) * 12 + lane] : make_uint2(0u, 0u);
+      u0[j] = *reinterpret_cast<const uint32_t*>(p0 + (kb0 + j) * KBB);
+      u1[j] = *reinterpret_cast<const uint32_t*>(p1 + (kb0 + j) * KBB);
+      if constexpr (BITS == 8) {
+        v0[j] = *reinterpret_cast<const uint32_t*>(p0 + (kb0 + j) * KBB + 16);
+        v1[j] = *reinterpret_cast<const uint32_t*>(p1 + (kb0 + j) * KBB + 16);
+      }
+    }
+    int d[4][4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) d[q][0] = d[q][1] = d[q][2] = d[q][3] = 0;
+#pragma unroll
+    for (int kk = 0; kk < KPG; ++kk)
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int j = q * KPG + kk;
+        uint32_t a[4];
+        if constexpr (BITS == 4) {
+          a[0] = u0[j] & 0x0F0F0F0Fu;
+          a[2] = (u0[j] >> 4) & 0x0F0F0F0Fu;
+          a[1] = u1[j] & 0x0F0F0F0Fu;
+          a[3] = (u1[j] >> 4) & 0x0F0F0F0Fu;
+        } else {
+          a[0] = u0[j];
+          a[2] = v0[j];
+          a[1] = u1[j];
+          a[3] = v1[j];
+        }
+        mma_u8s8(d[q], a, b[j]);
+      }
+    const float4 sc0 = sm_scalar4<DT>(s0, g), sc1 = sm_scalar4<DT>(s1, g);
+    const float4 bb0 = sm_scalar4<DT>(b0, g), bb1 = sm_scalar4<DT>(b1, g);
+    const float4 xg = *reinterpret_cast<const float4*>(gsum + g);
+    const float4 rg = *reinterpret_cast<const float4*>(grs + g);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float c0 = f4_at(sc0, q) * f4_at(rg, q), c1 = f4_at(sc1, q) * f4_at(rg, q);
+      f[0] = fmaf(c0, i2f_small(d[q][0]), f[0]);
+      f[1] = fmaf(c0, i2f_small(d[q][1]), f[1]);
+      f[2] = fmaf(c1, i2f_small(d[q][2]), f[2]);
+      f[3] = fmaf(c1, i2f_small(d[q][3]), f[3]);
+      ba0 = fmaf(f4_at(bb0, q), f4_at(xg, q), ba0);
+      ba1 = fmaf(f4_at(bb1, q), f4_at(xg, q), ba1);
+    }
+  }
+  // lane t == 1 holds digit 2 (column 2) of the same rows
+  const float e0 = __shfl_down_sync(0xffffffffu, f[0], 1);
+  const float e1 = __shfl_down_sync(0xffffffffu, f[2], 1);
+  y0 = (f[0] + (f[1] + e0 * (1.f / 254.f)) * (1.f / 254.f)) + ba0;
+  y1 = (f[2] + (f[3] + e1 * (1.f / 254.f)) * (1.f / 254.f)) + ba1;
+}
+
+// Dispatch on the blocks per group (group sizes 32, 64, 128).
+template <int BITS, int DT>
+__device__ __forceinline__ void imma_rows_any(int kpg, const uint8_t* w0, const uint8_t* w1, const uint8_t* s0,
+                                              const uint8_t* s1, const uint8_t* b0, const uint8_t* b1, const uint2* bt,
+                                              const float* gsum, const float* grs, int g_begin, int g_end, float& y0,
+                                              float& y1) {
+  if (kpg == 2) imma_rows<BITS, DT, 2>(w0, w1, s0, s1, b0, b1, bt, gsum, grs, g_begin, g_end, y0, y1);
+  else if (kpg == 1) imma_rows<BITS, DT, 1>(w0, w1, s0, s1, b0, b1, bt, gsum, grs, g_begin, g_end, y0, y1);
+  else imma_rows<BITS, DT, 4>(w0, w1, s0, s1, b0, b1, bt, gsum, grs, g_begin, g_end, y0, y1);
+}
+
+// Issues the bulk copies of rows [row, row + n) (n <= cap) of one matrix into
+// a slot laid out as [cap rows at pitch rbp][cap scale rows][cap bias rows]
+// (rows copied one by one so that the padded pitch spreads them over the
+// shared-memory banks).
+__device__ __forceinline__ void imma_copy(const SliceTab& T, int rbp, int sb, int cap, uint8_t* d, uint64_t* bar,
+                                          const uint8_t* w, const uint8_t* s, const uint8_t* b, int row, int n,
+                                          uint64_t pol) {
+  const int ss = T.srow * sb;
+  for (int r = 0; r < n; ++r) bulk_g2s(d + r * rbp, w + int64_t(row + r) * T.rb, unsigned(T.rb), bar, pol);
+  bulk_g2s(d + cap * rbp, s + int64_t(row) * ss, unsigned(n * ss), bar, pol);
+  bulk_g2s(d + cap * rbp + cap * ss, b + int64_t(row) * ss, unsigned(n * ss), bar, pol);
+}
+__device__ __forceinline__ void imma_init_barriers(uint64_t* full, uint64_t* empty, int S) {
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(full + i, 1);
+      mbar_init(empty + i, 1);  // one consumer warp per tile
+    }
+    mbar_init_fence();
+  }
+  __syncthreads();
+}
+
+// Tiles are reduced by groups of KS = T.W consumer warps (KS in {1, 2, 4}):
+// tile i goes to warp group i % (SL_CW / KS), whose warp kw covers the
+// quantisation groups [kw * ng / KS, (kw + 1) * ng / KS). With KS > 1 the
+// partials meet in `kp` (two buffers of SL_CW * 16 floats, alternating per
+// round so that the next round's writes cannot overtake the reads), behind
+// named barrier 2 + group.
+struct KSplit {
+  int ks, ng_warps, grp, kw;
+  __device__ __forceinline__ KSplit(int ks_, int warp) : ks(ks_), ng_warps(SL_CW / ks_), grp(warp / ks_), kw(warp % ks_) {}
+  __device__ __forceinline__ bool mine(int tile) const { return tile % ng_warps == grp; }
+  __device__ __forceinline__ int round(int tile) const { return tile / ng_warps; }
+  __device__ __forceinline__ void range(int ngroups, int& g0, int& g1) const {
+    g0 = kw * ngroups / ks;
+    g1 = (kw + 1) * ngroups / ks;
+  }
+  // Sums the KS partials of rows gi / gi + 8 into warp kw == 0 (t == 0 lanes).
+  __device__ __forceinline__ void combine(float* kp, int rnd, int gi, int t, float& y0, float& y1) const {
+    if (ks == 1) return;
+    float* buf = kp + (rnd & 1) * SL_CW * 16;
+    const int warp = threadIdx.x >> 5;
+    if (t == 0) { buf[warp * 16 + gi] = y0; buf[warp * 16 + gi + 8] = y1; }
+    asm volatile("bar.sync %0, %1;" ::"r"(2 + grp), "r"(ks * 32) : "memory");
+    if (kw == 0 && t == 0) {
+      y0 = 0.f;
+      y1 = 0.f;
+      for (int q = 0; q < ks; ++q) {
+        y0 += buf[(grp * ks + q) * 16 + gi];
+        y1 += buf[(grp * ks + q) * 16 + gi + 8];
+      }
+    }
+  }
+};
+
+// ------------------------------------------------------------ dense GEMV --
+// As k_sgemv (same tiles of 16 rows, producer, prologues and epilogues); tile
+// i is reduced by consumer warp i % SL_CW on the tensor cores.
+template <int BITS, int DT>
+__global__ void __launch_bounds__(SL_T, 2) k_igemv(const GemvArgs a, const SliceTab T, const RouterTail rt) {
+  constexpr int SB = DT == DT_F32 ? 4 : 2;
+  extern __shared__ __align__(128) uint8_t sm[];
+  uint8_t* ring = sm;
+  float* plain = reinterpret_cast<float*>(sm + T.off_raw);
+  float* red = reinterpret_cast<float*>(sm + T.off_red);
+  float* gsum = reinterpret_cast<float*>(sm + T.off_cs);
+  uint2* bt = reinterpret_cast<uint2*>(sm + T.off_xs);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + T.off_bar);
+  uint64_t* empty = full + T.S;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r0 = blockIdx.x * T.rpc, r1 = min(T.total, r0 + T.rpc);
+  const int rbp = T.rb + 16, ss = T.srow * SB;
+  auto tiles = [&](auto&& f) {
+    int idx = 0;
+    for (int sg = 0; sg < T.nseg; ++sg) {
+      const int a0 = max(r0, T.cum[sg]), a1 = min(r1, T.cum[sg + 1]);
+      for (int r = a0; r < a1; r += 16) f(idx++, sg, r - T.cum[sg], min(16, a1 - r));
+    }
+  };
+  imma_init_barriers(full, empty, T.S);
+  if (warp == SL_CW) {  // producer
+    if (lane == 0) {
+      const uint64_t pol = l2_evict_first();
+      int issued = 0;
+      bool ok = true;
+      tiles([&](int i, int sg, int row, int n) {
+        if (!ok) return;
+        const int s = i % T.S;
+        if (i >= T.S && !mbar_wait(empty + s, unsigned(i / T.S - 1) & 1u)) { ok = false; return; }
+        mbar_expect_tx(full + s, sl_bytes<BITS, DT>(T, n));
+        imma_copy(T, rbp, SB, 16, ring + size_t(s) * T.slot, full + s, seg_pick(T.w, sg), seg_pick(T.s, sg),
+                  seg_pick(T.b, sg), row, n, pol);
+        issued = i + 1;
+      });
+      if (!ok) sl_fail(T);
+      pdl_launch();
+      sl_drain(full, T.S, issued);
+    }
+    return;
+  }
+  TraceRec trc;
+  trc.start(a.trace);
+  pdl_wait();
+  trc.waited(a.trace);
+  sl_stage_plain(a, red, plain);
+  const int ngroups = a.in >> T.gs_shift, kpg = (1 << T.gs_shift) >> 5, gi = lane >> 2, t = lane & 3;
+  float* grs = gsum + ((ngroups + 3) & ~3);
+  stage_digits_any<BITS>(kpg, plain, 0, 1, a.in, bt, gsum, grs);
+  bar_sync_n(SL_NT);
+  pdl_launch();
+  trc.staged(a.trace);
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  auto epi = [&](int sg, int row, float v) {
+    float* y = seg_pick(T.y, sg);
+    if (a.epilogue == EPI_RESIDUAL) y[row] += v;
+    else y[row] = v;
+    if (sg == 0 && (v > bv || (v == bv && row < bi))) { bv = v; bi = row; }
+  };
+  const KSplit ksp(T.W, warp);
+  float* kp = reinterpret_cast<float*>(sm + T.off_part);
+  int g0, g1;
+  ksp.range(ngroups, g0, g1);
+  bool dead = false;
+  // A warp whose bounded wait gave up keeps taking part in its group's
+  // combine barriers (with zeros), so no partner waits on it forever.
+  tiles([&](int i, int sg, int row, int n) {
+    if (!ksp.mine(i)) return;
+    const int s = i % T.S;
+    const bool ok = !dead && __all_sync(0xffffffffu, mbar_wait(full + s, unsigned(i / T.S) & 1u));
+    dead = !ok;
+    float y0 = 0.f, y1 = 0.f;
+    if (ok) {
+      const uint8_t* wt = ring + size_t(s) * T.slot;
+      const uint8_t* st = wt + 16 * rbp;
+      const uint8_t* btt = st + 16 * ss;
+      imma_rows_any<BITS, DT>(kpg, wt + gi * rbp, wt + (gi + 8) * rbp, st + gi * ss, st + (gi + 8) * ss,
+                              btt + gi * ss, btt + (gi + 8) * ss, bt, gsum, grs, g0, g1, y0, y1);
+    }
+    ksp.combine(kp, ksp.round(i), gi, t, y0, y1);
+    __syncwarp();
+    if (ksp.kw == 0 && ok) {
+      if (lane == 0) mbar_arrive(empty + s);
+      if (t == 0) {
+        if (gi < n) epi(sg, row + gi, y0);
+        if (gi + 8 < n) epi(sg, row + gi + 8, y1);
+      }
+    }
+  });
+  trc.looped(a.trace);
+  if (dead) sl_fail(T);
+  if (a.argmax_out) sl_argmax_tail(a, bv, bi, red);
+  if (rt.logits) sl_router_done(rt, plain, red);
+  trc.end(a.trace);
+}
+
+// ---------------------------------------------------------------- MoE ----
+// Gate/up of the shared and routed experts (tiles and producer as k_sgateup,
+// 8 row pairs per tile): the 16-row MMA tile is 8 gate rows over the same 8
+// up rows, so the lane holding gate row p also holds up row p.
+template <int BITS, int DT>
+__global__ void __launch_bounds__(SL_T, 2) k_igateup(const MoeArgs m, const SliceTab T) {
+  constexpr int SB = DT == DT_F32 ? 4 : 2;
+  extern __shared__ __align__(128) uint8_t sm[];
+  uint8_t* ring = sm;
+  float* plain = reinterpret_cast<float*>(sm + T.off_raw);
+  float* red = reinterpret_cast<float*>(sm + T.off_red);
+  float* gsum = reinterpret_cast<float*>(sm + T.off_cs);
+  uint2* bt = reinterpret_cast<uint2*>(sm + T.off_xs);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + T.off_bar);
+  uint64_t* empty = full + T.S;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = m.topk, inter = m.g.lin.out, sh = m.sg.out, nq = K * inter;
+  const int s0 = min(sh, int(blockIdx.x) * T.sh_rpc), s1 = min(sh, s0 + T.sh_rpc);
+  const int q0 = min(nq, int(blockIdx.x) * T.rt_rpc), q1 = min(nq, q0 + T.rt_rpc);
+  const int rbp = T.rb + 16, ss = T.srow * SB, half = T.slot / 2;
+  auto tiles = [&](auto&& f) {  // f(tile, slot (K = shared), row, n)
+    int idx = 0;
+    for (int r = s0; r < s1; r += 8) f(idx++, K, r, min(8, s1 - r));
+    for (int q = q0; q < q1;) {
+      const int k = q / inter, row = q - k * inter;
+      const int n = min(8, min(q1 - q, inter - row));
+      f(idx++, k, row, n);
+      q += n;
+    }
+  };
+  __shared__ int r_ids[16];
+  __shared__ float r_w[16], r_sh;
+  imma_init_barriers(full, empty, T.S);
+  if (warp == SL_CW) {  // producer
+    const uint64_t pol = l2_evict_first();
+    int issued = 0;
+    bool ok = true;
+    auto issue = [&](int i, int k, int row, int n, int id) {
+      if (!ok) return;
+      const int s = i % T.S;
+      if (i >= T.S && !mbar_wait(empty + s, unsigned(i / T.S - 1) & 1u)) { ok = false; return; }
+      QLin G = m.sg, U = m.su;
+      if (k < K) {
+        G = expert_lin(m.g, id);
+        U = expert_lin(m.u, id);
+      }
+      uint8_t* d = ring + size_t(s) * T.slot;
+      mbar_expect_tx(full + s, 2u * sl_bytes<BITS, DT>(T, n));
+      imma_copy(T, rbp, SB, 8, d, full + s, G.w, G.s, G.b, row, n, pol);
+      imma_copy(T, rbp, SB, 8, d + half, full + s, U.w, U.s, U.b, row, n, pol);
+      issued = i + 1;
+    };
+    // shared-expert tiles first: their weights do not depend on the routing
+    if (lane == 0) tiles([&](int i, int k, int row, int n) { if (k == K) issue(i, k, row, n, 0); });
+    pdl_wait();  // the routing comes from the previous (router) grid
+    if (m.logits) {
+      warp_route(m.logits, m.experts, K, m.norm_topk, r_ids, r_w, &r_sh);
+      if (blockIdx.x == 0 && lane < K) {
+        m.pick_ids[lane] = r_ids[lane];
+        m.pick_w[lane] = r_w[lane];
+      }
+      if (blockIdx.x == 0 && lane == 0) *m.shared_scale = r_sh;
+    }
+    if (lane == 0) {
+      tiles([&](int i, int k, int row, int n) {
+        if (k < K) issue(i, k, row, n, m.logits ? r_ids[k] : __ldcg(m.pick_ids + k));
+      });
+      if (!ok) sl_fail(T);
+      // Dependents are released only after the router grid is complete: the
+      // down kernel reads the router's output before its own dependency wait.
+      pdl_launch();
+      sl_drain(full, T.S, issued);
+    }
+    return;
+  }
+  TraceRec trc;
+  trc.start(m.trace);
+  pdl_wait();
+  trc.waited(m.trace);
+  GemvArgs a;
+  a.in = m.g.lin.in; a.prologue = PRO_COPY; a.x = m.x;
+  sl_stage_plain(a, red, plain);
+  const int ngroups = a.in >> T.gs_shift, kpg = (1 << T.gs_shift) >> 5, gi = lane >> 2, t = lane & 3;
+  float* grs = gsum + ((ngroups + 3) & ~3);
+  stage_digits_any<BITS>(kpg, plain, 0, 1, a.in, bt, gsum, grs);
+  bar_sync_n(SL_NT);
+  pdl_launch();
+  trc.staged(m.trace);
+  const KSplit ksp(T.W, warp);
+  float* kp = reinterpret_cast<float*>(sm + T.off_part);
+  int g0, g1;
+  ksp.range(ngroups, g0, g1);
+  bool dead = false;
+  tiles([&](int i, int k, int row, int n) {
+    if (!ksp.mine(i)) return;
+    const int s = i % T.S;
+    const bool ok = !dead && __all_sync(0xffffffffu, mbar_wait(full + s, unsigned(i / T.S) & 1u));
+    dead = !ok;
+    float gv = 0.f, uv = 0.f;
+    if (ok) {
+      const uint8_t* gt = ring + size_t(s) * T.slot;
+      const uint8_t* ut = gt + half;
+      const int so = 8 * rbp, bo = 8 * rbp + 8 * ss;
+      imma_rows_any<BITS, DT>(kpg, gt + gi * rbp, ut + gi * rbp, gt + so + gi * ss, ut + so + gi * ss,
+                              gt + bo + gi * ss, ut + bo + gi * ss, bt, gsum, grs, g0, g1, gv, uv);
+    }
+    ksp.combine(kp, ksp.round(i), gi, t, gv, uv);
+    __syncwarp();
+    if (ksp.kw == 0 && ok) {
+      if (lane == 0) mbar_arrive(empty + s);
+      if (t == 0 && gi < n) m.hmid[k * m.hmid_stride + row + gi] = silu_ref(gv) * uv;
+    }
+  });
+  trc.looped(m.trace);
+  if (dead) sl_fail(T);
+  trc.end(m.trace);
+}
+
+// Down projections, combine and residual (as k_sdown): tile e holds expert
+// slot e's rows of the CTA (at most 16); warp e % SL_CW stages that slot's
+// digits and reduces the tile into part[e][row]; the consumers then combine
+// part over the experts with the routing weights.
+template <int BITS, int DT>
+__global__ void __launch_bounds__(SL_T, 2) k_idown(const MoeArgs m, const SliceTab T) {
+  constexpr int SB = DT == DT_F32 ? 4 : 2;
+  extern __shared__ __align__(128) uint8_t sm[];
+  uint8_t* ring = sm;
+  float* raw = reinterpret_cast<float*>(sm + T.off_raw);
+  float* part = reinterpret_cast<float*>(sm + T.off_part);
+  float* gsum = reinterpret_cast<float*>(sm + T.off_cs);
+  uint2* bt = reinterpret_cast<uint2*>(sm + T.off_xs);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + T.off_bar);
+  uint64_t* empty = full + T.S;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int K = m.topk, D = m.d.lin.out, inter = m.d.lin.in;
+  const int o0 = int(blockIdx.x) * T.rpc, o1 = min(D, o0 + T.rpc), nrow = o1 - o0;
+  const int rbp = T.rb + 16, ss = T.srow * SB;
+  __shared__ int r_ids[16];
+  __shared__ float r_w[16], r_sh;
+  imma_init_barriers(full, empty, T.S);
+  if (warp == SL_CW) {  // producer
+    // The router grid completed before this grid was launched, so its output
+    // (logits, or the routing it stored) can be read before the dependency wait.
+    if (m.logits) warp_route(m.logits, m.experts, K, m.norm_topk, r_ids, r_w, &r_sh);
+    if (lane == 0) {
+      const uint64_t pol = l2_evict_first();
+      int issued = 0;
+      bool ok = true;
+      for (int e = 0; e <= K && ok; ++e) {
+        const int s = e % T.S;
+        if (e >= T.S && !mbar_wait(empty + s, unsigned(e / T.S - 1) & 1u)) { ok = false; break; }
+        const QLin L = e < K ? expert_lin(m.d, m.logits ? r_ids[e] : __ldcg(m.pick_ids + e)) : m.sd;
+        mbar_expect_tx(full + s, sl_bytes<BITS, DT>(T, nrow));
+        imma_copy(T, rbp, SB, 16, ring + size_t(s) * T.slot, full + s, L.w, L.s, L.b, o0, nrow, pol);
+        issued = e + 1;
+      }
+      if (!ok) sl_fail(T);
+      pdl_launch();
+      sl_drain(full, T.S, issued);
+    }
+    return;
+  }
+  TraceRec trc;
+  trc.start(m.trace);
+  pdl_wait();
+  trc.waited(m.trace);
+  const int nfl = (K + 1) * m.hmid_stride;
+  for (int i = tid; i < (nfl >> 2); i += SL_NT) cp_async16(raw + 4 * i, m.hmid + 4 * i);
+  cp_async_wait_all();
+  bar_sync_n(SL_NT);
+  const int nkb = inter >> 5, ngroups = inter >> T.gs_shift, kpg = (1 << T.gs_shift) >> 5;
+  float* grs = gsum + (((K + 1) * ngroups + 3) & ~3);
+  stage_digits_any<BITS>(kpg, raw, m.hmid_stride, K + 1, inter, bt, gsum, grs);
+  bar_sync_n(SL_NT);
+  pdl_launch();
+  trc.staged(m.trace);
+  const int gi = lane >> 2, t = lane & 3;
+  bool dead = false;
+  for (int e = warp; e <= K && !dead; e += SL_CW) {
+    const int s = e % T.S;
+    if (!__all_sync(0xffffffffu, mbar_wait(full + s, unsigned(e / T.S) & 1u))) { dead = true; break; }
+    const uint8_t* dt = ring + size_t(s) * T.slot;
+    const uint8_t* st = dt + 16 * rbp;
+    const uint8_t* btt = st + 16 * ss;
+    float y0, y1;
+    imma_rows_any<BITS, DT>(kpg, dt + gi * rbp, dt + (gi + 8) * rbp, st + gi * ss, st + (gi + 8) * ss, btt + gi * ss,
+                            btt + (gi + 8) * ss, bt + e * nkb * 12, gsum + e * ngroups, grs + e * ngroups, 0, ngroups,
+                            y0, y1);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty + s);
+    if (t == 0) {
+      if (gi < nrow) part[e * T.rpc + gi] = y0;
+      if (gi + 8 < nrow) part[e * T.rpc + gi + 8] = y1;
+    }
+  }
+  trc.looped(m.trace);
+  if (dead) sl_fail(T);
+  bar_sync_n(SL_NT);
+  // combine weights: computed by this CTA's producer (released to the
+  // consumers by the arrivals that completed the tiles' barriers) or stored
+  // by the router grid
+  for (int rl = tid; rl < nrow; rl += SL_NT) {
+    float acc = 0.f;
+    for (int e = 0; e <= K; ++e) {
+      const float we = m.logits ? (e < K ? r_w[e] : r_sh) : (e < K ? __ldcg(m.pick_w + e) : __ldcg(m.shared_scale));
+      acc = fmaf(we, part[e * T.rpc + rl], acc);
+    }
+    m.h[o0 + rl] += acc;
+  }
+  if (m.advance_sd && blockIdx.x == 0 && tid == 0) {
+    // Advance the sequence position and the token cursor once the last
+    // layer of the step is done (no other CTA of this grid reads them;
+    // dependents read them only after this grid completes).
+    *m.advance_sd->pos += 1;
+    *m.advance_cursor += 1;
+  }
+  trc.end(m.trace);
+}
+
+// ------------------------------------------------- per-format launchers --
+template <int B, int D>
+void igemv_fmt(const GemvArgs& a, const SliceTab& T, const RouterTail& rt, int grid, size_t smem, cudaStream_t st,
+               bool pdl) {
+  launch(k_igemv<B, D>, dim3(grid), dim3(SL_T), smem, st, pdl, a, T, rt);
+}
+template <int B, int D>
+void igateup_fmt(const MoeArgs& m, const SliceTab& T, int grid, size_t smem, cudaStream_t st, bool pdl) {
+  launch(k_igateup<B, D>, dim3(grid), dim3(SL_T), smem, st, pdl, m, T);
+}
+template <int B, int D>
+void idown_fmt(const MoeArgs& m, const SliceTab& T, int grid, size_t smem, cudaStream_t st, bool pdl) {
+  launch(k_idown<B, D>, dim3(grid), dim3(SL_T), smem, st, pdl, m, T);
+}
+
+#define SWL_INSTANTIATE_IMMA(B, D)                                                                                   \
+  template void igemv_fmt<B, D>(const GemvArgs&, const SliceTab&, const RouterTail&, int, size_t, cudaStream_t, bool); \
+  template void igateup_fmt<B, D>(const MoeArgs&, const SliceTab&, int, size_t, cudaStream_t, bool);                  \
+  template void idown_fmt<B, D>(const MoeArgs&, const SliceTab&, int, size_t, cudaStream_t, bool);
+
+}  // namespace swl

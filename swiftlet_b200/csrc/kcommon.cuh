@@ -52,21 +52,79 @@ __device__ __forceinline__ unsigned long long gtimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+
+// ---- mbarriers and bulk (TMA, non-tensor) copies into shared memory ----
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ void mbar_init(uint64_t* b, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+// Makes initialised barriers visible to the async (bulk copy) proxy.
+__device__ __forceinline__ void mbar_init_fence() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Waits for the phase of parity `parity` to complete, for at most about two
+// seconds (then returns false: the caller records an error and gives up).
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity) {
+  if (mbar_try(b, parity)) return true;
+  const unsigned long long t0 = gtimer();
+  for (int i = 0; i < (1 << 26); ++i) {
+    if (mbar_try(b, parity)) return true;
+    if (gtimer() - t0 > kWaitLimitNs) break;
+  }
+  return false;
+}
+// L2 policy for weights that are read once per token: evict them first, so
+// activations, recurrent state and the KV cache stay resident.
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+// Bulk copy of `bytes` (multiple of 16; both addresses 16-byte aligned) from
+// global to this CTA's shared memory, completing on mbarrier `b`.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* b, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(b)), "l"(policy)
+      : "memory");
+}
+// Named barrier 1 over the first n threads (the consumer warps of a
+// warp-specialised block; the producer warp never joins it).
+__device__ __forceinline__ void bar_sync_n(int n) { asm volatile("bar.sync 1, %0;" ::"r"(n) : "memory"); }
 // Per-block timeline record (thread 0): see Trace.
 struct TraceRec {
-  unsigned long long t0 = 0, t1 = 0;
+  unsigned long long t0 = 0, t1 = 0, t2 = 0, t3 = 0;
   __device__ __forceinline__ void start(const Trace& tr) { if (tr.buf && threadIdx.x == 0) t0 = gtimer(); }
   __device__ __forceinline__ void waited(const Trace& tr) { if (tr.buf && threadIdx.x == 0) t1 = gtimer(); }
+  __device__ __forceinline__ void staged(const Trace& tr) { if (tr.buf && threadIdx.x == 0) t2 = gtimer(); }
+  __device__ __forceinline__ void looped(const Trace& tr) { if (tr.buf && threadIdx.x == 0) t3 = gtimer(); }
   __device__ __forceinline__ void end(const Trace& tr) {
     if (tr.buf && threadIdx.x == 0) {
       const unsigned i = atomicAdd(tr.count, 1u);
       if (i < tr.cap) {
-        unsigned long long* r = tr.buf + 5ull * i;
+        unsigned long long* r = tr.buf + static_cast<unsigned long long>(kTraceFields) * i;
         r[0] = tr.tag;
         r[1] = blockIdx.x + 65536ull * blockIdx.y;
         r[2] = t0;
         r[3] = t1;
-        r[4] = gtimer();
+        r[4] = t2;
+        r[5] = t3;
+        r[6] = gtimer();
       }
     }
   }

@@ -18,9 +18,12 @@ struct StateDev {
 };
 
 // Optional per-block timeline (SWL_TRACE): each CTA appends one record of
-// {kernel tag, block, start ns, after-dependency-wait ns, end ns}.
+// {kernel tag, block, start ns, after-dependency-wait ns, inputs-staged ns,
+// main-loop-done ns, end ns} (the two middle marks are 0 where a kernel does
+// not set them).
+constexpr int kTraceFields = 7;
 struct Trace {
-  unsigned long long* buf = nullptr;  // [cap][5]
+  unsigned long long* buf = nullptr;  // [cap][kTraceFields]
   unsigned* count = nullptr;
   unsigned cap = 0;
   unsigned tag = 0;
@@ -30,7 +33,7 @@ struct Trace {
 enum Prologue : int {
   PRO_COPY = 0,      // x as given
   PRO_RMSNORM = 1,   // rmsnorm(x) * w (eps)
-  PRO_GATEDNORM = 2, // per head: rmsnorm(y) * w * silu(z) (DeltaNet output gate)
+  PRO_GATEDNORM = 2, // per head: rmsnorm(y) * w * g, g = silu(z) given (DeltaNet output gate)
 };
 enum Epilogue : int {
   EPI_STORE = 0,     // y[row] = acc
@@ -49,7 +52,7 @@ struct GemvArgs {
   int prologue = PRO_COPY;
   int epilogue = EPI_STORE;
   const float* x = nullptr;     // input vector [in] (PRO_GATEDNORM: y)
-  const float* aux = nullptr;   // norm weight (RMSNORM) / z vector (GATEDNORM)
+  const float* aux = nullptr;   // norm weight (RMSNORM) / silu(z) vector (GATEDNORM)
   const float* aux2 = nullptr;  // GATEDNORM: per-dim norm weight [head_dim]
   int head_dim = 0;             // GATEDNORM head size
   float eps = 1e-6f;
@@ -58,6 +61,7 @@ struct GemvArgs {
   float* argmax_val = nullptr;  // scratch [gridDim] values for argmax
   int* argmax_idx = nullptr;    // scratch [gridDim] indices
   unsigned* counter = nullptr;  // last-block counter for argmax
+  int* status = nullptr;        // bit 0: a bounded wait inside the kernel gave up
   Trace trace;
 };
 
@@ -78,6 +82,8 @@ struct RouterArgs {
   const uint8_t* pool;        // expert blobs of this layer (L2 prefetch of the picks), may be null
   int64_t pool_stride;
   uint32_t prefetch_bytes;    // bytes per expert to prefetch (multiple of 16)
+  int* status = nullptr;      // bit 0: a bounded wait inside the kernel gave up
+  int skip_topk = 0;          // the expert kernels route from the logits themselves
   Trace trace;
 };
 
@@ -85,15 +91,23 @@ struct MoeArgs {
   ExpertProj g, u, d;          // routed experts of this layer (pool addressing)
   QLin sg, su, sd;             // shared expert
   const float* x;              // [D] normalised
-  const int* pick_ids;
-  const float* pick_w;
-  const float* shared_scale;
+  int* pick_ids;
+  float* pick_w;
+  float* shared_scale;
   float* hmid;                 // [(K+1) * max_inter]
   int hmid_stride;
   int topk;
   float* h;                    // residual stream (down + combine adds here)
   const StateDev* advance_sd;  // when set: ++*advance_sd->pos and ++*advance_cursor after the layer
   int* advance_cursor;
+  int* status = nullptr;       // bit 0: a bounded wait inside the kernel gave up
+  // When set (integer tensor-core kernels only): the expert kernels compute
+  // the routing themselves from the router's E + 1 logits (the router then
+  // skips its top-k); gate/up CTA 0 also stores pick_ids / pick_w /
+  // shared_scale for observers.
+  const float* logits = nullptr;
+  int experts = 0;
+  int norm_topk = 0;
   Trace trace;
 };
 
@@ -108,7 +122,7 @@ struct DeltaArgs {
   int layer;
   int rows_per_block;      // dv rows per block
   float* y;                // [nv*dv] raw recurrence output
-  float* z;                // [nv*dv] gate input, de-interleaved
+  float* z;                // [nv*dv] silu of the gate input, de-interleaved
   Trace trace;
 };
 
@@ -147,6 +161,9 @@ void launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl);
 void launch_router(const RouterArgs& a, int experts, cudaStream_t stream, bool pdl);
 void launch_moe_gateup(const MoeArgs& a, cudaStream_t stream, bool pdl);
 void launch_moe_down(const MoeArgs& a, cudaStream_t stream, bool pdl);
+// True when both expert launches for `a` take the integer tensor-core kernels,
+// which can compute the routing from the router logits (MoeArgs::logits).
+bool moe_routes_from_logits(const MoeArgs& a, int experts);
 void launch_delta(const DeltaArgs& a, cudaStream_t stream, bool pdl);
 void launch_attn(const AttnArgs& a, cudaStream_t stream, bool pdl);
 void launch_embed(const EmbedArgs& a, int hidden, cudaStream_t stream, bool pdl);

@@ -113,7 +113,7 @@ __global__ void __launch_bounds__(DELTA_THREADS) k_delta(const DeltaArgs a) {
   }
   for (int i = threadIdx.x; i < RB; i += blockDim.x) {
     const int d = slice * RB + i;
-    a.z[hv * dv + d] = a.proj[delta_z(a, hv, d)];
+    a.z[hv * dv + d] = silu_ref(a.proj[delta_z(a, hv, d)]);  // the output gate's activation
   }
   __syncthreads();
   pdl_launch();

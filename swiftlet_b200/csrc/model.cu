@@ -111,6 +111,7 @@ struct Model {
   float *rlogits = nullptr, *pick_w = nullptr, *sscale = nullptr, *hmid = nullptr, *part = nullptr, *logits = nullptr;
   float* amax_v = nullptr;
   int *pick_ids = nullptr, *tokens = nullptr, *cursor = nullptr, *err = nullptr, *amax_i = nullptr, *greedy = nullptr;
+  int* kstatus = nullptr;  // bit 0: a bounded wait in a kernel gave up (word after the logits)
   unsigned *ctr_router = nullptr, *ctr_attn = nullptr, *ctr_amax = nullptr;
   StateDev* cur = nullptr;
   int hmid_stride = 0, max_tokens = 0, attn_chunks = 64, chunk_cap = 0, max_ctx_cap = 0;
@@ -154,6 +155,15 @@ struct Model {
   void ensure_graphs();
   void ensure_tokens(int n);
   void run(State* s, int n, bool amax);
+  // Throws when a kernel of the last steps reported a bounded wait that gave
+  // up (its results are then unreliable); clears the word for the next step.
+  void check_status(const int* host_word) {
+    if (*host_word == 0) return;
+    SWL_CUDA(cudaMemsetAsync(kstatus, 0, 4, stream));
+    SWL_CUDA(cudaStreamSynchronize(stream));
+    throw Error(ERR_CUDA, "a decode kernel timed out waiting for its weight copies (status " +
+                              std::to_string(*host_word) + ")");
+  }
 };
 
 Model::~Model() {
@@ -466,7 +476,8 @@ void Model::alloc_scratch() {
   rlogits = f(c.experts + 1); pick_w = f(c.topk); sscale = f(1);
   hmid = f(size_t(c.topk + 1) * hmid_stride);
   part = f(size_t(KVH) * attn_chunks * G * (hd + 2));
-  logits = f(c.vocab);
+  logits = f(size_t(c.vocab) + 4);
+  kstatus = reinterpret_cast<int*>(logits + c.vocab);  // read back with the logits
   amax_v = f(1024);
   pick_ids = reinterpret_cast<int*>(dmalloc(size_t(std::max(c.topk, 1)) * 4));
   cursor = reinterpret_cast<int*>(dmalloc(4));
@@ -481,12 +492,13 @@ void Model::alloc_scratch() {
   SWL_CUDA(cudaMemset(ctr_attn, 0, size_t(KVH) * 4));
   SWL_CUDA(cudaMemset(ctr_amax, 0, 4));
   SWL_CUDA(cudaMemset(err, 0, 4));
+  SWL_CUDA(cudaMemset(kstatus, 0, 4));
   {
     std::vector<int> ids(std::max(c.topk, 1));
     for (size_t i = 0; i < ids.size(); ++i) ids[i] = int(i % c.experts);
     SWL_CUDA(cudaMemcpy(pick_ids, ids.data(), ids.size() * 4, cudaMemcpyHostToDevice));
   }
-  SWL_CUDA(cudaMallocHost(&h_logits, size_t(c.vocab) * 4));
+  SWL_CUDA(cudaMallocHost(&h_logits, (size_t(c.vocab) + 1) * 4));
   ensure_tokens(4096);
   // GEMV segment outputs
   for (auto& ld : L) {
@@ -548,7 +560,7 @@ void Model::open(const std::string& d, double pool_gb, int dev) {
     const long cap = atol(tr);
     if (cap > 0) {
       trace.cap = unsigned(cap);
-      trace.buf = reinterpret_cast<unsigned long long*>(dmalloc(size_t(cap) * 5 * 8));
+      trace.buf = reinterpret_cast<unsigned long long*>(dmalloc(size_t(cap) * kTraceFields * 8));
       trace.count = reinterpret_cast<unsigned*>(dmalloc(4));
       SWL_CUDA(cudaMemset(trace.count, 0, 4));
     }
@@ -589,7 +601,7 @@ void Model::enqueue_layer(int l, cudaStream_t st, bool advance) {
   GemvArgs g;
   for (int s = 0; s < ld.n_in; ++s) { g.seg[s].lin = ld.in_lin[s]; g.seg[s].y = ld.in_y[s]; }
   g.nseg = ld.n_in; g.in = c.hidden; g.prologue = PRO_RMSNORM; g.epilogue = EPI_STORE;
-  g.x = h; g.aux = ld.in_norm; g.eps = float(c.eps);
+  g.x = h; g.aux = ld.in_norm; g.eps = float(c.eps); g.status = kstatus;
   const unsigned lt = 16u * unsigned(l + 1);
   g.trace = tagged(lt + 2);
   launch_gemv(g, st, pdl);
@@ -603,7 +615,7 @@ void Model::enqueue_layer(int l, cudaStream_t st, bool advance) {
     GemvArgs o;
     o.seg[0].lin = ld.out_lin; o.seg[0].y = h; o.nseg = 1; o.in = c.value_dim();
     o.prologue = PRO_GATEDNORM; o.epilogue = EPI_RESIDUAL; o.x = yv; o.aux = zv; o.aux2 = ld.dnorm;
-    o.head_dim = c.dv; o.eps = float(c.eps);
+    o.head_dim = c.dv; o.eps = float(c.eps); o.status = kstatus;
     o.trace = tagged(lt + 4);
     launch_gemv(o, st, pdl);
   } else {
@@ -616,22 +628,24 @@ void Model::enqueue_layer(int l, cudaStream_t st, bool advance) {
     launch_attn(a, st, pdl);
     GemvArgs o;
     o.seg[0].lin = ld.out_lin; o.seg[0].y = h; o.nseg = 1; o.in = c.heads * c.head_dim;
-    o.prologue = PRO_COPY; o.epilogue = EPI_RESIDUAL; o.x = att;
+    o.prologue = PRO_COPY; o.epilogue = EPI_RESIDUAL; o.x = att; o.status = kstatus;
     o.trace = tagged(lt + 4);
     launch_gemv(o, st, pdl);
   }
-  RouterArgs r;
-  r.gate = ld.router; r.sgate = ld.sgate; r.h = h; r.norm_w = ld.post_norm; r.eps = float(c.eps);
-  r.x_out = xmoe; r.logits = rlogits; r.pick_ids = pick_ids; r.pick_w = pick_w; r.shared_scale = sscale;
-  r.counter = ctr_router; r.topk = c.topk; r.norm_topk = c.norm_topk;
-  r.pool = nullptr; r.pool_stride = stride; r.prefetch_bytes = 0;
-  r.trace = tagged(lt + 5);
-  launch_router(r, c.experts, st, pdl);
   MoeArgs m;
   m.g = ld.eg; m.u = ld.eu; m.d = ld.ed; m.sg = ld.sh_g; m.su = ld.sh_u; m.sd = ld.sh_d;
   m.x = xmoe; m.pick_ids = pick_ids; m.pick_w = pick_w; m.shared_scale = sscale;
   m.hmid = hmid; m.hmid_stride = hmid_stride; m.topk = c.topk; m.h = h;
-  m.advance_sd = advance ? cur : nullptr; m.advance_cursor = cursor;
+  m.advance_sd = advance ? cur : nullptr; m.advance_cursor = cursor; m.status = kstatus;
+  const bool route_in_moe = moe_routes_from_logits(m, c.experts);
+  if (route_in_moe) { m.logits = rlogits; m.experts = c.experts; m.norm_topk = c.norm_topk; }
+  RouterArgs r;
+  r.gate = ld.router; r.sgate = ld.sgate; r.h = h; r.norm_w = ld.post_norm; r.eps = float(c.eps);
+  r.x_out = xmoe; r.logits = rlogits; r.pick_ids = pick_ids; r.pick_w = pick_w; r.shared_scale = sscale;
+  r.counter = ctr_router; r.topk = c.topk; r.norm_topk = c.norm_topk;
+  r.pool = nullptr; r.pool_stride = stride; r.prefetch_bytes = 0; r.status = kstatus; r.skip_topk = route_in_moe;
+  r.trace = tagged(lt + 5);
+  launch_router(r, c.experts, st, pdl);
   m.trace = tagged(lt + 6);
   launch_moe_gateup(m, st, pdl);
   m.trace = tagged(lt + 7);
@@ -650,6 +664,7 @@ void Model::enqueue_head(cudaStream_t st, bool amax) {
   GemvArgs g;
   g.seg[0].lin = lm_head; g.seg[0].y = logits; g.nseg = 1; g.in = cfg.hidden;
   g.prologue = PRO_RMSNORM; g.epilogue = EPI_STORE; g.x = h; g.aux = final_norm; g.eps = float(cfg.eps);
+  g.status = kstatus;
   if (amax) { g.argmax_out = greedy; g.argmax_val = amax_v; g.argmax_idx = amax_i; g.counter = ctr_amax; }
   g.trace = tagged(8);
   launch_gemv(g, st, use_pdl);
@@ -854,8 +869,9 @@ int swl_step(swl_model* model, swl_state* state, const int32_t* tokens, int32_t 
   memcpy(m.h_tokens, tokens, size_t(n) * 4);
   SWL_CUDA(cudaMemcpyAsync(m.tokens, m.h_tokens, size_t(n) * 4, cudaMemcpyHostToDevice, m.stream));
   m.run(&state->s, n, false);
-  SWL_CUDA(cudaMemcpyAsync(m.h_logits, m.logits, size_t(m.cfg.vocab) * 4, cudaMemcpyDeviceToHost, m.stream));
+  SWL_CUDA(cudaMemcpyAsync(m.h_logits, m.logits, (size_t(m.cfg.vocab) + 1) * 4, cudaMemcpyDeviceToHost, m.stream));
   SWL_CUDA(cudaStreamSynchronize(m.stream));
+  m.check_status(reinterpret_cast<const int*>(m.h_logits + m.cfg.vocab));
   memcpy(logits_out, m.h_logits, size_t(m.cfg.vocab) * 4);
   API_END
 }
@@ -1083,13 +1099,15 @@ int swl_trace_dump(swl_model* model, const char* path) {
   unsigned n = 0;
   SWL_CUDA(cudaMemcpy(&n, m.trace.count, 4, cudaMemcpyDeviceToHost));
   n = std::min(n, m.trace.cap);
-  std::vector<unsigned long long> buf(size_t(n) * 5);
+  std::vector<unsigned long long> buf(size_t(n) * kTraceFields);
   if (n) SWL_CUDA(cudaMemcpy(buf.data(), m.trace.buf, buf.size() * 8, cudaMemcpyDeviceToHost));
   FILE* f = fopen(path, "w");
   if (!f) throw Error(ERR_IO, std::string("cannot write ") + path);
-  fprintf(f, "tag,block,start_ns,waited_ns,end_ns\n");
-  for (unsigned i = 0; i < n; ++i)
-    fprintf(f, "%llu,%llu,%llu,%llu,%llu\n", buf[5 * i], buf[5 * i + 1], buf[5 * i + 2], buf[5 * i + 3], buf[5 * i + 4]);
+  fprintf(f, "tag,block,start_ns,waited_ns,staged_ns,looped_ns,end_ns\n");
+  for (unsigned i = 0; i < n; ++i) {
+    const unsigned long long* r = buf.data() + size_t(i) * kTraceFields;
+    fprintf(f, "%llu,%llu,%llu,%llu,%llu,%llu,%llu\n", r[0], r[1], r[2], r[3], r[4], r[5], r[6]);
+  }
   fclose(f);
   SWL_CUDA(cudaMemset(m.trace.count, 0, 4));
   API_END
