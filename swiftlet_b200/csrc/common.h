@@ -68,6 +68,7 @@ struct QLin {
 struct ExpertProj {
   QLin lin;
   int64_t wstride = 0, sstride = 0, bstride = 0;
+  int count = 0;  // experts in the pool (0: unknown)
 };
 
 __host__ __device__ inline int dtype_bytes(int dt) { return dt == DT_F32 ? 4 : 2; }

@@ -6,6 +6,9 @@
 // launch) can start on the rest of each SM.
 #include <algorithm>
 #include <cstdlib>
+#include <mutex>
+
+#include <cudaTypedefs.h>
 
 #include "kernels.h"
 #include "slice.h"
@@ -37,11 +40,13 @@ void sgateup_fmt(const MoeArgs&, const SliceTab&, int, size_t, cudaStream_t, boo
 template <int B, int D>
 void sdown_fmt(const MoeArgs&, const SliceTab&, int, size_t, cudaStream_t, bool);
 template <int B, int D>
-void igemv_fmt(const GemvArgs&, const SliceTab&, const RouterTail&, int, size_t, cudaStream_t, bool);
+void igemv_fmt(const GemvArgs&, const SliceTab&, const TileMaps&, const RouterTail&, int, int, size_t, cudaStream_t,
+               bool);
 template <int B, int D>
-void igateup_fmt(const MoeArgs&, const SliceTab&, int, size_t, cudaStream_t, bool);
+void igateup_fmt(const MoeArgs&, const SliceTab&, const TileMaps&, int, int, size_t, cudaStream_t, bool);
 template <int B, int D>
-void idown_fmt(const MoeArgs&, const SliceTab&, int, size_t, cudaStream_t, bool);
+void idown_fmt(const MoeArgs&, const SliceTab&, const TileMaps&, int, int, size_t, cudaStream_t, bool);
+constexpr int kImmaWarps = 8;  // consumer warps of the tensor-core kernels (IW)
 
 constexpr int GT = 128;
 static constexpr int kBlocksPerSm = 2;
@@ -139,6 +144,15 @@ static SegTab make_tab(const QLin* lins, float* const* ys, int n, int R) {
 // the next kernel (programmatic dependent launch) fits beside it and copies
 // its weights while this one runs.
 static constexpr size_t kSliceSmem = 110 * 1024;
+// Budget of the launch being planned (GemvArgs / MoeArgs::smem_kb, else the
+// default above): a kernel whose neighbours in the launch sequence are small
+// may take more, so that all of its tiles are copied before its wait.
+static thread_local size_t g_budget = kSliceSmem;
+struct BudgetScope {
+  size_t old;
+  explicit BudgetScope(int kb) : old(g_budget) { g_budget = kb > 0 ? size_t(kb) * 1024 : kSliceSmem; }
+  ~BudgetScope() { g_budget = old; }
+};
 
 static bool slice_enabled() {
   static const int on = std::getenv("SWL_LEGACY_GEMV") ? 0 : 1;  // diagnostics: the register-streaming kernels
@@ -190,11 +204,11 @@ static size_t slice_layout(SliceTab& T, int xs_f, int cs_f, int part_f, int raw_
 static bool slice_ring(SliceTab& T, int max_tiles, int xs_f, int cs_f, int part_f, int raw_f, size_t& smem) {
   T.S = 0;
   const size_t stage = slice_layout(T, xs_f, cs_f, part_f, raw_f);
-  if (stage + size_t(T.slot) + 16 > kSliceSmem) return false;
-  const int fit = int((kSliceSmem - stage - 16) / (size_t(T.slot) + 16));
+  if (stage + size_t(T.slot) + 16 > g_budget) return false;
+  const int fit = int((g_budget - stage - 16) / (size_t(T.slot) + 16));
   T.S = std::max(1, std::min({max_tiles, fit, 32}));
   smem = slice_layout(T, xs_f, cs_f, part_f, raw_f);
-  return smem <= kSliceSmem;
+  return smem <= g_budget;
 }
 
 // Dense GEMV over up to four same-format segments; R = rows per sub-warp and tile.
@@ -228,6 +242,41 @@ static bool plan_dense(const QLin* lins, float* const* ys, int nseg, int in, int
   return slice_ring(T, max_tiles, in, in / wpc + 4, T.W > 1 ? T.W * T.rpc : 0, in, smem);
 }
 
+// ------------------------------------------------------- tensor maps -----
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// against the driver library).
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    cudaGetLastError();
+  });
+  return fn;
+}
+// Map of a row-major matrix of `rows` rows of rb bytes (rb % 128 == 0) as
+// {128 bytes, rows, rb / 128 segments[, experts at estride bytes]}: a box of
+// `box` rows lands in shared memory as [segment][row][128 bytes], 128-byte
+// swizzled (16-byte chunk c of row r at chunk c ^ (r & 7)).
+static bool encode_rows(CUtensorMap* m, const void* base, int64_t rows, int64_t rb, int box, int experts,
+                        int64_t estride) {
+  auto enc = tensor_map_encoder();
+  if (!enc || rows < 1 || rb % 128 || rb / 128 > 256 || !aligned16(base) || (experts > 0 && estride % 16)) return false;
+  const int rank = experts > 0 ? 4 : 3;
+  cuuint64_t dims[4] = {128, cuuint64_t(rows), cuuint64_t(rb / 128), cuuint64_t(experts > 0 ? experts : 1)};
+  cuuint64_t strides[3] = {cuuint64_t(rb), 128, cuuint64_t(estride)};
+  cuuint32_t boxd[4] = {128, cuuint32_t(box), cuuint32_t(rb / 128), 1};
+  cuuint32_t es[4] = {1, 1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, rank, const_cast<void*>(base), dims, strides, boxd, es,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+static int round1024(int v) { return (v + 1023) / 1024 * 1024; }
+
 // ------------------------------------------- integer tensor-core planning --
 // 4/8-bit weights with groups of >= 32 take the mma.sync (u8 x s8) kernels of
 // imma_impl.cuh; slots hold rows at a 16-byte padded pitch.
@@ -238,27 +287,44 @@ static bool imma_enabled() {
 static bool imma_fmt_ok(const QLin& l) {
   return slice_fmt_ok(l) && (l.bits == 4 || l.bits == 8) && l.gs >= 32 && l.gs <= 128 && (l.in / l.gs) % 4 == 0;
 }
-// Warps per tile (K split) for a CTA of `tiles` tiles and `ngroups`
-// quantisation groups per row: the fewest rounds of tile work, counting a
-// split tile as 1 / KS of a tile plus a small cost for the combine.
-static int choose_ks(int tiles, int ngroups) {
-  int best = 0;
+// Warps per tile (K split) and ring slots for a CTA of `tiles` tiles
+// (`max_tiles` at most) and `ngroups` quantisation groups per row: the fewest
+// rounds of tile work, counting a split tile as 1 / KS of a tile plus a small
+// cost for the combine. Tile i goes to warp group i % NG (NG = warps / KS);
+// when slots are reused (more tiles than slots) the slot count must be a
+// multiple of NG, so that every slot belongs to one group, which waits for its
+// phases in order (a wait on the parity of a phase two ahead would alias).
+// Lays out the shared memory for the chosen slot count.
+static bool settle_ks(SliceTab& T, int tiles, int max_tiles, int ngroups, int xs_f, int cs_f, int part_f, int raw_f,
+                      size_t& smem) {
+  int best = 0, best_s = 0;
   double best_cost = 1e30;
-  for (int ks : {1, 2, 4}) {
-    if (ngroups % (4 * ks)) continue;  // whole steps of four groups per warp
-    const int groups = SL_CW / ks;
-    const double cost = double((tiles + groups - 1) / groups) * (1.0 / ks + (ks > 1 ? 0.08 : 0.0));
-    if (cost < best_cost - 1e-9) { best_cost = cost; best = ks; }
+  for (int ks : {1, 2, 4, 8}) {
+    if (ngroups % (4 * ks)) continue;  // whole steps of four groups per warp, each starting on a 128-byte segment
+    const int ng = kImmaWarps / ks;
+    int S = T.S;
+    if (max_tiles > S) S = S / ng * ng;
+    if (S < 1) continue;
+    const double cost = double((tiles + ng - 1) / ng) * (1.0 / ks + (ks > 1 ? 0.08 : 0.0));
+    if (cost < best_cost - 1e-9) { best_cost = cost; best = ks; best_s = S; }
   }
-  return best;
+  if (!best) return false;
+  T.W = best;
+  T.S = best_s;
+  smem = slice_layout(T, xs_f, cs_f, part_f, raw_f);
+  if (smem > g_budget) return false;
+  smem += 1024;  // the kernel aligns its ring to 1024 bytes
+  return true;
 }
-static int imma_rows_bytes(const QLin& l, int rows) {
-  return rows * (int(l.row_bytes) + 16 + 2 * int(l.srow) * scale_bytes(l.dt));
+// One matrix block of a slot: box rows of weights, scale rows and bias rows,
+// rounded to 1024 bytes (the next block's swizzled weights stay aligned).
+static int imma_block_bytes(const QLin& l, int box) {
+  return round1024(box * (int(l.row_bytes) + 2 * int(l.srow) * scale_bytes(l.dt)));
 }
 
 static bool plan_idense(const QLin* lins, float* const* ys, int nseg, int in, int prologue, int head_dim,
                         const float* x, const float* aux, const float* aux2, const float* x_out, int* status,
-                        SliceTab& T, int& grid, size_t& smem) {
+                        SliceTab& T, TileMaps& M, int& grid, size_t& smem) {
   if (!slice_enabled() || !imma_enabled()) return false;
   const QLin& l0 = lins[0];
   for (int s = 0; s < nseg; ++s) if (!imma_fmt_ok(lins[s]) || lins[s].in != in) return false;
@@ -280,15 +346,16 @@ static bool plan_idense(const QLin* lins, float* const* ys, int nseg, int in, in
   if (T.total <= 0) return false;
   T.rpc = std::max((T.total + sm_count() - 1) / sm_count(), 16);
   grid = (T.total + T.rpc - 1) / T.rpc;
-  T.slot = imma_rows_bytes(l0, 16);
+  for (int sg = 0; sg < nseg; ++sg)
+    if (!encode_rows(&M.m[sg], lins[sg].w, lins[sg].out, lins[sg].row_bytes, 16, 0, 0)) return false;
+  T.slot = imma_block_bytes(l0, 16);
   const int max_tiles = (T.rpc + 15) / 16 + nseg - 1;
-  T.W = choose_ks((T.rpc + 15) / 16, in >> T.gs_shift);
-  if (!T.W) return false;
   T.status = status;
-  // xs: B table (3 bytes per input), cs: group sums, part: K-split partials,
-  // raw: the staged input
-  // cs: group sums then group digit scales
-  return slice_ring(T, max_tiles, 3 * in / 4, 2 * (((in >> T.gs_shift) + 3) & ~3) + 4, 2 * SL_CW * 16, in, smem);
+  // xs: B table (3 bytes per input), cs: group sums then group digit scales,
+  // part: K-split partials, raw: the staged input
+  const int xs_f = 3 * in / 4, cs_f = 2 * (((in >> T.gs_shift) + 3) & ~3) + 4, part_f = 2 * kImmaWarps * 16;
+  return slice_ring(T, max_tiles, xs_f, cs_f, part_f, in, smem) &&
+         settle_ks(T, (T.rpc + 15) / 16, max_tiles, in >> T.gs_shift, xs_f, cs_f, part_f, in, smem);
 }
 
 static bool expert_strides_ok(const ExpertProj& p) {
@@ -317,7 +384,7 @@ static bool plan_gateup(const MoeArgs& m, SliceTab& T, int& grid, size_t& smem) 
   return slice_ring(T, max_tiles, g.in, g.in / wpc + 4, 0, g.in, smem);
 }
 
-static bool plan_igateup(const MoeArgs& m, SliceTab& T, int& grid, size_t& smem) {
+static bool plan_igateup(const MoeArgs& m, SliceTab& T, TileMaps& M, int& grid, size_t& smem) {
   if (!slice_enabled() || !imma_enabled()) return false;
   const QLin& g = m.g.lin;
   if (!imma_fmt_ok(g) || !imma_fmt_ok(m.u.lin) || !imma_fmt_ok(m.sg) || !imma_fmt_ok(m.su)) return false;
@@ -332,16 +399,23 @@ static bool plan_igateup(const MoeArgs& m, SliceTab& T, int& grid, size_t& smem)
   T.sh_rpc = std::max(1, (sh + n - 1) / n);
   T.rt_rpc = nq > 0 ? std::max(1, (nq + n - 1) / n) : 0;
   grid = std::max(1, std::max((sh + T.sh_rpc - 1) / T.sh_rpc, nq > 0 ? (nq + T.rt_rpc - 1) / T.rt_rpc : 0));
-  T.slot = 2 * imma_rows_bytes(g, 8);
+  if (!encode_rows(&M.m[0], m.sg.w, m.sg.out, m.sg.row_bytes, 8, 0, 0) ||
+      !encode_rows(&M.m[1], m.su.w, m.su.out, m.su.row_bytes, 8, 0, 0))
+    return false;
+  if (m.topk > 0 && (m.g.count < 1 || m.u.count < 1 ||
+                     !encode_rows(&M.m[2], g.w, g.out, g.row_bytes, 8, m.g.count, m.g.wstride) ||
+                     !encode_rows(&M.m[3], m.u.lin.w, m.u.lin.out, m.u.lin.row_bytes, 8, m.u.count, m.u.wstride)))
+    return false;
+  T.slot = 2 * imma_block_bytes(g, 8);
   const int max_tiles = (T.sh_rpc + 7) / 8 + (nq > 0 ? (T.rt_rpc + 7) / 8 + (T.rt_rpc + g.out - 1) / g.out + 1 : 0);
-  T.W = choose_ks((T.sh_rpc + 7) / 8 + (T.rt_rpc + 7) / 8, g.in >> T.gs_shift);
-  if (!T.W) return false;
   T.status = m.status;
-  return slice_ring(T, max_tiles, 3 * g.in / 4, 2 * (((g.in >> T.gs_shift) + 3) & ~3) + 4, 2 * SL_CW * 16, g.in,
-                    smem);
+  const int xs_f = 3 * g.in / 4, cs_f = 2 * (((g.in >> T.gs_shift) + 3) & ~3) + 4, part_f = 2 * kImmaWarps * 16;
+  return slice_ring(T, max_tiles, xs_f, cs_f, part_f, g.in, smem) &&
+         settle_ks(T, (T.sh_rpc + 7) / 8 + (T.rt_rpc + 7) / 8, max_tiles, g.in >> T.gs_shift, xs_f, cs_f, part_f,
+                   g.in, smem);
 }
 
-static bool plan_idown(const MoeArgs& m, SliceTab& T, int& grid, size_t& smem) {
+static bool plan_idown(const MoeArgs& m, SliceTab& T, TileMaps& M, int& grid, size_t& smem) {
   if (!slice_enabled() || !imma_enabled()) return false;
   const QLin& d = m.d.lin;
   if (!imma_fmt_ok(d) || !imma_fmt_ok(m.sd) || !expert_strides_ok(m.d)) return false;
@@ -355,18 +429,26 @@ static bool plan_idown(const MoeArgs& m, SliceTab& T, int& grid, size_t& smem) {
   T.rpc = std::min(16, (D + sm_count() - 1) / sm_count());
   T.TR = T.rpc;
   grid = (D + T.rpc - 1) / T.rpc;
-  T.slot = imma_rows_bytes(d, 16);
+  if (!encode_rows(&M.m[0], m.sd.w, m.sd.out, m.sd.row_bytes, 16, 0, 0)) return false;
+  if (m.topk > 0 && (m.d.count < 1 || !encode_rows(&M.m[2], d.w, d.out, d.row_bytes, 16, m.d.count, m.d.wstride)))
+    return false;
+  T.slot = imma_block_bytes(d, 16);
   T.status = m.status;
   const int nkb = d.in >> 5;
-  return slice_ring(T, K1, K1 * nkb * 24, 2 * ((K1 * (d.in >> T.gs_shift) + 3) & ~3) + 4, K1 * T.rpc,
-                    K1 * m.hmid_stride, smem);
+  // one slot per expert slot (warp e % 8 waits on slot e only once)
+  if (!slice_ring(T, K1, K1 * nkb * 24, 2 * ((K1 * (d.in >> T.gs_shift) + 3) & ~3) + 4, K1 * T.rpc,
+                  K1 * m.hmid_stride, smem) || T.S != K1)
+    return false;
+  smem += 1024;  // the kernel aligns its ring to 1024 bytes
+  return true;
 }
 
 bool moe_routes_from_logits(const MoeArgs& m, int experts) {
   SliceTab T;
+  TileMaps M;
   int grid = 0;
   size_t smem = 0;
-  return experts <= 512 && m.topk <= 16 && plan_igateup(m, T, grid, smem) && plan_idown(m, T, grid, smem);
+  return experts <= 512 && m.topk <= 16 && plan_igateup(m, T, M, grid, smem) && plan_idown(m, T, M, grid, smem);
 }
 
 // Down: CTA b takes output rows [b*rpc, (b+1)*rpc) of every picked expert.
@@ -392,6 +474,7 @@ static bool plan_down(const MoeArgs& m, SliceTab& T, int& grid, size_t& smem) {
 }
 
 void launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl) {
+  const BudgetScope budget(a.smem_kb);
   const QLin& l0 = a.seg[0].lin;
   for (int s = 1; s < a.nseg; ++s)
     if (a.seg[s].lin.bits != l0.bits || a.seg[s].lin.dt != l0.dt || a.seg[s].lin.row_bytes != l0.row_bytes ||
@@ -409,10 +492,11 @@ void launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl) {
     SliceTab ST;
     int sgrid = 0, sR = 1;
     size_t ssmem = 0;
-    if (plan_idense(lins, ys, a.nseg, a.in, a.prologue, a.head_dim, a.x, a.aux, a.aux2, a.x_out, a.status, ST,
+    TileMaps TM;
+    if (plan_idense(lins, ys, a.nseg, a.in, a.prologue, a.head_dim, a.x, a.aux, a.aux2, a.x_out, a.status, ST, TM,
                     sgrid, ssmem)) {
       const RouterTail none;
-#define CALL(B, D) igemv_fmt<B, D>(a, ST, none, sgrid, ssmem, st, pdl)
+#define CALL(B, D) igemv_fmt<B, D>(a, ST, TM, none, ST.kpg(), sgrid, ssmem, st, pdl)
       SWL_DISPATCH_IMMA(l0.bits, l0.dt, CALL);
 #undef CALL
       return;
@@ -450,8 +534,9 @@ void launch_router(const RouterArgs& r, int E, cudaStream_t st, bool pdl) {
     SliceTab ST;
     int sgrid = 0, sR = 1;
     size_t ssmem = 0;
+    TileMaps TM;
     const bool imma = E <= r.gate.in && plan_idense(lins, ys, 2, r.gate.in, PRO_RMSNORM, 0, r.h, r.norm_w, nullptr,
-                                                    r.x_out, r.status, ST, sgrid, ssmem);
+                                                    r.x_out, r.status, ST, TM, sgrid, ssmem);
     if (imma || (E <= r.gate.in && plan_dense(lins, ys, 2, r.gate.in, PRO_RMSNORM, 0, r.h, r.norm_w, nullptr, r.x_out,
                                               r.status, ST, sR, sgrid, ssmem))) {
       GemvArgs a;
@@ -463,7 +548,7 @@ void launch_router(const RouterArgs& r, int E, cudaStream_t st, bool pdl) {
       rt.E = E; rt.topk = r.topk; rt.norm_topk = r.norm_topk;
       rt.pick_ids = r.pick_ids; rt.pick_w = r.pick_w; rt.shared_scale = r.shared_scale; rt.counter = r.counter;
       if (imma) {
-#define CALL(B, D) igemv_fmt<B, D>(a, ST, rt, sgrid, ssmem, st, pdl)
+#define CALL(B, D) igemv_fmt<B, D>(a, ST, TM, rt, ST.kpg(), sgrid, ssmem, st, pdl)
         SWL_DISPATCH_IMMA(r.gate.bits, r.gate.dt, CALL);
 #undef CALL
       } else {
@@ -487,6 +572,7 @@ void launch_router(const RouterArgs& r, int E, cudaStream_t st, bool pdl) {
 }
 
 void launch_moe_gateup(const MoeArgs& m, cudaStream_t st, bool pdl) {
+  const BudgetScope budget(m.smem_kb);
   const QLin& g = m.g.lin;
   if (m.sg.bits != g.bits || m.sg.dt != g.dt || m.sg.row_bytes != g.row_bytes || m.u.lin.row_bytes != g.row_bytes ||
       m.su.row_bytes != g.row_bytes || m.sg.srow != g.srow)
@@ -495,8 +581,9 @@ void launch_moe_gateup(const MoeArgs& m, cudaStream_t st, bool pdl) {
     SliceTab ST;
     int sgrid = 0;
     size_t ssmem = 0;
-    if (plan_igateup(m, ST, sgrid, ssmem)) {
-#define CALL(B, D) igateup_fmt<B, D>(m, ST, sgrid, ssmem, st, pdl)
+    TileMaps TM;
+    if (plan_igateup(m, ST, TM, sgrid, ssmem)) {
+#define CALL(B, D) igateup_fmt<B, D>(m, ST, TM, ST.kpg(), sgrid, ssmem, st, pdl)
       SWL_DISPATCH_IMMA(g.bits, g.dt, CALL);
 #undef CALL
       return;
@@ -530,8 +617,9 @@ void launch_moe_down(const MoeArgs& m, cudaStream_t st, bool pdl) {
     SliceTab ST;
     int sgrid = 0;
     size_t ssmem = 0;
-    if (plan_idown(m, ST, sgrid, ssmem)) {
-#define CALL(B, D_) idown_fmt<B, D_>(m, ST, sgrid, ssmem, st, pdl)
+    TileMaps TM;
+    if (plan_idown(m, ST, TM, sgrid, ssmem)) {
+#define CALL(B, D_) idown_fmt<B, D_>(m, ST, TM, ST.kpg(), sgrid, ssmem, st, pdl)
       SWL_DISPATCH_IMMA(d.bits, d.dt, CALL);
 #undef CALL
       return;

@@ -26,6 +26,10 @@
 
 namespace swl {
 
+constexpr int IW = 8;               // consumer warps of the tensor-core kernels
+constexpr int IM_NT = IW * 32;      // consumer threads
+constexpr int IM_T = IM_NT + 32;    // + one producer warp
+
 // D += A * B on the integer tensor cores (16x8x32, u8 x s8 -> s32).
 __device__ __forceinline__ void mma_u8s8(int (&d)[4], const uint32_t (&a)[4], uint2 b) {
   asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
@@ -117,7 +121,7 @@ __device__ __forceinline__ void stage_digits(const float* x, int stride, int nve
                                              float* grs) {
   const int tid = threadIdx.x, t = tid & 3;
   const int gpv = n / (32 * KPG), items = nvec * gpv * 4;
-  for (int base = 0; base < items; base += SL_NT) {
+  for (int base = 0; base < items; base += IM_NT) {
     const int it = base + tid;
     const bool ok = it < items;
     const int G = ok ? it >> 2 : 0, vec = G / gpv, g = G - vec * gpv;
@@ -154,14 +158,6 @@ __device__ __forceinline__ void stage_digits(const float* x, int stride, int nve
     }
   }
 }
-template <int BITS>
-__device__ __forceinline__ void stage_digits_any(int kpg, const float* x, int stride, int nvec, int n, uint2* bt,
-                                                 float* gsum, float* grs) {
-  if (kpg == 2) stage_digits<BITS, 2>(x, stride, nvec, n, bt, gsum, grs);
-  else if (kpg == 1) stage_digits<BITS, 1>(x, stride, nvec, n, bt, gsum, grs);
-  else stage_digits<BITS, 4>(x, stride, nvec, n, bt, gsum, grs);
-}
-
 // Order-preserving unsigned key of a float (larger float, larger key).
 __device__ __forceinline__ unsigned f_key(float f) {
   const unsigned u = __float_as_uint(f);
@@ -258,38 +254,58 @@ __device__ __forceinline__ float4 sm_scalar4(const uint8_t* p, int g) {
 }
 __device__ __forceinline__ float f4_at(const float4 v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
 
+// Weight tiles arrive by tensor TMA with the 128-byte swizzle, laid out
+// [row segment of 128 bytes][row][128 bytes] (segb = rows per box * 128 bytes
+// per segment) with 16-byte chunk c of row r stored at chunk c ^ (r & 7): the
+// 8 rows a warp reads at once then fall on distinct shared-memory banks.
+__device__ __forceinline__ int swz_off(int k16, int rx, int segb) {
+  return (k16 >> 3) * segb + (((k16 & 7) << 4) ^ rx);
+}
+
 // One 16-row tile against staged digits over quantisation groups
 // [g_begin, g_end) ((g_end - g_begin) % 4 == 0, KPG 32-weight blocks per
-// group): rows r0 = T/4 and r1 = T/4 + 8 of the tile, whose weights start at
-// w0 / w1 (row pitch already applied) and whose scale / bias rows start at
+// group): rows r0 (of the box at W0) and r1 (of the box at W1), with
+// r0 & 7 == r1 & 7, held by lane quad T/4; their scale / bias rows start at
 // s0, s1 / b0, b1. Four groups run per step with independent accumulators
 // (all their fragment loads issued first), so the MMA chains overlap. Lane
 // t == 0 of each quad returns the two rows' partial results (others return
 // garbage); partials over disjoint group ranges add up to the full result.
 template <int BITS, int DT, int KPG>
-__device__ __forceinline__ void imma_rows(const uint8_t* w0, const uint8_t* w1, const uint8_t* s0, const uint8_t* s1,
-                                          const uint8_t* b0, const uint8_t* b1, const uint2* bt, const float* gsum,
-                                          const float* grs, int g_begin, int g_end, float& y0, float& y1) {
-  constexpr int KBB = BITS == 4 ? 16 : 32;  // bytes of one 32-weight block in a row
-  constexpr int NB = 4 * KPG;               // blocks per step
-  const int lane = threadIdx.x & 31, t = lane & 3;
-  const uint8_t* p0 = w0 + 4 * t;
-  const uint8_t* p1 = w1 + 4 * t;
+__device__ __forceinline__ void imma_rows(const uint8_t* W0, const uint8_t* W1, int r0, int r1, int segb,
+                                          const uint8_t* s0, const uint8_t* s1, const uint8_t* b0, const uint8_t* b1,
+                                          const uint2* bt, const float* gsum, const float* grs, int g_begin,
+                                          int g_end, float& y0, float& y1) {
+  constexpr int NB = 4 * KPG;                        // 32-weight blocks per step
+  constexpr int CPB = BITS == 4 ? 1 : 2;              // 16-byte chunks per block
+  constexpr bool ALIGNED = (NB * CPB) % 8 == 0;       // every step starts on a 128-byte segment
+  const int lane = threadIdx.x & 31, t = lane & 3, rx = (r0 & 7) << 4;
+  const uint8_t* p0 = W0 + r0 * 128 + 4 * t;
+  const uint8_t* p1 = W1 + r1 * 128 + 4 * t;
+  int xo[8];  // swizzled offset of chunk c inside a segment (lane constant)
+#pragma unroll
+  for (int c = 0; c < 8; ++c) xo[c] = (c << 4) ^ rx;
   const bool blane = lane < 12;
   float f[4] = {0.f, 0.f, 0.f, 0.f};
   float ba0 = 0.f, ba1 = 0.f;
   for (int g = g_begin; g < g_end; g += 4) {
     const int kb0 = g * KPG;
+    const int sbase = ((kb0 * CPB) >> 3) * segb;  // segment of the step's first chunk
     uint2 b[NB];
     uint32_t u0[NB], u1[NB], v0[NB], v1[NB];
 #pragma unroll
     for (int j = 0; j < NB; ++j) {
-      b[j] = blane ? bt[(kb0 + j) * 12 + lane] : make_uint2(0u, 0u);
-      u0[j] = *reinterpret_cast<const uint32_t*>(p0 + (kb0 + j) * KBB);
-      u1[j] = *reinterpret_cast<const uint32_t*>(p1 + (kb0 + j) * KBB);
-      if constexpr (BITS == 8) {
-        v0[j] = *reinterpret_cast<const uint32_t*>(p0 + (kb0 + j) * KBB + 16);
-        v1[j] = *reinterpret_cast<const uint32_t*>(p1 + (kb0 + j) * KBB + 16);
+      const int kb = kb0 + j;
+      b[j] = blane ? bt[kb * 12 + lane] : make_uint2(0u, 0u);
+#pragma unroll
+      for (int h = 0; h < CPB; ++h) {
+        // chunk CPB * kb + h; with aligned steps its segment and slot are
+        // compile-time offsets from the step's first segment
+        const int o = ALIGNED ? sbase + ((CPB * j + h) >> 3) * segb + xo[(CPB * j + h) & 7]
+                              : swz_off(CPB * kb + h, rx, segb);
+        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(p0 + o);
+        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(p1 + o);
+        if (h == 0) { u0[j] = w0; u1[j] = w1; }
+        else { v0[j] = w0; v1[j] = w1; }
       }
     }
     int d[4][4];
@@ -336,29 +352,37 @@ __device__ __forceinline__ void imma_rows(const uint8_t* w0, const uint8_t* w1, 
   y1 = (f[2] + (f[3] + e1 * (1.f / 254.f)) * (1.f / 254.f)) + ba1;
 }
 
-// Dispatch on the blocks per group (group sizes 32, 64, 128).
-template <int BITS, int DT>
-__device__ __forceinline__ void imma_rows_any(int kpg, const uint8_t* w0, const uint8_t* w1, const uint8_t* s0,
-                                              const uint8_t* s1, const uint8_t* b0, const uint8_t* b1, const uint2* bt,
-                                              const float* gsum, const float* grs, int g_begin, int g_end, float& y0,
-                                              float& y1) {
-  if (kpg == 2) imma_rows<BITS, DT, 2>(w0, w1, s0, s1, b0, b1, bt, gsum, grs, g_begin, g_end, y0, y1);
-  else if (kpg == 1) imma_rows<BITS, DT, 1>(w0, w1, s0, s1, b0, b1, bt, gsum, grs, g_begin, g_end, y0, y1);
-  else imma_rows<BITS, DT, 4>(w0, w1, s0, s1, b0, b1, bt, gsum, grs, g_begin, g_end, y0, y1);
+// Tensor maps of the matrices a launch streams (see TileMaps in slice.h).
+__device__ __forceinline__ void tma_rows(uint8_t* dst, const CUtensorMap* m, int row, int expert, uint64_t* bar,
+                                         uint64_t pol) {
+  if (expert < 0)
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+        "l"(m), "r"(0), "r"(row), "r"(0), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+  else
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
+        "l"(m), "r"(0), "r"(row), "r"(0), "r"(expert), "r"(smem_u32(bar)), "l"(pol)
+        : "memory");
+}
+// One matrix block of a slot: [box rows of weights, swizzled][box scale rows]
+// [box bias rows]. The weights box is always copied whole (rows past the
+// matrix end read as zeros); scales and biases for the n rows in use.
+__device__ __forceinline__ unsigned tile_bytes(const SliceTab& T, int sb, int box, int n) {
+  return unsigned(box * T.rb) + 2u * unsigned(n * T.srow * sb);
+}
+__device__ __forceinline__ void tile_copy(const SliceTab& T, int sb, int box, uint8_t* d, uint64_t* bar,
+                                          const CUtensorMap* m, int expert, const uint8_t* s, const uint8_t* b,
+                                          int row, int n, uint64_t pol) {
+  const int ss = T.srow * sb;
+  tma_rows(d, m, row, expert, bar, pol);
+  bulk_g2s(d + box * T.rb, s + int64_t(row) * ss, unsigned(n * ss), bar, pol);
+  bulk_g2s(d + box * T.rb + box * ss, b + int64_t(row) * ss, unsigned(n * ss), bar, pol);
 }
 
-// Issues the bulk copies of rows [row, row + n) (n <= cap) of one matrix into
-// a slot laid out as [cap rows at pitch rbp][cap scale rows][cap bias rows]
-// (rows copied one by one so that the padded pitch spreads them over the
-// shared-memory banks).
-__device__ __forceinline__ void imma_copy(const SliceTab& T, int rbp, int sb, int cap, uint8_t* d, uint64_t* bar,
-                                          const uint8_t* w, const uint8_t* s, const uint8_t* b, int row, int n,
-                                          uint64_t pol) {
-  const int ss = T.srow * sb;
-  for (int r = 0; r < n; ++r) bulk_g2s(d + r * rbp, w + int64_t(row + r) * T.rb, unsigned(T.rb), bar, pol);
-  bulk_g2s(d + cap * rbp, s + int64_t(row) * ss, unsigned(n * ss), bar, pol);
-  bulk_g2s(d + cap * rbp + cap * ss, b + int64_t(row) * ss, unsigned(n * ss), bar, pol);
-}
 __device__ __forceinline__ void imma_init_barriers(uint64_t* full, uint64_t* empty, int S) {
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) {
@@ -370,15 +394,15 @@ __device__ __forceinline__ void imma_init_barriers(uint64_t* full, uint64_t* emp
   __syncthreads();
 }
 
-// Tiles are reduced by groups of KS = T.W consumer warps (KS in {1, 2, 4}):
-// tile i goes to warp group i % (SL_CW / KS), whose warp kw covers the
+// Tiles are reduced by groups of KS = T.W consumer warps (KS in {1, 2, 4, 8}):
+// tile i goes to warp group i % (IW / KS), whose warp kw covers the
 // quantisation groups [kw * ng / KS, (kw + 1) * ng / KS). With KS > 1 the
-// partials meet in `kp` (two buffers of SL_CW * 16 floats, alternating per
+// partials meet in `kp` (two buffers of IW * 16 floats, alternating per
 // round so that the next round's writes cannot overtake the reads), behind
 // named barrier 2 + group.
 struct KSplit {
   int ks, ng_warps, grp, kw;
-  __device__ __forceinline__ KSplit(int ks_, int warp) : ks(ks_), ng_warps(SL_CW / ks_), grp(warp / ks_), kw(warp % ks_) {}
+  __device__ __forceinline__ KSplit(int ks_, int warp) : ks(ks_), ng_warps(IW / ks_), grp(warp / ks_), kw(warp % ks_) {}
   __device__ __forceinline__ bool mine(int tile) const { return tile % ng_warps == grp; }
   __device__ __forceinline__ int round(int tile) const { return tile / ng_warps; }
   __device__ __forceinline__ void range(int ngroups, int& g0, int& g1) const {
@@ -388,7 +412,7 @@ struct KSplit {
   // Sums the KS partials of rows gi / gi + 8 into warp kw == 0 (t == 0 lanes).
   __device__ __forceinline__ void combine(float* kp, int rnd, int gi, int t, float& y0, float& y1) const {
     if (ks == 1) return;
-    float* buf = kp + (rnd & 1) * SL_CW * 16;
+    float* buf = kp + (rnd & 1) * IW * 16;
     const int warp = threadIdx.x >> 5;
     if (t == 0) { buf[warp * 16 + gi] = y0; buf[warp * 16 + gi + 8] = y1; }
     asm volatile("bar.sync %0, %1;" ::"r"(2 + grp), "r"(ks * 32) : "memory");
@@ -405,11 +429,14 @@ struct KSplit {
 
 // ------------------------------------------------------------ dense GEMV --
 // As k_sgemv (same tiles of 16 rows, producer, prologues and epilogues); tile
-// i is reduced by consumer warp i % SL_CW on the tensor cores.
-template <int BITS, int DT>
-__global__ void __launch_bounds__(SL_T, 2) k_igemv(const GemvArgs a, const SliceTab T, const RouterTail rt) {
+// i is reduced by consumer warp i % IW on the tensor cores.
+template <int BITS, int DT, int KPG>
+__global__ void __launch_bounds__(IM_T, 2) k_igemv(const GemvArgs a, const SliceTab T, const __grid_constant__ TileMaps M,
+                                                 const RouterTail rt) {
   constexpr int SB = DT == DT_F32 ? 4 : 2;
-  extern __shared__ __align__(128) uint8_t sm[];
+  extern __shared__ __align__(1024) uint8_t sm_raw[];
+  // the swizzled tensor copies need 1024-byte aligned slots
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = sm;
   float* plain = reinterpret_cast<float*>(sm + T.off_raw);
   float* red = reinterpret_cast<float*>(sm + T.off_red);
@@ -419,7 +446,7 @@ __global__ void __launch_bounds__(SL_T, 2) k_igemv(const GemvArgs a, const Slice
   uint64_t* empty = full + T.S;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r0 = blockIdx.x * T.rpc, r1 = min(T.total, r0 + T.rpc);
-  const int rbp = T.rb + 16, ss = T.srow * SB;
+  const int ss = T.srow * SB, segb = 16 * 128;
   auto tiles = [&](auto&& f) {
     int idx = 0;
     for (int sg = 0; sg < T.nseg; ++sg) {
@@ -428,7 +455,7 @@ __global__ void __launch_bounds__(SL_T, 2) k_igemv(const GemvArgs a, const Slice
     }
   };
   imma_init_barriers(full, empty, T.S);
-  if (warp == SL_CW) {  // producer
+  if (warp == IW) {  // producer
     if (lane == 0) {
       const uint64_t pol = l2_evict_first();
       int issued = 0;
@@ -437,9 +464,9 @@ __global__ void __launch_bounds__(SL_T, 2) k_igemv(const GemvArgs a, const Slice
         if (!ok) return;
         const int s = i % T.S;
         if (i >= T.S && !mbar_wait(empty + s, unsigned(i / T.S - 1) & 1u)) { ok = false; return; }
-        mbar_expect_tx(full + s, sl_bytes<BITS, DT>(T, n));
-        imma_copy(T, rbp, SB, 16, ring + size_t(s) * T.slot, full + s, seg_pick(T.w, sg), seg_pick(T.s, sg),
-                  seg_pick(T.b, sg), row, n, pol);
+        mbar_expect_tx(full + s, tile_bytes(T, SB, 16, n));
+        tile_copy(T, SB, 16, ring + size_t(s) * T.slot, full + s, &M.m[sg], -1, seg_pick(T.s, sg), seg_pick(T.b, sg),
+                  row, n, pol);
         issued = i + 1;
       });
       if (!ok) sl_fail(T);
@@ -452,11 +479,11 @@ __global__ void __launch_bounds__(SL_T, 2) k_igemv(const GemvArgs a, const Slice
   trc.start(a.trace);
   pdl_wait();
   trc.waited(a.trace);
-  sl_stage_plain(a, red, plain);
-  const int ngroups = a.in >> T.gs_shift, kpg = (1 << T.gs_shift) >> 5, gi = lane >> 2, t = lane & 3;
+  sl_stage_plain<IM_NT>(a, red, plain);
+  const int ngroups = a.in >> T.gs_shift, gi = lane >> 2, t = lane & 3;
   float* grs = gsum + ((ngroups + 3) & ~3);
-  stage_digits_any<BITS>(kpg, plain, 0, 1, a.in, bt, gsum, grs);
-  bar_sync_n(SL_NT);
+  stage_digits<BITS, KPG>(plain, 0, 1, a.in, bt, gsum, grs);
+  bar_sync_n(IM_NT);
   pdl_launch();
   trc.staged(a.trace);
   float bv = -INFINITY;
@@ -482,10 +509,10 @@ __global__ void __launch_bounds__(SL_T, 2) k_igemv(const GemvArgs a, const Slice
     float y0 = 0.f, y1 = 0.f;
     if (ok) {
       const uint8_t* wt = ring + size_t(s) * T.slot;
-      const uint8_t* st = wt + 16 * rbp;
+      const uint8_t* st = wt + 16 * T.rb;
       const uint8_t* btt = st + 16 * ss;
-      imma_rows_any<BITS, DT>(kpg, wt + gi * rbp, wt + (gi + 8) * rbp, st + gi * ss, st + (gi + 8) * ss,
-                              btt + gi * ss, btt + (gi + 8) * ss, bt, gsum, grs, g0, g1, y0, y1);
+      imma_rows<BITS, DT, KPG>(wt, wt, gi, gi + 8, segb, st + gi * ss, st + (gi + 8) * ss, btt + gi * ss,
+                               btt + (gi + 8) * ss, bt, gsum, grs, g0, g1, y0, y1);
     }
     ksp.combine(kp, ksp.round(i), gi, t, y0, y1);
     __syncwarp();
@@ -499,8 +526,8 @@ __global__ void __launch_bounds__(SL_T, 2) k_igemv(const GemvArgs a, const Slice
   });
   trc.looped(a.trace);
   if (dead) sl_fail(T);
-  if (a.argmax_out) sl_argmax_tail(a, bv, bi, red);
-  if (rt.logits) sl_router_done(rt, plain, red);
+  if (a.argmax_out) sl_argmax_tail<IM_NT>(a, bv, bi, red);
+  if (rt.logits) sl_router_done<IM_NT>(rt, plain, red);
   trc.end(a.trace);
 }
 
@@ -508,10 +535,13 @@ __global__ void __launch_bounds__(SL_T, 2) k_igemv(const GemvArgs a, const Slice
 // Gate/up of the shared and routed experts (tiles and producer as k_sgateup,
 // 8 row pairs per tile): the 16-row MMA tile is 8 gate rows over the same 8
 // up rows, so the lane holding gate row p also holds up row p.
-template <int BITS, int DT>
-__global__ void __launch_bounds__(SL_T, 2) k_igateup(const MoeArgs m, const SliceTab T) {
+template <int BITS, int DT, int KPG>
+__global__ void __launch_bounds__(IM_T, 2) k_igateup(const MoeArgs m, const SliceTab T,
+                                                   const __grid_constant__ TileMaps M) {
   constexpr int SB = DT == DT_F32 ? 4 : 2;
-  extern __shared__ __align__(128) uint8_t sm[];
+  extern __shared__ __align__(1024) uint8_t sm_raw[];
+  // the swizzled tensor copies need 1024-byte aligned slots
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = sm;
   float* plain = reinterpret_cast<float*>(sm + T.off_raw);
   float* red = reinterpret_cast<float*>(sm + T.off_red);
@@ -523,7 +553,7 @@ __global__ void __launch_bounds__(SL_T, 2) k_igateup(const MoeArgs m, const Slic
   const int K = m.topk, inter = m.g.lin.out, sh = m.sg.out, nq = K * inter;
   const int s0 = min(sh, int(blockIdx.x) * T.sh_rpc), s1 = min(sh, s0 + T.sh_rpc);
   const int q0 = min(nq, int(blockIdx.x) * T.rt_rpc), q1 = min(nq, q0 + T.rt_rpc);
-  const int rbp = T.rb + 16, ss = T.srow * SB, half = T.slot / 2;
+  const int ss = T.srow * SB, half = T.slot / 2, segb = 8 * 128;
   auto tiles = [&](auto&& f) {  // f(tile, slot (K = shared), row, n)
     int idx = 0;
     for (int r = s0; r < s1; r += 8) f(idx++, K, r, min(8, s1 - r));
@@ -537,7 +567,7 @@ __global__ void __launch_bounds__(SL_T, 2) k_igateup(const MoeArgs m, const Slic
   __shared__ int r_ids[16];
   __shared__ float r_w[16], r_sh;
   imma_init_barriers(full, empty, T.S);
-  if (warp == SL_CW) {  // producer
+  if (warp == IW) {  // producer
     const uint64_t pol = l2_evict_first();
     int issued = 0;
     bool ok = true;
@@ -551,9 +581,9 @@ __global__ void __launch_bounds__(SL_T, 2) k_igateup(const MoeArgs m, const Slic
         U = expert_lin(m.u, id);
       }
       uint8_t* d = ring + size_t(s) * T.slot;
-      mbar_expect_tx(full + s, 2u * sl_bytes<BITS, DT>(T, n));
-      imma_copy(T, rbp, SB, 8, d, full + s, G.w, G.s, G.b, row, n, pol);
-      imma_copy(T, rbp, SB, 8, d + half, full + s, U.w, U.s, U.b, row, n, pol);
+      mbar_expect_tx(full + s, 2u * tile_bytes(T, SB, 8, n));
+      tile_copy(T, SB, 8, d, full + s, &M.m[k < K ? 2 : 0], k < K ? id : -1, G.s, G.b, row, n, pol);
+      tile_copy(T, SB, 8, d + half, full + s, &M.m[k < K ? 3 : 1], k < K ? id : -1, U.s, U.b, row, n, pol);
       issued = i + 1;
     };
     // shared-expert tiles first: their weights do not depend on the routing
@@ -585,11 +615,11 @@ __global__ void __launch_bounds__(SL_T, 2) k_igateup(const MoeArgs m, const Slic
   trc.waited(m.trace);
   GemvArgs a;
   a.in = m.g.lin.in; a.prologue = PRO_COPY; a.x = m.x;
-  sl_stage_plain(a, red, plain);
-  const int ngroups = a.in >> T.gs_shift, kpg = (1 << T.gs_shift) >> 5, gi = lane >> 2, t = lane & 3;
+  sl_stage_plain<IM_NT>(a, red, plain);
+  const int ngroups = a.in >> T.gs_shift, gi = lane >> 2, t = lane & 3;
   float* grs = gsum + ((ngroups + 3) & ~3);
-  stage_digits_any<BITS>(kpg, plain, 0, 1, a.in, bt, gsum, grs);
-  bar_sync_n(SL_NT);
+  stage_digits<BITS, KPG>(plain, 0, 1, a.in, bt, gsum, grs);
+  bar_sync_n(IM_NT);
   pdl_launch();
   trc.staged(m.trace);
   const KSplit ksp(T.W, warp);
@@ -606,9 +636,9 @@ __global__ void __launch_bounds__(SL_T, 2) k_igateup(const MoeArgs m, const Slic
     if (ok) {
       const uint8_t* gt = ring + size_t(s) * T.slot;
       const uint8_t* ut = gt + half;
-      const int so = 8 * rbp, bo = 8 * rbp + 8 * ss;
-      imma_rows_any<BITS, DT>(kpg, gt + gi * rbp, ut + gi * rbp, gt + so + gi * ss, ut + so + gi * ss,
-                              gt + bo + gi * ss, ut + bo + gi * ss, bt, gsum, grs, g0, g1, gv, uv);
+      const int so = 8 * T.rb, bo = 8 * T.rb + 8 * ss;
+      imma_rows<BITS, DT, KPG>(gt, ut, gi, gi, segb, gt + so + gi * ss, ut + so + gi * ss, gt + bo + gi * ss,
+                               ut + bo + gi * ss, bt, gsum, grs, g0, g1, gv, uv);
     }
     ksp.combine(kp, ksp.round(i), gi, t, gv, uv);
     __syncwarp();
@@ -623,13 +653,16 @@ __global__ void __launch_bounds__(SL_T, 2) k_igateup(const MoeArgs m, const Slic
 }
 
 // Down projections, combine and residual (as k_sdown): tile e holds expert
-// slot e's rows of the CTA (at most 16); warp e % SL_CW stages that slot's
+// slot e's rows of the CTA (at most 16); warp e % IW stages that slot's
 // digits and reduces the tile into part[e][row]; the consumers then combine
 // part over the experts with the routing weights.
-template <int BITS, int DT>
-__global__ void __launch_bounds__(SL_T, 2) k_idown(const MoeArgs m, const SliceTab T) {
+template <int BITS, int DT, int KPG>
+__global__ void __launch_bounds__(IM_T, 2) k_idown(const MoeArgs m, const SliceTab T,
+                                                 const __grid_constant__ TileMaps M) {
   constexpr int SB = DT == DT_F32 ? 4 : 2;
-  extern __shared__ __align__(128) uint8_t sm[];
+  extern __shared__ __align__(1024) uint8_t sm_raw[];
+  // the swizzled tensor copies need 1024-byte aligned slots
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = sm;
   float* raw = reinterpret_cast<float*>(sm + T.off_raw);
   float* part = reinterpret_cast<float*>(sm + T.off_part);
@@ -640,11 +673,11 @@ __global__ void __launch_bounds__(SL_T, 2) k_idown(const MoeArgs m, const SliceT
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = m.topk, D = m.d.lin.out, inter = m.d.lin.in;
   const int o0 = int(blockIdx.x) * T.rpc, o1 = min(D, o0 + T.rpc), nrow = o1 - o0;
-  const int rbp = T.rb + 16, ss = T.srow * SB;
+  const int ss = T.srow * SB, segb = 16 * 128;
   __shared__ int r_ids[16];
   __shared__ float r_w[16], r_sh;
   imma_init_barriers(full, empty, T.S);
-  if (warp == SL_CW) {  // producer
+  if (warp == IW) {  // producer
     // The router grid completed before this grid was launched, so its output
     // (logits, or the routing it stored) can be read before the dependency wait.
     if (m.logits) warp_route(m.logits, m.experts, K, m.norm_topk, r_ids, r_w, &r_sh);
@@ -655,9 +688,10 @@ __global__ void __launch_bounds__(SL_T, 2) k_idown(const MoeArgs m, const SliceT
       for (int e = 0; e <= K && ok; ++e) {
         const int s = e % T.S;
         if (e >= T.S && !mbar_wait(empty + s, unsigned(e / T.S - 1) & 1u)) { ok = false; break; }
-        const QLin L = e < K ? expert_lin(m.d, m.logits ? r_ids[e] : __ldcg(m.pick_ids + e)) : m.sd;
-        mbar_expect_tx(full + s, sl_bytes<BITS, DT>(T, nrow));
-        imma_copy(T, rbp, SB, 16, ring + size_t(s) * T.slot, full + s, L.w, L.s, L.b, o0, nrow, pol);
+        const int id = e < K ? (m.logits ? r_ids[e] : __ldcg(m.pick_ids + e)) : -1;
+        const QLin L = e < K ? expert_lin(m.d, id) : m.sd;
+        mbar_expect_tx(full + s, tile_bytes(T, SB, 16, nrow));
+        tile_copy(T, SB, 16, ring + size_t(s) * T.slot, full + s, &M.m[e < K ? 2 : 0], id, L.s, L.b, o0, nrow, pol);
         issued = e + 1;
       }
       if (!ok) sl_fail(T);
@@ -671,27 +705,27 @@ __global__ void __launch_bounds__(SL_T, 2) k_idown(const MoeArgs m, const SliceT
   pdl_wait();
   trc.waited(m.trace);
   const int nfl = (K + 1) * m.hmid_stride;
-  for (int i = tid; i < (nfl >> 2); i += SL_NT) cp_async16(raw + 4 * i, m.hmid + 4 * i);
+  for (int i = tid; i < (nfl >> 2); i += IM_NT) cp_async16(raw + 4 * i, m.hmid + 4 * i);
   cp_async_wait_all();
-  bar_sync_n(SL_NT);
-  const int nkb = inter >> 5, ngroups = inter >> T.gs_shift, kpg = (1 << T.gs_shift) >> 5;
+  bar_sync_n(IM_NT);
+  const int nkb = inter >> 5, ngroups = inter >> T.gs_shift;
   float* grs = gsum + (((K + 1) * ngroups + 3) & ~3);
-  stage_digits_any<BITS>(kpg, raw, m.hmid_stride, K + 1, inter, bt, gsum, grs);
-  bar_sync_n(SL_NT);
+  stage_digits<BITS, KPG>(raw, m.hmid_stride, K + 1, inter, bt, gsum, grs);
+  bar_sync_n(IM_NT);
   pdl_launch();
   trc.staged(m.trace);
   const int gi = lane >> 2, t = lane & 3;
   bool dead = false;
-  for (int e = warp; e <= K && !dead; e += SL_CW) {
+  for (int e = warp; e <= K && !dead; e += IW) {
     const int s = e % T.S;
     if (!__all_sync(0xffffffffu, mbar_wait(full + s, unsigned(e / T.S) & 1u))) { dead = true; break; }
     const uint8_t* dt = ring + size_t(s) * T.slot;
-    const uint8_t* st = dt + 16 * rbp;
+    const uint8_t* st = dt + 16 * T.rb;
     const uint8_t* btt = st + 16 * ss;
     float y0, y1;
-    imma_rows_any<BITS, DT>(kpg, dt + gi * rbp, dt + (gi + 8) * rbp, st + gi * ss, st + (gi + 8) * ss, btt + gi * ss,
-                            btt + (gi + 8) * ss, bt + e * nkb * 12, gsum + e * ngroups, grs + e * ngroups, 0, ngroups,
-                            y0, y1);
+    imma_rows<BITS, DT, KPG>(dt, dt, gi, gi + 8, segb, st + gi * ss, st + (gi + 8) * ss, btt + gi * ss,
+                             btt + (gi + 8) * ss, bt + e * nkb * 12, gsum + e * ngroups, grs + e * ngroups, 0, ngroups,
+                             y0, y1);
     __syncwarp();
     if (lane == 0) mbar_arrive(empty + s);
     if (t == 0) {
@@ -701,11 +735,11 @@ __global__ void __launch_bounds__(SL_T, 2) k_idown(const MoeArgs m, const SliceT
   }
   trc.looped(m.trace);
   if (dead) sl_fail(T);
-  bar_sync_n(SL_NT);
+  bar_sync_n(IM_NT);
   // combine weights: computed by this CTA's producer (released to the
   // consumers by the arrivals that completed the tiles' barriers) or stored
   // by the router grid
-  for (int rl = tid; rl < nrow; rl += SL_NT) {
+  for (int rl = tid; rl < nrow; rl += IM_NT) {
     float acc = 0.f;
     for (int e = 0; e <= K; ++e) {
       const float we = m.logits ? (e < K ? r_w[e] : r_sh) : (e < K ? __ldcg(m.pick_w + e) : __ldcg(m.shared_scale));
@@ -724,23 +758,36 @@ __global__ void __launch_bounds__(SL_T, 2) k_idown(const MoeArgs m, const SliceT
 }
 
 // ------------------------------------------------- per-format launchers --
+// kpg: 32-weight blocks per quantisation group (group size 32, 64 or 128).
+#define SWL_KPG_LAUNCH(KERNEL, ...)                                                                 \
+  do {                                                                                              \
+    if (kpg == 2) launch(KERNEL<B, D, 2>, dim3(grid), dim3(IM_T), smem, st, pdl, __VA_ARGS__);      \
+    else if (kpg == 4) launch(KERNEL<B, D, 4>, dim3(grid), dim3(IM_T), smem, st, pdl, __VA_ARGS__); \
+    else launch(KERNEL<B, D, 1>, dim3(grid), dim3(IM_T), smem, st, pdl, __VA_ARGS__);               \
+  } while (0)
 template <int B, int D>
-void igemv_fmt(const GemvArgs& a, const SliceTab& T, const RouterTail& rt, int grid, size_t smem, cudaStream_t st,
+void igemv_fmt(const GemvArgs& a, const SliceTab& T, const TileMaps& M, const RouterTail& rt, int kpg, int grid,
+               size_t smem, cudaStream_t st, bool pdl) {
+  SWL_KPG_LAUNCH(k_igemv, a, T, M, rt);
+}
+template <int B, int D>
+void igateup_fmt(const MoeArgs& m, const SliceTab& T, const TileMaps& M, int kpg, int grid, size_t smem,
+                 cudaStream_t st, bool pdl) {
+  SWL_KPG_LAUNCH(k_igateup, m, T, M);
+}
+template <int B, int D>
+void idown_fmt(const MoeArgs& m, const SliceTab& T, const TileMaps& M, int kpg, int grid, size_t smem, cudaStream_t st,
                bool pdl) {
-  launch(k_igemv<B, D>, dim3(grid), dim3(SL_T), smem, st, pdl, a, T, rt);
+  SWL_KPG_LAUNCH(k_idown, m, T, M);
 }
-template <int B, int D>
-void igateup_fmt(const MoeArgs& m, const SliceTab& T, int grid, size_t smem, cudaStream_t st, bool pdl) {
-  launch(k_igateup<B, D>, dim3(grid), dim3(SL_T), smem, st, pdl, m, T);
-}
-template <int B, int D>
-void idown_fmt(const MoeArgs& m, const SliceTab& T, int grid, size_t smem, cudaStream_t st, bool pdl) {
-  launch(k_idown<B, D>, dim3(grid), dim3(SL_T), smem, st, pdl, m, T);
-}
+#undef SWL_KPG_LAUNCH
 
-#define SWL_INSTANTIATE_IMMA(B, D)                                                                                   \
-  template void igemv_fmt<B, D>(const GemvArgs&, const SliceTab&, const RouterTail&, int, size_t, cudaStream_t, bool); \
-  template void igateup_fmt<B, D>(const MoeArgs&, const SliceTab&, int, size_t, cudaStream_t, bool);                  \
-  template void idown_fmt<B, D>(const MoeArgs&, const SliceTab&, int, size_t, cudaStream_t, bool);
+#define SWL_INSTANTIATE_IMMA(B, D)                                                                                 \
+  template void igemv_fmt<B, D>(const GemvArgs&, const SliceTab&, const TileMaps&, const RouterTail&, int, int,     \
+                                size_t, cudaStream_t, bool);                                                       \
+  template void igateup_fmt<B, D>(const MoeArgs&, const SliceTab&, const TileMaps&, int, int, size_t, cudaStream_t, \
+                                  bool);                                                                           \
+  template void idown_fmt<B, D>(const MoeArgs&, const SliceTab&, const TileMaps&, int, int, size_t, cudaStream_t,   \
+                                bool);
 
 }  // namespace swl

@@ -77,12 +77,16 @@ __device__ __forceinline__ bool mbar_try(uint64_t* b, unsigned parity) {
 }
 // Waits for the phase of parity `parity` to complete, for at most about two
 // seconds (then returns false: the caller records an error and gives up).
+// After a short burst of polls the waiting thread sleeps between polls, so a
+// long wait (a producer waiting for a free slot) leaves the issue slots to
+// the warps doing the work.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity) {
   if (mbar_try(b, parity)) return true;
   const unsigned long long t0 = gtimer();
   for (int i = 0; i < (1 << 26); ++i) {
     if (mbar_try(b, parity)) return true;
+    if (i >= 16) __nanosleep(i < 64 ? 64 : 256);
     if (gtimer() - t0 > kWaitLimitNs) break;
   }
   return false;
@@ -317,6 +321,32 @@ __device__ __forceinline__ float dot_row(const RowFrag<BITS, DT, CPL>& f, const 
     else acc += d;
   }
   return acc;
+}
+
+// Transposed reduction of R per-lane partials (one per row) over the LPR
+// lanes of a sub-warp (R <= LPR, powers of two): each exchange round halves
+// the rows a lane holds, so R rows cost R - 1 + log2(LPR / R) shuffles
+// instead of R * log2(LPR). Returns the full sum of row `row` of this lane;
+// the lanes with sl % (LPR / R) == 0 hold distinct rows.
+template <int R>
+__device__ __forceinline__ float reduce_rows(float (&p)[R], int LPR, int sl, int& row) {
+  row = 0;
+  int o = LPR >> 1;
+#pragma unroll
+  for (int h = R >> 1; h >= 1; h >>= 1) {
+    const bool hi = (sl & o) != 0;
+#pragma unroll
+    for (int i = 0; i < h; ++i) {
+      const float send = hi ? p[i] : p[i + h];
+      const float keep = hi ? p[i + h] : p[i];
+      p[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+    if (hi) row += h;
+    o >>= 1;
+  }
+  float v = p[0];
+  for (; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
 }
 
 // Reduction over the LPR lanes of a sub-warp (all 32 lanes must call it).

@@ -62,6 +62,7 @@ struct GemvArgs {
   int* argmax_idx = nullptr;    // scratch [gridDim] indices
   unsigned* counter = nullptr;  // last-block counter for argmax
   int* status = nullptr;        // bit 0: a bounded wait inside the kernel gave up
+  int smem_kb = 0;              // shared-memory budget of the streaming kernel (0: default)
   Trace trace;
 };
 
@@ -108,6 +109,7 @@ struct MoeArgs {
   const float* logits = nullptr;
   int experts = 0;
   int norm_topk = 0;
+  int smem_kb = 0;             // shared-memory budget of the gate/up kernel (0: default)
   Trace trace;
 };
 

@@ -175,10 +175,22 @@ __global__ void __launch_bounds__(DELTA_THREADS) k_delta(const DeltaArgs a) {
 // ----------------------------------------------------------- attention ----
 // Gated GQA decode for one token: q/k RMSNorm with weight, partial NeoX
 // RoPE, KV append, causal softmax(q k^T / sqrt(hd)) v split over context
-// chunks, combined by the last CTA of each kv head, times sigmoid(gate)
+// chunks of at least ATTN_MINP positions, times sigmoid(gate)
 // (QwenCPUModel.swift:285-367). KV layout: [kv_head][max_ctx][head_dim].
+// A CTA walks its chunk in sub-tiles of ATTN_TP positions: the K and V rows
+// are copied to shared memory in one asynchronous round trip, scores are
+// half-dots by thread pairs (row index rotated by position: no bank
+// conflicts), and an online softmax carries (max, sum, output) across
+// sub-tiles. With one chunk the CTA writes the output; otherwise the last CTA
+// of each kv head combines the chunks' partials.
+// Output gate sigmoid with the fast exponential and divide (within a few
+// ulp of 1 / (1 + exp(-v)); one per output element).
+__device__ __forceinline__ float fast_sigmoid(float v) { return __fdividef(1.f, 1.f + __expf(-v)); }
+
 constexpr int ATTN_THREADS = 256;
-constexpr int ATTN_MINP = 16;  // minimum positions per chunk
+constexpr int ATTN_MINP = 64;  // minimum positions per chunk
+constexpr int ATTN_TP = 16;    // positions per staged sub-tile
+constexpr int ATTN_MAXO = 16;  // output values per thread: G * hd <= ATTN_MAXO * ATTN_THREADS
 
 __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
   extern __shared__ __align__(16) float sm[];
@@ -187,12 +199,15 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
   float* q = sm;                      // [G][hd]
   float* kn = q + G * hd;             // [hd]
   float* vn = kn + hd;                // [hd]
-  float* cs = vn + hd;                // [half] cos
+  float* kt = vn + hd;                // [TP][hd]
+  float* vt = kt + ATTN_TP * hd;      // [TP][hd]
+  float* sc = vt + ATTN_TP * hd;      // [G][TP]
+  float* fw = sc + G * ATTN_TP;       // [G][nchunks] combine weights
+  float* cs = fw + G * a.nchunks;     // [half] cos
   float* sn = cs + half;              // [half] sin
-  float* sc = sn + half;              // [G][chunk_cap]
-  __shared__ float hm[64], hl[64], hn[72];
+  __shared__ float hm[64], hl[64], hal[64], hn[72];
   __shared__ bool last;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
   const StateDev* sd = a.sd;
   TraceRec trc;
   trc.start(a.trace);
@@ -204,19 +219,20 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
   float* Kc = sd->kc[a.layer] + int64_t(kvh) * sd->max_ctx * hd;
   float* Vc = sd->vc[a.layer] + int64_t(kvh) * sd->max_ctx * hd;
   // before the wait: L2 prefetch of this chunk's cached rows, RoPE table
-  if (threadIdx.x == 0 && n > 0) {
+  if (tid == 0 && n > 0) {
     const int old = min(p1, pos) - p0;  // rows < pos are already cached
     if (old > 0) {
       prefetch_l2(Kc + int64_t(p0) * hd, uint32_t(old) * hd * 4);
       prefetch_l2(Vc + int64_t(p0) * hd, uint32_t(old) * hd * 4);
     }
   }
-  for (int j = threadIdx.x; j < half; j += blockDim.x) {
+  for (int j = tid; j < half; j += blockDim.x) {
     const float invf = powf(a.rope_theta, -float(2 * j) / float(a.rot));
     const float ang = float(pos) * invf;
     cs[j] = cosf(ang);
     sn[j] = sinf(ang);
   }
+  for (int h = tid; h < G; h += blockDim.x) { hm[h] = -INFINITY; hl[h] = 0.f; }
   pdl_wait();
   trc.waited(a.trace);
   for (int h = 0; h < G; ++h) copy_async(q + h * hd, a.qout + (kvh * G + h) * 2 * hd, hd);
@@ -225,81 +241,183 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
   cp_async_wait_all();
   __syncthreads();
   pdl_launch();
-  // RMSNorm of G q heads and the new k head, one warp per head
-  for (int h = warp; h <= G; h += nw) {
-    float* x = h < G ? q + h * hd : kn;
-    float ss = 0.f;
-    for (int i = lane; i < hd; i += 32) ss += x[i] * x[i];
-    ss = warp_sum(ss);
-    if (lane == 0) hn[h] = 1.f / sqrtf(ss / float(hd) + a.eps);
+  if (hd % 32 == 0 && hd <= 256 && half % 32 == 0) {
+    // one warp per head (G q heads and the new k head), in registers: lane l
+    // holds elements l + 32e, so RoPE partners (j, j + half) share a lane
+    const int E = hd >> 5, hs = half >> 5;
+    for (int h = warp; h <= G; h += nw) {
+      float* x = h < G ? q + h * hd : kn;
+      const float* w = h < G ? a.qn : a.kn;
+      float v[8];
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        v[e] = e < E ? x[lane + 32 * e] : 0.f;
+        ss += v[e] * v[e];
+      }
+      ss = warp_sum(ss);
+      const float sc = 1.f / sqrtf(ss / float(hd) + a.eps);
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (e < E) v[e] *= sc * w[lane + 32 * e];
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (e < hs) {
+          const int j = lane + 32 * e;
+          const float xa = v[e], xb = v[e + hs];
+          v[e] = xa * cs[j] - xb * sn[j];
+          v[e + hs] = xb * cs[j] + xa * sn[j];
+        }
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (e < E) x[lane + 32 * e] = v[e];
+    }
+    __syncthreads();
+  } else {
+    // RMSNorm of G q heads and the new k head, one warp per head
+    for (int h = warp; h <= G; h += nw) {
+      float* x = h < G ? q + h * hd : kn;
+      float ss = 0.f;
+      for (int i = lane; i < hd; i += 32) ss += x[i] * x[i];
+      ss = warp_sum(ss);
+      if (lane == 0) hn[h] = 1.f / sqrtf(ss / float(hd) + a.eps);
+    }
+    __syncthreads();
+    for (int i = tid; i < (G + 1) * hd; i += blockDim.x) {
+      const int h = i / hd, d = i % hd;
+      float* x = h < G ? q + h * hd : kn;
+      const float* w = h < G ? a.qn : a.kn;
+      x[d] *= hn[h] * w[d];
+    }
+    __syncthreads();
+    for (int i = tid; i < (G + 1) * half; i += blockDim.x) {
+      const int h = i / half, j = i % half;
+      float* x = h < G ? q + h * hd : kn;
+      const float xa = x[j], xb = x[half + j];
+      x[j] = xa * cs[j] - xb * sn[j];
+      x[half + j] = xb * cs[j] + xa * sn[j];
+    }
+    __syncthreads();
   }
-  __syncthreads();
-  for (int i = threadIdx.x; i < (G + 1) * hd; i += blockDim.x) {
-    const int h = i / hd, d = i % hd;
-    float* x = h < G ? q + h * hd : kn;
-    const float* w = h < G ? a.qn : a.kn;
-    x[d] *= hn[h] * w[d];
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < (G + 1) * half; i += blockDim.x) {
-    const int h = i / half, j = i % half;
-    float* x = h < G ? q + h * hd : kn;
-    const float xa = x[j], xb = x[half + j];
-    x[j] = xa * cs[j] - xb * sn[j];
-    x[half + j] = xb * cs[j] + xa * sn[j];
-  }
-  __syncthreads();
   if (chunk == 0)
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+    for (int i = tid; i < hd; i += blockDim.x) {
       Kc[int64_t(pos) * hd + i] = kn[i];
       Vc[int64_t(pos) * hd + i] = vn[i];
     }
+  trc.staged(a.trace);
   const float scale = 1.f / sqrtf(float(hd));
-  // scores: one warp per position
-  for (int j = warp; j < n; j += nw) {
-    const int p = p0 + j;
-    const float* kr = p == pos ? kn : Kc + int64_t(p) * hd;
-    float kv[8];
+  const int nout = G * hd;
+  float acc[ATTN_MAXO];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) kv[e] = (lane + 32 * e < hd) ? kr[lane + 32 * e] : 0.f;
-    for (int h = 0; h < G; ++h) {
-      float d = 0.f;
+  for (int o = 0; o < ATTN_MAXO; ++o) acc[o] = 0.f;
+  const int hq = hd >> 2;  // float4 per row
+  for (int t0 = p0; t0 < p0 + n; t0 += ATTN_TP) {
+    const int nt = min(ATTN_TP, p0 + n - t0);
+    // stage rows t0 .. t0 + nt of K and V (the new position from kn / vn)
+    for (int i = tid; i < nt * hq; i += blockDim.x) {
+      const int j = i / hq, c = i - j * hq, p = t0 + j;
+      if (p == pos) {
+        reinterpret_cast<float4*>(kt + j * hd)[c] = reinterpret_cast<const float4*>(kn)[c];
+        reinterpret_cast<float4*>(vt + j * hd)[c] = reinterpret_cast<const float4*>(vn)[c];
+      } else {
+        cp_async16(kt + j * hd + 4 * c, Kc + int64_t(p) * hd + 4 * c);
+        cp_async16(vt + j * hd + 4 * c, Vc + int64_t(p) * hd + 4 * c);
+      }
+    }
+    cp_async_wait_all();
+    __syncthreads();
+    // scores: one warp per position; lane l covers elements l + 32e of the
+    // row, and the G head partials are reduced together, eight heads at a
+    // time (transposed reduction)
+    for (int j = warp; j < ATTN_TP; j += nw) {
+      const bool live = j < nt;
+      float kv[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (lane + 32 * e < hd) d += q[h * hd + lane + 32 * e] * kv[e];
-      d = warp_sum(d);
-      if (lane == 0) sc[h * a.chunk_cap + j] = d * scale;
+      for (int e = 0; e < 8; ++e) kv[e] = live && lane + 32 * e < hd ? kt[j * hd + lane + 32 * e] : 0.f;
+      for (int h0 = 0; h0 < G; h0 += 8) {
+        float p[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          float d = 0.f;
+          if (h0 + r < G)
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              if (lane + 32 * e < hd) d += q[(h0 + r) * hd + lane + 32 * e] * kv[e];
+          p[r] = d;
+        }
+        int rr;
+        const float d = reduce_rows<8>(p, 32, lane, rr);
+        if ((lane & 3) == 0 && h0 + rr < G) sc[(h0 + rr) * ATTN_TP + j] = live ? d * scale : -INFINITY;
+      }
     }
-  }
-  __syncthreads();
-  for (int h = warp; h < G; h += nw) {
-    float m = -INFINITY;
-    for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[h * a.chunk_cap + j]);
-    m = warp_max(m);
-    float l = 0.f;
-    for (int j = lane; j < n; j += 32) {
-      const float e = expf(sc[h * a.chunk_cap + j] - m);
-      sc[h * a.chunk_cap + j] = e;
-      l += e;
+    __syncthreads();
+    // online softmax: per head the new max, the rescale of what came before,
+    // the weights of this sub-tile
+    for (int h = warp; h < G; h += nw) {
+      const float v = lane < ATTN_TP ? sc[h * ATTN_TP + lane] : -INFINITY;
+      const float mt = warp_max(v);
+      const float mo = hm[h], mn = fmaxf(mo, mt);
+      const float e = lane < ATTN_TP && v != -INFINITY ? expf(v - mn) : 0.f;
+      const float s = warp_sum(e);
+      if (lane < ATTN_TP) sc[h * ATTN_TP + lane] = e;
+      if (lane == 0) {
+        const float al = mo == -INFINITY ? 0.f : expf(mo - mn);
+        hal[h] = al;
+        hl[h] = hl[h] * al + s;
+        hm[h] = mn;
+      }
     }
-    l = warp_sum(l);
-    if (lane == 0) { hm[h] = n > 0 ? m : -INFINITY; hl[h] = l; }
+    __syncthreads();
+#pragma unroll
+    for (int o = 0; o < ATTN_MAXO; ++o) {
+      const int i = tid + o * ATTN_THREADS;
+      if (i < nout) {
+        const int h = i / hd, d = i - h * hd;
+        float v = acc[o] * hal[h];
+        for (int j = 0; j < nt; ++j) v += sc[h * ATTN_TP + j] * vt[j * hd + d];
+        acc[o] = v;
+      }
+    }
+    __syncthreads();
   }
-  __syncthreads();
+  trc.looped(a.trace);
+  if (nvalid == 1) {  // the whole context in this CTA: finish here
+    if (chunk == 0) {
+      for (int h = tid; h < G; h += blockDim.x) hal[h] = 1.f / hl[h];
+      // every gate value is loaded before the first output is stored (the
+      // stores would otherwise order each following load behind them)
+      float gate[ATTN_MAXO];
+#pragma unroll
+      for (int o = 0; o < ATTN_MAXO; ++o) {
+        const int i = tid + o * ATTN_THREADS;
+        const int h = i / hd, d = i - h * hd;
+        gate[o] = i < nout ? __ldcg(a.qout + (kvh * G + h) * 2 * hd + hd + d) : 0.f;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int o = 0; o < ATTN_MAXO; ++o) {
+        const int i = tid + o * ATTN_THREADS;
+        if (i < nout) {
+          const int h = i / hd, d = i - h * hd;
+          a.out[(kvh * G + h) * hd + d] = (acc[o] * hal[h]) * fast_sigmoid(gate[o]);
+        }
+      }
+    }
+    trc.end(a.trace);
+    return;
+  }
   float* part = a.part + (int64_t(kvh) * a.nchunks + chunk) * G * (hd + 2);
-  for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
-    const int h = i / hd, d = i % hd;
-    float acc = 0.f;
-    for (int j = 0; j < n; ++j) {
-      const int p = p0 + j;
-      const float vv = p == pos ? vn[d] : Vc[int64_t(p) * hd + d];
-      acc += sc[h * a.chunk_cap + j] * vv;
+#pragma unroll
+  for (int o = 0; o < ATTN_MAXO; ++o) {
+    const int i = tid + o * ATTN_THREADS;
+    if (i < nout) {
+      const int h = i / hd, d = i - h * hd;
+      part[h * (hd + 2) + 2 + d] = acc[o];
     }
-    part[h * (hd + 2) + 2 + d] = acc;
   }
-  for (int h = threadIdx.x; h < G; h += blockDim.x) { part[h * (hd + 2)] = hm[h]; part[h * (hd + 2) + 1] = hl[h]; }
+  for (int h = tid; h < G; h += blockDim.x) { part[h * (hd + 2)] = n > 0 ? hm[h] : -INFINITY; part[h * (hd + 2) + 1] = hl[h]; }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     __threadfence();
     last = atomicAdd(a.counters + kvh, 1u) == unsigned(a.nchunks) - 1;
   }
@@ -311,7 +429,6 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
   __threadfence();
   // combine: per head the chunk weights f_c = exp(m_c - m) first
   const float* pk = a.part + int64_t(kvh) * a.nchunks * G * (hd + 2);
-  float* fw = sc;  // [G][nvalid] reused
   for (int h = warp; h < G; h += nw) {
     float m = -INFINITY;
     for (int c = lane; c < nvalid; c += 32) m = fmaxf(m, __ldcg(pk + (int64_t(c) * G + h) * (hd + 2)));
@@ -321,22 +438,42 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
       const float* pc = pk + (int64_t(c) * G + h) * (hd + 2);
       const float mc = __ldcg(pc);
       const float f = mc == -INFINITY ? 0.f : expf(mc - m);
-      fw[h * a.chunk_cap + c] = f;
+      fw[h * a.nchunks + c] = f;
       l += __ldcg(pc + 1) * f;
     }
     l = warp_sum(l);
     if (lane == 0) hl[h] = l;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
-    const int h = i / hd, d = i % hd;
-    float o = 0.f;
-    for (int c = 0; c < nvalid; ++c) o += __ldcg(pk + (int64_t(c) * G + h) * (hd + 2) + 2 + d) * fw[h * a.chunk_cap + c];
-    const int head = kvh * G + h;
-    const float gate = a.qout[head * 2 * hd + hd + d];
-    a.out[head * hd + d] = (o / hl[h]) * sigmoid_ref(gate);
+  for (int h = tid; h < G; h += blockDim.x) hal[h] = 1.f / hl[h];
+  __syncthreads();
+  // all partial reads and gate loads first, then the stores (see above)
+#pragma unroll
+  for (int o = 0; o < ATTN_MAXO; ++o) {
+    const int i = tid + o * ATTN_THREADS;
+    acc[o] = 0.f;
+    if (i < nout) {
+      const int h = i / hd, d = i - h * hd;
+      for (int c = 0; c < nvalid; ++c)
+        acc[o] += __ldcg(pk + (int64_t(c) * G + h) * (hd + 2) + 2 + d) * fw[h * a.nchunks + c];
+    }
   }
-  if (threadIdx.x == 0) a.counters[kvh] = 0u;
+  float gate[ATTN_MAXO];
+#pragma unroll
+  for (int o = 0; o < ATTN_MAXO; ++o) {
+    const int i = tid + o * ATTN_THREADS;
+    const int h = i / hd, d = i - h * hd;
+    gate[o] = i < nout ? __ldcg(a.qout + (kvh * G + h) * 2 * hd + hd + d) : 0.f;
+  }
+#pragma unroll
+  for (int o = 0; o < ATTN_MAXO; ++o) {
+    const int i = tid + o * ATTN_THREADS;
+    if (i < nout) {
+      const int h = i / hd, d = i - h * hd;
+      a.out[(kvh * G + h) * hd + d] = (acc[o] * hal[h]) * fast_sigmoid(gate[o]);
+    }
+  }
+  if (tid == 0) a.counters[kvh] = 0u;
   trc.end(a.trace);
 }
 
@@ -402,7 +539,9 @@ void launch_delta(const DeltaArgs& a, cudaStream_t st, bool pdl) {
 void launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl) {
   const int G = a.H / a.Hkv;
   if (G > 63 || a.hd > 256 || a.rot > a.hd) throw Error(ERR_UNSUPPORTED, "attention geometry outside the decode kernel's range");
-  const size_t smem = size_t(G * a.hd + 2 * a.hd + a.rot + G * std::max(a.chunk_cap, a.nchunks)) * 4;
+  if (G * a.hd > ATTN_MAXO * ATTN_THREADS || G > 64 || a.hd % 4 || a.nchunks > 64)
+    throw Error(ERR_UNSUPPORTED, "attention shape outside the decode kernel's limits");
+  const size_t smem = size_t(G * a.hd + 2 * a.hd + 2 * ATTN_TP * a.hd + G * ATTN_TP + G * a.nchunks + a.rot) * 4;
   launch(k_attn, dim3(a.Hkv, a.nchunks), dim3(ATTN_THREADS), smem, st, pdl, a);
 }
 

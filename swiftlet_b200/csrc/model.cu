@@ -357,6 +357,7 @@ ExpertProj Model::expert_proj(uint8_t* pool_l, const std::string& proj, int out,
   }
   if (q.row_bytes % 16 || (w->offset % 16)) throw Error(ERR_UNSUPPORTED, "expert rows are not 16-byte aligned: " + proj);
   e.wstride = e.sstride = e.bstride = stride;
+  e.count = cfg.experts;
   return e;
 }
 
@@ -602,6 +603,9 @@ void Model::enqueue_layer(int l, cudaStream_t st, bool advance) {
   for (int s = 0; s < ld.n_in; ++s) { g.seg[s].lin = ld.in_lin[s]; g.seg[s].y = ld.in_y[s]; }
   g.nseg = ld.n_in; g.in = c.hidden; g.prologue = PRO_RMSNORM; g.epilogue = EPI_STORE;
   g.x = h; g.aux = ld.in_norm; g.eps = float(c.eps); g.status = kstatus;
+  // in_proj runs between the expert down kernel and the small mixer kernels:
+  // it may take more shared memory, enough to copy its whole slice early
+  g.smem_kb = 148;
   const unsigned lt = 16u * unsigned(l + 1);
   g.trace = tagged(lt + 2);
   launch_gemv(g, st, pdl);
@@ -637,6 +641,7 @@ void Model::enqueue_layer(int l, cudaStream_t st, bool advance) {
   m.x = xmoe; m.pick_ids = pick_ids; m.pick_w = pick_w; m.shared_scale = sscale;
   m.hmid = hmid; m.hmid_stride = hmid_stride; m.topk = c.topk; m.h = h;
   m.advance_sd = advance ? cur : nullptr; m.advance_cursor = cursor; m.status = kstatus;
+  m.smem_kb = 136;  // gate/up sits between the router and down kernels
   const bool route_in_moe = moe_routes_from_logits(m, c.experts);
   if (route_in_moe) { m.logits = rlogits; m.experts = c.experts; m.norm_topk = c.norm_topk; }
   RouterArgs r;

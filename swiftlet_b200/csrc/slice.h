@@ -7,6 +7,8 @@
 
 #include <cstdint>
 
+#include <cuda.h>
+
 namespace swl {
 
 constexpr int SL_CW = 4;                // consumer warps per CTA
@@ -36,6 +38,16 @@ struct SliceTab {
   int gs_shift;      // log2(group size)
   int off_xs, off_cs, off_red, off_part, off_raw, off_bar;  // dynamic smem offsets (ring at 0)
   int* status;       // bit 0 set when a bounded wait gave up (may be null)
+  int kpg() const { return (1 << gs_shift) >> 5; }  // 32-weight blocks per group
+};
+
+// Tensor maps of the weight matrices an integer tensor-core launch streams,
+// each {128 bytes, rows, row / 128 segments[, experts]} with the 128-byte
+// swizzle (dense: one per segment; gate/up: shared gate, shared up, routed
+// gate, routed up; down: shared down, -, routed down). Passed by value as a
+// __grid_constant__ kernel parameter.
+struct TileMaps {
+  CUtensorMap m[4];
 };
 
 // Router epilogue run by the last CTA: softmax over E logits, top-k and the

@@ -104,14 +104,15 @@ __device__ __forceinline__ void sl_init_barriers(uint64_t* full, uint64_t* empty
   __syncthreads();
 }
 
-// Sum over the consumer threads; `red` holds >= SL_CW floats.
+// Sum over the NT consumer threads; `red` holds >= NT / 32 floats.
+template <int NT = SL_NT>
 __device__ __forceinline__ float sl_sum(float v, float* red) {
   v = warp_sum(v);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  bar_sync_n(SL_NT);
+  bar_sync_n(NT);
   if (l == 0) red[w] = v;
-  bar_sync_n(SL_NT);
-  v = l < SL_CW ? red[l] : 0.f;
+  bar_sync_n(NT);
+  v = l < NT / 32 ? red[l] : 0.f;
   return warp_sum(v);
 }
 
@@ -120,13 +121,13 @@ __device__ __forceinline__ float sl_sum(float v, float* red) {
 // and after). Work item idx covers float4 jq of chunk c with c = idx % nch and
 // jq rotated by c, so that consecutive threads read and write distinct bank
 // groups; each chunk sum reads its chunk in the same rotated order.
-template <int BITS, int DT>
+template <int BITS, int DT, int NT = SL_NT>
 __device__ __forceinline__ void sl_interleave(const float* plain, int n, float* xs, float* cs) {
   constexpr int WPC = ChunkInfo<BITS, DT>::WPC, Q = WPC / 4;
   const int tid = threadIdx.x, nch = n / WPC;
   const float4* p4 = reinterpret_cast<const float4*>(plain);
   float4* x4 = reinterpret_cast<float4*>(xs);
-  for (int idx = tid; idx < nch * Q; idx += SL_NT) {
+  for (int idx = tid; idx < nch * Q; idx += NT) {
     const int c = idx % nch, jq = (idx / nch + c) % Q;
     float4 v = p4[c * Q + jq];
     if constexpr (BITS != 0) {
@@ -139,7 +140,7 @@ __device__ __forceinline__ void sl_interleave(const float* plain, int n, float* 
     x4[jq * nch + c] = v;
   }
   if constexpr (BITS != 0) {
-    for (int c = tid; c < nch; c += SL_NT) {
+    for (int c = tid; c < nch; c += NT) {
       float s = 0.f;
 #pragma unroll
       for (int t = 0; t < Q; ++t) {
@@ -159,8 +160,9 @@ __device__ __forceinline__ float f4_sq(const float4 v) { return (v.x * v.x + v.y
 // to register i), transformed (Prologue) and written plain to `plain` (in
 // floats of shared memory; sl_stage then interleaves it into xs / cs). red
 // holds SL_RED floats.
+template <int NT = SL_NT>
 __device__ __forceinline__ void sl_stage_plain(const GemvArgs& a, float* red, float* plain) {
-  constexpr int MAXQ = 4096 / (4 * SL_NT);
+  constexpr int MAXQ = 4096 / (4 * NT);
   const int in = a.in, nq = in >> 2, tid = threadIdx.x, lane = tid & 31;
   const bool norm = a.prologue == PRO_RMSNORM, gated = a.prologue == PRO_GATEDNORM;
   const float4* x4 = reinterpret_cast<const float4*>(a.x);
@@ -170,7 +172,7 @@ __device__ __forceinline__ void sl_stage_plain(const GemvArgs& a, float* red, fl
   float4 v[MAXQ], u[MAXQ], w[MAXQ];
 #pragma unroll
   for (int i = 0; i < MAXQ; ++i) {
-    const int q = i * SL_NT + tid;
+    const int q = i * NT + tid;
     const bool ok = q < nq;
     v[i] = ok ? __ldcg(x4 + q) : f4_zero();
     u[i] = ok && (norm || gated) ? __ldcg(u4 + q) : f4_zero();
@@ -181,7 +183,7 @@ __device__ __forceinline__ void sl_stage_plain(const GemvArgs& a, float* red, fl
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < MAXQ; ++i) ss += f4_sq(v[i]);
-    ss = sl_sum(ss, red);
+    ss = sl_sum<NT>(ss, red);
     const float scale = 1.f / sqrtf(ss / float(in) + a.eps);
 #pragma unroll
     for (int i = 0; i < MAXQ; ++i) {
@@ -206,20 +208,20 @@ __device__ __forceinline__ void sl_stage_plain(const GemvArgs& a, float* red, fl
       for (int i = 0; i < MAXQ; ++i) q2[i] += __shfl_xor_sync(0xffffffffu, q2[i], o);
 #pragma unroll
     for (int i = 0; i < MAXQ; ++i) {
-      const int q = i * SL_NT + tid;
+      const int q = i * NT + tid;
       if ((lane & 7) == 0 && q < nq) hs[q >> 3] = q2[i];
     }
-    bar_sync_n(SL_NT);
+    bar_sync_n(NT);
     const int hd = a.head_dim, per = hd >> 5, nh = in / hd;
-    for (int h = tid; h < nh; h += SL_NT) {
+    for (int h = tid; h < nh; h += NT) {
       float t = 0.f;
       for (int p = 0; p < per; ++p) t += hs[h * per + p];
       hsc[h] = 1.f / sqrtf(t / float(hd) + a.eps);
     }
-    bar_sync_n(SL_NT);
+    bar_sync_n(NT);
 #pragma unroll
     for (int i = 0; i < MAXQ; ++i) {
-      const int q = i * SL_NT + tid;
+      const int q = i * NT + tid;
       const float sc = q < nq ? hsc[q / hq] : 0.f;
       v[i].x = (v[i].x * (sc * w[i].x)) * u[i].x;
       v[i].y = (v[i].y * (sc * w[i].y)) * u[i].y;
@@ -231,13 +233,13 @@ __device__ __forceinline__ void sl_stage_plain(const GemvArgs& a, float* red, fl
   float4* o4 = (a.x_out && blockIdx.x == 0) ? reinterpret_cast<float4*>(a.x_out) : nullptr;
 #pragma unroll
   for (int i = 0; i < MAXQ; ++i) {
-    const int q = i * SL_NT + tid;
+    const int q = i * NT + tid;
     if (q < nq) {
       p4[q] = v[i];
       if (o4) o4[q] = v[i];
     }
   }
-  bar_sync_n(SL_NT);
+  bar_sync_n(NT);
 }
 
 template <int BITS, int DT>
@@ -247,56 +249,31 @@ __device__ __forceinline__ void sl_stage(const GemvArgs& a, float* xs, float* cs
   bar_sync_n(SL_NT);
 }
 
-// Transposed reduction of R per-lane partials (one per row) over the LPR
-// lanes of a sub-warp (R <= LPR, powers of two): each exchange round halves
-// the rows a lane holds, so R rows cost R - 1 + log2(LPR / R) shuffles
-// instead of R * log2(LPR). Returns the full sum of row `row` of this lane;
-// the lanes with sl % (LPR / R) == 0 hold distinct rows.
-template <int R>
-__device__ __forceinline__ float reduce_rows(float (&p)[R], int LPR, int sl, int& row) {
-  row = 0;
-  int o = LPR >> 1;
-#pragma unroll
-  for (int h = R >> 1; h >= 1; h >>= 1) {
-    const bool hi = (sl & o) != 0;
-#pragma unroll
-    for (int i = 0; i < h; ++i) {
-      const float send = hi ? p[i] : p[i + h];
-      const float keep = hi ? p[i + h] : p[i];
-      p[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-    }
-    if (hi) row += h;
-    o >>= 1;
-  }
-  float v = p[0];
-  for (; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-
 // Router epilogue (last CTA, consumer threads): softmax over E, top-k, combine
 // weights (QwenCPUModel.swift:506-521, 546-550; routerPicks
 // QwenMetalModel.swift:875-892). p holds E floats of shared memory.
+template <int NT = SL_NT>
 __device__ __forceinline__ void sl_router_tail(const RouterTail& rt, float* p, float* red) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, E = rt.E;
   float m = -INFINITY;
-  for (int e = tid; e < E; e += SL_NT) {
+  for (int e = tid; e < E; e += NT) {
     p[e] = __ldcg(rt.logits + e);
     m = fmaxf(m, p[e]);
   }
   m = warp_max(m);
-  bar_sync_n(SL_NT);
+  bar_sync_n(NT);
   if (lane == 0) red[warp] = m;
-  bar_sync_n(SL_NT);
+  bar_sync_n(NT);
   m = -INFINITY;
-  for (int w = 0; w < SL_CW; ++w) m = fmaxf(m, red[w]);
+  for (int w = 0; w < (NT / 32); ++w) m = fmaxf(m, red[w]);
   float sum = 0.f;
-  for (int e = tid; e < E; e += SL_NT) {
+  for (int e = tid; e < E; e += NT) {
     p[e] = expf(p[e] - m);
     sum += p[e];
   }
-  sum = sl_sum(sum, red + 8);
-  for (int e = tid; e < E; e += SL_NT) p[e] = p[e] / sum;
-  bar_sync_n(SL_NT);
+  sum = sl_sum<NT>(sum, red + 8);
+  for (int e = tid; e < E; e += NT) p[e] = p[e] / sum;
+  bar_sync_n(NT);
   if (warp != 0) return;
   // top-k by repeated warp argmax; ties keep the lower expert id, the outcome
   // of the reference's insertion scan with a strict `>` (:516).
@@ -333,6 +310,7 @@ __device__ __forceinline__ void sl_router_tail(const RouterTail& rt, float* p, f
 // Greedy argmax over the rows this CTA wrote (consumer threads; (bv, bi) is
 // the thread's best): per-CTA best, then the last CTA reduces them (first
 // index wins on ties, TextGenerator.swift:90).
+template <int NT = SL_NT>
 __device__ __forceinline__ void sl_argmax_tail(const GemvArgs& a, float bv, int bi, float* red) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   for (int o = 16; o; o >>= 1) {
@@ -341,19 +319,19 @@ __device__ __forceinline__ void sl_argmax_tail(const GemvArgs& a, float bv, int 
     if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
   }
   int* ired = reinterpret_cast<int*>(red);
-  bar_sync_n(SL_NT);
+  bar_sync_n(NT);
   if (lane == 0) { red[warp] = bv; ired[8 + warp] = bi; }
   __threadfence();
-  bar_sync_n(SL_NT);
+  bar_sync_n(NT);
   if (tid == 0) {
-    for (int w = 1; w < SL_CW; ++w)
+    for (int w = 1; w < (NT / 32); ++w)
       if (red[w] > bv || (red[w] == bv && ired[8 + w] < bi)) { bv = red[w]; bi = ired[8 + w]; }
     a.argmax_val[blockIdx.x] = bv;
     a.argmax_idx[blockIdx.x] = bi;
     __threadfence();
     ired[16] = atomicAdd(a.counter, 1u) == gridDim.x - 1;
   }
-  bar_sync_n(SL_NT);
+  bar_sync_n(NT);
   if (ired[16] && warp == 0) {
     __threadfence();
     float gv = -INFINITY;
@@ -376,16 +354,17 @@ __device__ __forceinline__ void sl_argmax_tail(const GemvArgs& a, float bv, int 
 }
 
 // Router epilogue trigger: the last CTA to finish runs sl_router_tail.
+template <int NT = SL_NT>
 __device__ __forceinline__ void sl_router_done(const RouterTail& rt, float* p, float* red) {
   const int tid = threadIdx.x;
   int* ired = reinterpret_cast<int*>(red);
   __threadfence();
-  bar_sync_n(SL_NT);
+  bar_sync_n(NT);
   if (tid == 0) ired[16] = atomicAdd(rt.counter, 1u) == gridDim.x - 1;
-  bar_sync_n(SL_NT);
+  bar_sync_n(NT);
   if (ired[16]) {
     __threadfence();
-    sl_router_tail(rt, p, red);
+    sl_router_tail<NT>(rt, p, red);
   }
 }
 

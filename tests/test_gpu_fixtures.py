@@ -115,3 +115,21 @@ def test_dequant_is_bit_exact():
         a = cpu.dequant(mod, rows[0], rows[1], cols)
         b = gpu.debug_dequant(mod, rows[0], rows[1], cols)
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), mod
+
+
+def test_long_context_matches_oracle():
+    # 200 positions: the attention layer splits the context over several
+    # chunks (and sub-tiles) whose partial softmax results are combined.
+    d = os.path.join(REF_FIXTURES, "tiny-model-q4")
+    cpu = oracle.OracleModel(d)
+    gpu = swl.QwenCUDAModel(d)
+    cs, gs = oracle.DecodeState(), swl.DecodeState(256)
+    vocab = json.load(open(os.path.join(d, "config.json")))["vocab_size"]
+    rng = np.random.default_rng(5)
+    toks = [int(t) for t in rng.integers(0, vocab, 200)]
+    for i, t in enumerate(toks):
+        cl = cpu.step([t], cs)
+        gl = gpu.step([t], gs)
+        if i % 25 == 24 or i == len(toks) - 1:
+            assert np.abs(cl - gl).max() < 2e-3, i
+            assert int(np.argmax(cl)) == int(np.argmax(gl)), i
