@@ -290,7 +290,7 @@ def run_ours(args) -> None:
         "step_roofline": {"bound": "hbm", "bytes_per_token": bt["total"], "achieved": bt["total"] * value / world / 1e9,
                           "peak": hbm, "unit": "GB/s", "frac": bt["total"] * value / world / 1e9 / hbm,
                           "peak_kind": peak_kind},
-        "roofline": {"kernel": "k_moe_gateup + k_moe_down (8 routed + 1 shared expert, one layer)", "bound": "hbm",
+        "roofline": {"kernel": "k_igateup + k_idown (8 routed + 1 shared expert, one layer)", "bound": "hbm",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "bytes_per_launch_pair": bytes_layer, "avg_pair_us": per_launch_s * 1e6,
                      "traffic": traffic, "peak_kind": peak_kind},

@@ -1066,26 +1066,32 @@ int swl_bench_expert_sweep(swl_model* model, int32_t iters, float* ms_out, doubl
   Model& m = model->m;
   if (!m.stepped) throw Error(ERR_INVALID, "run one step before the expert sweep");
   SWL_CUDA(cudaSetDevice(m.device));
-  cudaEvent_t e0, e1;
-  SWL_CUDA(cudaEventCreate(&e0));
-  SWL_CUDA(cudaEventCreate(&e1));
-  SWL_CUDA(cudaEventRecord(e0, m.stream));
-  for (int it = 0; it < iters; ++it)
+  // One sweep over every layer's expert pair (routing as the last step left
+  // it), captured once as a graph so the timing is device time only.
+  cudaGraphExec_t sweep = capture(m.stream, [&] {
     for (int l = 0; l < m.cfg.layers; ++l) {
       const LayerDev& ld = m.L[l];
       MoeArgs a;
       a.g = ld.eg; a.u = ld.eu; a.d = ld.ed; a.sg = ld.sh_g; a.su = ld.sh_u; a.sd = ld.sh_d;
       a.x = m.xmoe; a.pick_ids = m.pick_ids; a.pick_w = m.pick_w; a.shared_scale = m.sscale;
       a.hmid = m.hmid; a.hmid_stride = m.hmid_stride; a.topk = m.cfg.topk; a.h = m.h;
-      a.advance_sd = nullptr; a.advance_cursor = nullptr;
+      a.advance_sd = nullptr; a.advance_cursor = nullptr; a.smem_kb = 136;
       launch_moe_gateup(a, m.stream, m.use_pdl);
       launch_moe_down(a, m.stream, m.use_pdl);
     }
+  });
+  cudaEvent_t e0, e1;
+  SWL_CUDA(cudaEventCreate(&e0));
+  SWL_CUDA(cudaEventCreate(&e1));
+  SWL_CUDA(cudaGraphLaunch(sweep, m.stream));  // warm-up
+  SWL_CUDA(cudaEventRecord(e0, m.stream));
+  for (int it = 0; it < iters; ++it) SWL_CUDA(cudaGraphLaunch(sweep, m.stream));
   SWL_CUDA(cudaEventRecord(e1, m.stream));
   SWL_CUDA(cudaEventSynchronize(e1));
   SWL_CUDA(cudaEventElapsedTime(ms_out, e0, e1));
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
+  cudaGraphExecDestroy(sweep);
   const LayerDev& l0 = m.L[0];
   if (bytes_per_layer)
     *bytes_per_layer = double(m.cfg.topk) * double(qlin_bytes(l0.eg.lin) + qlin_bytes(l0.eu.lin) + qlin_bytes(l0.ed.lin)) +
