@@ -42,6 +42,10 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
 }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Waits until at most N committed groups of this thread are still in flight.
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 // Block-wide copy of n floats (n % 4 == 0, both pointers 16-byte aligned).
 __device__ __forceinline__ void copy_async(float* dst, const float* src, int n) {
   for (int i = threadIdx.x; i < (n >> 2); i += blockDim.x) cp_async16(dst + 4 * i, src + 4 * i);

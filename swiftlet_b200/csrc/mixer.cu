@@ -177,12 +177,17 @@ __global__ void __launch_bounds__(DELTA_THREADS) k_delta(const DeltaArgs a) {
 // RoPE, KV append, causal softmax(q k^T / sqrt(hd)) v split over context
 // chunks of at least ATTN_MINP positions, times sigmoid(gate)
 // (QwenCPUModel.swift:285-367). KV layout: [kv_head][max_ctx][head_dim].
-// A CTA walks its chunk in sub-tiles of ATTN_TP positions: the K and V rows
-// are copied to shared memory in one asynchronous round trip, scores are
-// half-dots by thread pairs (row index rotated by position: no bank
-// conflicts), and an online softmax carries (max, sum, output) across
-// sub-tiles. With one chunk the CTA writes the output; otherwise the last CTA
-// of each kv head combines the chunks' partials.
+// A CTA walks its chunk in sub-tiles of ATTN_TP positions, double-buffered:
+// the K and V rows of the next sub-tile are copied to shared memory
+// (asynchronously; the first sub-tile's cached rows before the dependency
+// wait) while the current one is scored. Scores take one warp per position
+// with the G heads reduced together; an online softmax carries (max, sum,
+// output) across sub-tiles. Every inner loop has a compile-time trip count
+// (head size HD, sub-tile ATTN_TP; the rows of a short sub-tile are zero), so
+// its loads issue together rather than one dependent round trip at a time.
+// With one chunk the CTA writes the output; otherwise the last CTA of each kv
+// head combines the chunks' partials.
+//
 // Output gate sigmoid with the fast exponential and divide (within a few
 // ulp of 1 / (1 + exp(-v)); one per output element).
 __device__ __forceinline__ float fast_sigmoid(float v) { return __fdividef(1.f, 1.f + __expf(-v)); }
@@ -192,16 +197,18 @@ constexpr int ATTN_MINP = 64;  // minimum positions per chunk
 constexpr int ATTN_TP = 16;    // positions per staged sub-tile
 constexpr int ATTN_MAXO = 16;  // output values per thread: G * hd <= ATTN_MAXO * ATTN_THREADS
 
+template <int HD>
 __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
+  constexpr int E = HD >= 32 ? HD / 32 : 1;  // row elements per lane (l + 32e)
+  constexpr int HQ = HD / 4;                 // float4 per row
   extern __shared__ __align__(16) float sm[];
-  const int hd = a.hd, G = a.H / a.Hkv, kvh = blockIdx.x, chunk = blockIdx.y;
+  const int G = a.H / a.Hkv, kvh = blockIdx.x, chunk = blockIdx.y;
   const int half = a.rot / 2;
-  float* q = sm;                      // [G][hd]
-  float* kn = q + G * hd;             // [hd]
-  float* vn = kn + hd;                // [hd]
-  float* kt = vn + hd;                // [TP][hd]
-  float* vt = kt + ATTN_TP * hd;      // [TP][hd]
-  float* sc = vt + ATTN_TP * hd;      // [G][TP]
+  float* q = sm;                      // [G][HD]
+  float* kn = q + G * HD;             // [HD]
+  float* vn = kn + HD;                // [HD]
+  float* kvb = vn + HD;               // 2 x ([TP][HD] keys, [TP][HD] values)
+  float* sc = kvb + 4 * ATTN_TP * HD; // [G][TP]
   float* fw = sc + G * ATTN_TP;       // [G][nchunks] combine weights
   float* cs = fw + G * a.nchunks;     // [half] cos
   float* sn = cs + half;              // [half] sin
@@ -216,16 +223,29 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
   const int nvalid = min(a.nchunks, (ctx + ATTN_MINP - 1) / ATTN_MINP);
   const int per = (ctx + nvalid - 1) / nvalid;
   const int p0 = chunk * per, p1 = min(ctx, p0 + per), n = chunk < nvalid ? max(0, p1 - p0) : 0;
-  float* Kc = sd->kc[a.layer] + int64_t(kvh) * sd->max_ctx * hd;
-  float* Vc = sd->vc[a.layer] + int64_t(kvh) * sd->max_ctx * hd;
-  // before the wait: L2 prefetch of this chunk's cached rows, RoPE table
-  if (tid == 0 && n > 0) {
-    const int old = min(p1, pos) - p0;  // rows < pos are already cached
-    if (old > 0) {
-      prefetch_l2(Kc + int64_t(p0) * hd, uint32_t(old) * hd * 4);
-      prefetch_l2(Vc + int64_t(p0) * hd, uint32_t(old) * hd * 4);
+  const int ntiles = (n + ATTN_TP - 1) / ATTN_TP;
+  float* Kc = sd->kc[a.layer] + int64_t(kvh) * sd->max_ctx * HD;
+  float* Vc = sd->vc[a.layer] + int64_t(kvh) * sd->max_ctx * HD;
+  // copies of sub-tile t into buffer t & 1: cached rows asynchronously, the
+  // rows past the chunk's end zeroed (the new position's row is written from
+  // kn / vn once they are ready)
+  auto stage = [&](int t) {
+    float* kt = kvb + (t & 1) * 2 * ATTN_TP * HD;
+    float* vt = kt + ATTN_TP * HD;
+    const int t0 = p0 + t * ATTN_TP, nt = min(ATTN_TP, p0 + n - t0);
+    for (int i = tid; i < ATTN_TP * HQ; i += ATTN_THREADS) {
+      const int j = i / HQ, c = i - j * HQ, p = t0 + j;
+      if (j < nt && p != pos) {
+        cp_async16(kt + j * HD + 4 * c, Kc + int64_t(p) * HD + 4 * c);
+        cp_async16(vt + j * HD + 4 * c, Vc + int64_t(p) * HD + 4 * c);
+      } else if (j >= nt) {
+        reinterpret_cast<float4*>(vt + j * HD)[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
     }
-  }
+    cp_async_commit();
+  };
+  // before the wait: the first sub-tile's cached rows, RoPE table, norm weights
+  if (ntiles > 0) stage(0);
   for (int j = tid; j < half; j += blockDim.x) {
     const float invf = powf(a.rope_theta, -float(2 * j) / float(a.rot));
     const float ang = float(pos) * invf;
@@ -233,126 +253,136 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
     sn[j] = sinf(ang);
   }
   for (int h = tid; h < G; h += blockDim.x) { hm[h] = -INFINITY; hl[h] = 0.f; }
+  float wq[E], wk[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int d = lane + 32 * e;
+    wq[e] = d < HD ? a.qn[d] : 0.f;
+    wk[e] = d < HD ? a.kn[d] : 0.f;
+  }
   pdl_wait();
   trc.waited(a.trace);
-  for (int h = 0; h < G; ++h) copy_async(q + h * hd, a.qout + (kvh * G + h) * 2 * hd, hd);
-  copy_async(kn, a.knew + kvh * hd, hd);
-  copy_async(vn, a.vnew + kvh * hd, hd);
-  cp_async_wait_all();
+  for (int h = 0; h < G; ++h) copy_async(q + h * HD, a.qout + (kvh * G + h) * 2 * HD, HD);
+  copy_async(kn, a.knew + kvh * HD, HD);
+  copy_async(vn, a.vnew + kvh * HD, HD);
+  cp_async_commit();
+  cp_async_wait_group<0>();
   __syncthreads();
   pdl_launch();
-  if (hd % 32 == 0 && hd <= 256 && half % 32 == 0) {
+  if (HD >= 32 && half % 32 == 0) {
     // one warp per head (G q heads and the new k head), in registers: lane l
     // holds elements l + 32e, so RoPE partners (j, j + half) share a lane
-    const int E = hd >> 5, hs = half >> 5;
+    const int hs = half >> 5;
     for (int h = warp; h <= G; h += nw) {
-      float* x = h < G ? q + h * hd : kn;
-      const float* w = h < G ? a.qn : a.kn;
-      float v[8];
+      float* x = h < G ? q + h * HD : kn;
+      float v[E];
       float ss = 0.f;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        v[e] = e < E ? x[lane + 32 * e] : 0.f;
+      for (int e = 0; e < E; ++e) {
+        v[e] = x[lane + 32 * e];
         ss += v[e] * v[e];
       }
       ss = warp_sum(ss);
-      const float sc = 1.f / sqrtf(ss / float(hd) + a.eps);
+      const float sc0 = 1.f / sqrtf(ss / float(HD) + a.eps);
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (e < E) v[e] *= sc * w[lane + 32 * e];
+      for (int e = 0; e < E; ++e) v[e] *= sc0 * (h < G ? wq[e] : wk[e]);
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
+      for (int e = 0; e < E; ++e)
         if (e < hs) {
           const int j = lane + 32 * e;
-          const float xa = v[e], xb = v[e + hs];
+          float xb = 0.f;
+#pragma unroll
+          for (int f = 0; f < E; ++f)
+            if (f == e + hs) xb = v[f];
+          const float xa = v[e];
           v[e] = xa * cs[j] - xb * sn[j];
-          v[e + hs] = xb * cs[j] + xa * sn[j];
+#pragma unroll
+          for (int f = 0; f < E; ++f)
+            if (f == e + hs) v[f] = xb * cs[j] + xa * sn[j];
         }
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (e < E) x[lane + 32 * e] = v[e];
+      for (int e = 0; e < E; ++e) x[lane + 32 * e] = v[e];
     }
-    __syncthreads();
   } else {
     // RMSNorm of G q heads and the new k head, one warp per head
     for (int h = warp; h <= G; h += nw) {
-      float* x = h < G ? q + h * hd : kn;
+      float* x = h < G ? q + h * HD : kn;
       float ss = 0.f;
-      for (int i = lane; i < hd; i += 32) ss += x[i] * x[i];
+      for (int i = lane; i < HD; i += 32) ss += x[i] * x[i];
       ss = warp_sum(ss);
-      if (lane == 0) hn[h] = 1.f / sqrtf(ss / float(hd) + a.eps);
+      if (lane == 0) hn[h] = 1.f / sqrtf(ss / float(HD) + a.eps);
     }
     __syncthreads();
-    for (int i = tid; i < (G + 1) * hd; i += blockDim.x) {
-      const int h = i / hd, d = i % hd;
-      float* x = h < G ? q + h * hd : kn;
+    for (int i = tid; i < (G + 1) * HD; i += blockDim.x) {
+      const int h = i / HD, d = i % HD;
+      float* x = h < G ? q + h * HD : kn;
       const float* w = h < G ? a.qn : a.kn;
       x[d] *= hn[h] * w[d];
     }
     __syncthreads();
     for (int i = tid; i < (G + 1) * half; i += blockDim.x) {
       const int h = i / half, j = i % half;
-      float* x = h < G ? q + h * hd : kn;
+      float* x = h < G ? q + h * HD : kn;
       const float xa = x[j], xb = x[half + j];
       x[j] = xa * cs[j] - xb * sn[j];
       x[half + j] = xb * cs[j] + xa * sn[j];
     }
-    __syncthreads();
   }
+  __syncthreads();
   if (chunk == 0)
-    for (int i = tid; i < hd; i += blockDim.x) {
-      Kc[int64_t(pos) * hd + i] = kn[i];
-      Vc[int64_t(pos) * hd + i] = vn[i];
+    for (int i = tid; i < HD; i += blockDim.x) {
+      Kc[int64_t(pos) * HD + i] = kn[i];
+      Vc[int64_t(pos) * HD + i] = vn[i];
     }
   trc.staged(a.trace);
-  const float scale = 1.f / sqrtf(float(hd));
-  const int nout = G * hd;
+  const float scale = 1.f / sqrtf(float(HD));
+  const int nout = G * HD;
   float acc[ATTN_MAXO];
 #pragma unroll
   for (int o = 0; o < ATTN_MAXO; ++o) acc[o] = 0.f;
-  const int hq = hd >> 2;  // float4 per row
-  for (int t0 = p0; t0 < p0 + n; t0 += ATTN_TP) {
-    const int nt = min(ATTN_TP, p0 + n - t0);
-    // stage rows t0 .. t0 + nt of K and V (the new position from kn / vn)
-    for (int i = tid; i < nt * hq; i += blockDim.x) {
-      const int j = i / hq, c = i - j * hq, p = t0 + j;
-      if (p == pos) {
-        reinterpret_cast<float4*>(kt + j * hd)[c] = reinterpret_cast<const float4*>(kn)[c];
-        reinterpret_cast<float4*>(vt + j * hd)[c] = reinterpret_cast<const float4*>(vn)[c];
-      } else {
-        cp_async16(kt + j * hd + 4 * c, Kc + int64_t(p) * hd + 4 * c);
-        cp_async16(vt + j * hd + 4 * c, Vc + int64_t(p) * hd + 4 * c);
-      }
+  for (int t = 0; t < ntiles; ++t) {
+    float* kt = kvb + (t & 1) * 2 * ATTN_TP * HD;
+    float* vt = kt + ATTN_TP * HD;
+    const int t0 = p0 + t * ATTN_TP, nt = min(ATTN_TP, p0 + n - t0);
+    if (t + 1 < ntiles) {
+      stage(t + 1);
+      cp_async_wait_group<1>();  // sub-tile t landed, t + 1 may still fly
+    } else {
+      cp_async_wait_group<0>();
     }
-    cp_async_wait_all();
+    if (pos >= t0 && pos < t0 + nt)  // the new position: its normalised, rotated key and its value
+      for (int i = tid; i < HD; i += blockDim.x) {
+        kt[(pos - t0) * HD + i] = kn[i];
+        vt[(pos - t0) * HD + i] = vn[i];
+      }
     __syncthreads();
     // scores: one warp per position; lane l covers elements l + 32e of the
-    // row, and the G head partials are reduced together, eight heads at a
-    // time (transposed reduction)
+    // row, and the head partials are reduced eight heads at a time
     for (int j = warp; j < ATTN_TP; j += nw) {
       const bool live = j < nt;
-      float kv[8];
+      float kv[E];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) kv[e] = live && lane + 32 * e < hd ? kt[j * hd + lane + 32 * e] : 0.f;
+      for (int e = 0; e < E; ++e) kv[e] = live && lane + 32 * e < HD ? kt[j * HD + lane + 32 * e] : 0.f;
       for (int h0 = 0; h0 < G; h0 += 8) {
-        float p[8];
+        float pr[8];
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
           float d = 0.f;
-          if (h0 + r < G)
 #pragma unroll
-            for (int e = 0; e < 8; ++e)
-              if (lane + 32 * e < hd) d += q[(h0 + r) * hd + lane + 32 * e] * kv[e];
-          p[r] = d;
+          for (int e = 0; e < E; ++e) {
+            const bool ok = h0 + r < G && lane + 32 * e < HD;
+            d += (ok ? q[(h0 + r) * HD + lane + 32 * e] : 0.f) * kv[e];
+          }
+          pr[r] = d;
         }
         int rr;
-        const float d = reduce_rows<8>(p, 32, lane, rr);
+        const float d = reduce_rows<8>(pr, 32, lane, rr);
         if ((lane & 3) == 0 && h0 + rr < G) sc[(h0 + rr) * ATTN_TP + j] = live ? d * scale : -INFINITY;
       }
     }
     __syncthreads();
     // online softmax: per head the new max, the rescale of what came before,
-    // the weights of this sub-tile
+    // the weights of this sub-tile (0 for rows past the chunk)
     for (int h = warp; h < G; h += nw) {
       const float v = lane < ATTN_TP ? sc[h * ATTN_TP + lane] : -INFINITY;
       const float mt = warp_max(v);
@@ -372,9 +402,10 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
     for (int o = 0; o < ATTN_MAXO; ++o) {
       const int i = tid + o * ATTN_THREADS;
       if (i < nout) {
-        const int h = i / hd, d = i - h * hd;
+        const int h = i / HD, d = i - h * HD;
         float v = acc[o] * hal[h];
-        for (int j = 0; j < nt; ++j) v += sc[h * ATTN_TP + j] * vt[j * hd + d];
+#pragma unroll
+        for (int j = 0; j < ATTN_TP; ++j) v += sc[h * ATTN_TP + j] * vt[j * HD + d];
         acc[o] = v;
       }
     }
@@ -390,32 +421,32 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
 #pragma unroll
       for (int o = 0; o < ATTN_MAXO; ++o) {
         const int i = tid + o * ATTN_THREADS;
-        const int h = i / hd, d = i - h * hd;
-        gate[o] = i < nout ? __ldcg(a.qout + (kvh * G + h) * 2 * hd + hd + d) : 0.f;
+        const int h = i / HD, d = i - h * HD;
+        gate[o] = i < nout ? __ldcg(a.qout + (kvh * G + h) * 2 * HD + HD + d) : 0.f;
       }
       __syncthreads();
 #pragma unroll
       for (int o = 0; o < ATTN_MAXO; ++o) {
         const int i = tid + o * ATTN_THREADS;
         if (i < nout) {
-          const int h = i / hd, d = i - h * hd;
-          a.out[(kvh * G + h) * hd + d] = (acc[o] * hal[h]) * fast_sigmoid(gate[o]);
+          const int h = i / HD, d = i - h * HD;
+          a.out[(kvh * G + h) * HD + d] = (acc[o] * hal[h]) * fast_sigmoid(gate[o]);
         }
       }
     }
     trc.end(a.trace);
     return;
   }
-  float* part = a.part + (int64_t(kvh) * a.nchunks + chunk) * G * (hd + 2);
+  float* part = a.part + (int64_t(kvh) * a.nchunks + chunk) * G * (HD + 2);
 #pragma unroll
   for (int o = 0; o < ATTN_MAXO; ++o) {
     const int i = tid + o * ATTN_THREADS;
     if (i < nout) {
-      const int h = i / hd, d = i - h * hd;
-      part[h * (hd + 2) + 2 + d] = acc[o];
+      const int h = i / HD, d = i - h * HD;
+      part[h * (HD + 2) + 2 + d] = acc[o];
     }
   }
-  for (int h = tid; h < G; h += blockDim.x) { part[h * (hd + 2)] = n > 0 ? hm[h] : -INFINITY; part[h * (hd + 2) + 1] = hl[h]; }
+  for (int h = tid; h < G; h += blockDim.x) { part[h * (HD + 2)] = n > 0 ? hm[h] : -INFINITY; part[h * (HD + 2) + 1] = hl[h]; }
   __syncthreads();
   if (tid == 0) {
     __threadfence();
@@ -428,14 +459,14 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
   }
   __threadfence();
   // combine: per head the chunk weights f_c = exp(m_c - m) first
-  const float* pk = a.part + int64_t(kvh) * a.nchunks * G * (hd + 2);
+  const float* pk = a.part + int64_t(kvh) * a.nchunks * G * (HD + 2);
   for (int h = warp; h < G; h += nw) {
     float m = -INFINITY;
-    for (int c = lane; c < nvalid; c += 32) m = fmaxf(m, __ldcg(pk + (int64_t(c) * G + h) * (hd + 2)));
+    for (int c = lane; c < nvalid; c += 32) m = fmaxf(m, __ldcg(pk + (int64_t(c) * G + h) * (HD + 2)));
     m = warp_max(m);
     float l = 0.f;
     for (int c = lane; c < nvalid; c += 32) {
-      const float* pc = pk + (int64_t(c) * G + h) * (hd + 2);
+      const float* pc = pk + (int64_t(c) * G + h) * (HD + 2);
       const float mc = __ldcg(pc);
       const float f = mc == -INFINITY ? 0.f : expf(mc - m);
       fw[h * a.nchunks + c] = f;
@@ -446,31 +477,39 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
   }
   __syncthreads();
   for (int h = tid; h < G; h += blockDim.x) hal[h] = 1.f / hl[h];
-  __syncthreads();
-  // all partial reads and gate loads first, then the stores (see above)
+  // all partial reads (every chunk's values of this thread's outputs in one
+  // batch per chunk) and gate loads first, then the stores
 #pragma unroll
-  for (int o = 0; o < ATTN_MAXO; ++o) {
-    const int i = tid + o * ATTN_THREADS;
-    acc[o] = 0.f;
-    if (i < nout) {
-      const int h = i / hd, d = i - h * hd;
-      for (int c = 0; c < nvalid; ++c)
-        acc[o] += __ldcg(pk + (int64_t(c) * G + h) * (hd + 2) + 2 + d) * fw[h * a.nchunks + c];
+  for (int o = 0; o < ATTN_MAXO; ++o) acc[o] = 0.f;
+  for (int c = 0; c < nvalid; ++c) {
+    const float* pc = pk + int64_t(c) * G * (HD + 2) + 2;
+    float v[ATTN_MAXO];
+#pragma unroll
+    for (int o = 0; o < ATTN_MAXO; ++o) {
+      const int i = tid + o * ATTN_THREADS;
+      const int h = i / HD, d = i - h * HD;
+      v[o] = i < nout ? __ldcg(pc + h * (HD + 2) + d) : 0.f;
+    }
+#pragma unroll
+    for (int o = 0; o < ATTN_MAXO; ++o) {
+      const int i = tid + o * ATTN_THREADS;
+      if (i < nout) acc[o] += v[o] * fw[(i / HD) * a.nchunks + c];
     }
   }
   float gate[ATTN_MAXO];
 #pragma unroll
   for (int o = 0; o < ATTN_MAXO; ++o) {
     const int i = tid + o * ATTN_THREADS;
-    const int h = i / hd, d = i - h * hd;
-    gate[o] = i < nout ? __ldcg(a.qout + (kvh * G + h) * 2 * hd + hd + d) : 0.f;
+    const int h = i / HD, d = i - h * HD;
+    gate[o] = i < nout ? __ldcg(a.qout + (kvh * G + h) * 2 * HD + HD + d) : 0.f;
   }
+  __syncthreads();
 #pragma unroll
   for (int o = 0; o < ATTN_MAXO; ++o) {
     const int i = tid + o * ATTN_THREADS;
     if (i < nout) {
-      const int h = i / hd, d = i - h * hd;
-      a.out[(kvh * G + h) * hd + d] = (acc[o] * hal[h]) * fast_sigmoid(gate[o]);
+      const int h = i / HD, d = i - h * HD;
+      a.out[(kvh * G + h) * HD + d] = (acc[o] * hal[h]) * fast_sigmoid(gate[o]);
     }
   }
   if (tid == 0) a.counters[kvh] = 0u;
@@ -539,10 +578,17 @@ void launch_delta(const DeltaArgs& a, cudaStream_t st, bool pdl) {
 void launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl) {
   const int G = a.H / a.Hkv;
   if (G > 63 || a.hd > 256 || a.rot > a.hd) throw Error(ERR_UNSUPPORTED, "attention geometry outside the decode kernel's range");
-  if (G * a.hd > ATTN_MAXO * ATTN_THREADS || G > 64 || a.hd % 4 || a.nchunks > 64)
+  if (G * a.hd > ATTN_MAXO * ATTN_THREADS || a.nchunks > 64)
     throw Error(ERR_UNSUPPORTED, "attention shape outside the decode kernel's limits");
-  const size_t smem = size_t(G * a.hd + 2 * a.hd + 2 * ATTN_TP * a.hd + G * ATTN_TP + G * a.nchunks + a.rot) * 4;
-  launch(k_attn, dim3(a.Hkv, a.nchunks), dim3(ATTN_THREADS), smem, st, pdl, a);
+  const size_t smem = size_t(G * a.hd + 2 * a.hd + 4 * ATTN_TP * a.hd + G * ATTN_TP + G * a.nchunks + a.rot) * 4;
+  switch (a.hd) {
+    case 16: launch(k_attn<16>, dim3(a.Hkv, a.nchunks), dim3(ATTN_THREADS), smem, st, pdl, a); break;
+    case 32: launch(k_attn<32>, dim3(a.Hkv, a.nchunks), dim3(ATTN_THREADS), smem, st, pdl, a); break;
+    case 64: launch(k_attn<64>, dim3(a.Hkv, a.nchunks), dim3(ATTN_THREADS), smem, st, pdl, a); break;
+    case 128: launch(k_attn<128>, dim3(a.Hkv, a.nchunks), dim3(ATTN_THREADS), smem, st, pdl, a); break;
+    case 256: launch(k_attn<256>, dim3(a.Hkv, a.nchunks), dim3(ATTN_THREADS), smem, st, pdl, a); break;
+    default: throw Error(ERR_UNSUPPORTED, "attention head size must be 16, 32, 64, 128 or 256");
+  }
 }
 
 void launch_embed(const EmbedArgs& a, int hidden, cudaStream_t st, bool pdl) {
