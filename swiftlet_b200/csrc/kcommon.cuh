@@ -111,9 +111,51 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
       "l"(src), "r"(bytes), "r"(smem_u32(b)), "l"(policy)
       : "memory");
 }
+// The same bulk copy with the default L2 policy (data that is read again, such
+// as the KV cache).
+__device__ __forceinline__ void bulk_g2s_keep(void* dst, const void* src, unsigned bytes, uint64_t* b) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(b))
+               : "memory");
+}
+// Orders this thread's earlier shared-memory accesses (generic proxy) before
+// its later bulk copies into the same memory (async proxy).
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 // Named barrier 1 over the first n threads (the consumer warps of a
 // warp-specialised block; the producer warp never joins it).
 __device__ __forceinline__ void bar_sync_n(int n) { asm volatile("bar.sync 1, %0;" ::"r"(n) : "memory"); }
+
+// ---- thread-block clusters: rank, barrier, distributed shared memory ----
+__device__ __forceinline__ unsigned cluster_rank() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Barrier over every thread of the cluster; shared-memory writes before it
+// are visible to every CTA of the cluster after it. All threads of all CTAs
+// must reach it (no thread of the cluster may have exited).
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The two halves of cluster_sync, for work between them: after arrive the
+// thread may not touch what it released to the cluster.
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// Address of the variable at `p` (this CTA's shared memory) in the shared
+// memory of cluster CTA `rank` (same offset).
+__device__ __forceinline__ uint32_t dsmem_map(const void* p, unsigned rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float dsmem_ld(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void dsmem_st(uint32_t addr, unsigned v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
 // Per-block timeline record (thread 0): see Trace.
 struct TraceRec {
   unsigned long long t0 = 0, t1 = 0, t2 = 0, t3 = 0;

@@ -142,9 +142,10 @@ struct AttnArgs {
   int chunk_cap;           // max positions per chunk (smem sizing)
   const StateDev* sd;
   int layer;
-  float* part;             // [Hkv][nchunks][G][hd + 2]
-  unsigned* counters;      // [Hkv]
+  float* part;             // [Hkv][nchunks / 8][G][hd + 2] per-cluster partials
+  unsigned* counters;      // [Hkv][8] per kv head and combine slice
   float* out;              // [H * hd] gated attention output
+  int* status = nullptr;   // bit 0: a bounded wait inside the kernel gave up
   Trace trace;
 };
 

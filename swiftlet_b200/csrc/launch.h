@@ -23,4 +23,25 @@ void launch(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pd
   SWL_CUDA(cudaLaunchKernelEx(&cfg, k, args...));
 }
 
+// The same with thread-block clusters of `cluster` CTAs (grid divisible by it).
+template <typename Kern, typename... Args>
+void launch_cluster(Kern k, dim3 grid, dim3 block, dim3 cluster, size_t smem, cudaStream_t st, bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster.x;
+  attr[0].val.clusterDim.y = cluster.y;
+  attr[0].val.clusterDim.z = cluster.z;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  if (smem > 48 * 1024) SWL_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  SWL_CUDA(cudaLaunchKernelEx(&cfg, k, args...));
+}
+
 }  // namespace swl

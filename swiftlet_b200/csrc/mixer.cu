@@ -174,85 +174,136 @@ __global__ void __launch_bounds__(DELTA_THREADS) k_delta(const DeltaArgs a) {
 
 // ----------------------------------------------------------- attention ----
 // Gated GQA decode for one token: q/k RMSNorm with weight, partial NeoX
-// RoPE, KV append, causal softmax(q k^T / sqrt(hd)) v split over context
-// chunks of at least ATTN_MINP positions, times sigmoid(gate)
+// RoPE, KV append, causal softmax(q k^T / sqrt(hd)) v, times sigmoid(gate)
 // (QwenCPUModel.swift:285-367). KV layout: [kv_head][max_ctx][head_dim].
-// A CTA walks its chunk in sub-tiles of ATTN_TP positions, double-buffered:
-// the K and V rows of the next sub-tile are copied to shared memory
-// (asynchronously; the first sub-tile's cached rows before the dependency
-// wait) while the current one is scored. Scores take one warp per position
-// with the G heads reduced together; an online softmax carries (max, sum,
-// output) across sub-tiles. Every inner loop has a compile-time trip count
-// (head size HD, sub-tile ATTN_TP; the rows of a short sub-tile are zero), so
-// its loads issue together rather than one dependent round trip at a time.
-// With one chunk the CTA writes the output; otherwise the last CTA of each kv
-// head combines the chunks' partials.
+//
+// Grid (kv heads, chunks); the context is cut into chunks of at least
+// ATTN_MINP positions, one per CTA, and clusters of ATTN_CL consecutive
+// chunks of one kv head combine their partial results through distributed
+// shared memory. A CTA walks its chunk in sub-tiles of ATTN_TP positions held
+// in a ring of shared-memory slots, each filled by two bulk copies (the keys
+// and the values of consecutive positions are contiguous); the first slots
+// are filled before the dependency wait, since the cached positions were
+// written by earlier tokens. Scores take one warp per position with the G
+// heads reduced together; an online softmax carries (max, sum, output) across
+// sub-tiles; in P.V each thread owns one head-dimension column and reads each
+// value once for all its heads. Every inner loop has a compile-time trip
+// count (head size HD, sub-tile ATTN_TP; the value rows past the chunk are
+// zero). Each CTA of a cluster then combines one slice of the G x HD outputs
+// over the cluster's CTAs; with one busy cluster per kv head it writes the
+// gated output, otherwise the slice's cluster partial goes to global memory
+// and, per slice, the CTA of that rank in the last cluster to finish it
+// combines the (at most eight) cluster partials.
 //
 // Output gate sigmoid with the fast exponential and divide (within a few
 // ulp of 1 / (1 + exp(-v)); one per output element).
 __device__ __forceinline__ float fast_sigmoid(float v) { return __fdividef(1.f, 1.f + __expf(-v)); }
 
 constexpr int ATTN_THREADS = 256;
-constexpr int ATTN_MINP = 64;  // minimum positions per chunk
+constexpr int ATTN_MINP = 16;  // minimum positions per chunk
 constexpr int ATTN_TP = 16;    // positions per staged sub-tile
-constexpr int ATTN_MAXO = 16;  // output values per thread: G * hd <= ATTN_MAXO * ATTN_THREADS
+constexpr int ATTN_MAXO = 16;  // heads per thread in P.V: G * hd <= ATTN_MAXO * ATTN_THREADS
+constexpr int ATTN_CL = 8;     // CTAs (chunks) per cluster
+constexpr int ATTN_KO = ATTN_MAXO / ATTN_CL;  // combine outputs per thread
+// ring slots: about 64 KiB of keys and values, at least two sub-tiles
+template <int HD>
+constexpr int attn_ring() {
+  return 65536 / (8 * ATTN_TP * HD) < 2 ? 2 : (65536 / (8 * ATTN_TP * HD) > 8 ? 8 : 65536 / (8 * ATTN_TP * HD));
+}
+template <int HD>
+size_t attn_smem_bytes(int G, int rot) {
+  return size_t(G * HD + 2 * HD + attn_ring<HD>() * 2 * ATTN_TP * HD + G * ATTN_TP + rot) * 4;
+}
+
+constexpr int ATTN_JW = ATTN_TP / (ATTN_THREADS / 32);  // positions per warp in the scores
+static_assert(ATTN_JW * 8 <= 32, "the score reduction spreads 8 * ATTN_JW rows over a warp");
+// The E = max(HD / 32, 1) elements of a row that lane l holds in the scores:
+// float4 chunks l + 32u (HD >= 128), a float2 (HD = 64) or one element
+// (elements past HD are zero).
+template <int HD>
+__device__ __forceinline__ void attn_row_ld(const float* row, int lane, float (&v)[HD >= 32 ? HD / 32 : 1]) {
+  constexpr int E = HD >= 32 ? HD / 32 : 1;
+  if constexpr (E % 4 == 0) {
+#pragma unroll
+    for (int u = 0; u < E / 4; ++u) {
+      const float4 t = reinterpret_cast<const float4*>(row)[lane + 32 * u];
+      v[4 * u] = t.x, v[4 * u + 1] = t.y, v[4 * u + 2] = t.z, v[4 * u + 3] = t.w;
+    }
+  } else if constexpr (E == 2) {
+    const float2 t = reinterpret_cast<const float2*>(row)[lane];
+    v[0] = t.x, v[1] = t.y;
+  } else {
+    v[0] = lane < HD ? row[lane] : 0.f;
+  }
+}
 
 template <int HD>
 __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
-  constexpr int E = HD >= 32 ? HD / 32 : 1;  // row elements per lane (l + 32e)
-  constexpr int HQ = HD / 4;                 // float4 per row
+  constexpr int E = HD >= 32 ? HD / 32 : 1;      // row elements per lane (l + 32e)
+  constexpr int RING = attn_ring<HD>();
+  constexpr int SLOT = 2 * ATTN_TP * HD;         // floats per slot: keys, then values
+  constexpr int HSTEP = ATTN_THREADS / HD;       // heads per pass of the block in P.V
   extern __shared__ __align__(16) float sm[];
   const int G = a.H / a.Hkv, kvh = blockIdx.x, chunk = blockIdx.y;
   const int half = a.rot / 2;
-  float* q = sm;                      // [G][HD]
-  float* kn = q + G * HD;             // [HD]
-  float* vn = kn + HD;                // [HD]
-  float* kvb = vn + HD;               // 2 x ([TP][HD] keys, [TP][HD] values)
-  float* sc = kvb + 4 * ATTN_TP * HD; // [G][TP]
-  float* fw = sc + G * ATTN_TP;       // [G][nchunks] combine weights
-  float* cs = fw + G * a.nchunks;     // [half] cos
+  float* q = sm;                      // [G][HD] rotated queries; after the loop this CTA's partial
+  float* kn = q + G * HD;             // [HD] the new key (normalised, rotated)
+  float* vn = kn + HD;                // [HD] the new value
+  float* ring = vn + HD;              // RING x SLOT
+  float* sc = ring + RING * SLOT;     // [G][TP] scores, then weights
+  float* cs = sc + G * ATTN_TP;       // [half] cos
   float* sn = cs + half;              // [half] sin
   __shared__ float hm[64], hl[64], hal[64], hn[72];
-  __shared__ bool last;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+  __shared__ __align__(8) uint64_t full[RING];
+  __shared__ unsigned last_flag;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = ATTN_THREADS / 32;
   const StateDev* sd = a.sd;
   TraceRec trc;
   trc.start(a.trace);
   const int pos = *sd->pos;  // written by the previous token: complete
   const int ctx = pos + 1;
-  const int nvalid = min(a.nchunks, (ctx + ATTN_MINP - 1) / ATTN_MINP);
-  const int per = (ctx + nvalid - 1) / nvalid;
-  const int p0 = chunk * per, p1 = min(ctx, p0 + per), n = chunk < nvalid ? max(0, p1 - p0) : 0;
+  const int per = max(ATTN_MINP, (ctx + a.nchunks - 1) / a.nchunks);
+  const int nvalid = (ctx + per - 1) / per;               // busy chunks (<= nchunks)
+  const int ncl = (nvalid + ATTN_CL - 1) / ATTN_CL;       // busy clusters
+  const int cl = chunk / ATTN_CL;
+  if (cl >= ncl) {  // the whole cluster is idle: no cluster barrier is reached
+    trc.end(a.trace);
+    return;
+  }
+  const unsigned rank = cluster_rank();
+  const int p0 = chunk * per;
+  const int n = chunk < nvalid ? min(ctx, p0 + per) - p0 : 0;
   const int ntiles = (n + ATTN_TP - 1) / ATTN_TP;
-  float* Kc = sd->kc[a.layer] + int64_t(kvh) * sd->max_ctx * HD;
-  float* Vc = sd->vc[a.layer] + int64_t(kvh) * sd->max_ctx * HD;
-  // copies of sub-tile t into buffer t & 1: cached rows asynchronously, the
-  // rows past the chunk's end zeroed (the new position's row is written from
-  // kn / vn once they are ready)
-  auto stage = [&](int t) {
-    float* kt = kvb + (t & 1) * 2 * ATTN_TP * HD;
-    float* vt = kt + ATTN_TP * HD;
+  const float* Kc = sd->kc[a.layer] + int64_t(kvh) * sd->max_ctx * HD;
+  const float* Vc = sd->vc[a.layer] + int64_t(kvh) * sd->max_ctx * HD;
+  uint64_t* fb = full;
+  // sub-tile t into slot t % RING: the cached rows (every row but the new
+  // position, which is always the chunk's last) by two bulk copies
+  auto issue = [=](int t) {
     const int t0 = p0 + t * ATTN_TP, nt = min(ATTN_TP, p0 + n - t0);
-    for (int i = tid; i < ATTN_TP * HQ; i += ATTN_THREADS) {
-      const int j = i / HQ, c = i - j * HQ, p = t0 + j;
-      if (j < nt && p != pos) {
-        cp_async16(kt + j * HD + 4 * c, Kc + int64_t(p) * HD + 4 * c);
-        cp_async16(vt + j * HD + 4 * c, Vc + int64_t(p) * HD + 4 * c);
-      } else if (j >= nt) {
-        reinterpret_cast<float4*>(vt + j * HD)[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
+    const int nc = pos < t0 + nt ? nt - 1 : nt;
+    float* kt = ring + (t % RING) * SLOT;
+    uint64_t* bar = fb + t % RING;
+    const unsigned bytes = unsigned(nc) * HD * 4;
+    mbar_expect_tx(bar, 2 * bytes);
+    if (bytes) {
+      bulk_g2s_keep(kt, Kc + int64_t(t0) * HD, bytes, bar);
+      bulk_g2s_keep(kt + ATTN_TP * HD, Vc + int64_t(t0) * HD, bytes, bar);
     }
-    cp_async_commit();
   };
-  // before the wait: the first sub-tile's cached rows, RoPE table, norm weights
-  if (ntiles > 0) stage(0);
-  for (int j = tid; j < half; j += blockDim.x) {
+  if (tid == 0) {
+    for (int s = 0; s < RING; ++s) mbar_init(&full[s], 1);
+    mbar_init_fence();
+    for (int t = 0; t < min(RING, ntiles); ++t) issue(t);
+  }
+  // before the wait: RoPE table, norm weights, softmax state
+  for (int j = tid; j < half; j += ATTN_THREADS) {
     const float invf = powf(a.rope_theta, -float(2 * j) / float(a.rot));
     const float ang = float(pos) * invf;
     cs[j] = cosf(ang);
     sn[j] = sinf(ang);
   }
-  for (int h = tid; h < G; h += blockDim.x) { hm[h] = -INFINITY; hl[h] = 0.f; }
+  for (int h = tid; h < G; h += ATTN_THREADS) { hm[h] = -INFINITY; hl[h] = 0.f; }
   float wq[E], wk[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) {
@@ -260,50 +311,48 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
     wq[e] = d < HD ? a.qn[d] : 0.f;
     wk[e] = d < HD ? a.kn[d] : 0.f;
   }
+  const int SL = G * HD / ATTN_CL;  // combine slice of this CTA: outputs [rank * SL, (rank + 1) * SL)
+  __syncthreads();  // RoPE table and barrier initialisation visible to all
   pdl_wait();
   trc.waited(a.trace);
-  for (int h = 0; h < G; ++h) copy_async(q + h * HD, a.qout + (kvh * G + h) * 2 * HD, HD);
-  copy_async(kn, a.knew + kvh * HD, HD);
-  copy_async(vn, a.vnew + kvh * HD, HD);
-  cp_async_commit();
-  cp_async_wait_group<0>();
-  __syncthreads();
-  pdl_launch();
-  if (HD >= 32 && half % 32 == 0) {
-    // one warp per head (G q heads and the new k head), in registers: lane l
-    // holds elements l + 32e, so RoPE partners (j, j + half) share a lane
-    const int hs = half >> 5;
+  for (int i = tid; i < HD; i += ATTN_THREADS) vn[i] = __ldcg(a.vnew + kvh * HD + i);
+  // gate values of the combine slice (used if this CTA writes the output)
+  float gate[ATTN_KO];
+#pragma unroll
+  for (int k = 0; k < ATTN_KO; ++k) {
+    const int li = tid + k * ATTN_THREADS, i = int(rank) * SL + li;
+    gate[k] = li < SL ? __ldcg(a.qout + (kvh * G + i / HD) * 2 * HD + HD + i % HD) : 0.f;
+  }
+  if constexpr (HD >= 32) {
+    // one warp per head (G q heads and the new k head): RMSNorm in
+    // registers (lane l holds elements l + 32e), then RoPE in place
     for (int h = warp; h <= G; h += nw) {
-      float* x = h < G ? q + h * HD : kn;
+      const float* src = h < G ? a.qout + (kvh * G + h) * 2 * HD : a.knew + kvh * HD;
       float v[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) v[e] = __ldcg(src + lane + 32 * e);
       float ss = 0.f;
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-        v[e] = x[lane + 32 * e];
-        ss += v[e] * v[e];
-      }
+      for (int e = 0; e < E; ++e) ss += v[e] * v[e];
       ss = warp_sum(ss);
       const float sc0 = 1.f / sqrtf(ss / float(HD) + a.eps);
 #pragma unroll
       for (int e = 0; e < E; ++e) v[e] *= sc0 * (h < G ? wq[e] : wk[e]);
-#pragma unroll
-      for (int e = 0; e < E; ++e)
-        if (e < hs) {
-          const int j = lane + 32 * e;
-          float xb = 0.f;
-#pragma unroll
-          for (int f = 0; f < E; ++f)
-            if (f == e + hs) xb = v[f];
-          const float xa = v[e];
-          v[e] = xa * cs[j] - xb * sn[j];
-#pragma unroll
-          for (int f = 0; f < E; ++f)
-            if (f == e + hs) v[f] = xb * cs[j] + xa * sn[j];
-        }
+      float* x = h < G ? q + h * HD : kn;
 #pragma unroll
       for (int e = 0; e < E; ++e) x[lane + 32 * e] = v[e];
+      __syncwarp();
+      for (int j = lane; j < half; j += 32) {  // RoPE pairs (j, j + half)
+        const float xa = x[j], xb = x[half + j];
+        x[j] = xa * cs[j] - xb * sn[j];
+        x[half + j] = xb * cs[j] + xa * sn[j];
+      }
     }
   } else {
+    for (int h = 0; h < G; ++h) copy_async(q + h * HD, a.qout + (kvh * G + h) * 2 * HD, HD);
+    copy_async(kn, a.knew + kvh * HD, HD);
+    cp_async_wait_all();
+    __syncthreads();
     // RMSNorm of G q heads and the new k head, one warp per head
     for (int h = warp; h <= G; h += nw) {
       float* x = h < G ? q + h * HD : kn;
@@ -313,14 +362,14 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
       if (lane == 0) hn[h] = 1.f / sqrtf(ss / float(HD) + a.eps);
     }
     __syncthreads();
-    for (int i = tid; i < (G + 1) * HD; i += blockDim.x) {
+    for (int i = tid; i < (G + 1) * HD; i += ATTN_THREADS) {
       const int h = i / HD, d = i % HD;
       float* x = h < G ? q + h * HD : kn;
       const float* w = h < G ? a.qn : a.kn;
       x[d] *= hn[h] * w[d];
     }
     __syncthreads();
-    for (int i = tid; i < (G + 1) * half; i += blockDim.x) {
+    for (int i = tid; i < (G + 1) * half; i += ATTN_THREADS) {
       const int h = i / half, j = i % half;
       float* x = h < G ? q + h * HD : kn;
       const float xa = x[j], xb = x[half + j];
@@ -329,56 +378,54 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
     }
   }
   __syncthreads();
+  pdl_launch();
   if (chunk == 0)
-    for (int i = tid; i < HD; i += blockDim.x) {
-      Kc[int64_t(pos) * HD + i] = kn[i];
-      Vc[int64_t(pos) * HD + i] = vn[i];
+    for (int i = tid; i < HD; i += ATTN_THREADS) {
+      const_cast<float*>(Kc)[int64_t(pos) * HD + i] = kn[i];
+      const_cast<float*>(Vc)[int64_t(pos) * HD + i] = vn[i];
     }
   trc.staged(a.trace);
   const float scale = 1.f / sqrtf(float(HD));
-  const int nout = G * HD;
+  const int dcol = tid % HD, hb = tid / HD;
   float acc[ATTN_MAXO];
 #pragma unroll
   for (int o = 0; o < ATTN_MAXO; ++o) acc[o] = 0.f;
+  bool ok = true;
   for (int t = 0; t < ntiles; ++t) {
-    float* kt = kvb + (t & 1) * 2 * ATTN_TP * HD;
+    float* kt = ring + (t % RING) * SLOT;
     float* vt = kt + ATTN_TP * HD;
     const int t0 = p0 + t * ATTN_TP, nt = min(ATTN_TP, p0 + n - t0);
-    if (t + 1 < ntiles) {
-      stage(t + 1);
-      cp_async_wait_group<1>();  // sub-tile t landed, t + 1 may still fly
-    } else {
-      cp_async_wait_group<0>();
-    }
-    if (pos >= t0 && pos < t0 + nt)  // the new position: its normalised, rotated key and its value
-      for (int i = tid; i < HD; i += blockDim.x) {
+    if (!mbar_wait(&full[t % RING], unsigned(t / RING) & 1u)) ok = false;
+    if (pos < t0 + nt)  // the new position (the last row): its key and value
+      for (int i = tid; i < HD; i += ATTN_THREADS) {
         kt[(pos - t0) * HD + i] = kn[i];
         vt[(pos - t0) * HD + i] = vn[i];
       }
+    for (int i = nt * HD + tid; i < ATTN_TP * HD; i += ATTN_THREADS) vt[i] = 0.f;
     __syncthreads();
-    // scores: one warp per position; lane l covers elements l + 32e of the
-    // row, and the head partials are reduced eight heads at a time
-    for (int j = warp; j < ATTN_TP; j += nw) {
-      const bool live = j < nt;
-      float kv[E];
+    // scores: warp w takes positions w and w + 8 for all heads, eight heads
+    // at a time; the 16 partial dot products of a lane are reduced together
+    for (int h0 = 0; h0 < G; h0 += 8) {
+      float qr[8][E];
 #pragma unroll
-      for (int e = 0; e < E; ++e) kv[e] = live && lane + 32 * e < HD ? kt[j * HD + lane + 32 * e] : 0.f;
-      for (int h0 = 0; h0 < G; h0 += 8) {
-        float pr[8];
+      for (int r = 0; r < 8; ++r) attn_row_ld<HD>(q + min(h0 + r, G - 1) * HD, lane, qr[r]);
+      float kv[ATTN_JW][E];
+#pragma unroll
+      for (int jj = 0; jj < ATTN_JW; ++jj) attn_row_ld<HD>(kt + (warp + jj * nw) * HD, lane, kv[jj]);
+      float pr[8 * ATTN_JW];
+#pragma unroll
+      for (int jj = 0; jj < ATTN_JW; ++jj)
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
           float d = 0.f;
 #pragma unroll
-          for (int e = 0; e < E; ++e) {
-            const bool ok = h0 + r < G && lane + 32 * e < HD;
-            d += (ok ? q[(h0 + r) * HD + lane + 32 * e] : 0.f) * kv[e];
-          }
-          pr[r] = d;
+          for (int e = 0; e < E; ++e) d += qr[r][e] * kv[jj][e];
+          pr[jj * 8 + r] = d;
         }
-        int rr;
-        const float d = reduce_rows<8>(pr, 32, lane, rr);
-        if ((lane & 3) == 0 && h0 + rr < G) sc[(h0 + rr) * ATTN_TP + j] = live ? d * scale : -INFINITY;
-      }
+      int rr;
+      const float d = reduce_rows<8 * ATTN_JW>(pr, 32, lane, rr);
+      const int jj = rr >> 3, h = h0 + (rr & 7), j = warp + jj * nw;
+      if ((lane & (32 / (8 * ATTN_JW) - 1)) == 0 && h < G) sc[h * ATTN_TP + j] = j < nt ? d * scale : -INFINITY;
     }
     __syncthreads();
     // online softmax: per head the new max, the rescale of what came before,
@@ -398,121 +445,138 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
       }
     }
     __syncthreads();
+    // P.V: column dcol of heads hb, hb + HSTEP, ...: each value read once
+    {
+      float v[ATTN_TP];
 #pragma unroll
-    for (int o = 0; o < ATTN_MAXO; ++o) {
-      const int i = tid + o * ATTN_THREADS;
-      if (i < nout) {
-        const int h = i / HD, d = i - h * HD;
-        float v = acc[o] * hal[h];
-#pragma unroll
-        for (int j = 0; j < ATTN_TP; ++j) v += sc[h * ATTN_TP + j] * vt[j * HD + d];
-        acc[o] = v;
-      }
-    }
-    __syncthreads();
-  }
-  trc.looped(a.trace);
-  if (nvalid == 1) {  // the whole context in this CTA: finish here
-    if (chunk == 0) {
-      for (int h = tid; h < G; h += blockDim.x) hal[h] = 1.f / hl[h];
-      // every gate value is loaded before the first output is stored (the
-      // stores would otherwise order each following load behind them)
-      float gate[ATTN_MAXO];
+      for (int j = 0; j < ATTN_TP; ++j) v[j] = vt[j * HD + dcol];
 #pragma unroll
       for (int o = 0; o < ATTN_MAXO; ++o) {
-        const int i = tid + o * ATTN_THREADS;
-        const int h = i / HD, d = i - h * HD;
-        gate[o] = i < nout ? __ldcg(a.qout + (kvh * G + h) * 2 * HD + HD + d) : 0.f;
-      }
-      __syncthreads();
+        const int h = hb + o * HSTEP;
+        if (h < G) {
+          const float4* p4 = reinterpret_cast<const float4*>(sc + h * ATTN_TP);
+          float r = acc[o] * hal[h];
 #pragma unroll
-      for (int o = 0; o < ATTN_MAXO; ++o) {
-        const int i = tid + o * ATTN_THREADS;
-        if (i < nout) {
-          const int h = i / HD, d = i - h * HD;
-          a.out[(kvh * G + h) * HD + d] = (acc[o] * hal[h]) * fast_sigmoid(gate[o]);
+          for (int j4 = 0; j4 < ATTN_TP / 4; ++j4) {
+            const float4 p = p4[j4];
+            r += p.x * v[4 * j4] + p.y * v[4 * j4 + 1] + p.z * v[4 * j4 + 2] + p.w * v[4 * j4 + 3];
+          }
+          acc[o] = r;
         }
       }
     }
+    __syncthreads();
+    if (tid == 0 && t + RING < ntiles) {
+      fence_proxy_async();
+      issue(t + RING);
+    }
+  }
+  if (!ok && a.status) atomicOr(a.status, 1);
+  trc.looped(a.trace);
+  // this CTA's partial: unnormalised outputs (against its running max hm)
+  // in the query buffer, max and sum in hm / hl (-inf / 0 for an idle chunk)
+#pragma unroll
+  for (int o = 0; o < ATTN_MAXO; ++o) {
+    const int h = hb + o * HSTEP;
+    if (h < G) q[h * HD + dcol] = acc[o];
+  }
+  cluster_sync();
+  // slice `rank` of the outputs, combined over the cluster's CTAs
+  float res[ATTN_KO], rm[ATTN_KO], rl[ATTN_KO];
+#pragma unroll
+  for (int k = 0; k < ATTN_KO; ++k) {
+    const int li = tid + k * ATTN_THREADS, i = int(rank) * SL + li, h = i / HD;
+    res[k] = 0.f, rm[k] = -INFINITY, rl[k] = 0.f;
+    if (li < SL) {
+      float mc[ATTN_CL], lc[ATTN_CL], ac[ATTN_CL];
+#pragma unroll
+      for (int c = 0; c < ATTN_CL; ++c) {
+        mc[c] = dsmem_ld(dsmem_map(&hm[h], c));
+        lc[c] = dsmem_ld(dsmem_map(&hl[h], c));
+        ac[c] = dsmem_ld(dsmem_map(&q[i], c));
+      }
+      float m = mc[0];
+#pragma unroll
+      for (int c = 1; c < ATTN_CL; ++c) m = fmaxf(m, mc[c]);
+      float l = 0.f, r = 0.f;
+#pragma unroll
+      for (int c = 0; c < ATTN_CL; ++c) {
+        const float f = mc[c] == -INFINITY ? 0.f : expf(mc[c] - m);
+        l += lc[c] * f;
+        r += ac[c] * f;
+      }
+      res[k] = r, rm[k] = m, rl[k] = l;
+    }
+  }
+  // done with the other CTAs' shared memory; the matching wait before the
+  // exit keeps this CTA's alive until every CTA has read it
+  cluster_arrive();
+  if (ncl == 1) {
+#pragma unroll
+    for (int k = 0; k < ATTN_KO; ++k) {
+      const int li = tid + k * ATTN_THREADS;
+      if (li < SL) a.out[kvh * G * HD + int(rank) * SL + li] = (res[k] / rl[k]) * fast_sigmoid(gate[k]);
+    }
+    cluster_wait();
     trc.end(a.trace);
     return;
   }
-  float* part = a.part + (int64_t(kvh) * a.nchunks + chunk) * G * (HD + 2);
+  // several busy clusters: the slice's partial to global memory; the CTA of
+  // this rank in the last cluster to finish combines the slice over them
+  const int NCL = a.nchunks / ATTN_CL;
+  float* pcl = a.part + (int64_t(kvh) * NCL + cl) * G * (HD + 2);
 #pragma unroll
-  for (int o = 0; o < ATTN_MAXO; ++o) {
-    const int i = tid + o * ATTN_THREADS;
-    if (i < nout) {
-      const int h = i / HD, d = i - h * HD;
-      part[h * (HD + 2) + 2 + d] = acc[o];
+  for (int k = 0; k < ATTN_KO; ++k) {
+    const int li = tid + k * ATTN_THREADS, i = int(rank) * SL + li, h = i / HD, d = i % HD;
+    if (li < SL) {
+      pcl[h * (HD + 2) + 2 + d] = res[k];
+      if (d == 0) {
+        pcl[h * (HD + 2)] = rm[k];
+        pcl[h * (HD + 2) + 1] = rl[k];
+      }
     }
   }
-  for (int h = tid; h < G; h += blockDim.x) { part[h * (HD + 2)] = n > 0 ? hm[h] : -INFINITY; part[h * (HD + 2) + 1] = hl[h]; }
   __syncthreads();
   if (tid == 0) {
+    unsigned* ctr = a.counters + kvh * ATTN_CL + rank;
     __threadfence();
-    last = atomicAdd(a.counters + kvh, 1u) == unsigned(a.nchunks) - 1;
+    const bool lst = atomicAdd(ctr, 1u) == unsigned(ncl) - 1;
+    if (lst) {
+      __threadfence();
+      *ctr = 0u;
+    }
+    last_flag = lst ? 1u : 0u;
   }
   __syncthreads();
-  if (!last) {
-    trc.end(a.trace);
-    return;
-  }
-  __threadfence();
-  // combine: per head the chunk weights f_c = exp(m_c - m) first
-  const float* pk = a.part + int64_t(kvh) * a.nchunks * G * (HD + 2);
-  for (int h = warp; h < G; h += nw) {
-    float m = -INFINITY;
-    for (int c = lane; c < nvalid; c += 32) m = fmaxf(m, __ldcg(pk + (int64_t(c) * G + h) * (HD + 2)));
-    m = warp_max(m);
-    float l = 0.f;
-    for (int c = lane; c < nvalid; c += 32) {
-      const float* pc = pk + (int64_t(c) * G + h) * (HD + 2);
-      const float mc = __ldcg(pc);
-      const float f = mc == -INFINITY ? 0.f : expf(mc - m);
-      fw[h * a.nchunks + c] = f;
-      l += __ldcg(pc + 1) * f;
-    }
-    l = warp_sum(l);
-    if (lane == 0) hl[h] = l;
-  }
-  __syncthreads();
-  for (int h = tid; h < G; h += blockDim.x) hal[h] = 1.f / hl[h];
-  // all partial reads (every chunk's values of this thread's outputs in one
-  // batch per chunk) and gate loads first, then the stores
+  if (last_flag) {
+    __threadfence();
 #pragma unroll
-  for (int o = 0; o < ATTN_MAXO; ++o) acc[o] = 0.f;
-  for (int c = 0; c < nvalid; ++c) {
-    const float* pc = pk + int64_t(c) * G * (HD + 2) + 2;
-    float v[ATTN_MAXO];
+    for (int k = 0; k < ATTN_KO; ++k) {
+      const int li = tid + k * ATTN_THREADS, i = int(rank) * SL + li, h = i / HD, d = i % HD;
+      if (li < SL) {
+        float mc[ATTN_CL], lc[ATTN_CL], ac[ATTN_CL];
 #pragma unroll
-    for (int o = 0; o < ATTN_MAXO; ++o) {
-      const int i = tid + o * ATTN_THREADS;
-      const int h = i / HD, d = i - h * HD;
-      v[o] = i < nout ? __ldcg(pc + h * (HD + 2) + d) : 0.f;
-    }
+        for (int c = 0; c < ATTN_CL; ++c) {
+          const float* pc = a.part + ((int64_t(kvh) * NCL + c) * G + h) * (HD + 2);
+          mc[c] = c < ncl ? __ldcg(pc) : -INFINITY;
+          lc[c] = c < ncl ? __ldcg(pc + 1) : 0.f;
+          ac[c] = c < ncl ? __ldcg(pc + 2 + d) : 0.f;
+        }
+        float m = mc[0];
 #pragma unroll
-    for (int o = 0; o < ATTN_MAXO; ++o) {
-      const int i = tid + o * ATTN_THREADS;
-      if (i < nout) acc[o] += v[o] * fw[(i / HD) * a.nchunks + c];
+        for (int c = 1; c < ATTN_CL; ++c) m = fmaxf(m, mc[c]);
+        float l = 0.f, r = 0.f;
+#pragma unroll
+        for (int c = 0; c < ATTN_CL; ++c) {
+          const float f = mc[c] == -INFINITY ? 0.f : expf(mc[c] - m);
+          l += lc[c] * f;
+          r += ac[c] * f;
+        }
+        a.out[kvh * G * HD + i] = (r / l) * fast_sigmoid(gate[k]);
+      }
     }
   }
-  float gate[ATTN_MAXO];
-#pragma unroll
-  for (int o = 0; o < ATTN_MAXO; ++o) {
-    const int i = tid + o * ATTN_THREADS;
-    const int h = i / HD, d = i - h * HD;
-    gate[o] = i < nout ? __ldcg(a.qout + (kvh * G + h) * 2 * HD + HD + d) : 0.f;
-  }
-  __syncthreads();
-#pragma unroll
-  for (int o = 0; o < ATTN_MAXO; ++o) {
-    const int i = tid + o * ATTN_THREADS;
-    if (i < nout) {
-      const int h = i / HD, d = i - h * HD;
-      a.out[(kvh * G + h) * HD + d] = (acc[o] * hal[h]) * fast_sigmoid(gate[o]);
-    }
-  }
-  if (tid == 0) a.counters[kvh] = 0u;
+  cluster_wait();
   trc.end(a.trace);
 }
 
@@ -577,16 +641,16 @@ void launch_delta(const DeltaArgs& a, cudaStream_t st, bool pdl) {
 
 void launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl) {
   const int G = a.H / a.Hkv;
-  if (G > 63 || a.hd > 256 || a.rot > a.hd) throw Error(ERR_UNSUPPORTED, "attention geometry outside the decode kernel's range");
-  if (G * a.hd > ATTN_MAXO * ATTN_THREADS || a.nchunks > 64)
+  if (G > 63 || a.hd > 256 || a.rot > a.hd || a.rot % 2) throw Error(ERR_UNSUPPORTED, "attention geometry outside the decode kernel's range");
+  if (G * a.hd > ATTN_MAXO * ATTN_THREADS || a.nchunks > ATTN_CL * ATTN_CL || a.nchunks % ATTN_CL)
     throw Error(ERR_UNSUPPORTED, "attention shape outside the decode kernel's limits");
-  const size_t smem = size_t(G * a.hd + 2 * a.hd + 4 * ATTN_TP * a.hd + G * ATTN_TP + G * a.nchunks + a.rot) * 4;
+  const dim3 grid(a.Hkv, a.nchunks), block(ATTN_THREADS), cluster(1, ATTN_CL, 1);
   switch (a.hd) {
-    case 16: launch(k_attn<16>, dim3(a.Hkv, a.nchunks), dim3(ATTN_THREADS), smem, st, pdl, a); break;
-    case 32: launch(k_attn<32>, dim3(a.Hkv, a.nchunks), dim3(ATTN_THREADS), smem, st, pdl, a); break;
-    case 64: launch(k_attn<64>, dim3(a.Hkv, a.nchunks), dim3(ATTN_THREADS), smem, st, pdl, a); break;
-    case 128: launch(k_attn<128>, dim3(a.Hkv, a.nchunks), dim3(ATTN_THREADS), smem, st, pdl, a); break;
-    case 256: launch(k_attn<256>, dim3(a.Hkv, a.nchunks), dim3(ATTN_THREADS), smem, st, pdl, a); break;
+    case 16: launch_cluster(k_attn<16>, grid, block, cluster, attn_smem_bytes<16>(G, a.rot), st, pdl, a); break;
+    case 32: launch_cluster(k_attn<32>, grid, block, cluster, attn_smem_bytes<32>(G, a.rot), st, pdl, a); break;
+    case 64: launch_cluster(k_attn<64>, grid, block, cluster, attn_smem_bytes<64>(G, a.rot), st, pdl, a); break;
+    case 128: launch_cluster(k_attn<128>, grid, block, cluster, attn_smem_bytes<128>(G, a.rot), st, pdl, a); break;
+    case 256: launch_cluster(k_attn<256>, grid, block, cluster, attn_smem_bytes<256>(G, a.rot), st, pdl, a); break;
     default: throw Error(ERR_UNSUPPORTED, "attention head size must be 16, 32, 64, 128 or 256");
   }
 }

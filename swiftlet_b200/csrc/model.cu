@@ -486,11 +486,11 @@ void Model::alloc_scratch() {
   amax_i = reinterpret_cast<int*>(dmalloc(1024 * 4));
   greedy = reinterpret_cast<int*>(dmalloc(4));
   ctr_router = reinterpret_cast<unsigned*>(dmalloc(4));
-  ctr_attn = reinterpret_cast<unsigned*>(dmalloc(size_t(KVH) * 4));
+  ctr_attn = reinterpret_cast<unsigned*>(dmalloc(size_t(KVH) * 8 * 4));  // per kv head and combine slice
   ctr_amax = reinterpret_cast<unsigned*>(dmalloc(4));
   cur = reinterpret_cast<StateDev*>(dmalloc(sizeof(StateDev)));
   SWL_CUDA(cudaMemset(ctr_router, 0, 4));
-  SWL_CUDA(cudaMemset(ctr_attn, 0, size_t(KVH) * 4));
+  SWL_CUDA(cudaMemset(ctr_attn, 0, size_t(KVH) * 8 * 4));
   SWL_CUDA(cudaMemset(ctr_amax, 0, 4));
   SWL_CUDA(cudaMemset(err, 0, 4));
   SWL_CUDA(cudaMemset(kstatus, 0, 4));
@@ -627,7 +627,7 @@ void Model::enqueue_layer(int l, cudaStream_t st, bool advance) {
     a.qout = ld.in_y[0]; a.knew = ld.in_y[1]; a.vnew = ld.in_y[2]; a.qn = ld.qn; a.kn = ld.kn;
     a.eps = float(c.eps); a.rope_theta = float(c.rope_theta); a.rot = c.rot_dims();
     a.H = c.heads; a.Hkv = c.kv_heads; a.hd = c.head_dim; a.nchunks = attn_chunks; a.chunk_cap = chunk_cap;
-    a.sd = cur; a.layer = l; a.part = part; a.counters = ctr_attn; a.out = att;
+    a.sd = cur; a.layer = l; a.part = part; a.counters = ctr_attn; a.out = att; a.status = kstatus;
     a.trace = tagged(lt + 3);
     launch_attn(a, st, pdl);
     GemvArgs o;
