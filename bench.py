@@ -31,7 +31,7 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-METRIC = "35B-A3B q4 decode tok/s (B=1)"
+METRIC = "35B-A3B q4 decode tok/s (B=1; B=64 under batched)"
 PROMPT_SEED = 4242
 MODEL_SEED = 35
 
@@ -184,6 +184,87 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def expected_unique_experts(E: int, K: int, B: int) -> float:
+    """Expected distinct experts per layer when B tokens each pick K of E
+    uniformly (the synthetic router's logits are i.i.d.)."""
+    return E * (1.0 - (1.0 - K / E) ** B)
+
+
+def batched_decode(model, cfg, stream, args, rank, local, dist) -> dict:
+    """B sequences, each with its own seeded prompt of args.batch_prompt
+    tokens (run through the batched rounds), then greedy decode with the
+    tokens fed back on the device; e2e through swl_step_batch (H2D tokens,
+    D2H logits of every sequence, host argmax)."""
+    import numpy as np
+    import torch
+    B = args.batch
+    steps, e2e_steps = args.batch_steps, min(args.batch_steps, 8)
+    rng = np.random.default_rng(PROMPT_SEED + 1000 + rank)
+    max_ctx = args.batch_prompt + args.warmup + steps + e2e_steps + 8
+    states = [model.new_state(max_ctx=max_ctx) for _ in range(B)]
+    prompts = rng.integers(0, cfg.vocab_size, (B, args.batch_prompt)).astype(np.int32)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    ev[0].record(stream)
+    logits = model.step_batch(list(prompts), states)
+    ev[1].record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = ev[0].elapsed_time(ev[1])
+    tok = torch.tensor(np.argmax(logits, axis=1).astype(np.int32), device=f"cuda:{local}")
+    for _ in range(args.warmup):
+        model.step_batch_device(states, tok.data_ptr(), 0, tok.data_ptr())
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        ev[2].record(stream)
+        for _ in range(steps):
+            model.step_batch_device(states, tok.data_ptr(), 0, tok.data_ptr())
+        ev[3].record(stream)
+        torch.cuda.synchronize()
+    ms = ev[2].elapsed_time(ev[3])
+    host = tok.cpu().numpy().tolist()
+    ev[4].record(stream)
+    for _ in range(e2e_steps):
+        lg = model.step_batch([[t] for t in host], states)
+        host = np.argmax(lg, axis=1).tolist()
+    ev[5].record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = ev[4].elapsed_time(ev[5])
+    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=f"cuda:{local}")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, e2e_ms = t.tolist()
+    for s in states:
+        s.free()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    bt = algorithmic_bytes_per_token(cfg, args.batch_prompt + args.warmup + steps / 2)
+    L = cfg.num_hidden_layers
+    uniq = expected_unique_experts(cfg.num_experts, cfg.num_experts_per_tok, B)
+    per_seq = bt["delta_state"] + bt["conv_ring"] + bt["kv"] + bt["embed_row"]
+    dense = bt["total"] - bt["experts"] - per_seq
+    step_bytes = dense + L * (uniq + 1) * bt["expert_blob"] + B * per_seq
+    peaks, peak_kind = measured_peaks()
+    hbm = float(peaks["hbm_gbs"])
+    step_s = ms / steps / 1000.0
+    return {
+        "B": B, "value": world * B * steps / (ms / 1000.0), "unit": "tok/s", "steps": steps,
+        "ms_per_step": ms / steps, "prompt": args.batch_prompt,
+        "prefill": {"tokens": B * args.batch_prompt, "ms": prefill_ms,
+                    "tok_s": B * args.batch_prompt / (prefill_ms / 1000.0),
+                    "mode": "batched rounds (token r of every sequence per round)"},
+        "step_roofline": {"bound": "hbm", "bytes_per_step": step_bytes, "achieved": step_bytes / step_s / 1e9,
+                          "peak": hbm, "unit": "GB/s", "frac": step_bytes / step_s / 1e9 / hbm,
+                          "peak_kind": peak_kind,
+                          "bytes": "dense weights once + (expected distinct routed experts %.1f + shared) blobs per "
+                                   "layer + per-sequence delta state r/w, conv ring and f32 KV" % uniq},
+        "e2e": {"value": world * B * e2e_steps / (e2e_ms / 1000.0), "unit": "tok/s",
+                "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B * cfg.vocab_size},
+        "gpu_launches_per_step": 3 + 11 * L + 3,
+        "clocks": clk.summary(),
+    }
+
+
 def run_ours(args) -> None:
     import numpy as np
     import torch
@@ -253,6 +334,12 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     e2e_ms = ev[4].elapsed_time(ev[5])
 
+    # batched decode: args.batch sequences advancing together through the
+    # batched kernels (one weight stream per step for all of them)
+    bres = None
+    if args.batch > 1:
+        bres = batched_decode(model, cfg, stream, args, rank, local, dist)
+
     # roofline of the dominant kernels: the fused expert GEMV pair, swept over all layers
     sweep_iters = 4
     sweep_ms, bytes_layer, sweep_launches = model.bench_expert_sweep(sweep_iters)
@@ -299,6 +386,8 @@ def run_ours(args) -> None:
         "gpu_launches": launches_per_token * args.steps,
         "clocks": clk.summary(),
     }
+    if bres is not None:
+        line["batched"] = bres
     if world == 1 and not args.no_cpu_baseline:
         cb = cpu_decode_sample(mdir, 2, 1)
         line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
@@ -316,6 +405,9 @@ def main() -> None:
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=64, help="sequences of the batched-decode leg (<= 1: skip it)")
+    ap.add_argument("--batch-prompt", type=int, default=128)
+    ap.add_argument("--batch-steps", type=int, default=32)
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling only: same shapes with fewer layers (keeps ncu captures to a few GB)")
     args = ap.parse_args()

@@ -89,9 +89,28 @@ int32_t swl_state_position(const swl_state* state);
 int swl_step(swl_model* model, swl_state* state, const int32_t* tokens, int32_t n, float* logits_out);
 
 /* Batched form: sequence i consumes counts[i] tokens (concatenated in
- * `tokens`); logits_out receives nseq rows of vocab_size floats. */
+ * `tokens`); logits_out receives nseq rows of vocab_size floats (each
+ * sequence's last position). Replaces the per-session loop a caller runs
+ * over InferenceModel.step (TextGenerator.swift:84-94) for several sessions.
+ * With two or more sequences and a model whose formats the batched kernels
+ * take (swl_batch_supported), the sequences advance together: round r runs
+ * the r-th token of every sequence that has one, up to 64 sequences per
+ * launch. A state may appear only once per call. */
 int swl_step_batch(swl_model* model, swl_state** states, const int32_t* tokens, const int32_t* counts, int32_t nseq,
                    float* logits_out);
+
+/* One decode token for each of nseq sequences with device-resident inputs
+ * and outputs: d_tokens [nseq]; d_logits (may be NULL) [nseq][vocab_size];
+ * d_greedy (may be NULL, may equal d_tokens) [nseq] the first argmax of each
+ * row (TextGenerator.swift:90). Work is queued on the model's stream. */
+int swl_step_batch_device(swl_model* model, swl_state** states, int32_t nseq, const int32_t* d_tokens, float* d_logits,
+                          int32_t* d_greedy);
+
+/* 1 when swl_step_batch runs this model's sequences through the batched
+ * kernels (every linear module MLX-affine 4/8-bit with group 32/64/128,
+ * routed and shared experts of one format), 0 when it steps them one by one;
+ * `why` (may be NULL) receives the reason for 0. Negative on error. */
+int swl_batch_supported(swl_model* model, char* why, int32_t why_len);
 
 /* Same as swl_step with device-resident tokens and logits (either logits
  * pointer may be NULL); `greedy_out` (device, may be NULL) receives the

@@ -76,6 +76,8 @@ _SIGNATURES = {
     "swl_step": (_I, [_P, _P, _P, C.c_int32, _P]),
     "swl_step_batch": (_I, [_P, _P, _P, _P, C.c_int32, _P]),
     "swl_step_device": (_I, [_P, _P, _P, C.c_int32, _P, _P]),
+    "swl_step_batch_device": (_I, [_P, _P, C.c_int32, _P, _P, _P]),
+    "swl_batch_supported": (_I, [_P, C.c_char_p, C.c_int32]),
     "swl_pool_stats": (_I, [_P, C.POINTER(swl_pool_info)]),
     "swl_pool_resize": (_I, [_P, _D]),
     "swl_set_stream": (_I, [_P, _P]),
@@ -260,6 +262,20 @@ class QwenCUDAModel:
         out = np.empty((len(states), self.config.vocab_size), np.float32)
         _check(lib().swl_step_batch(self._h, handles, _ptr(flat), _ptr(counts), len(states), _ptr(out)))
         return out
+
+    def step_batch_device(self, states, d_tokens: int, d_logits: int = 0, d_greedy: int = 0) -> None:
+        """One token for each state, device-resident tokens / logits / greedy ids."""
+        handles = (C.c_void_p * len(states))(*[s._bind(self) for s in states])
+        _check(lib().swl_step_batch_device(self._h, handles, len(states), C.c_void_p(d_tokens),
+                                           C.c_void_p(d_logits or None), C.c_void_p(d_greedy or None)))
+
+    def batch_supported(self) -> tuple[bool, str]:
+        """Whether step_batch runs the batched kernels for this model (and why not)."""
+        buf = C.create_string_buffer(256)
+        rc = lib().swl_batch_supported(self._h, buf, 256)
+        if rc < 0:
+            _check(rc)
+        return rc == 1, buf.value.decode()
 
     def step_device(self, d_tokens: int, n: int, state: DecodeState, d_logits: int = 0, d_greedy: int = 0) -> None:
         """Device-pointer form (tokens/logits already in HBM)."""

@@ -125,6 +125,9 @@ struct DeltaArgs {
   int rows_per_block;      // dv rows per block
   float* y;                // [nv*dv] raw recurrence output
   float* z;                // [nv*dv] silu of the gate input, de-interleaved
+  // Batched decode (grid.z = sequences): sequence b reads sd[b], proj +
+  // b * proj_stride and writes y / z + b * nv * dv. 0 for one sequence.
+  int64_t proj_stride = 0;
   Trace trace;
 };
 
@@ -146,18 +149,147 @@ struct AttnArgs {
   unsigned* counters;      // [Hkv][8] per kv head and combine slice
   float* out;              // [H * hd] gated attention output
   int* status = nullptr;   // bit 0: a bounded wait inside the kernel gave up
+  // Batched decode (grid.z = sequences): sequence b reads sd[b] and its
+  // projections at qout / knew / vnew + b * proj_stride, uses its own
+  // partials and counters, and writes out + b * H * hd.
+  int64_t proj_stride = 0;
   Trace trace;
 };
 
 struct EmbedArgs {
   QLin table;
   const int* tokens;
-  const int* cursor;
+  const int* cursor;       // token index; null: row blockIdx.y takes tokens[blockIdx.y] (batched)
   float* h;
   int vocab;
   int* err;
   Trace trace;
 };
+
+// ---------------------------------------------------- batched decode ----
+// Several sequences, one token each, go through every layer together: the
+// dense projections, the router and lm_head run as one weight stream for all
+// of them, and the routed experts as a grouped GEMM over the tokens that
+// picked each expert (QwenCPUModel.swift:500-569 computes the same per token).
+constexpr int BT_MAX = 64;   // sequences per batched step
+constexpr int BG_TOK = 16;   // tokens per GEMM token tile
+constexpr int BG_ROWS = 64;  // weight rows per GEMM item (two halves of 32)
+
+// One MLX-affine matrix in HBM, or a stack of same-shaped experts (expert e
+// at w + e * ew, s + e * es, b + e * eb).
+struct BMat {
+  const uint8_t* w = nullptr;
+  const uint8_t* s = nullptr;
+  const uint8_t* b = nullptr;
+  int64_t wrow = 0;  // bytes per weight row
+  int64_t srow = 0;  // bytes per scale (and bias) row
+  int64_t ew = 0, es = 0, eb = 0;
+  int rows = 0;
+};
+
+// Activation rows -> integer digit tables for k_bgemm: per row, the
+// prologue's output split into three signed base-254 digits per value
+// (B-fragment order of the 4-bit weights) and per quantisation group the
+// reconstruction scale and the sum of the values.
+struct DigitArgs {
+  const float* x = nullptr;
+  int64_t x_stride = 0;        // floats between input rows
+  int rows = 0, in = 0, gs = 0;
+  int prologue = PRO_COPY;     // PRO_COPY, PRO_RMSNORM, PRO_GATEDNORM
+  const float* aux = nullptr;  // RMSNORM: weight [in]; GATEDNORM: silu(z) rows (x_stride apart)
+  const float* aux2 = nullptr; // GATEDNORM: norm weight [head_dim]
+  int head_dim = 0;
+  float eps = 1e-6f;
+  float* x_out = nullptr;      // optional copy of the prepared rows (x_stride apart)
+  uint2* bt = nullptr;         // [rows][bt_row]
+  float2* meta = nullptr;      // [rows][meta_row] (scale, sum) per group
+  int64_t bt_row = 0, meta_row = 0;
+};
+
+enum BMode : int { BM_STORE = 0, BM_RESIDUAL = 1, BM_SWIGLU = 2 };
+
+// Shared-memory layout of k_bgemm (bytes), chosen by the launcher.
+struct BGLayout {
+  int kc = 0;           // input values per pipeline chunk
+  int kcb = 0;          // weight bytes per row per chunk
+  int gpc = 0, kpg = 0; // quantisation groups per chunk, 32-value blocks per group
+  int sw = 0;           // bytes per row of a staged scale (or bias) window
+  int bstride = 0;      // uint2 per token in a staged digit table
+  int w_off = 0, s_off = 0, b_off = 0, x_off = 0, m_off = 0, stage = 0;
+  int o_off = 0;        // epilogue buffer; < 0: reuse the stage just consumed
+  int total = 0;
+};
+
+struct BGemmArgs {
+  int mode = BM_STORE;
+  int in = 0;
+  BGLayout L;
+  // dense launches: up to four segments over one input; item = 64-row block
+  // x token tile, rows of segment s at y[s] + token * y_stride
+  BMat seg[4];
+  float* y[4] = {nullptr, nullptr, nullptr, nullptr};
+  int nseg = 0;
+  int seg_rb[5] = {0, 0, 0, 0, 0};  // cumulative 64-row blocks
+  int64_t y_stride = 0;
+  int ntok = 0;
+  // expert launches: items {expert, first row, first slot, tokens} from
+  // k_broute; expert == experts selects the shared expert
+  int expert_mode = 0;
+  BMat eg, eu;  // routed: gate and up (SWIGLU) or down (STORE)
+  BMat sg, su;  // shared expert: the same roles
+  int experts = 0;
+  const int4* items = nullptr;
+  const int* nitems = nullptr;
+  int max_items = 0;
+  const int* in_map = nullptr;  // input row of slot s (null: s)
+  float* out = nullptr;         // expert outputs, slot-major
+  int64_t out_stride = 0;
+  // digitised inputs (k_digitize)
+  const uint2* xbt = nullptr;
+  const float2* xmeta = nullptr;
+  int64_t bt_row = 0, meta_row = 0;
+};
+
+// Routing and grouping of a batch: per token the softmax top-k of the router
+// logits (QwenCPUModel.swift:506-521), then picks sorted by expert into
+// slots (expert-major, tokens ascending within an expert; the shared expert
+// takes slots T*K + t) and the gate/up and down work items.
+struct BRouteArgs {
+  const float* logits = nullptr;  // [T][E + 1] (router logits, shared-gate logit)
+  int T = 0, E = 0, K = 0, norm_topk = 0;
+  int* ids = nullptr;             // [T][K]
+  float* w = nullptr;             // [T][K] combine weights
+  float* sh = nullptr;            // [T] sigmoid of the shared-gate logit
+  int* slot_of = nullptr;         // [T][K]
+  int* slot_tok = nullptr;        // [T * (K + 1)]
+  int4* items_gu = nullptr;       // gate/up items (32 intermediate rows each)
+  int4* items_dn = nullptr;       // down items (64 hidden rows each)
+  int* nitems = nullptr;          // [2] gate/up, down
+  int inter = 0, shared_inter = 0, hidden = 0;
+  int max_gu = 0, max_dn = 0;
+};
+
+struct BCombineArgs {
+  float* h = nullptr;             // [T][D] residual stream
+  const float* ydown = nullptr;   // [slots][ystride]
+  int64_t ystride = 0;
+  const int* slot_of = nullptr;
+  const float* w = nullptr;
+  const float* sh = nullptr;
+  int T = 0, K = 0, D = 0;
+};
+
+void launch_digitize(const DigitArgs& a, cudaStream_t stream, bool pdl);
+// Fills a.L for the matrices of the launch (all with these bits / scale
+// dtype / group size) and returns whether the shapes are supported.
+bool bgemm_layout(int in, int bits, int dt, int gs, BGLayout& L);
+void launch_bgemm(const BGemmArgs& a, int bits, int dt, int grid, cudaStream_t stream, bool pdl);
+int bgemm_grid(int bits, int dt, const BGLayout& L);
+void launch_broute(const BRouteArgs& a, cudaStream_t stream, bool pdl);
+void launch_bcombine(const BCombineArgs& a, cudaStream_t stream, bool pdl);
+void launch_badvance(const StateDev* sds, int T, cudaStream_t stream, bool pdl);
+void launch_bargmax(const float* logits, int T, int V, int* out, cudaStream_t stream, bool pdl);
+void launch_bembed(const EmbedArgs& a, int hidden, int T, cudaStream_t stream, bool pdl);
 
 // All launches go to `stream`; `pdl` enables programmatic dependent launch.
 void launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl);
@@ -168,7 +300,10 @@ void launch_moe_down(const MoeArgs& a, cudaStream_t stream, bool pdl);
 // which can compute the routing from the router logits (MoeArgs::logits).
 bool moe_routes_from_logits(const MoeArgs& a, int experts);
 void launch_delta(const DeltaArgs& a, cudaStream_t stream, bool pdl);
-void launch_attn(const AttnArgs& a, cudaStream_t stream, bool pdl);
+// The same for T sequences of a batched step (grid.z = T).
+void launch_delta_batch(const DeltaArgs& a, int T, cudaStream_t stream, bool pdl);
+// T > 1: T sequences of a batched step (grid.z = T).
+void launch_attn(const AttnArgs& a, cudaStream_t stream, bool pdl, int T = 1);
 void launch_embed(const EmbedArgs& a, int hidden, cudaStream_t stream, bool pdl);
 // Debug/test helper: dequantise rows [r0, r1) of a module to f32.
 void launch_dequant(const QLin& l, int64_t r0, int64_t r1, float* out, cudaStream_t stream);

@@ -57,7 +57,11 @@ __global__ void __launch_bounds__(DELTA_THREADS) k_delta(const DeltaArgs a) {
   float* cw = taps + nch * (K - 1);  // [nch][K] conv weights
   __shared__ float gb[2], nrm[2];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  const StateDev* sd = a.sd;
+  // sequence blockIdx.z of a batched step (0 for one sequence)
+  const StateDev* sd = a.sd + blockIdx.z;
+  const float* proj = a.proj + blockIdx.z * a.proj_stride;
+  float* yout = a.y + int64_t(blockIdx.z) * a.nv * dv;
+  float* zout = a.z + int64_t(blockIdx.z) * a.nv * dv;
   TraceRec trc;
   trc.start(a.trace);
   // ---- before the wait: everything written by earlier tokens ----
@@ -97,7 +101,7 @@ __global__ void __launch_bounds__(DELTA_THREADS) k_delta(const DeltaArgs a) {
   const bool own_qk = (hv % rep) == 0 && slice == 0;
   for (int t = threadIdx.x; t < nch; t += blockDim.x) {
     const int c = chan(t);
-    const float xn = a.proj[delta_src(a, c)];
+    const float xn = proj[delta_src(a, c)];
     float acc = 0.f;
     for (int j = 0; j < K - 1; ++j) acc += cw[t * K + j] * taps[t * (K - 1) + j];
     acc += cw[t * K + K - 1] * xn;
@@ -108,12 +112,12 @@ __global__ void __launch_bounds__(DELTA_THREADS) k_delta(const DeltaArgs a) {
   if (threadIdx.x == 0) {
     int bi, ai;
     delta_ba(a, hv, bi, ai);
-    gb[0] = expf(-expf(alog) * softplus_ref(a.proj[ai] + dtb));
-    gb[1] = sigmoid_ref(a.proj[bi]);
+    gb[0] = expf(-expf(alog) * softplus_ref(proj[ai] + dtb));
+    gb[1] = sigmoid_ref(proj[bi]);
   }
   for (int i = threadIdx.x; i < RB; i += blockDim.x) {
     const int d = slice * RB + i;
-    a.z[hv * dv + d] = silu_ref(a.proj[delta_z(a, hv, d)]);  // the output gate's activation
+    zout[hv * dv + d] = silu_ref(proj[delta_z(a, hv, d)]);  // the output gate's activation
   }
   __syncthreads();
   pdl_launch();
@@ -167,7 +171,7 @@ __global__ void __launch_bounds__(DELTA_THREADS) k_delta(const DeltaArgs a) {
       const int i = lane + 32 * e;
       if (i < dk) Sr[i] = st[j][e];
     }
-    if (lane == 0) a.y[hv * dv + slice * RB + r] = y[j];
+    if (lane == 0) yout[hv * dv + slice * RB + r] = y[j];
   }
   trc.end(a.trace);
 }
@@ -257,7 +261,16 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
   __shared__ __align__(8) uint64_t full[RING];
   __shared__ unsigned last_flag;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = ATTN_THREADS / 32;
-  const StateDev* sd = a.sd;
+  // sequence blockIdx.z of a batched step (0 for one sequence)
+  const int seq = blockIdx.z;
+  const StateDev* sd = a.sd + seq;
+  const float* qout = a.qout + seq * a.proj_stride;
+  const float* knew = a.knew + seq * a.proj_stride;
+  const float* vnew = a.vnew + seq * a.proj_stride;
+  float* aout = a.out + int64_t(seq) * a.H * HD;
+  const int NCL = a.nchunks / ATTN_CL;
+  float* apart = a.part + int64_t(seq) * a.Hkv * NCL * G * (HD + 2);
+  unsigned* actr = a.counters + seq * a.Hkv * ATTN_CL;
   TraceRec trc;
   trc.start(a.trace);
   const int pos = *sd->pos;  // written by the previous token: complete
@@ -315,19 +328,19 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
   __syncthreads();  // RoPE table and barrier initialisation visible to all
   pdl_wait();
   trc.waited(a.trace);
-  for (int i = tid; i < HD; i += ATTN_THREADS) vn[i] = __ldcg(a.vnew + kvh * HD + i);
+  for (int i = tid; i < HD; i += ATTN_THREADS) vn[i] = __ldcg(vnew + kvh * HD + i);
   // gate values of the combine slice (used if this CTA writes the output)
   float gate[ATTN_KO];
 #pragma unroll
   for (int k = 0; k < ATTN_KO; ++k) {
     const int li = tid + k * ATTN_THREADS, i = int(rank) * SL + li;
-    gate[k] = li < SL ? __ldcg(a.qout + (kvh * G + i / HD) * 2 * HD + HD + i % HD) : 0.f;
+    gate[k] = li < SL ? __ldcg(qout + (kvh * G + i / HD) * 2 * HD + HD + i % HD) : 0.f;
   }
   if constexpr (HD >= 32) {
     // one warp per head (G q heads and the new k head): RMSNorm in
     // registers (lane l holds elements l + 32e), then RoPE in place
     for (int h = warp; h <= G; h += nw) {
-      const float* src = h < G ? a.qout + (kvh * G + h) * 2 * HD : a.knew + kvh * HD;
+      const float* src = h < G ? qout + (kvh * G + h) * 2 * HD : knew + kvh * HD;
       float v[E];
 #pragma unroll
       for (int e = 0; e < E; ++e) v[e] = __ldcg(src + lane + 32 * e);
@@ -349,8 +362,8 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
       }
     }
   } else {
-    for (int h = 0; h < G; ++h) copy_async(q + h * HD, a.qout + (kvh * G + h) * 2 * HD, HD);
-    copy_async(kn, a.knew + kvh * HD, HD);
+    for (int h = 0; h < G; ++h) copy_async(q + h * HD, qout + (kvh * G + h) * 2 * HD, HD);
+    copy_async(kn, knew + kvh * HD, HD);
     cp_async_wait_all();
     __syncthreads();
     // RMSNorm of G q heads and the new k head, one warp per head
@@ -515,7 +528,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
 #pragma unroll
     for (int k = 0; k < ATTN_KO; ++k) {
       const int li = tid + k * ATTN_THREADS;
-      if (li < SL) a.out[kvh * G * HD + int(rank) * SL + li] = (res[k] / rl[k]) * fast_sigmoid(gate[k]);
+      if (li < SL) aout[kvh * G * HD + int(rank) * SL + li] = (res[k] / rl[k]) * fast_sigmoid(gate[k]);
     }
     cluster_wait();
     trc.end(a.trace);
@@ -523,8 +536,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
   }
   // several busy clusters: the slice's partial to global memory; the CTA of
   // this rank in the last cluster to finish combines the slice over them
-  const int NCL = a.nchunks / ATTN_CL;
-  float* pcl = a.part + (int64_t(kvh) * NCL + cl) * G * (HD + 2);
+  float* pcl = apart + (int64_t(kvh) * NCL + cl) * G * (HD + 2);
 #pragma unroll
   for (int k = 0; k < ATTN_KO; ++k) {
     const int li = tid + k * ATTN_THREADS, i = int(rank) * SL + li, h = i / HD, d = i % HD;
@@ -538,7 +550,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
   }
   __syncthreads();
   if (tid == 0) {
-    unsigned* ctr = a.counters + kvh * ATTN_CL + rank;
+    unsigned* ctr = actr + kvh * ATTN_CL + rank;
     __threadfence();
     const bool lst = atomicAdd(ctr, 1u) == unsigned(ncl) - 1;
     if (lst) {
@@ -557,7 +569,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
         float mc[ATTN_CL], lc[ATTN_CL], ac[ATTN_CL];
 #pragma unroll
         for (int c = 0; c < ATTN_CL; ++c) {
-          const float* pc = a.part + ((int64_t(kvh) * NCL + c) * G + h) * (HD + 2);
+          const float* pc = apart + ((int64_t(kvh) * NCL + c) * G + h) * (HD + 2);
           mc[c] = c < ncl ? __ldcg(pc) : -INFINITY;
           lc[c] = c < ncl ? __ldcg(pc + 1) : 0.f;
           ac[c] = c < ncl ? __ldcg(pc + 2 + d) : 0.f;
@@ -572,7 +584,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
           l += lc[c] * f;
           r += ac[c] * f;
         }
-        a.out[kvh * G * HD + i] = (r / l) * fast_sigmoid(gate[k]);
+        aout[kvh * G * HD + i] = (r / l) * fast_sigmoid(gate[k]);
       }
     }
   }
@@ -586,12 +598,13 @@ __global__ void k_embed(const EmbedArgs a, int D) {
   trc.start(a.trace);
   pdl_wait();
   trc.waited(a.trace);
-  const int tok = a.tokens[*a.cursor];
+  const int tok = a.cursor ? a.tokens[*a.cursor] : a.tokens[blockIdx.y];
   pdl_launch();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  float* h = a.h + int64_t(blockIdx.y) * D;
   if (tok < 0 || tok >= a.vocab) {
     if (i == 0) *a.err = 1;
-    if (i < D) a.h[i] = 0.f;
+    if (i < D) h[i] = 0.f;
     trc.end(a.trace);
     return;
   }
@@ -608,7 +621,7 @@ __global__ void k_embed(const EmbedArgs a, int D) {
   } else {
     v = load_scalar(L.w, L.dt, int64_t(tok) * D + i);
   }
-  a.h[i] = v;
+  h[i] = v;
 }
 
 // Dequantised rows (bit-exact w = fl(fl(scale * q) + bias), two roundings).
@@ -639,12 +652,20 @@ void launch_delta(const DeltaArgs& a, cudaStream_t st, bool pdl) {
   launch(k_delta, dim3(a.nv, a.dv / a.rows_per_block), dim3(DELTA_THREADS), smem, st, pdl, a);
 }
 
-void launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl) {
+void launch_delta_batch(const DeltaArgs& a, int T, cudaStream_t st, bool pdl) {
+  if (a.dk > 32 * DELTA_EPL || a.rows_per_block > DELTA_RPW * (DELTA_THREADS / 32) || a.dv % a.rows_per_block)
+    throw Error(ERR_UNSUPPORTED, "DeltaNet head dims outside the decode kernel's range");
+  const int nch = 2 * a.dk + a.rows_per_block;
+  const size_t smem = size_t(2 * a.dk + a.rows_per_block + nch * (2 * a.conv_k - 1)) * 4;
+  launch(k_delta, dim3(a.nv, a.dv / a.rows_per_block, T), dim3(DELTA_THREADS), smem, st, pdl, a);
+}
+
+void launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl, int T) {
   const int G = a.H / a.Hkv;
   if (G > 63 || a.hd > 256 || a.rot > a.hd || a.rot % 2) throw Error(ERR_UNSUPPORTED, "attention geometry outside the decode kernel's range");
   if (G * a.hd > ATTN_MAXO * ATTN_THREADS || a.nchunks > ATTN_CL * ATTN_CL || a.nchunks % ATTN_CL)
     throw Error(ERR_UNSUPPORTED, "attention shape outside the decode kernel's limits");
-  const dim3 grid(a.Hkv, a.nchunks), block(ATTN_THREADS), cluster(1, ATTN_CL, 1);
+  const dim3 grid(a.Hkv, a.nchunks, T), block(ATTN_THREADS), cluster(1, ATTN_CL, 1);
   switch (a.hd) {
     case 16: launch_cluster(k_attn<16>, grid, block, cluster, attn_smem_bytes<16>(G, a.rot), st, pdl, a); break;
     case 32: launch_cluster(k_attn<32>, grid, block, cluster, attn_smem_bytes<32>(G, a.rot), st, pdl, a); break;
@@ -657,6 +678,12 @@ void launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl) {
 
 void launch_embed(const EmbedArgs& a, int hidden, cudaStream_t st, bool pdl) {
   launch(k_embed, dim3((hidden + 255) / 256), dim3(256), 0, st, pdl, a, hidden);
+}
+
+void launch_bembed(const EmbedArgs& a, int hidden, int T, cudaStream_t st, bool pdl) {
+  EmbedArgs b = a;
+  b.cursor = nullptr;
+  launch(k_embed, dim3((hidden + 255) / 256, T), dim3(256), 0, st, pdl, b, hidden);
 }
 
 void launch_dequant(const QLin& l, int64_t r0, int64_t r1, float* out, cudaStream_t st) {

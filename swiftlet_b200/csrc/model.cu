@@ -76,6 +76,25 @@ struct State {
   float** ptr_arrays = nullptr;
   std::vector<float*> conv, dstate, kc, vc;
   int* d_pos = nullptr;
+  StateDev host_desc{};  // the descriptor copied to `desc` (batched steps gather these)
+};
+
+// Device buffers of the batched decode path (BT_MAX sequences, one token
+// each), allocated on the first batched step.
+struct BatchBufs {
+  bool ready = false;
+  float *h = nullptr, *proj = nullptr, *yv = nullptr, *zv = nullptr, *att = nullptr, *xmoe = nullptr;
+  float *rlog = nullptr, *w = nullptr, *sh = nullptr, *hmid = nullptr, *ydown = nullptr, *logits = nullptr;
+  float* part = nullptr;
+  unsigned* ctr = nullptr;
+  int *ids = nullptr, *slot_of = nullptr, *slot_tok = nullptr, *nitems = nullptr, *tokens = nullptr, *greedy = nullptr;
+  int4 *items_gu = nullptr, *items_dn = nullptr;
+  int max_gu = 0, max_dn = 0;
+  uint2 *bt_a = nullptr, *bt_b = nullptr;
+  float2 *meta_a = nullptr, *meta_b = nullptr;
+  StateDev* sds = nullptr;
+  int64_t projn = 0, hmid_stride = 0;
+  std::map<int, cudaGraphExec_t> graphs;  // per batch size
 };
 
 struct Model {
@@ -125,6 +144,9 @@ struct Model {
   int* h_tokens = nullptr;
   int h_tokens_cap = 0;
   std::vector<State*> live;  // states created on this model and not yet freed
+  BatchBufs bb;              // batched decode
+  int batch_ok = -1;         // -1 unchecked; 1 every module fits the batched kernels
+  std::string batch_why;     // why not
   Trace trace;               // SWL_TRACE=<records>: per-block kernel timeline
   Trace tagged(unsigned tag) const { Trace t = trace; t.tag = tag; return t; }
 
@@ -155,6 +177,14 @@ struct Model {
   void ensure_graphs();
   void ensure_tokens(int n);
   void run(State* s, int n, bool amax);
+  // batched decode: T sequences, one token each (tokens already in bb.tokens,
+  // descriptors in bb.sds); logits [T][vocab] in bb.logits, greedy in bb.greedy
+  bool batch_supported();
+  void ensure_batch();
+  void enqueue_batch(int T, cudaStream_t st);
+  void run_batch(State* const* s, int T);
+  void bdense(const std::vector<std::pair<QLin, float*>>& segs, int64_t y_stride, int mode, const uint2* bt,
+              const float2* meta, int T, cudaStream_t st);
   // Throws when a kernel of the last steps reported a bounded wait that gave
   // up (its results are then unreliable); clears the word for the next step.
   void check_status(const int* host_word) {
@@ -185,6 +215,8 @@ void Model::drop_graphs() {
   if (g_head) cudaGraphExecDestroy(g_head);
   if (g_head_amax) cudaGraphExecDestroy(g_head_amax);
   g_body = g_head = g_head_amax = nullptr;
+  for (auto& kv : bb.graphs) cudaGraphExecDestroy(kv.second);
+  bb.graphs.clear();
 }
 
 // Quantised or plain linear module `path` with logical shape [out, in]
@@ -719,6 +751,231 @@ void Model::run(State* s, int n, bool amax) {
   hits += int64_t(n) * cfg.topk * cfg.layers;
 }
 
+// ------------------------------------------------------- batched decode --
+static BMat bmat(const QLin& q) {
+  BMat m;
+  m.w = q.w; m.s = q.s; m.b = q.b;
+  m.wrow = q.row_bytes;
+  m.srow = q.srow * dtype_bytes(q.dt);
+  m.rows = q.out;
+  return m;
+}
+static BMat bmat(const ExpertProj& e) {
+  BMat m = bmat(e.lin);
+  m.ew = e.wstride; m.es = e.sstride; m.eb = e.bstride;
+  return m;
+}
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Whether every projection of the model fits the batched kernels: quantised
+// 4/8-bit weights with 16-byte aligned rows, one group size per digitised
+// input, routed and shared experts of one format and intermediate size.
+bool Model::batch_supported() {
+  if (batch_ok >= 0) return batch_ok == 1;
+  const ModelConfig& c = cfg;
+  auto no = [&](const std::string& why) { batch_why = why; batch_ok = 0; return false; };
+  auto fits = [&](const QLin& q, int gs, int in) {
+    BGLayout L;
+    return q.bits && q.gs == gs && q.in == in && bgemm_layout(q.in, q.bits, q.dt, q.gs, L) && aligned16(q.w) &&
+           q.row_bytes % 16 == 0;
+  };
+  auto same_fmt = [](const QLin& a, const QLin& b) { return a.bits == b.bits && a.dt == b.dt && a.gs == b.gs; };
+  if (c.experts > 512 || c.topk > 32 || c.moe_inter != c.shared_inter) return no("expert geometry outside the batched kernels");
+  if (c.hidden > 16384 || c.value_dim() > 16384 || c.heads * c.head_dim > 16384 || c.moe_inter > 16384)
+    return no("dimensions above the batched kernels' limits");
+  for (int l = 0; l < c.layers; ++l) {
+    const LayerDev& ld = L[l];
+    const int gs_in = ld.in_lin[0].gs;
+    for (int i = 0; i < ld.n_in; ++i)
+      if (!fits(ld.in_lin[i], gs_in, c.hidden)) return no("layer " + std::to_string(l) + " in-projection format");
+    if (!fits(ld.out_lin, ld.out_lin.gs, ld.out_lin.in)) return no("layer " + std::to_string(l) + " out-projection format");
+    const int gs_r = ld.router.gs;
+    if (!fits(ld.router, gs_r, c.hidden) || !fits(ld.sgate, gs_r, c.hidden) || !fits(ld.sh_g, gs_r, c.hidden) ||
+        !fits(ld.sh_u, gs_r, c.hidden) || !fits(ld.eg.lin, gs_r, c.hidden) || !fits(ld.eu.lin, gs_r, c.hidden))
+      return no("layer " + std::to_string(l) + " router / expert input format");
+    if (!same_fmt(ld.eg.lin, ld.eu.lin) || !same_fmt(ld.eg.lin, ld.sh_g) || !same_fmt(ld.eg.lin, ld.sh_u))
+      return no("layer " + std::to_string(l) + " gate/up formats differ");
+    if (!fits(ld.ed.lin, ld.ed.lin.gs, c.moe_inter) || !fits(ld.sh_d, ld.ed.lin.gs, c.shared_inter) ||
+        !same_fmt(ld.ed.lin, ld.sh_d))
+      return no("layer " + std::to_string(l) + " down-projection format");
+    for (const ExpertProj* e : {&ld.eg, &ld.eu, &ld.ed})
+      if (e->wstride % 16) return no("expert stride not 16-byte aligned");
+  }
+  if (!fits(lm_head, lm_head.gs, c.hidden)) return no("lm_head format");
+  batch_ok = 1;
+  return true;
+}
+
+void Model::ensure_batch() {
+  if (bb.ready) return;
+  const ModelConfig& c = cfg;
+  const int T = BT_MAX, K = c.topk, D = c.hidden, H = c.heads, KVH = c.kv_heads, hd = c.head_dim, G = H / KVH;
+  const int slots = T * (K + 1);
+  bb.projn = int64_t(std::max<size_t>({size_t(c.conv_dim() + c.value_dim() + 2 * c.nv),
+                                       size_t(2 * c.key_dim() + 2 * c.value_dim() + 2 * c.nv),
+                                       size_t(2 * H * hd + 2 * KVH * hd)}));
+  bb.projn = (bb.projn + 3) & ~int64_t(3);
+  bb.hmid_stride = (std::max(c.moe_inter, c.shared_inter) + 3) & ~3;
+  const int max_in = std::max({D, c.value_dim(), H * hd});
+  auto f = [&](size_t n) { return reinterpret_cast<float*>(dmalloc(std::max<size_t>(n, 1) * 4)); };
+  auto i4 = [&](size_t n) { return reinterpret_cast<int*>(dmalloc(std::max<size_t>(n, 1) * 4)); };
+  bb.h = f(size_t(T) * D); bb.proj = f(size_t(T) * bb.projn);
+  bb.yv = f(size_t(T) * c.value_dim()); bb.zv = f(size_t(T) * c.value_dim());
+  bb.att = f(size_t(T) * H * hd); bb.xmoe = f(size_t(T) * D);
+  bb.rlog = f(size_t(T) * (c.experts + 1)); bb.w = f(size_t(T) * K); bb.sh = f(T);
+  bb.hmid = f(size_t(slots) * bb.hmid_stride); bb.ydown = f(size_t(slots) * D);
+  bb.logits = f(size_t(T) * c.vocab);
+  bb.part = f(size_t(T) * KVH * (attn_chunks / 8) * G * (hd + 2));
+  bb.ctr = reinterpret_cast<unsigned*>(i4(size_t(T) * KVH * 8));
+  SWL_CUDA(cudaMemset(bb.ctr, 0, size_t(T) * KVH * 8 * 4));
+  bb.ids = i4(size_t(T) * K); bb.slot_of = i4(size_t(T) * K); bb.slot_tok = i4(slots);
+  bb.nitems = i4(2); bb.tokens = i4(T); bb.greedy = i4(T);
+  const int tiles = std::min(c.experts, T * K) + (T * K) / BG_TOK + 1 + (T + BG_TOK - 1) / BG_TOK;
+  bb.max_gu = tiles * ((c.moe_inter + 31) / 32);
+  bb.max_dn = tiles * ((D + 63) / 64);
+  bb.items_gu = reinterpret_cast<int4*>(dmalloc(size_t(bb.max_gu) * sizeof(int4)));
+  bb.items_dn = reinterpret_cast<int4*>(dmalloc(size_t(bb.max_dn) * sizeof(int4)));
+  bb.bt_a = reinterpret_cast<uint2*>(dmalloc(size_t(T) * (max_in / 32) * 12 * sizeof(uint2)));
+  bb.meta_a = reinterpret_cast<float2*>(dmalloc(size_t(T) * (max_in / 32) * sizeof(float2)));
+  bb.bt_b = reinterpret_cast<uint2*>(dmalloc(size_t(slots) * (c.moe_inter / 32 + 1) * 12 * sizeof(uint2)));
+  bb.meta_b = reinterpret_cast<float2*>(dmalloc(size_t(slots) * (c.moe_inter / 32 + 1) * sizeof(float2)));
+  bb.sds = reinterpret_cast<StateDev*>(dmalloc(size_t(T) * sizeof(StateDev)));
+  bb.ready = true;
+}
+
+// Segments over one digitised input, launched in groups of one weight format.
+void Model::bdense(const std::vector<std::pair<QLin, float*>>& segs, int64_t y_stride, int mode, const uint2* bt,
+                   const float2* meta, int T, cudaStream_t st) {
+  size_t i = 0;
+  while (i < segs.size()) {
+    const QLin& q0 = segs[i].first;
+    BGemmArgs a;
+    a.mode = mode;
+    a.in = q0.in;
+    if (!bgemm_layout(q0.in, q0.bits, q0.dt, q0.gs, a.L)) throw Error(ERR_UNSUPPORTED, "batched GEMM layout");
+    a.nseg = 0;
+    a.seg_rb[0] = 0;
+    while (i < segs.size() && a.nseg < 4 && segs[i].first.bits == q0.bits && segs[i].first.dt == q0.dt) {
+      a.seg[a.nseg] = bmat(segs[i].first);
+      a.y[a.nseg] = segs[i].second;
+      a.seg_rb[a.nseg + 1] = a.seg_rb[a.nseg] + (segs[i].first.out + BG_ROWS - 1) / BG_ROWS;
+      ++a.nseg;
+      ++i;
+    }
+    a.y_stride = y_stride;
+    a.ntok = T;
+    a.xbt = bt;
+    a.xmeta = meta;
+    a.bt_row = q0.in / 32 * 12;
+    a.meta_row = q0.in / q0.gs;
+    const int items = a.seg_rb[a.nseg] * ((T + BG_TOK - 1) / BG_TOK);
+    launch_bgemm(a, q0.bits, q0.dt, std::min(bgemm_grid(q0.bits, q0.dt, a.L), items), st, use_pdl);
+  }
+}
+
+void Model::enqueue_batch(int T, cudaStream_t st) {
+  const ModelConfig& c = cfg;
+  const int D = c.hidden, K = c.topk, E = c.experts, H = c.heads, hd = c.head_dim;
+  const int slots = T * (K + 1);
+  const bool pdl = use_pdl;
+  EmbedArgs e;
+  e.table = embed; e.tokens = bb.tokens; e.cursor = nullptr; e.h = bb.h; e.vocab = c.vocab; e.err = err;
+  e.trace = tagged(1);
+  launch_bembed(e, D, T, st, pdl);
+  auto digit = [&](const float* x, int64_t xs, int rows, int in, int gs, int pro, const float* aux, const float* aux2,
+                   int head_dim, float* x_out, uint2* bt, float2* meta) {
+    DigitArgs d;
+    d.x = x; d.x_stride = xs; d.rows = rows; d.in = in; d.gs = gs; d.prologue = pro;
+    d.aux = aux; d.aux2 = aux2; d.head_dim = head_dim; d.eps = float(c.eps); d.x_out = x_out;
+    d.bt = bt; d.meta = meta; d.bt_row = in / 32 * 12; d.meta_row = in / gs;
+    launch_digitize(d, st, pdl);
+  };
+  for (int l = 0; l < c.layers; ++l) {
+    const LayerDev& ld = L[l];
+    digit(bb.h, D, T, D, ld.in_lin[0].gs, PRO_RMSNORM, ld.in_norm, nullptr, 0, nullptr, bb.bt_a, bb.meta_a);
+    std::vector<std::pair<QLin, float*>> segs;
+    for (int s = 0; s < ld.n_in; ++s) segs.push_back({ld.in_lin[s], bb.proj + (ld.in_y[s] - proj)});
+    bdense(segs, bb.projn, BM_STORE, bb.bt_a, bb.meta_a, T, st);
+    if (ld.delta) {
+      DeltaArgs d;
+      d.proj = bb.proj; d.proj_stride = bb.projn; d.split = c.split_layout; d.nk = c.nk; d.nv = c.nv; d.dk = c.dk;
+      d.dv = c.dv; d.conv_k = c.conv_k; d.conv_dim = c.conv_dim(); d.conv_w = ld.conv_w; d.a_log = ld.a_log;
+      d.dt_bias = ld.dt_bias; d.sd = bb.sds; d.layer = l; d.rows_per_block = std::min(c.dv, 32); d.y = bb.yv;
+      d.z = bb.zv;
+      d.trace = tagged(16u * unsigned(l + 1) + 3);
+      launch_delta_batch(d, T, st, pdl);
+      digit(bb.yv, c.value_dim(), T, c.value_dim(), ld.out_lin.gs, PRO_GATEDNORM, bb.zv, ld.dnorm, c.dv, nullptr,
+            bb.bt_a, bb.meta_a);
+    } else {
+      AttnArgs a;
+      a.qout = bb.proj + (ld.in_y[0] - proj); a.knew = bb.proj + (ld.in_y[1] - proj);
+      a.vnew = bb.proj + (ld.in_y[2] - proj); a.proj_stride = bb.projn; a.qn = ld.qn; a.kn = ld.kn;
+      a.eps = float(c.eps); a.rope_theta = float(c.rope_theta); a.rot = c.rot_dims();
+      a.H = H; a.Hkv = c.kv_heads; a.hd = hd; a.nchunks = attn_chunks; a.chunk_cap = chunk_cap;
+      a.sd = bb.sds; a.layer = l; a.part = bb.part; a.counters = bb.ctr; a.out = bb.att; a.status = kstatus;
+      a.trace = tagged(16u * unsigned(l + 1) + 3);
+      launch_attn(a, st, pdl, T);
+      digit(bb.att, int64_t(H) * hd, T, H * hd, ld.out_lin.gs, PRO_COPY, nullptr, nullptr, 0, nullptr, bb.bt_a,
+            bb.meta_a);
+    }
+    bdense({{ld.out_lin, bb.h}}, D, BM_RESIDUAL, bb.bt_a, bb.meta_a, T, st);
+    const int gs_r = ld.router.gs;
+    digit(bb.h, D, T, D, gs_r, PRO_RMSNORM, ld.post_norm, nullptr, 0, bb.xmoe, bb.bt_a, bb.meta_a);
+    bdense({{ld.router, bb.rlog}, {ld.sgate, bb.rlog + E}}, E + 1, BM_STORE, bb.bt_a, bb.meta_a, T, st);
+    BRouteArgs r;
+    r.logits = bb.rlog; r.T = T; r.E = E; r.K = K; r.norm_topk = c.norm_topk;
+    r.ids = bb.ids; r.w = bb.w; r.sh = bb.sh; r.slot_of = bb.slot_of; r.slot_tok = bb.slot_tok;
+    r.items_gu = bb.items_gu; r.items_dn = bb.items_dn; r.nitems = bb.nitems;
+    r.inter = c.moe_inter; r.shared_inter = c.shared_inter; r.hidden = D; r.max_gu = bb.max_gu; r.max_dn = bb.max_dn;
+    launch_broute(r, st, pdl);
+    BGemmArgs gu;
+    gu.mode = BM_SWIGLU; gu.in = D;
+    if (!bgemm_layout(D, ld.eg.lin.bits, ld.eg.lin.dt, gs_r, gu.L)) throw Error(ERR_UNSUPPORTED, "batched gate/up layout");
+    gu.expert_mode = 1; gu.eg = bmat(ld.eg); gu.eu = bmat(ld.eu); gu.sg = bmat(ld.sh_g); gu.su = bmat(ld.sh_u);
+    gu.experts = E; gu.items = bb.items_gu; gu.nitems = bb.nitems; gu.max_items = bb.max_gu; gu.in_map = bb.slot_tok;
+    gu.out = bb.hmid; gu.out_stride = bb.hmid_stride;
+    gu.xbt = bb.bt_a; gu.xmeta = bb.meta_a; gu.bt_row = D / 32 * 12; gu.meta_row = D / gs_r;
+    launch_bgemm(gu, ld.eg.lin.bits, ld.eg.lin.dt, bgemm_grid(ld.eg.lin.bits, ld.eg.lin.dt, gu.L), st, pdl);
+    const int gs_d = ld.ed.lin.gs, I = c.moe_inter;
+    digit(bb.hmid, bb.hmid_stride, slots, I, gs_d, PRO_COPY, nullptr, nullptr, 0, nullptr, bb.bt_b, bb.meta_b);
+    BGemmArgs dn;
+    dn.mode = BM_STORE; dn.in = I;
+    if (!bgemm_layout(I, ld.ed.lin.bits, ld.ed.lin.dt, gs_d, dn.L)) throw Error(ERR_UNSUPPORTED, "batched down layout");
+    dn.expert_mode = 1; dn.eg = bmat(ld.ed); dn.sg = bmat(ld.sh_d);
+    dn.experts = E; dn.items = bb.items_dn; dn.nitems = bb.nitems + 1; dn.max_items = bb.max_dn; dn.in_map = nullptr;
+    dn.out = bb.ydown; dn.out_stride = D;
+    dn.xbt = bb.bt_b; dn.xmeta = bb.meta_b; dn.bt_row = I / 32 * 12; dn.meta_row = I / gs_d;
+    launch_bgemm(dn, ld.ed.lin.bits, ld.ed.lin.dt, bgemm_grid(ld.ed.lin.bits, ld.ed.lin.dt, dn.L), st, pdl);
+    BCombineArgs cb;
+    cb.h = bb.h; cb.ydown = bb.ydown; cb.ystride = D; cb.slot_of = bb.slot_of; cb.w = bb.w; cb.sh = bb.sh;
+    cb.T = T; cb.K = K; cb.D = D;
+    launch_bcombine(cb, st, pdl);
+  }
+  launch_badvance(bb.sds, T, st, pdl);
+  digit(bb.h, D, T, D, lm_head.gs, PRO_RMSNORM, final_norm, nullptr, 0, nullptr, bb.bt_a, bb.meta_a);
+  bdense({{lm_head, bb.logits}}, c.vocab, BM_STORE, bb.bt_a, bb.meta_a, T, st);
+  launch_bargmax(bb.logits, T, c.vocab, bb.greedy, st, pdl);
+}
+
+// T sequences with their tokens already in bb.tokens.
+void Model::run_batch(State* const* s, int T) {
+  if (T < 1 || T > BT_MAX) throw Error(ERR_INVALID, "batched step of 1.." + std::to_string(BT_MAX) + " sequences");
+  ensure_batch();
+  std::vector<StateDev> sd(T);
+  for (int t = 0; t < T; ++t) sd[t] = s[t]->host_desc;
+  SWL_CUDA(cudaMemcpyAsync(bb.sds, sd.data(), size_t(T) * sizeof(StateDev), cudaMemcpyHostToDevice, stream));
+  if (use_graph) {
+    auto it = bb.graphs.find(T);
+    if (it == bb.graphs.end()) it = bb.graphs.emplace(T, capture(stream, [&] { enqueue_batch(T, stream); })).first;
+    SWL_CUDA(cudaGraphLaunch(it->second, stream));
+  } else {
+    enqueue_batch(T, stream);
+  }
+  for (int t = 0; t < T; ++t) s[t]->pos += 1;
+  stepped = true;
+  hits += int64_t(T) * cfg.topk * cfg.layers;
+}
+
 static State* new_state(Model* m, int max_ctx) {
   if (max_ctx < 1) throw Error(ERR_INVALID, "max_ctx must be positive");
   if (max_ctx > m->max_ctx_cap)
@@ -760,6 +1017,7 @@ static State* new_state(Model* m, int max_ctx) {
   StateDev sd;
   sd.pos = s->d_pos; sd.conv = arrays; sd.dstate = arrays + c.layers; sd.kc = arrays + 2 * c.layers; sd.vc = arrays + 3 * c.layers;
   sd.max_ctx = max_ctx;
+  s->host_desc = sd;
   SWL_CUDA(cudaMemcpyAsync(s->desc, &sd, sizeof sd, cudaMemcpyHostToDevice, m->stream));
   SWL_CUDA(cudaStreamSynchronize(m->stream));
   return s.release();
@@ -881,16 +1139,119 @@ int swl_step(swl_model* model, swl_state* state, const int32_t* tokens, int32_t 
   API_END
 }
 
+// Batches of two or more sequences run through the batched kernels when the
+// model's formats allow it: in rounds, round r taking the r-th token of every
+// sequence that has one (up to BT_MAX sequences per launch); a sequence's
+// logits are those of its last round. Otherwise each sequence steps alone.
 int swl_step_batch(swl_model* model, swl_state** states, const int32_t* tokens, const int32_t* counts, int32_t nseq,
                    float* logits_out) {
   API_BEGIN
   if (!model || !states || !tokens || !counts || !logits_out || nseq < 1) throw Error(ERR_INVALID, "null argument");
+  Model& m = model->m;
+  SWL_CUDA(cudaSetDevice(m.device));
+  std::vector<int64_t> first(nseq);
   int64_t off = 0;
+  int maxc = 0;
   for (int i = 0; i < nseq; ++i) {
-    int rc = swl_step(model, states[i], tokens + off, counts[i], logits_out + int64_t(i) * model->m.cfg.vocab);
-    if (rc) return rc;
+    if (!states[i]) throw Error(ERR_INVALID, "null state");
+    if (states[i]->s.model != &m) throw Error(ERR_INVALID, "state belongs to another model");
+    if (counts[i] < 1) throw Error(ERR_INVALID, "every sequence needs at least one token");
+    for (int j = 0; j < i; ++j)
+      if (states[j] == states[i]) throw Error(ERR_INVALID, "a state appears twice in one batch");
+    check_tokens(m, tokens + off, counts[i]);
+    if (states[i]->s.pos + counts[i] > states[i]->s.max_ctx)
+      throw Error(ERR_CAPACITY, "context capacity exceeded (max_ctx " + std::to_string(states[i]->s.max_ctx) + ")");
+    first[i] = off;
     off += counts[i];
+    maxc = std::max(maxc, counts[i]);
   }
+  if (nseq < 2 || !m.batch_supported()) {
+    for (int i = 0; i < nseq; ++i) {
+      int rc = swl_step(model, states[i], tokens + first[i], counts[i], logits_out + int64_t(i) * m.cfg.vocab);
+      if (rc) return rc;
+    }
+    return SWL_OK;
+  }
+  const int64_t V = m.cfg.vocab;
+  for (int r = 0; r < maxc; ++r) {
+    std::vector<int> active;
+    for (int i = 0; i < nseq; ++i)
+      if (counts[i] > r) active.push_back(i);
+    for (size_t b0 = 0; b0 < active.size(); b0 += BT_MAX) {
+      const int T = int(std::min<size_t>(BT_MAX, active.size() - b0));
+      std::vector<int32_t> tok(T);
+      std::vector<State*> ss(T);
+      for (int t = 0; t < T; ++t) {
+        const int i = active[b0 + t];
+        tok[t] = tokens[first[i] + r];
+        ss[t] = &states[i]->s;
+      }
+      m.ensure_batch();
+      SWL_CUDA(cudaMemcpyAsync(m.bb.tokens, tok.data(), size_t(T) * 4, cudaMemcpyHostToDevice, m.stream));
+      m.run_batch(ss.data(), T);
+      for (int t = 0; t < T; ++t) {
+        const int i = active[b0 + t];
+        if (counts[i] == r + 1)
+          SWL_CUDA(cudaMemcpyAsync(logits_out + int64_t(i) * V, m.bb.logits + int64_t(t) * V, size_t(V) * 4,
+                                   cudaMemcpyDeviceToHost, m.stream));
+      }
+    }
+  }
+  int status = 0;
+  SWL_CUDA(cudaMemcpyAsync(&status, m.kstatus, 4, cudaMemcpyDeviceToHost, m.stream));
+  SWL_CUDA(cudaStreamSynchronize(m.stream));
+  m.check_status(&status);
+  API_END
+}
+
+int swl_step_batch_device(swl_model* model, swl_state** states, int32_t nseq, const int32_t* d_tokens, float* d_logits,
+                          int32_t* d_greedy) {
+  API_BEGIN
+  if (!model || !states || !d_tokens || nseq < 1) throw Error(ERR_INVALID, "null argument");
+  Model& m = model->m;
+  SWL_CUDA(cudaSetDevice(m.device));
+  for (int i = 0; i < nseq; ++i) {
+    if (!states[i] || states[i]->s.model != &m) throw Error(ERR_INVALID, "null state or state of another model");
+    for (int j = 0; j < i; ++j)
+      if (states[j] == states[i]) throw Error(ERR_INVALID, "a state appears twice in one batch");
+    if (states[i]->s.pos + 1 > states[i]->s.max_ctx)
+      throw Error(ERR_CAPACITY, "context capacity exceeded (max_ctx " + std::to_string(states[i]->s.max_ctx) + ")");
+  }
+  if (nseq < 2 || !m.batch_supported()) {
+    for (int i = 0; i < nseq; ++i) {
+      int rc = swl_step_device(model, states[i], d_tokens + i, 1, d_logits ? d_logits + int64_t(i) * m.cfg.vocab : nullptr,
+                               d_greedy ? d_greedy + i : nullptr);
+      if (rc) return rc;
+    }
+    return SWL_OK;
+  }
+  const int64_t V = m.cfg.vocab;
+  m.ensure_batch();
+  for (int b0 = 0; b0 < nseq; b0 += BT_MAX) {
+    const int T = std::min(BT_MAX, nseq - b0);
+    std::vector<State*> ss(T);
+    for (int t = 0; t < T; ++t) ss[t] = &states[b0 + t]->s;
+    SWL_CUDA(cudaMemcpyAsync(m.bb.tokens, d_tokens + b0, size_t(T) * 4, cudaMemcpyDeviceToDevice, m.stream));
+    m.run_batch(ss.data(), T);
+    if (d_logits)
+      SWL_CUDA(cudaMemcpyAsync(d_logits + int64_t(b0) * V, m.bb.logits, size_t(T) * V * 4, cudaMemcpyDeviceToDevice,
+                               m.stream));
+    if (d_greedy)
+      SWL_CUDA(cudaMemcpyAsync(d_greedy + b0, m.bb.greedy, size_t(T) * 4, cudaMemcpyDeviceToDevice, m.stream));
+  }
+  API_END
+}
+
+// Whether swl_step_batch takes the batched kernels for this model (1) or
+// steps the sequences one by one (0); `why` (may be NULL) gets the reason.
+int swl_batch_supported(swl_model* model, char* why, int32_t why_len) {
+  API_BEGIN
+  if (!model) throw Error(ERR_INVALID, "null model");
+  const bool ok = model->m.batch_supported();
+  if (why && why_len > 0) {
+    snprintf(why, size_t(why_len), "%s", ok ? "" : model->m.batch_why.c_str());
+  }
+  return ok ? 1 : 0;
   API_END
 }
 
