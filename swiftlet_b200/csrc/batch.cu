@@ -210,45 +210,85 @@ __device__ __forceinline__ BItem bitem(const BGemmArgs& a, int it) {
   return d;
 }
 
-// Issues the copies of chunk kc of item d into stage buffer st.
+// Per-thread copy plan of one item: chunk-0 sources and shared-memory
+// offsets, computed once per item (later chunks add fixed strides). Thread
+// tid copies weight chunks tid + 256u, the scale (even tid) or bias (odd
+// tid) window of row tid / 2, digit chunks tid + 256u of the tile's tokens
+// and metadata entry tid.
+template <int BITS>
+struct BPlan {
+  static constexpr int WMAX = BITS == 4 ? 2 : 4;  // 64 rows x kcb / 16 chunks (kc <= 256)
+  static constexpr int XMAX = 3;                  // 16 tokens x 48 chunks (kc <= 256)
+  const uint8_t* wp[WMAX];
+  const uint8_t* xp[XMAX];
+  const uint8_t* sp;
+  const uint8_t* mp;
+  int wd[WMAX], xd[XMAX], sd, md;
+  unsigned wm, xm;
+  bool sv, mv;
+};
+
 template <int BITS, int DT>
-__device__ __forceinline__ void bg_load(const BGemmArgs& a, const BGLayout& L, const BItem& d, int kc, uint8_t* st) {
-  constexpr int SB = DT == DT_F32 ? 4 : 2;
+__device__ __forceinline__ void bg_plan(const BGemmArgs& a, const BGLayout& L, const BItem& d, BPlan<BITS>& p) {
   const int tid = threadIdx.x;
   const int cpr = L.kcb >> 4, mask = min(cpr, 8) - 1;
-  for (int i = tid; i < BG_ROWS * cpr; i += BG_THREADS) {
-    const int r = i / cpr, ch = i - r * cpr, hf = r >> 5, rr = r & 31;
-    if (rr < d.nv(hf)) {
-      const uint8_t* src = d.w(hf) + int64_t(d.row(hf) + rr) * d.wrow + int64_t(kc) * L.kcb + ch * 16;
-      cp_async16(st + L.w_off + r * L.kcb + ((ch ^ (r & mask)) << 4), src);
-    }
+  p.wm = 0u;
+#pragma unroll
+  for (int u = 0; u < BPlan<BITS>::WMAX; ++u) {
+    const int i = tid + u * BG_THREADS, r = i / cpr, ch = i - r * cpr, hf = r >> 5, rr = r & 31;
+    const bool ok = r < BG_ROWS && rr < d.nv(hf);
+    p.wp[u] = ok ? d.w(hf) + int64_t(d.row(hf) + rr) * d.wrow + ch * 16 : nullptr;
+    p.wd[u] = L.w_off + r * L.kcb + ((ch ^ (r & mask)) << 4);
+    p.wm |= ok ? 1u << u : 0u;
   }
-  // scale and bias windows: the 4-byte aligned words covering the chunk's
-  // entries of the row
-  const int sbytes = L.gpc * SB;
-  for (int i = tid; i < 2 * BG_ROWS; i += BG_THREADS) {
-    const int r = i >> 1, which = i & 1, hf = r >> 5, rr = r & 31;
-    if (rr < d.nv(hf)) {
-      const uint8_t* base = (which ? d.b(hf) : d.s(hf)) + int64_t(d.row(hf) + rr) * d.srow + int64_t(kc) * sbytes;
-      const uintptr_t a0 = reinterpret_cast<uintptr_t>(base) & ~uintptr_t(3);
-      const uintptr_t a1 = (reinterpret_cast<uintptr_t>(base) + sbytes + 3) & ~uintptr_t(3);
-      uint8_t* dst = st + (which ? L.b_off : L.s_off) + r * L.sw;
-      for (uintptr_t p = a0; p < a1; p += 4) cp_async4(dst + (p - a0), reinterpret_cast<const void*>(p));
-    }
+  {
+    const int r = tid >> 1, which = tid & 1, hf = r >> 5, rr = r & 31;
+    p.sv = r < BG_ROWS && rr < d.nv(hf);
+    p.sp = p.sv ? (which ? d.b(hf) : d.s(hf)) + int64_t(d.row(hf) + rr) * d.srow : nullptr;
+    p.sd = (which ? L.b_off : L.s_off) + r * L.sw;
   }
-  // digit tables and group metadata of the tile's tokens
-  const int kbc = L.kc >> 5, n16 = kbc * 6;  // 96 bytes per 32-value block
-  for (int i = tid; i < d.c * n16; i += BG_THREADS) {
-    const int j = i / n16, p = i - j * n16, slot = d.s0 + j;
-    const int row = a.in_map ? a.in_map[slot] : slot;
-    const uint8_t* src = reinterpret_cast<const uint8_t*>(a.xbt + row * a.bt_row + int64_t(kc) * kbc * 12) + p * 16;
-    cp_async16(st + L.x_off + j * L.bstride * 8 + p * 16, src);
+  const int n16 = (L.kc >> 5) * 6;  // 16-byte digit chunks per token per chunk (96 bytes per 32 values)
+  p.xm = 0u;
+#pragma unroll
+  for (int u = 0; u < BPlan<BITS>::XMAX; ++u) {
+    const int i = tid + u * BG_THREADS, j = i / n16, c16 = i - j * n16;
+    const bool ok = j < d.c;
+    int row = 0;
+    if (ok) row = a.in_map ? a.in_map[d.s0 + j] : d.s0 + j;
+    p.xp[u] = ok ? reinterpret_cast<const uint8_t*>(a.xbt + row * a.bt_row) + c16 * 16 : nullptr;
+    p.xd[u] = L.x_off + j * L.bstride * 8 + c16 * 16;
+    p.xm |= ok ? 1u << u : 0u;
   }
-  for (int i = tid; i < d.c * L.gpc; i += BG_THREADS) {
-    const int j = i / L.gpc, g = i - j * L.gpc, slot = d.s0 + j;
-    const int row = a.in_map ? a.in_map[slot] : slot;
-    cp_async8(st + L.m_off + (j * L.gpc + g) * 8, a.xmeta + row * a.meta_row + int64_t(kc) * L.gpc + g);
+  {
+    const int j = tid / L.gpc, g = tid - j * L.gpc;
+    p.mv = j < d.c;
+    int row = 0;
+    if (p.mv) row = a.in_map ? a.in_map[d.s0 + j] : d.s0 + j;
+    p.mp = p.mv ? reinterpret_cast<const uint8_t*>(a.xmeta + row * a.meta_row + g) : nullptr;
+    p.md = L.m_off + (j * L.gpc + g) * 8;
   }
+}
+
+// Issues the copies of chunk kc of the planned item into stage buffer st.
+template <int BITS, int DT>
+__device__ __forceinline__ void bg_issue(const BGLayout& L, const BPlan<BITS>& p, int kc, uint8_t* st) {
+  constexpr int SB = DT == DT_F32 ? 4 : 2;
+#pragma unroll
+  for (int u = 0; u < BPlan<BITS>::WMAX; ++u)
+    if (p.wm & (1u << u)) cp_async16(st + p.wd[u], p.wp[u] + int64_t(kc) * L.kcb);
+  if (p.sv) {
+    // the 4-byte aligned words covering the chunk's entries of the row
+    const int sbytes = L.gpc * SB;
+    const uint8_t* base = p.sp + int64_t(kc) * sbytes;
+    const uintptr_t a0 = reinterpret_cast<uintptr_t>(base) & ~uintptr_t(3);
+    const uintptr_t a1 = (reinterpret_cast<uintptr_t>(base) + sbytes + 3) & ~uintptr_t(3);
+    for (uintptr_t q = a0; q < a1; q += 4) cp_async4(st + p.sd + (q - a0), reinterpret_cast<const void*>(q));
+  }
+  const int64_t xstep = int64_t(L.kc >> 5) * 96;
+#pragma unroll
+  for (int u = 0; u < BPlan<BITS>::XMAX; ++u)
+    if (p.xm & (1u << u)) cp_async16(st + p.xd[u], p.xp[u] + kc * xstep);
+  if (p.mv) cp_async8(st + p.md, p.mp + int64_t(kc) * L.gpc * 8);
 }
 
 template <int DT>
@@ -272,13 +312,21 @@ __global__ void __launch_bounds__(BG_THREADS) k_bgemm(const BGemmArgs a) {
   const int mine = nitems > int(blockIdx.x) ? (nitems - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
   const int nq = mine * nkc;
   auto item_of = [&](int q) { return int(blockIdx.x) + (q / nkc) * int(gridDim.x); };
+  // loader: re-planned when the item of the chunk it issues changes
+  BPlan<BITS> lp;
+  int l_m = -1;
+  auto load = [&](int q) {
+    const int m = q / nkc;
+    if (m != l_m) {
+      l_m = m;
+      bg_plan<BITS, DT>(a, L, bitem(a, int(blockIdx.x) + m * int(gridDim.x)), lp);
+    }
+    bg_issue<BITS, DT>(L, lp, q - m * nkc, sm + (q % BG_STAGES) * L.stage);
+  };
   // prologue: the first BG_STAGES - 1 chunks
 #pragma unroll
   for (int q = 0; q < BG_STAGES - 1; ++q) {
-    if (q < nq) {
-      const BItem d = bitem(a, item_of(q));
-      bg_load<BITS, DT>(a, L, d, q % nkc, sm + q * L.stage);
-    }
+    if (q < nq) load(q);
     cp_async_commit();
   }
   const int mask = min(L.kcb >> 4, 8) - 1;
@@ -294,14 +342,8 @@ __global__ void __launch_bounds__(BG_THREADS) k_bgemm(const BGemmArgs a) {
   for (int q = 0; q < nq; ++q) {
     cp_async_wait_group<BG_STAGES - 2>();
     __syncthreads();
-    {
-      const int qn = q + BG_STAGES - 1;
-      if (qn < nq) {
-        const BItem dn = bitem(a, item_of(qn));
-        bg_load<BITS, DT>(a, L, dn, qn % nkc, sm + (qn % BG_STAGES) * L.stage);
-      }
-      cp_async_commit();
-    }
+    if (q + BG_STAGES - 1 < nq) load(q + BG_STAGES - 1);
+    cp_async_commit();
     const int kc = q % nkc;
     if (kc == 0) {
       d = bitem(a, item_of(q));
