@@ -298,7 +298,76 @@ __device__ __forceinline__ float sm_entry(const uint8_t* p) {
   else return f16_bits_to_f32(*reinterpret_cast<const uint16_t*>(p));
 }
 
-template <int BITS, int DT>
+// Groups [G0, G0 + NG) of a chunk against NCB column blocks (1: the single
+// block of a tile of at most two tokens, the warp's half of the groups; 3:
+// blocks hw, hw + 2, hw + 4 over all groups) for the common layout of
+// 256-value chunks and 64-value groups, fully unrolled so that every
+// shared-memory access is a lane base plus a constant. W0 is the lane's
+// first weight row (+ its word offset), sx the lane's swizzle term, X the
+// stage's digit tables, M its metadata, S0/S1/B0/B1 the rows' scale and
+// bias entries of group 0.
+template <int BITS, int DT, int G0, int NG, int NCB>
+__device__ __forceinline__ void bg_fast(const uint8_t* W0, int sx, const uint2* X, const float2* M,
+                                        const int (&boff)[BG_MAXCB], const int (&cbv)[BG_MAXCB],
+                                        const int (&mo0)[BG_MAXCB], const int (&mo1)[BG_MAXCB],
+                                        const float (&wn0)[BG_MAXCB], const float (&wn1)[BG_MAXCB],
+                                        const float (&z0)[BG_MAXCB], const float (&z1)[BG_MAXCB], const uint8_t* S0,
+                                        const uint8_t* S1, const uint8_t* B0, const uint8_t* B1,
+                                        float (&acc)[BG_MAXCB][4]) {
+  constexpr int SB = DT == DT_F32 ? 4 : 2;
+  constexpr int KCB = 32 * BITS;  // weight bytes per row per chunk
+#pragma unroll
+  for (int gg = 0; gg < NG; ++gg) {
+    const int g = G0 + gg;
+    int dd[NCB][4];
+#pragma unroll
+    for (int j = 0; j < NCB; ++j) dd[j][0] = dd[j][1] = dd[j][2] = dd[j][3] = 0;
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      const int kb = 2 * g + kk;
+      uint32_t af[4];
+      if constexpr (BITS == 4) {
+        const int off = (kb << 4) ^ sx;
+        const uint32_t u0 = *reinterpret_cast<const uint32_t*>(W0 + off);
+        const uint32_t u1 = *reinterpret_cast<const uint32_t*>(W0 + 8 * KCB + off);
+        af[0] = u0 & 0x0F0F0F0Fu;
+        af[2] = (u0 >> 4) & 0x0F0F0F0Fu;
+        af[1] = u1 & 0x0F0F0F0Fu;
+        af[3] = (u1 >> 4) & 0x0F0F0F0Fu;
+      } else {
+        const int off = (kb << 5) ^ sx;
+        const uint2 x0 = *reinterpret_cast<const uint2*>(W0 + off);
+        const uint2 x1 = *reinterpret_cast<const uint2*>(W0 + 8 * KCB + off);
+        af[0] = prmt(x0.x, x0.y, 0x6420u);
+        af[2] = prmt(x0.x, x0.y, 0x7531u);
+        af[1] = prmt(x1.x, x1.y, 0x6420u);
+        af[3] = prmt(x1.x, x1.y, 0x7531u);
+      }
+#pragma unroll
+      for (int j = 0; j < NCB; ++j)
+        if (NCB == 1 || cbv[j]) {
+          const uint2 bv = boff[j] >= 0 ? X[kb * 12 + boff[j]] : make_uint2(0u, 0u);
+          mma_u8s8(dd[j], af, bv);
+        }
+    }
+    const float s0v = sm_entry<DT>(S0 + g * SB), s1v = sm_entry<DT>(S1 + g * SB);
+    const float b0v = sm_entry<DT>(B0 + g * SB), b1v = sm_entry<DT>(B1 + g * SB);
+#pragma unroll
+    for (int j = 0; j < NCB; ++j)
+      if (NCB == 1 || cbv[j]) {
+        const float2 m0 = mo0[j] >= 0 ? M[mo0[j] + g] : make_float2(0.f, 0.f);
+        const float2 m1 = mo1[j] >= 0 ? M[mo1[j] + g] : make_float2(0.f, 0.f);
+        const float f0 = m0.x * wn0[j], f1 = m1.x * wn1[j];
+        const float c0 = z0[j] * m0.y, c1 = z1[j] * m1.y;
+        acc[j][0] = fmaf(s0v * f0, i2f_small(dd[j][0]), fmaf(b0v, c0, acc[j][0]));
+        acc[j][1] = fmaf(s0v * f1, i2f_small(dd[j][1]), fmaf(b0v, c1, acc[j][1]));
+        acc[j][2] = fmaf(s1v * f0, i2f_small(dd[j][2]), fmaf(b1v, c0, acc[j][2]));
+        acc[j][3] = fmaf(s1v * f1, i2f_small(dd[j][3]), fmaf(b1v, c1, acc[j][3]));
+      }
+  }
+}
+
+template <int BITS, int DT, bool FAST>
 __global__ void __launch_bounds__(BG_THREADS) k_bgemm(const BGemmArgs a) {
   constexpr int SB = DT == DT_F32 ? 4 : 2;
   extern __shared__ __align__(128) uint8_t sm[];
@@ -381,9 +450,19 @@ __global__ void __launch_bounds__(BG_THREADS) k_bgemm(const BGemmArgs a) {
     const uint8_t* S1 = st + L.s_off + r1l * L.sw + ((mis_s1 + cadv) & 3);
     const uint8_t* B0 = st + L.b_off + r0l * L.sw + ((mis_b0 + cadv) & 3);
     const uint8_t* B1 = st + L.b_off + r1l * L.sw + ((mis_b1 + cadv) & 3);
+    if constexpr (FAST) {
+      const int sx = BITS == 4 ? (gi << 4) : ((((t >> 1) ^ gi) & 7) << 4);
+      const uint8_t* W0 = W + r0l * (32 * BITS) + (BITS == 4 ? 4 * t : 8 * (t & 1));
+      if (!ksplit)
+        bg_fast<BITS, DT, 0, 4, 3>(W0, sx, X, M, boff, cbv, mo0, mo1, wn0, wn1, z0, z1, S0, S1, B0, B1, acc);
+      else if (hw == 0)
+        bg_fast<BITS, DT, 0, 2, 1>(W0, sx, X, M, boff, cbv, mo0, mo1, wn0, wn1, z0, z1, S0, S1, B0, B1, acc);
+      else
+        bg_fast<BITS, DT, 2, 2, 1>(W0, sx, X, M, boff, cbv, mo0, mo1, wn0, wn1, z0, z1, S0, S1, B0, B1, acc);
+    }
     int g0 = 0, g1 = L.gpc;
     if (ksplit) { g0 = (hw * L.gpc) >> 1; g1 = ((hw + 1) * L.gpc) >> 1; }
-    if (cbv[0]) {
+    if (!FAST && cbv[0]) {
       for (int g = g0; g < g1; ++g) {
         int dd[BG_MAXCB][4];
 #pragma unroll
@@ -519,42 +598,55 @@ bool bgemm_layout(int in, int bits, int dt, int gs, BGLayout& L) {
   return L.total <= 200 * 1024;
 }
 
-template <int BITS, int DT>
+// The unrolled consumer serves 256-value chunks of 64-value groups.
+static bool bg_fast_layout(const BGLayout& L) { return L.kc == 256 && L.kpg == 2 && L.gpc == 4; }
+
+template <int BITS, int DT, bool FAST>
 static int bg_grid_for(int smem) {
   static int cached[64] = {0};
   const int key = std::min(63, smem >> 12);
   if (!cached[key]) {
-    SWL_CUDA(cudaFuncSetAttribute(k_bgemm<BITS, DT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    SWL_CUDA(cudaFuncSetAttribute(k_bgemm<BITS, DT, FAST>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     int per = 0;
-    SWL_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_bgemm<BITS, DT>, BG_THREADS, smem));
+    SWL_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_bgemm<BITS, DT, FAST>, BG_THREADS, smem));
     cached[key] = std::max(1, per);
   }
   return cached[key] * sm_count();
 }
 
+template <int BITS, int DT>
+static int bg_grid2(const BGLayout& L) {
+  return bg_fast_layout(L) ? bg_grid_for<BITS, DT, true>(L.total) : bg_grid_for<BITS, DT, false>(L.total);
+}
+
 int bgemm_grid(int bits, int dt, const BGLayout& L) {
-  const int smem = L.total;
   if (bits == 4) {
-    if (dt == DT_BF16) return bg_grid_for<4, DT_BF16>(smem);
-    if (dt == DT_F16) return bg_grid_for<4, DT_F16>(smem);
-    return bg_grid_for<4, DT_F32>(smem);
+    if (dt == DT_BF16) return bg_grid2<4, DT_BF16>(L);
+    if (dt == DT_F16) return bg_grid2<4, DT_F16>(L);
+    return bg_grid2<4, DT_F32>(L);
   }
-  if (dt == DT_BF16) return bg_grid_for<8, DT_BF16>(smem);
-  if (dt == DT_F16) return bg_grid_for<8, DT_F16>(smem);
-  return bg_grid_for<8, DT_F32>(smem);
+  if (dt == DT_BF16) return bg_grid2<8, DT_BF16>(L);
+  if (dt == DT_F16) return bg_grid2<8, DT_F16>(L);
+  return bg_grid2<8, DT_F32>(L);
+}
+
+template <int BITS, int DT>
+static void bg_launch(const BGemmArgs& a, dim3 g, cudaStream_t st, bool pdl) {
+  const size_t smem = size_t(a.L.total);
+  if (bg_fast_layout(a.L)) launch(k_bgemm<BITS, DT, true>, g, dim3(BG_THREADS), smem, st, pdl, a);
+  else launch(k_bgemm<BITS, DT, false>, g, dim3(BG_THREADS), smem, st, pdl, a);
 }
 
 void launch_bgemm(const BGemmArgs& a, int bits, int dt, int grid, cudaStream_t st, bool pdl) {
-  const size_t smem = size_t(a.L.total);
-  const dim3 g(std::max(grid, 1)), b(BG_THREADS);
+  const dim3 g(std::max(grid, 1));
   if (bits == 4) {
-    if (dt == DT_BF16) launch(k_bgemm<4, DT_BF16>, g, b, smem, st, pdl, a);
-    else if (dt == DT_F16) launch(k_bgemm<4, DT_F16>, g, b, smem, st, pdl, a);
-    else launch(k_bgemm<4, DT_F32>, g, b, smem, st, pdl, a);
+    if (dt == DT_BF16) bg_launch<4, DT_BF16>(a, g, st, pdl);
+    else if (dt == DT_F16) bg_launch<4, DT_F16>(a, g, st, pdl);
+    else bg_launch<4, DT_F32>(a, g, st, pdl);
   } else {
-    if (dt == DT_BF16) launch(k_bgemm<8, DT_BF16>, g, b, smem, st, pdl, a);
-    else if (dt == DT_F16) launch(k_bgemm<8, DT_F16>, g, b, smem, st, pdl, a);
-    else launch(k_bgemm<8, DT_F32>, g, b, smem, st, pdl, a);
+    if (dt == DT_BF16) bg_launch<8, DT_BF16>(a, g, st, pdl);
+    else if (dt == DT_F16) bg_launch<8, DT_F16>(a, g, st, pdl);
+    else bg_launch<8, DT_F32>(a, g, st, pdl);
   }
 }
 
