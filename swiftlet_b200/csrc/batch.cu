@@ -226,6 +226,7 @@ struct BPlan {
   int wd[WMAX], xd[XMAX], sd, md;
   unsigned wm, xm;
   bool sv, mv;
+  bool s8;  // the row's windows are 8 bytes per chunk and 8-byte aligned: one copy
 };
 
 template <int BITS, int DT>
@@ -246,6 +247,7 @@ __device__ __forceinline__ void bg_plan(const BGemmArgs& a, const BGLayout& L, c
     p.sv = r < BG_ROWS && rr < d.nv(hf);
     p.sp = p.sv ? (which ? d.b(hf) : d.s(hf)) + int64_t(d.row(hf) + rr) * d.srow : nullptr;
     p.sd = (which ? L.b_off : L.s_off) + r * L.sw;
+    p.s8 = p.sv && L.gpc * (DT == DT_F32 ? 4 : 2) == 8 && (reinterpret_cast<uintptr_t>(p.sp) & 7) == 0;
   }
   const int n16 = (L.kc >> 5) * 6;  // 16-byte digit chunks per token per chunk (96 bytes per 32 values)
   p.xm = 0u;
@@ -276,7 +278,9 @@ __device__ __forceinline__ void bg_issue(const BGLayout& L, const BPlan<BITS>& p
 #pragma unroll
   for (int u = 0; u < BPlan<BITS>::WMAX; ++u)
     if (p.wm & (1u << u)) cp_async16(st + p.wd[u], p.wp[u] + int64_t(kc) * L.kcb);
-  if (p.sv) {
+  if (p.s8) {
+    cp_async8(st + p.sd, p.sp + kc * 8);
+  } else if (p.sv) {
     // the 4-byte aligned words covering the chunk's entries of the row
     const int sbytes = L.gpc * SB;
     const uint8_t* base = p.sp + int64_t(kc) * sbytes;
@@ -380,17 +384,14 @@ __global__ void __launch_bounds__(BG_THREADS) k_bgemm(const BGemmArgs a) {
   const int nkc = a.in / L.kc;
   const int mine = nitems > int(blockIdx.x) ? (nitems - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
   const int nq = mine * nkc;
-  auto item_of = [&](int q) { return int(blockIdx.x) + (q / nkc) * int(gridDim.x); };
-  // loader: re-planned when the item of the chunk it issues changes
+  // loader: (item, chunk) of the next chunk it issues, counted without
+  // divisions; re-planned at each item's first chunk
   BPlan<BITS> lp;
-  int l_m = -1;
+  int l_m = 0, l_kc = 0;
   auto load = [&](int q) {
-    const int m = q / nkc;
-    if (m != l_m) {
-      l_m = m;
-      bg_plan<BITS, DT>(a, L, bitem(a, int(blockIdx.x) + m * int(gridDim.x)), lp);
-    }
-    bg_issue<BITS, DT>(L, lp, q - m * nkc, sm + (q % BG_STAGES) * L.stage);
+    if (l_kc == 0) bg_plan<BITS, DT>(a, L, bitem(a, int(blockIdx.x) + l_m * int(gridDim.x)), lp);
+    bg_issue<BITS, DT>(L, lp, l_kc, sm + (q & (BG_STAGES - 1)) * L.stage);
+    if (++l_kc == nkc) { l_kc = 0; ++l_m; }
   };
   // prologue: the first BG_STAGES - 1 chunks
 #pragma unroll
@@ -408,14 +409,14 @@ __global__ void __launch_bounds__(BG_THREADS) k_bgemm(const BGemmArgs a) {
   float wn0[BG_MAXCB], wn1[BG_MAXCB], z0[BG_MAXCB], z1[BG_MAXCB];
   float acc[BG_MAXCB][4];
   int mis_s0 = 0, mis_s1 = 0, mis_b0 = 0, mis_b1 = 0;  // byte offset of the rows' first entry in their windows
-  for (int q = 0; q < nq; ++q) {
+  int c_m = 0, kc = 0;  // consumer's item and chunk
+  for (int q = 0; q < nq; ++q, (++kc == nkc ? (kc = 0, ++c_m) : 0)) {
     cp_async_wait_group<BG_STAGES - 2>();
     __syncthreads();
     if (q + BG_STAGES - 1 < nq) load(q + BG_STAGES - 1);
     cp_async_commit();
-    const int kc = q % nkc;
     if (kc == 0) {
-      d = bitem(a, item_of(q));
+      d = bitem(a, int(blockIdx.x) + c_m * int(gridDim.x));
       ncb = (3 * d.c + 7) >> 3;
       ksplit = ncb == 1;
 #pragma unroll
@@ -441,7 +442,7 @@ __global__ void __launch_bounds__(BG_THREADS) k_bgemm(const BGemmArgs a) {
       mis_b0 = int(reinterpret_cast<uintptr_t>(d.b(h0) + int64_t(d.row(h0) + (r0l & 31)) * d.srow) & 3);
       mis_b1 = int(reinterpret_cast<uintptr_t>(d.b(h1) + int64_t(d.row(h1) + (r1l & 31)) * d.srow) & 3);
     }
-    const uint8_t* st = sm + (q % BG_STAGES) * L.stage;
+    const uint8_t* st = sm + (q & (BG_STAGES - 1)) * L.stage;
     const uint8_t* W = st + L.w_off;
     const uint2* X = reinterpret_cast<const uint2*>(st + L.x_off);
     const float2* M = reinterpret_cast<const float2*>(st + L.m_off);
