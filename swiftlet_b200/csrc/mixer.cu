@@ -40,11 +40,12 @@ __device__ __forceinline__ void delta_ba(const DeltaArgs& a, int hv, int& bi, in
   bi = base + ri; ai = base + rep + ri;
 }
 
-constexpr int DELTA_THREADS = 128;
+constexpr int DELTA_THREADS = 128;     // single-sequence launches
+constexpr int DELTA_MAX_THREADS = 512; // batched launches: one CTA per (v-head, sequence), 8 rows per warp
 constexpr int DELTA_RPW = 8;  // rows per warp (RB <= 32)
 constexpr int DELTA_EPL = 4;  // state elements per lane (dk <= 128)
 
-__global__ void __launch_bounds__(DELTA_THREADS) k_delta(const DeltaArgs a) {
+__global__ void __launch_bounds__(DELTA_MAX_THREADS) k_delta(const DeltaArgs a) {
   extern __shared__ __align__(16) float sm[];
   const int dk = a.dk, dv = a.dv, K = a.conv_k, RB = a.rows_per_block;
   const int hv = blockIdx.x, slice = blockIdx.y, rep = a.nv / a.nk, hk = hv / rep;
@@ -652,12 +653,15 @@ void launch_delta(const DeltaArgs& a, cudaStream_t st, bool pdl) {
   launch(k_delta, dim3(a.nv, a.dv / a.rows_per_block), dim3(DELTA_THREADS), smem, st, pdl, a);
 }
 
+// Batched: up to 128 rows per CTA (a whole 128-row value head), so the q/k
+// convolution and norms of a key head are computed by fewer CTAs.
 void launch_delta_batch(const DeltaArgs& a, int T, cudaStream_t st, bool pdl) {
-  if (a.dk > 32 * DELTA_EPL || a.rows_per_block > DELTA_RPW * (DELTA_THREADS / 32) || a.dv % a.rows_per_block)
+  const int threads = std::max(DELTA_THREADS, 32 * ((a.rows_per_block + DELTA_RPW - 1) / DELTA_RPW));
+  if (a.dk > 32 * DELTA_EPL || threads > DELTA_MAX_THREADS || a.dv % a.rows_per_block)
     throw Error(ERR_UNSUPPORTED, "DeltaNet head dims outside the decode kernel's range");
   const int nch = 2 * a.dk + a.rows_per_block;
   const size_t smem = size_t(2 * a.dk + a.rows_per_block + nch * (2 * a.conv_k - 1)) * 4;
-  launch(k_delta, dim3(a.nv, a.dv / a.rows_per_block, T), dim3(DELTA_THREADS), smem, st, pdl, a);
+  launch(k_delta, dim3(a.nv, a.dv / a.rows_per_block, T), dim3(threads), smem, st, pdl, a);
 }
 
 void launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl, int T) {

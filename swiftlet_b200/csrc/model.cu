@@ -900,7 +900,7 @@ void Model::enqueue_batch(int T, cudaStream_t st) {
       DeltaArgs d;
       d.proj = bb.proj; d.proj_stride = bb.projn; d.split = c.split_layout; d.nk = c.nk; d.nv = c.nv; d.dk = c.dk;
       d.dv = c.dv; d.conv_k = c.conv_k; d.conv_dim = c.conv_dim(); d.conv_w = ld.conv_w; d.a_log = ld.a_log;
-      d.dt_bias = ld.dt_bias; d.sd = bb.sds; d.layer = l; d.rows_per_block = std::min(c.dv, 32); d.y = bb.yv;
+      d.dt_bias = ld.dt_bias; d.sd = bb.sds; d.layer = l; d.rows_per_block = c.dv <= 128 ? c.dv : 32; d.y = bb.yv;
       d.z = bb.zv;
       d.trace = tagged(16u * unsigned(l + 1) + 3);
       launch_delta_batch(d, T, st, pdl);
