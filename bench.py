@@ -286,6 +286,15 @@ def run_ours(args) -> None:
     cfg = model.config
     stream = torch.cuda.Stream()
     model.set_stream(stream.cuda_stream)
+    if args.batch_only:
+        # profiling: the batched leg alone (its kernels without the B=1 ones)
+        res = batched_decode(model, cfg, stream, args, rank, local, dist)
+        model.close()
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "batched": res, "profiling_only": True}), flush=True)
+        if dist:
+            dist.destroy_process_group()
+        return
     rng = np.random.default_rng(PROMPT_SEED + rank)
     prompt = rng.integers(0, cfg.vocab_size, args.prompt).astype(np.int32)
     e2e_steps = min(args.steps, 32)
@@ -408,6 +417,8 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=64, help="sequences of the batched-decode leg (<= 1: skip it)")
     ap.add_argument("--batch-prompt", type=int, default=128)
     ap.add_argument("--batch-steps", type=int, default=32)
+    ap.add_argument("--batch-only", action="store_true",
+                    help="profiling only: run the batched leg alone and print its numbers")
     ap.add_argument("--layers", type=int, default=None,
                     help="profiling only: same shapes with fewer layers (keeps ncu captures to a few GB)")
     args = ap.parse_args()
