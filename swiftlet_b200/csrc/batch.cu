@@ -772,14 +772,14 @@ void launch_bcombine(const BCombineArgs& a, cudaStream_t st, bool pdl) {
   launch(k_bcombine, dim3((a.D + 255) / 256, a.T), dim3(256), 0, st, pdl, a);
 }
 
-// Every sequence of the batch has consumed one token.
-__global__ void k_badvance(const StateDev* sds, int T) {
+// Every sequence of the step has consumed its tokens.
+__global__ void k_badvance(const StateDev* sds, int S, const int* seq_n) {
   pdl_wait();
-  if (int(threadIdx.x) < T) ++*sds[threadIdx.x].pos;
+  if (int(threadIdx.x) < S) *sds[threadIdx.x].pos += seq_n ? seq_n[threadIdx.x] : 1;
 }
 
-void launch_badvance(const StateDev* sds, int T, cudaStream_t st, bool pdl) {
-  launch(k_badvance, dim3(1), dim3(BT_MAX), 0, st, pdl, sds, T);
+void launch_badvance(const StateDev* sds, int S, const int* seq_n, cudaStream_t st, bool pdl) {
+  launch(k_badvance, dim3(1), dim3(BT_MAX), 0, st, pdl, sds, S, seq_n);
 }
 
 // Greedy token per row: the first index of the largest logit

@@ -128,6 +128,10 @@ struct DeltaArgs {
   // Batched decode (grid.z = sequences): sequence b reads sd[b], proj +
   // b * proj_stride and writes y / z + b * nv * dv. 0 for one sequence.
   int64_t proj_stride = 0;
+  // Chunked steps (k_delta_seq, k_conv_ring): sequence s owns token rows
+  // [seq_first[s], seq_first[s] + seq_n[s]) of proj / y / z, in order.
+  const int* seq_first = nullptr;
+  const int* seq_n = nullptr;
   Trace trace;
 };
 
@@ -153,6 +157,11 @@ struct AttnArgs {
   // projections at qout / knew / vnew + b * proj_stride, uses its own
   // partials and counters, and writes out + b * H * hd.
   int64_t proj_stride = 0;
+  // Chunked steps (grid.z = tokens): token z belongs to sequence tok_seq[z]
+  // at position *pos + tok_off[z]; every key and value of the chunk is
+  // already in the cache (k_kv_append), so none is appended or injected.
+  const int* tok_seq = nullptr;
+  const int* tok_off = nullptr;
   Trace trace;
 };
 
@@ -287,7 +296,14 @@ void launch_bgemm(const BGemmArgs& a, int bits, int dt, int grid, cudaStream_t s
 int bgemm_grid(int bits, int dt, const BGLayout& L);
 void launch_broute(const BRouteArgs& a, cudaStream_t stream, bool pdl);
 void launch_bcombine(const BCombineArgs& a, cudaStream_t stream, bool pdl);
-void launch_badvance(const StateDev* sds, int T, cudaStream_t stream, bool pdl);
+// Sequence s of the step has consumed seq_n[s] tokens (1 when seq_n is null).
+void launch_badvance(const StateDev* sds, int S, const int* seq_n, cudaStream_t stream, bool pdl);
+// Chunked steps: the DeltaNet recurrence over each sequence's tokens in order
+// (grid: v-heads x sequences), then the conv rings' last conv_k positions.
+void launch_delta_seq(const DeltaArgs& a, int S, cudaStream_t stream, bool pdl);
+void launch_conv_ring(const DeltaArgs& a, int S, cudaStream_t stream, bool pdl);
+// Chunked steps: every token's key (RMSNorm, RoPE) and value into the cache.
+void launch_kv_append(const AttnArgs& a, int T, cudaStream_t stream, bool pdl);
 void launch_bargmax(const float* logits, int T, int V, int* out, cudaStream_t stream, bool pdl);
 void launch_bembed(const EmbedArgs& a, int hidden, int T, cudaStream_t stream, bool pdl);
 

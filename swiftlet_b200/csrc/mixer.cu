@@ -177,6 +177,189 @@ __global__ void __launch_bounds__(DELTA_MAX_THREADS) k_delta(const DeltaArgs a) 
   trc.end(a.trace);
 }
 
+// Chunked step: the recurrence of k_delta over a sequence's consecutive
+// tokens in order, the state rows in registers throughout (one CTA per
+// (v-head, sequence), the whole head's dv rows). The conv window of each
+// channel starts from the ring (positions pos - 3 .. pos - 1) and slides over
+// the chunk's inputs; the ring itself is updated afterwards by k_conv_ring
+// (other CTAs of the launch still read the old positions).
+__global__ void __launch_bounds__(DELTA_MAX_THREADS) k_delta_seq(const DeltaArgs a) {
+  extern __shared__ __align__(16) float sm[];
+  const int dk = a.dk, dv = a.dv, K = a.conv_k, RB = dv;
+  const int hv = blockIdx.x, s = blockIdx.y, rep = a.nv / a.nk, hk = hv / rep;
+  const int keyDim = a.nk * dk;
+  const int nch = 2 * dk + RB;
+  float* q = sm;                     // [dk]
+  float* k = q + dk;                 // [dk]
+  float* v = k + dk;                 // [RB]
+  float* win = v + RB;               // [nch][K-1] the channel's previous conv inputs, oldest first
+  float* cw = win + nch * (K - 1);   // [nch][K] conv weights
+  __shared__ float gb[2], nrm[2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const StateDev* sd = a.sd + s;
+  const int pos = *sd->pos;
+  const float* ring = sd->conv[a.layer];
+  float* S = sd->dstate[a.layer];
+  auto chan = [&](int t) {
+    if (t < dk) return hk * dk + t;
+    if (t < 2 * dk) return keyDim + hk * dk + (t - dk);
+    return 2 * keyDim + hv * dv + (t - 2 * dk);
+  };
+  for (int t = threadIdx.x; t < nch; t += blockDim.x) {
+    const int c = chan(t);
+    for (int j = 0; j < K - 1; ++j) {
+      const int rs = ((pos - (K - 1) + j) % K + K) % K;
+      win[t * (K - 1) + j] = ring[int64_t(rs) * a.conv_dim + c];
+    }
+    for (int j = 0; j < K; ++j) cw[t * K + j] = a.conv_w[c * K + j];
+  }
+  float st[DELTA_RPW][DELTA_EPL];
+#pragma unroll
+  for (int j = 0; j < DELTA_RPW; ++j) {
+    const int r = warp + j * nw;
+    const float* Sr = S + (int64_t(hv) * dv + r) * dk;
+#pragma unroll
+    for (int e = 0; e < DELTA_EPL; ++e) {
+      const int i = lane + 32 * e;
+      st[j][e] = (r < RB && i < dk) ? Sr[i] : 0.f;
+    }
+  }
+  const float alog = a.a_log[hv], dtb = a.dt_bias[hv];
+  pdl_wait();
+  const int t0 = a.seq_first[s], n = a.seq_n[s];
+  const float inv = 1.f / sqrtf(float(dk));
+  for (int i = 0; i < n; ++i) {
+    const int tok = t0 + i;
+    const float* proj = a.proj + tok * a.proj_stride;
+    float* yout = a.y + int64_t(tok) * a.nv * dv;
+    float* zout = a.z + int64_t(tok) * a.nv * dv;
+    for (int t = threadIdx.x; t < nch; t += blockDim.x) {
+      const int c = chan(t);
+      const float xn = proj[delta_src(a, c)];
+      float* w = win + t * (K - 1);
+      float acc = 0.f;
+      for (int j = 0; j < K - 1; ++j) acc += cw[t * K + j] * w[j];
+      acc += cw[t * K + K - 1] * xn;
+      for (int j = 0; j + 1 < K - 1; ++j) w[j] = w[j + 1];
+      if (K > 1) w[K - 2] = xn;
+      const float o = silu_ref(acc);
+      if (t < dk) q[t] = o; else if (t < 2 * dk) k[t - dk] = o; else v[t - 2 * dk] = o;
+    }
+    if (threadIdx.x == 0) {
+      int bi, ai;
+      delta_ba(a, hv, bi, ai);
+      gb[0] = expf(-expf(alog) * softplus_ref(proj[ai] + dtb));
+      gb[1] = sigmoid_ref(proj[bi]);
+    }
+    for (int d = threadIdx.x; d < RB; d += blockDim.x) zout[hv * dv + d] = silu_ref(proj[delta_z(a, hv, d)]);
+    __syncthreads();
+    if (warp < 2) {
+      const float* x = warp == 0 ? q : k;
+      float ss = 0.f;
+      for (int j = lane; j < dk; j += 32) ss += x[j] * x[j];
+      ss = warp_sum(ss);
+      if (lane == 0) nrm[warp] = 1.f / sqrtf(ss / float(dk) + 1e-6f);
+    }
+    __syncthreads();
+    float qr[DELTA_EPL], kr[DELTA_EPL];
+#pragma unroll
+    for (int e = 0; e < DELTA_EPL; ++e) {
+      const int j = lane + 32 * e;
+      qr[e] = j < dk ? (q[j] * nrm[0]) * (inv * inv) : 0.f;
+      kr[e] = j < dk ? (k[j] * nrm[1]) * inv : 0.f;
+    }
+    const float g = gb[0], beta = gb[1];
+    float kv[DELTA_RPW];
+#pragma unroll
+    for (int j = 0; j < DELTA_RPW; ++j) {
+      float p = 0.f;
+#pragma unroll
+      for (int e = 0; e < DELTA_EPL; ++e) { st[j][e] *= g; p += st[j][e] * kr[e]; }
+      kv[j] = p;
+    }
+#pragma unroll
+    for (int j = 0; j < DELTA_RPW; ++j) kv[j] = warp_sum(kv[j]);
+    float y[DELTA_RPW];
+#pragma unroll
+    for (int j = 0; j < DELTA_RPW; ++j) {
+      const int r = warp + j * nw;
+      const float delta = ((r < RB ? v[r] : 0.f) - kv[j]) * beta;
+      float p = 0.f;
+#pragma unroll
+      for (int e = 0; e < DELTA_EPL; ++e) { st[j][e] += kr[e] * delta; p += st[j][e] * qr[e]; }
+      y[j] = p;
+    }
+#pragma unroll
+    for (int j = 0; j < DELTA_RPW; ++j) y[j] = warp_sum(y[j]);
+#pragma unroll
+    for (int j = 0; j < DELTA_RPW; ++j) {
+      const int r = warp + j * nw;
+      if (r < RB && lane == 0) yout[hv * dv + r] = y[j];
+    }
+    __syncthreads();  // q / k / v / gates of the next token overwrite shared memory
+  }
+  pdl_launch();
+#pragma unroll
+  for (int j = 0; j < DELTA_RPW; ++j) {
+    const int r = warp + j * nw;
+    if (r >= RB) continue;
+    float* Sr = S + (int64_t(hv) * dv + r) * dk;
+#pragma unroll
+    for (int e = 0; e < DELTA_EPL; ++e) {
+      const int i2 = lane + 32 * e;
+      if (i2 < dk) Sr[i2] = st[j][e];
+    }
+  }
+}
+
+// The conv ring after a chunk: slot p % conv_k of every channel takes the
+// input of position p for the chunk's last min(n, conv_k) positions.
+__global__ void k_conv_ring(const DeltaArgs a) {
+  pdl_wait();
+  const int s = blockIdx.x, c = blockIdx.y * blockDim.x + threadIdx.x;
+  if (c >= a.conv_dim) return;
+  const StateDev* sd = a.sd + s;
+  const int pos = *sd->pos, n = a.seq_n[s], t0 = a.seq_first[s], K = a.conv_k;
+  float* ring = sd->conv[a.layer];
+  const int src = delta_src(a, c);
+  for (int i = max(0, n - K); i < n; ++i)
+    ring[int64_t((pos + i) % K) * a.conv_dim + c] = a.proj[(t0 + i) * a.proj_stride + src];
+}
+
+// Chunked step: token z's key (RMSNorm with weight, partial NeoX RoPE at its
+// position, as in k_attn) and value into the cache of its sequence.
+__global__ void k_kv_append(const AttnArgs a) {
+  pdl_wait();
+  const int z = blockIdx.x, kvh = blockIdx.y, HD = a.hd, tid = threadIdx.x;
+  const StateDev* sd = a.sd + a.tok_seq[z];
+  const int pos = *sd->pos + a.tok_off[z];
+  const float* kin = a.knew + z * a.proj_stride + kvh * HD;
+  const float* vin = a.vnew + z * a.proj_stride + kvh * HD;
+  float* Kr = sd->kc[a.layer] + (int64_t(kvh) * sd->max_ctx + pos) * HD;
+  float* Vr = sd->vc[a.layer] + (int64_t(kvh) * sd->max_ctx + pos) * HD;
+  extern __shared__ __align__(16) float xs[];
+  __shared__ float red[32];
+  for (int i = tid; i < HD; i += blockDim.x) { xs[i] = kin[i]; Vr[i] = vin[i]; }
+  float ss = 0.f;
+  for (int i = tid; i < HD; i += blockDim.x) ss += xs[i] * xs[i];
+  ss = block_sum(ss, red);
+  const float sc0 = 1.f / sqrtf(ss / float(HD) + a.eps);
+  __syncthreads();
+  for (int i = tid; i < HD; i += blockDim.x) xs[i] *= sc0 * a.kn[i];
+  __syncthreads();
+  const int half = a.rot / 2;
+  for (int j = tid; j < half; j += blockDim.x) {
+    const float invf = powf(a.rope_theta, -float(2 * j) / float(a.rot));
+    const float ang = float(pos) * invf;
+    const float cs = cosf(ang), sn = sinf(ang);
+    const float xa = xs[j], xb = xs[half + j];
+    xs[j] = xa * cs - xb * sn;
+    xs[half + j] = xb * cs + xa * sn;
+  }
+  __syncthreads();
+  for (int i = tid; i < HD; i += blockDim.x) Kr[i] = xs[i];
+}
+
 // ----------------------------------------------------------- attention ----
 // Gated GQA decode for one token: q/k RMSNorm with weight, partial NeoX
 // RoPE, KV append, causal softmax(q k^T / sqrt(hd)) v, times sigmoid(gate)
@@ -262,9 +445,12 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
   __shared__ __align__(8) uint64_t full[RING];
   __shared__ unsigned last_flag;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = ATTN_THREADS / 32;
-  // sequence blockIdx.z of a batched step (0 for one sequence)
+  // sequence blockIdx.z of a batched step (0 for one sequence); in a chunked
+  // step blockIdx.z is a token of sequence tok_seq[z] whose keys and values
+  // are all in the cache already
   const int seq = blockIdx.z;
-  const StateDev* sd = a.sd + seq;
+  const bool cached = a.tok_seq != nullptr;
+  const StateDev* sd = a.sd + (cached ? a.tok_seq[seq] : seq);
   const float* qout = a.qout + seq * a.proj_stride;
   const float* knew = a.knew + seq * a.proj_stride;
   const float* vnew = a.vnew + seq * a.proj_stride;
@@ -274,7 +460,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
   unsigned* actr = a.counters + seq * a.Hkv * ATTN_CL;
   TraceRec trc;
   trc.start(a.trace);
-  const int pos = *sd->pos;  // written by the previous token: complete
+  const int pos = *sd->pos + (cached ? a.tok_off[seq] : 0);  // written by an earlier step: complete
   const int ctx = pos + 1;
   const int per = max(ATTN_MINP, (ctx + a.nchunks - 1) / a.nchunks);
   const int nvalid = (ctx + per - 1) / per;               // busy chunks (<= nchunks)
@@ -295,7 +481,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
   // position, which is always the chunk's last) by two bulk copies
   auto issue = [=](int t) {
     const int t0 = p0 + t * ATTN_TP, nt = min(ATTN_TP, p0 + n - t0);
-    const int nc = pos < t0 + nt ? nt - 1 : nt;
+    const int nc = !cached && pos < t0 + nt ? nt - 1 : nt;
     float* kt = ring + (t % RING) * SLOT;
     uint64_t* bar = fb + t % RING;
     const unsigned bytes = unsigned(nc) * HD * 4;
@@ -308,7 +494,10 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
   if (tid == 0) {
     for (int s = 0; s < RING; ++s) mbar_init(&full[s], 1);
     mbar_init_fence();
-    for (int t = 0; t < min(RING, ntiles); ++t) issue(t);
+    // the chunk's own rows were written by the previous kernel: in a chunked
+    // step the first copies wait for it
+    if (!cached)
+      for (int t = 0; t < min(RING, ntiles); ++t) issue(t);
   }
   // before the wait: RoPE table, norm weights, softmax state
   for (int j = tid; j < half; j += ATTN_THREADS) {
@@ -329,6 +518,8 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
   __syncthreads();  // RoPE table and barrier initialisation visible to all
   pdl_wait();
   trc.waited(a.trace);
+  if (cached && tid == 0)
+    for (int t = 0; t < min(RING, ntiles); ++t) issue(t);
   for (int i = tid; i < HD; i += ATTN_THREADS) vn[i] = __ldcg(vnew + kvh * HD + i);
   // gate values of the combine slice (used if this CTA writes the output)
   float gate[ATTN_KO];
@@ -393,7 +584,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
   }
   __syncthreads();
   pdl_launch();
-  if (chunk == 0)
+  if (chunk == 0 && !cached)
     for (int i = tid; i < HD; i += ATTN_THREADS) {
       const_cast<float*>(Kc)[int64_t(pos) * HD + i] = kn[i];
       const_cast<float*>(Vc)[int64_t(pos) * HD + i] = vn[i];
@@ -410,7 +601,7 @@ __global__ void __launch_bounds__(ATTN_THREADS) k_attn(const AttnArgs a) {
     float* vt = kt + ATTN_TP * HD;
     const int t0 = p0 + t * ATTN_TP, nt = min(ATTN_TP, p0 + n - t0);
     if (!mbar_wait(&full[t % RING], unsigned(t / RING) & 1u)) ok = false;
-    if (pos < t0 + nt)  // the new position (the last row): its key and value
+    if (!cached && pos < t0 + nt)  // the new position (the last row): its key and value
       for (int i = tid; i < HD; i += ATTN_THREADS) {
         kt[(pos - t0) * HD + i] = kn[i];
         vt[(pos - t0) * HD + i] = vn[i];
@@ -662,6 +853,24 @@ void launch_delta_batch(const DeltaArgs& a, int T, cudaStream_t st, bool pdl) {
   const int nch = 2 * a.dk + a.rows_per_block;
   const size_t smem = size_t(2 * a.dk + a.rows_per_block + nch * (2 * a.conv_k - 1)) * 4;
   launch(k_delta, dim3(a.nv, a.dv / a.rows_per_block, T), dim3(threads), smem, st, pdl, a);
+}
+
+void launch_delta_seq(const DeltaArgs& a, int S, cudaStream_t st, bool pdl) {
+  const int threads = std::max(DELTA_THREADS, 32 * ((a.dv + DELTA_RPW - 1) / DELTA_RPW));
+  if (a.dk > 32 * DELTA_EPL || threads > DELTA_MAX_THREADS || !a.seq_first || !a.seq_n)
+    throw Error(ERR_UNSUPPORTED, "DeltaNet head dims outside the chunked kernel's range");
+  const int nch = 2 * a.dk + a.dv;
+  const size_t smem = size_t(2 * a.dk + a.dv + nch * (2 * a.conv_k - 1)) * 4;
+  launch(k_delta_seq, dim3(a.nv, S), dim3(threads), smem, st, pdl, a);
+}
+
+void launch_conv_ring(const DeltaArgs& a, int S, cudaStream_t st, bool pdl) {
+  launch(k_conv_ring, dim3(S, (a.conv_dim + 255) / 256), dim3(256), 0, st, pdl, a);
+}
+
+void launch_kv_append(const AttnArgs& a, int T, cudaStream_t st, bool pdl) {
+  if (!a.tok_seq || !a.tok_off) throw Error(ERR_INVALID, "kv append needs the token map");
+  launch(k_kv_append, dim3(T, a.Hkv), dim3(128), size_t(a.hd) * 4, st, pdl, a);
 }
 
 void launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl, int T) {

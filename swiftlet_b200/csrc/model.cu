@@ -93,8 +93,11 @@ struct BatchBufs {
   uint2 *bt_a = nullptr, *bt_b = nullptr;
   float2 *meta_a = nullptr, *meta_b = nullptr;
   StateDev* sds = nullptr;
+  // chunked steps (several consecutive tokens of a sequence in one launch):
+  // token -> (sequence, offset), sequence -> (first token, count)
+  int *tok_seq = nullptr, *tok_off = nullptr, *seq_first = nullptr, *seq_n = nullptr;
   int64_t projn = 0, hmid_stride = 0;
-  std::map<int, cudaGraphExec_t> graphs;  // per batch size
+  std::map<int, cudaGraphExec_t> graphs;  // per (tokens, sequences, chunked)
 };
 
 struct Model {
@@ -181,8 +184,14 @@ struct Model {
   // descriptors in bb.sds); logits [T][vocab] in bb.logits, greedy in bb.greedy
   bool batch_supported();
   void ensure_batch();
-  void enqueue_batch(int T, cudaStream_t st);
-  void run_batch(State* const* s, int T);
+  void enqueue_batch(int T, int S, bool chunked, cudaStream_t st);
+  // S sequences consume counts[i] tokens each (T in total, already in
+  // bb.tokens, sequence-major)
+  void run_batch(State* const* s, int S, const int* counts, int T);
+  // Runs token lists of several sequences through run_batch launches of at
+  // most BT_MAX tokens; logits of each sequence's last token go to
+  // logits_out[i] (host, may be null) and its greedy id to greedy_out[i]
+  void run_packed(State* const* s, int nseq, const int32_t* tokens, const int* counts, float* logits_out);
   void bdense(const std::vector<std::pair<QLin, float*>>& segs, int64_t y_stride, int mode, const uint2* bt,
               const float2* meta, int T, cudaStream_t st);
   // Throws when a kernel of the last steps reported a bounded wait that gave
@@ -840,6 +849,7 @@ void Model::ensure_batch() {
   bb.bt_b = reinterpret_cast<uint2*>(dmalloc(size_t(slots) * (c.moe_inter / 32 + 1) * 12 * sizeof(uint2)));
   bb.meta_b = reinterpret_cast<float2*>(dmalloc(size_t(slots) * (c.moe_inter / 32 + 1) * sizeof(float2)));
   bb.sds = reinterpret_cast<StateDev*>(dmalloc(size_t(T) * sizeof(StateDev)));
+  bb.tok_seq = i4(T); bb.tok_off = i4(T); bb.seq_first = i4(T); bb.seq_n = i4(T);
   bb.ready = true;
 }
 
@@ -873,7 +883,7 @@ void Model::bdense(const std::vector<std::pair<QLin, float*>>& segs, int64_t y_s
   }
 }
 
-void Model::enqueue_batch(int T, cudaStream_t st) {
+void Model::enqueue_batch(int T, int S, bool chunked, cudaStream_t st) {
   const ModelConfig& c = cfg;
   const int D = c.hidden, K = c.topk, E = c.experts, H = c.heads, hd = c.head_dim;
   const int slots = T * (K + 1);
@@ -903,7 +913,13 @@ void Model::enqueue_batch(int T, cudaStream_t st) {
       d.dt_bias = ld.dt_bias; d.sd = bb.sds; d.layer = l; d.rows_per_block = c.dv <= 128 ? c.dv : 32; d.y = bb.yv;
       d.z = bb.zv;
       d.trace = tagged(16u * unsigned(l + 1) + 3);
-      launch_delta_batch(d, T, st, pdl);
+      if (chunked) {
+        d.seq_first = bb.seq_first; d.seq_n = bb.seq_n;
+        launch_delta_seq(d, S, st, pdl);
+        launch_conv_ring(d, S, st, pdl);
+      } else {
+        launch_delta_batch(d, T, st, pdl);
+      }
       digit(bb.yv, c.value_dim(), T, c.value_dim(), ld.out_lin.gs, PRO_GATEDNORM, bb.zv, ld.dnorm, c.dv, nullptr,
             bb.bt_a, bb.meta_a);
     } else {
@@ -914,6 +930,10 @@ void Model::enqueue_batch(int T, cudaStream_t st) {
       a.H = H; a.Hkv = c.kv_heads; a.hd = hd; a.nchunks = attn_chunks; a.chunk_cap = chunk_cap;
       a.sd = bb.sds; a.layer = l; a.part = bb.part; a.counters = bb.ctr; a.out = bb.att; a.status = kstatus;
       a.trace = tagged(16u * unsigned(l + 1) + 3);
+      if (chunked) {
+        a.tok_seq = bb.tok_seq; a.tok_off = bb.tok_off;
+        launch_kv_append(a, T, st, pdl);
+      }
       launch_attn(a, st, pdl, T);
       digit(bb.att, int64_t(H) * hd, T, H * hd, ld.out_lin.gs, PRO_COPY, nullptr, nullptr, 0, nullptr, bb.bt_a,
             bb.meta_a);
@@ -951,29 +971,96 @@ void Model::enqueue_batch(int T, cudaStream_t st) {
     cb.T = T; cb.K = K; cb.D = D;
     launch_bcombine(cb, st, pdl);
   }
-  launch_badvance(bb.sds, T, st, pdl);
+  launch_badvance(bb.sds, S, chunked ? bb.seq_n : nullptr, st, pdl);
   digit(bb.h, D, T, D, lm_head.gs, PRO_RMSNORM, final_norm, nullptr, 0, nullptr, bb.bt_a, bb.meta_a);
   bdense({{lm_head, bb.logits}}, c.vocab, BM_STORE, bb.bt_a, bb.meta_a, T, st);
   launch_bargmax(bb.logits, T, c.vocab, bb.greedy, st, pdl);
 }
 
-// T sequences with their tokens already in bb.tokens.
-void Model::run_batch(State* const* s, int T) {
-  if (T < 1 || T > BT_MAX) throw Error(ERR_INVALID, "batched step of 1.." + std::to_string(BT_MAX) + " sequences");
+// S sequences consume counts[i] tokens each (T in total, in bb.tokens,
+// sequence-major). One token per sequence takes the decode kernels; longer
+// runs take the chunked mixers.
+void Model::run_batch(State* const* s, int S, const int* counts, int T) {
+  if (T < 1 || T > BT_MAX || S < 1 || S > T) throw Error(ERR_INVALID, "batched step of 1.." + std::to_string(BT_MAX) + " tokens");
   ensure_batch();
-  std::vector<StateDev> sd(T);
-  for (int t = 0; t < T; ++t) sd[t] = s[t]->host_desc;
-  SWL_CUDA(cudaMemcpyAsync(bb.sds, sd.data(), size_t(T) * sizeof(StateDev), cudaMemcpyHostToDevice, stream));
+  std::vector<StateDev> sd(S);
+  bool chunked = false;
+  for (int i = 0; i < S; ++i) {
+    sd[i] = s[i]->host_desc;
+    chunked = chunked || counts[i] > 1;
+  }
+  SWL_CUDA(cudaMemcpyAsync(bb.sds, sd.data(), size_t(S) * sizeof(StateDev), cudaMemcpyHostToDevice, stream));
+  if (chunked) {
+    std::vector<int> maps(2 * size_t(T) + 2 * size_t(S));
+    int* tseq = maps.data();
+    int* toff = tseq + T;
+    int* sfirst = toff + T;
+    int* sn = sfirst + S;
+    int t = 0;
+    for (int i = 0; i < S; ++i) {
+      sfirst[i] = t;
+      sn[i] = counts[i];
+      for (int j = 0; j < counts[i]; ++j, ++t) { tseq[t] = i; toff[t] = j; }
+    }
+    SWL_CUDA(cudaMemcpyAsync(bb.tok_seq, tseq, size_t(T) * 4, cudaMemcpyHostToDevice, stream));
+    SWL_CUDA(cudaMemcpyAsync(bb.tok_off, toff, size_t(T) * 4, cudaMemcpyHostToDevice, stream));
+    SWL_CUDA(cudaMemcpyAsync(bb.seq_first, sfirst, size_t(S) * 4, cudaMemcpyHostToDevice, stream));
+    SWL_CUDA(cudaMemcpyAsync(bb.seq_n, sn, size_t(S) * 4, cudaMemcpyHostToDevice, stream));
+  }
   if (use_graph) {
-    auto it = bb.graphs.find(T);
-    if (it == bb.graphs.end()) it = bb.graphs.emplace(T, capture(stream, [&] { enqueue_batch(T, stream); })).first;
+    const int key = chunked ? (1 << 20) | (T << 8) | S : T;
+    auto it = bb.graphs.find(key);
+    if (it == bb.graphs.end())
+      it = bb.graphs.emplace(key, capture(stream, [&] { enqueue_batch(T, S, chunked, stream); })).first;
     SWL_CUDA(cudaGraphLaunch(it->second, stream));
   } else {
-    enqueue_batch(T, stream);
+    enqueue_batch(T, S, chunked, stream);
   }
-  for (int t = 0; t < T; ++t) s[t]->pos += 1;
+  for (int i = 0; i < S; ++i) s[i]->pos += counts[i];
   stepped = true;
   hits += int64_t(T) * cfg.topk * cfg.layers;
+}
+
+void Model::run_packed(State* const* s, int nseq, const int32_t* tokens, const int* counts, float* logits_out) {
+  const int64_t V = cfg.vocab;
+  std::vector<int64_t> first(nseq);
+  int64_t off = 0;
+  for (int i = 0; i < nseq; ++i) { first[i] = off; off += counts[i]; }
+  std::vector<int> done(nseq, 0);
+  ensure_batch();
+  for (;;) {
+    std::vector<int> seqs, take;
+    int T = 0;
+    for (int i = 0; i < nseq && T < BT_MAX; ++i) {
+      const int rem = counts[i] - done[i];
+      if (rem <= 0) continue;
+      const int n = std::min(rem, BT_MAX - T);
+      seqs.push_back(i);
+      take.push_back(n);
+      T += n;
+    }
+    if (seqs.empty()) break;
+    const int S = int(seqs.size());
+    std::vector<int32_t> tok(T);
+    std::vector<State*> ss(S);
+    int t = 0;
+    for (int j = 0; j < S; ++j) {
+      const int i = seqs[j];
+      ss[j] = s[i];
+      for (int u = 0; u < take[j]; ++u) tok[t++] = tokens[first[i] + done[i] + u];
+    }
+    SWL_CUDA(cudaMemcpyAsync(bb.tokens, tok.data(), size_t(T) * 4, cudaMemcpyHostToDevice, stream));
+    run_batch(ss.data(), S, take.data(), T);
+    t = 0;
+    for (int j = 0; j < S; ++j) {
+      const int i = seqs[j];
+      t += take[j];
+      done[i] += take[j];
+      if (done[i] == counts[i] && logits_out)
+        SWL_CUDA(cudaMemcpyAsync(logits_out + int64_t(i) * V, bb.logits + int64_t(t - 1) * V, size_t(V) * 4,
+                                 cudaMemcpyDeviceToHost, stream));
+    }
+  }
 }
 
 static State* new_state(Model* m, int max_ctx) {
@@ -1128,6 +1215,19 @@ int swl_step(swl_model* model, swl_state* state, const int32_t* tokens, int32_t 
   if (state->s.model != &m) throw Error(ERR_INVALID, "state belongs to another model");
   SWL_CUDA(cudaSetDevice(m.device));
   check_tokens(m, tokens, n);
+  if (n >= 2 && m.batch_supported()) {
+    // prefill in chunks of up to BT_MAX tokens through the batched kernels
+    if (state->s.pos + n > state->s.max_ctx)
+      throw Error(ERR_CAPACITY, "context capacity exceeded (max_ctx " + std::to_string(state->s.max_ctx) + ")");
+    State* sp = &state->s;
+    const int cnt = n;
+    m.run_packed(&sp, 1, tokens, &cnt, logits_out);
+    int status = 0;
+    SWL_CUDA(cudaMemcpyAsync(&status, m.kstatus, 4, cudaMemcpyDeviceToHost, m.stream));
+    SWL_CUDA(cudaStreamSynchronize(m.stream));
+    m.check_status(&status);
+    return SWL_OK;
+  }
   m.ensure_tokens(n);
   memcpy(m.h_tokens, tokens, size_t(n) * 4);
   SWL_CUDA(cudaMemcpyAsync(m.tokens, m.h_tokens, size_t(n) * 4, cudaMemcpyHostToDevice, m.stream));
@@ -1151,7 +1251,6 @@ int swl_step_batch(swl_model* model, swl_state** states, const int32_t* tokens, 
   SWL_CUDA(cudaSetDevice(m.device));
   std::vector<int64_t> first(nseq);
   int64_t off = 0;
-  int maxc = 0;
   for (int i = 0; i < nseq; ++i) {
     if (!states[i]) throw Error(ERR_INVALID, "null state");
     if (states[i]->s.model != &m) throw Error(ERR_INVALID, "state belongs to another model");
@@ -1163,7 +1262,6 @@ int swl_step_batch(swl_model* model, swl_state** states, const int32_t* tokens, 
       throw Error(ERR_CAPACITY, "context capacity exceeded (max_ctx " + std::to_string(states[i]->s.max_ctx) + ")");
     first[i] = off;
     off += counts[i];
-    maxc = std::max(maxc, counts[i]);
   }
   if (nseq < 2 || !m.batch_supported()) {
     for (int i = 0; i < nseq; ++i) {
@@ -1172,31 +1270,9 @@ int swl_step_batch(swl_model* model, swl_state** states, const int32_t* tokens, 
     }
     return SWL_OK;
   }
-  const int64_t V = m.cfg.vocab;
-  for (int r = 0; r < maxc; ++r) {
-    std::vector<int> active;
-    for (int i = 0; i < nseq; ++i)
-      if (counts[i] > r) active.push_back(i);
-    for (size_t b0 = 0; b0 < active.size(); b0 += BT_MAX) {
-      const int T = int(std::min<size_t>(BT_MAX, active.size() - b0));
-      std::vector<int32_t> tok(T);
-      std::vector<State*> ss(T);
-      for (int t = 0; t < T; ++t) {
-        const int i = active[b0 + t];
-        tok[t] = tokens[first[i] + r];
-        ss[t] = &states[i]->s;
-      }
-      m.ensure_batch();
-      SWL_CUDA(cudaMemcpyAsync(m.bb.tokens, tok.data(), size_t(T) * 4, cudaMemcpyHostToDevice, m.stream));
-      m.run_batch(ss.data(), T);
-      for (int t = 0; t < T; ++t) {
-        const int i = active[b0 + t];
-        if (counts[i] == r + 1)
-          SWL_CUDA(cudaMemcpyAsync(logits_out + int64_t(i) * V, m.bb.logits + int64_t(t) * V, size_t(V) * 4,
-                                   cudaMemcpyDeviceToHost, m.stream));
-      }
-    }
-  }
+  std::vector<State*> ss(nseq);
+  for (int i = 0; i < nseq; ++i) ss[i] = &states[i]->s;
+  m.run_packed(ss.data(), nseq, tokens, counts, logits_out);
   int status = 0;
   SWL_CUDA(cudaMemcpyAsync(&status, m.kstatus, 4, cudaMemcpyDeviceToHost, m.stream));
   SWL_CUDA(cudaStreamSynchronize(m.stream));
@@ -1230,9 +1306,10 @@ int swl_step_batch_device(swl_model* model, swl_state** states, int32_t nseq, co
   for (int b0 = 0; b0 < nseq; b0 += BT_MAX) {
     const int T = std::min(BT_MAX, nseq - b0);
     std::vector<State*> ss(T);
+    std::vector<int> ones(T, 1);
     for (int t = 0; t < T; ++t) ss[t] = &states[b0 + t]->s;
     SWL_CUDA(cudaMemcpyAsync(m.bb.tokens, d_tokens + b0, size_t(T) * 4, cudaMemcpyDeviceToDevice, m.stream));
-    m.run_batch(ss.data(), T);
+    m.run_batch(ss.data(), T, ones.data(), T);
     if (d_logits)
       SWL_CUDA(cudaMemcpyAsync(d_logits + int64_t(b0) * V, m.bb.logits, size_t(T) * V * 4, cudaMemcpyDeviceToDevice,
                                m.stream));

@@ -20,6 +20,14 @@ pytestmark = pytest.mark.gpu
 MAX_ABS, REL_L2 = 2e-2, 1e-3
 
 
+def stepwise(gpu, tokens, state):
+    """Logits after feeding `tokens` one at a time through the single-token
+    decode kernels (the reference for chunked steps)."""
+    for t in tokens:
+        lg = gpu.step([t], state)
+    return lg
+
+
 def assert_close(got, ref, what):
     err = float(np.abs(got - ref).max())
     rel = float(np.linalg.norm(got - ref) / (np.linalg.norm(ref) + 1e-30))
@@ -96,7 +104,7 @@ def test_full_batch_matches_single_sequence_path(synth, nseq):
     ss = [gpu.new_state(16) for _ in range(nseq)]
     bl = gpu.step_batch(prompts, bs)
     for i, p in enumerate(prompts):
-        assert_close(bl[i], gpu.step(p, ss[i]), f"prompt {i}")
+        assert_close(bl[i], stepwise(gpu, p, ss[i]), f"prompt {i}")
     toks = rng.integers(0, V, nseq).tolist()
     bl = gpu.step_batch([[t] for t in toks], bs)
     for i in range(nseq):
@@ -116,9 +124,36 @@ def test_long_context_batch_matches_single_sequence_path(synth):
     ss = [gpu.new_state(512) for _ in prompts]
     bl = gpu.step_batch(prompts, bs)
     for i, p in enumerate(prompts):
-        assert_close(bl[i], gpu.step(p, ss[i]), f"prompt {i}")
+        assert_close(bl[i], stepwise(gpu, p, ss[i]), f"prompt {i}")
+    # decode continues from the chunked contexts
+    toks = [int(np.argmax(r)) for r in bl]
+    bl = gpu.step_batch([[t] for t in toks], bs)
+    for i in range(len(prompts)):
+        assert_close(bl[i], gpu.step([toks[i]], ss[i]), f"decode {i}")
     for s in bs + ss:
         s.free()
+
+
+@pytest.mark.parametrize("n", [2, 63, 64, 65, 130])
+def test_chunked_prefill_matches_stepwise(synth, n):
+    """A single sequence's prompt through swl_step runs in chunks of up to 64
+    tokens (one weight stream per chunk, the recurrence in order inside the
+    chunk); it matches feeding the tokens one at a time, and decoding goes on
+    from the same state."""
+    _, _, gpu = synth
+    V = gpu.config.vocab_size
+    rng = np.random.default_rng(1000 + n)
+    prompt = rng.integers(0, V, n).tolist()
+    a, b = gpu.new_state(256), gpu.new_state(256)
+    la = gpu.step(prompt, a)
+    assert a.position == n
+    assert_close(la, stepwise(gpu, prompt, b), f"prefill {n}")
+    for step in range(2):
+        t = int(np.argmax(la))
+        la, lb = gpu.step([t], a), gpu.step([t], b)
+        assert_close(la, lb, f"decode {step} after prefill {n}")
+    a.free()
+    b.free()
 
 
 def test_device_batch_greedy_feedback(synth):
