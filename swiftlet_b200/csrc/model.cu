@@ -1029,17 +1029,27 @@ void Model::run_packed(State* const* s, int nseq, const int32_t* tokens, const i
   std::vector<int> done(nseq, 0);
   ensure_batch();
   for (;;) {
+    // an equal share of the launch per sequence that has tokens left (the
+    // recurrences of a launch run in parallel over sequences, in order within
+    // one), then the remaining capacity to the same sequences in order
     std::vector<int> seqs, take;
-    int T = 0;
+    int T = 0, active = 0;
+    for (int i = 0; i < nseq; ++i) active += counts[i] > done[i];
+    if (!active) break;
+    const int share = std::max(1, BT_MAX / active);
     for (int i = 0; i < nseq && T < BT_MAX; ++i) {
       const int rem = counts[i] - done[i];
       if (rem <= 0) continue;
-      const int n = std::min(rem, BT_MAX - T);
+      const int n = std::min({rem, share, BT_MAX - T});
       seqs.push_back(i);
       take.push_back(n);
       T += n;
     }
-    if (seqs.empty()) break;
+    for (size_t j = 0; j < seqs.size() && T < BT_MAX; ++j) {
+      const int extra = std::min(counts[seqs[j]] - done[seqs[j]] - take[j], BT_MAX - T);
+      take[j] += extra;
+      T += extra;
+    }
     const int S = int(seqs.size());
     std::vector<int32_t> tok(T);
     std::vector<State*> ss(S);
