@@ -605,9 +605,15 @@ static bool bg_fast_layout(const BGLayout& L) { return L.kc == 256 && L.kpg == 2
 template <int BITS, int DT, bool FAST>
 static int bg_grid_for(int smem) {
   static int cached[64] = {0};
+  static bool opened = false;
   const int key = std::min(63, smem >> 12);
+  if (!opened) {
+    // the ceiling once, at the largest layout any launch uses: launches of
+    // one instantiation differ in size, and a lower ceiling would reject them
+    SWL_CUDA(cudaFuncSetAttribute(k_bgemm<BITS, DT, FAST>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+    opened = true;
+  }
   if (!cached[key]) {
-    SWL_CUDA(cudaFuncSetAttribute(k_bgemm<BITS, DT, FAST>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     int per = 0;
     SWL_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_bgemm<BITS, DT, FAST>, BG_THREADS, smem));
     cached[key] = std::max(1, per);
