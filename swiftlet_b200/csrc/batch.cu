@@ -720,21 +720,22 @@ __global__ void __launch_bounds__(BR_THREADS) k_broute(const BRouteArgs a) {
   }
   const int rbg = (a.inter + 31) / 32, rbd = (a.hidden + 63) / 64, rbs = (a.shared_inter + 31) / 32;
   const int ntt_s = (T + BG_TOK - 1) / BG_TOK;
-  for (int e = tid; e < E; e += BR_THREADS) {
-    const int c = __popcll(msk[e]);
-    const int ntt = (c + BG_TOK - 1) / BG_TOK;
-    for (int tt = 0; tt < ntt; ++tt) {
-      const int s0 = off[e] + tt * BG_TOK, cnt = min(BG_TOK, c - tt * BG_TOK);
-      for (int rb = 0; rb < rbg; ++rb) {
-        const int i = tb[e] * rbg + rb * ntt + tt;
-        if (i < a.max_gu) a.items_gu[i] = make_int4(e, rb * 32, s0, cnt);
-      }
-      for (int rb = 0; rb < rbd; ++rb) {
-        const int i = tb[e] * rbd + rb * ntt + tt;
-        if (i < a.max_dn) a.items_dn[i] = make_int4(e, rb * 64, s0, cnt);
-      }
+  // item i of a list belongs to the expert e with tb[e] * rb_n <= i <
+  // tb[e + 1] * rb_n (binary search over the tile prefix sums); every thread
+  // writes items, not one thread per expert
+  auto routed_item = [&](int i, int rb_n, int rows) {
+    int lo = 0, hi = E;
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (tb[mid] * rb_n <= i) lo = mid;
+      else hi = mid;
     }
-  }
+    const int e = lo, c = __popcll(msk[e]), ntt = (c + BG_TOK - 1) / BG_TOK;
+    const int r = i - tb[e] * rb_n, rb = r / ntt, tt = r - rb * ntt;
+    return make_int4(e, rb * rows, off[e] + tt * BG_TOK, min(BG_TOK, c - tt * BG_TOK));
+  };
+  for (int i = tid; i < min(tb[E] * rbg, a.max_gu); i += BR_THREADS) a.items_gu[i] = routed_item(i, rbg, 32);
+  for (int i = tid; i < min(tb[E] * rbd, a.max_dn); i += BR_THREADS) a.items_dn[i] = routed_item(i, rbd, 64);
   const int base_gu = tb[E] * rbg, base_dn = tb[E] * rbd;
   for (int i = tid; i < ntt_s * rbs; i += BR_THREADS) {
     const int rb = i / ntt_s, tt = i - rb * ntt_s;
