@@ -184,6 +184,22 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def max_over_ranks(values, dist, device) -> list:
+    """Elapsed times of this rank -> their maximum over all ranks (every rank
+    runs the same collective: a replica run is as slow as its slowest GPU)."""
+    import torch
+    t = torch.tensor([float(v) for v in values], dtype=torch.float64, device=device)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def replica_rate(world: int, units_per_rank: float, max_ms: float) -> float:
+    """Whole-job throughput of `world` replicas: all units over the slowest
+    rank's time."""
+    return world * units_per_rank / (max_ms / 1000.0)
+
+
 def expected_unique_experts(E: int, K: int, B: int) -> float:
     """Expected distinct experts per layer when B tokens each pick K of E
     uniformly (the synthetic router's logits are i.i.d.)."""
@@ -231,10 +247,7 @@ def batched_decode(model, cfg, stream, args, rank, local, dist) -> dict:
     ev[5].record(stream)
     torch.cuda.synchronize()
     e2e_ms = ev[4].elapsed_time(ev[5])
-    t = torch.tensor([ms, e2e_ms], dtype=torch.float64, device=f"cuda:{local}")
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, e2e_ms = t.tolist()
+    ms, e2e_ms = max_over_ranks([ms, e2e_ms], dist, f"cuda:{local}")
     for s in states:
         s.free()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -248,7 +261,7 @@ def batched_decode(model, cfg, stream, args, rank, local, dist) -> dict:
     hbm = float(peaks["hbm_gbs"])
     step_s = ms / steps / 1000.0
     return {
-        "B": B, "value": world * B * steps / (ms / 1000.0), "unit": "tok/s", "steps": steps,
+        "B": B, "value": replica_rate(world, B * steps, ms), "unit": "tok/s", "steps": steps,
         "ms_per_step": ms / steps, "prompt": args.batch_prompt,
         "prefill": {"tokens": B * args.batch_prompt, "ms": prefill_ms,
                     "tok_s": B * args.batch_prompt / (prefill_ms / 1000.0),
@@ -258,7 +271,7 @@ def batched_decode(model, cfg, stream, args, rank, local, dist) -> dict:
                           "peak_kind": peak_kind,
                           "bytes": "dense weights once + (expected distinct routed experts %.1f + shared) blobs per "
                                    "layer + per-sequence delta state r/w, conv ring and f32 KV" % uniq},
-        "e2e": {"value": world * B * e2e_steps / (e2e_ms / 1000.0), "unit": "tok/s",
+        "e2e": {"value": replica_rate(world, B * e2e_steps, e2e_ms), "unit": "tok/s",
                 "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B * cfg.vocab_size},
         "gpu_launches_per_step": 3 + 11 * L + 3,
         "clocks": clk.summary(),
@@ -352,10 +365,7 @@ def run_ours(args) -> None:
     # roofline of the dominant kernels: the fused expert GEMV pair, swept over all layers
     sweep_iters = 4
     sweep_ms, bytes_layer, sweep_launches = model.bench_expert_sweep(sweep_iters)
-    t = torch.tensor([ms, e2e_ms, sweep_ms], dtype=torch.float64, device=f"cuda:{local}")
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, e2e_ms, sweep_ms = t.tolist()
+    ms, e2e_ms, sweep_ms = max_over_ranks([ms, e2e_ms, sweep_ms], dist, f"cuda:{local}")
     if rank != 0:
         model.close()
         if dist:
@@ -366,7 +376,7 @@ def run_ours(args) -> None:
     hbm = float(peaks["hbm_gbs"])
     ctx_mean = args.prompt + args.warmup + args.steps / 2
     bt = algorithmic_bytes_per_token(cfg, ctx_mean)
-    value = world * args.steps / (ms / 1000.0)
+    value = replica_rate(world, args.steps, ms)
     per_launch_s = sweep_ms / 1000.0 / (sweep_iters * cfg.num_hidden_layers)
     achieved = bytes_layer / per_launch_s / 1e9
     traffic = profile_traffic().get("moe_expert_pair_bytes_per_layer")
@@ -390,7 +400,7 @@ def run_ours(args) -> None:
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "bytes_per_launch_pair": bytes_layer, "avg_pair_us": per_launch_s * 1e6,
                      "traffic": traffic, "peak_kind": peak_kind},
-        "e2e": {"value": world * e2e_steps / (e2e_ms / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": 4,
+        "e2e": {"value": replica_rate(world, e2e_steps, e2e_ms), "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4 * cfg.vocab_size},
         "gpu_launches": launches_per_token * args.steps,
         "clocks": clk.summary(),
