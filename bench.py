@@ -36,11 +36,12 @@ PROMPT_SEED = 4242
 MODEL_SEED = 35
 
 
-def model_dir(tmp: str, layers: int | None = None) -> str:
+def model_dir(tmp: str, layers: int | None = None, model: str = "35b") -> str:
     from swiftlet_b200 import formats
-    from swiftlet_b200.configs import Q35_35B, with_layers
-    cfg = with_layers(Q35_35B, layers) if layers else Q35_35B
-    return formats.write_synthetic(os.path.join(tmp, "q35-35b-synth"), cfg, seed=MODEL_SEED)
+    from swiftlet_b200.configs import NEXT_80B, Q35_35B, with_layers
+    base = NEXT_80B if model == "80b" else Q35_35B
+    cfg = with_layers(base, layers) if layers else base
+    return formats.write_synthetic(os.path.join(tmp, f"synth-{model}"), cfg, seed=MODEL_SEED)
 
 
 def algorithmic_bytes_per_token(cfg, ctx: float) -> dict:
@@ -216,12 +217,15 @@ def batched_decode(model, cfg, stream, args, rank, local, dist) -> dict:
     B = args.batch
     steps, e2e_steps = args.batch_steps, min(args.batch_steps, 8)
     rng = np.random.default_rng(PROMPT_SEED + 1000 + rank)
-    max_ctx = args.batch_prompt + args.warmup + steps + e2e_steps + 8
-    states = [model.new_state(max_ctx=max_ctx) for _ in range(B)]
-    prompts = rng.integers(0, cfg.vocab_size, (B, args.batch_prompt)).astype(np.int32)
+    # prompt lengths: all args.batch_prompt, or uniform in [batch_prompt, batch_prompt_max] (ragged)
+    hi = max(args.batch_prompt, args.batch_prompt_max or 0)
+    lens = rng.integers(args.batch_prompt, hi + 1, B) if hi > args.batch_prompt else np.full(B, args.batch_prompt)
+    extra = args.warmup + steps + e2e_steps + 8
+    states = [model.new_state(max_ctx=int(n) + extra) for n in lens]
+    prompts = [rng.integers(0, cfg.vocab_size, int(n)).astype(np.int32) for n in lens]
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
     ev[0].record(stream)
-    logits = model.step_batch(list(prompts), states)
+    logits = model.step_batch(prompts, states)
     ev[1].record(stream)
     torch.cuda.synchronize()
     prefill_ms = ev[0].elapsed_time(ev[1])
@@ -251,7 +255,7 @@ def batched_decode(model, cfg, stream, args, rank, local, dist) -> dict:
     for s in states:
         s.free()
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    bt = algorithmic_bytes_per_token(cfg, args.batch_prompt + args.warmup + steps / 2)
+    bt = algorithmic_bytes_per_token(cfg, float(np.mean(lens)) + args.warmup + steps / 2)
     L = cfg.num_hidden_layers
     uniq = expected_unique_experts(cfg.num_experts, cfg.num_experts_per_tok, B)
     per_seq = bt["delta_state"] + bt["conv_ring"] + bt["kv"] + bt["embed_row"]
@@ -262,9 +266,9 @@ def batched_decode(model, cfg, stream, args, rank, local, dist) -> dict:
     step_s = ms / steps / 1000.0
     return {
         "B": B, "value": replica_rate(world, B * steps, ms), "unit": "tok/s", "steps": steps,
-        "ms_per_step": ms / steps, "prompt": args.batch_prompt,
-        "prefill": {"tokens": B * args.batch_prompt, "ms": prefill_ms,
-                    "tok_s": B * args.batch_prompt / (prefill_ms / 1000.0),
+        "ms_per_step": ms / steps, "prompt": args.batch_prompt if hi == args.batch_prompt else [args.batch_prompt, hi],
+        "prefill": {"tokens": int(lens.sum()), "ms": prefill_ms,
+                    "tok_s": float(lens.sum()) / (prefill_ms / 1000.0),
                     "mode": "packed launches of up to 64 tokens, an equal share per sequence"},
         "step_roofline": {"bound": "hbm", "bytes_per_step": step_bytes, "achieved": step_bytes / step_s / 1e9,
                           "peak": hbm, "unit": "GB/s", "frac": step_bytes / step_s / 1e9 / hbm,
@@ -294,17 +298,29 @@ def run_ours(args) -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     tmp = tempfile.mkdtemp()
-    mdir = model_dir(tmp, args.layers)
+    mdir = model_dir(tmp, args.layers, args.model)
     model = swl.QwenCUDAModel(mdir, device=local)
     cfg = model.config
     stream = torch.cuda.Stream()
     model.set_stream(stream.cuda_stream)
-    if args.batch_only:
-        # profiling: the batched leg alone (its kernels without the B=1 ones)
+    if args.batch_only or args.model == "80b":
+        # the batched leg alone: profiling, or the 80B-shaped ragged batch
+        # (BASELINE config 5 on each GPU; expert parallelism is not built, so
+        # several GPUs run replicas)
         res = batched_decode(model, cfg, stream, args, rank, local, dist)
         model.close()
         if rank == 0:
-            print(json.dumps({"metric": METRIC, "batched": res, "profiling_only": True}), flush=True)
+            line = {"metric": METRIC, "batched": res, "profiling_only": True}
+            if args.model == "80b":
+                line = {"metric": "80B-A3B q4 ragged batched decode tok/s (B=64 per GPU)", "value": res["value"],
+                        "unit": "tok/s", "n_gpus": world, "steps": res["steps"], "warmup": args.warmup,
+                        "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+                        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                        "config": {"workload": "qwen3-next-80b-a3b shape (48 layers, 512 experts top-10 + shared), q4 "
+                                               "g64, 64 sequences with seeded prompts of ragged length per GPU",
+                                   "parallelism": "replica x%d (no expert parallelism)" % world},
+                        "batched": res}
+            print(json.dumps(line), flush=True)
         if dist:
             dist.destroy_process_group()
         return
@@ -427,6 +443,10 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=64, help="sequences of the batched-decode leg (<= 1: skip it)")
     ap.add_argument("--batch-prompt", type=int, default=128)
     ap.add_argument("--batch-steps", type=int, default=32)
+    ap.add_argument("--batch-prompt-max", type=int, default=None,
+                    help="ragged prompts: lengths uniform in [--batch-prompt, this]")
+    ap.add_argument("--model", default="35b", choices=["35b", "80b"],
+                    help="80b: the Qwen3-Next-80B-shaped batched leg alone (BASELINE config 5 per GPU)")
     ap.add_argument("--batch-only", action="store_true",
                     help="profiling only: run the batched leg alone and print its numbers")
     ap.add_argument("--layers", type=int, default=None,
