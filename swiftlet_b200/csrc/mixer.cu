@@ -45,7 +45,12 @@ constexpr int DELTA_MAX_THREADS = 512; // batched launches: one CTA per (v-head,
 constexpr int DELTA_RPW = 8;  // rows per warp (RB <= 32)
 constexpr int DELTA_EPL = 4;  // state elements per lane (dk <= 128)
 
-__global__ void __launch_bounds__(DELTA_MAX_THREADS) k_delta(const DeltaArgs a) {
+// RPW rows of state per warp: 8 for single-sequence launches (128 threads per
+// 32-row slice); 16 for batched launches, whose 256-thread CTAs hold a whole
+// 128-row head and fit two per SM, so one CTA's state loads overlap another's
+// update.
+template <int RPW>
+__global__ void __launch_bounds__(RPW == 8 ? DELTA_MAX_THREADS : 256, RPW == 8 ? 1 : 2) k_delta(const DeltaArgs a) {
   extern __shared__ __align__(16) float sm[];
   const int dk = a.dk, dv = a.dv, K = a.conv_k, RB = a.rows_per_block;
   const int hv = blockIdx.x, slice = blockIdx.y, rep = a.nv / a.nk, hk = hv / rep;
@@ -82,9 +87,9 @@ __global__ void __launch_bounds__(DELTA_MAX_THREADS) k_delta(const DeltaArgs a) 
     }
     for (int j = 0; j < K; ++j) cw[t * K + j] = a.conv_w[c * K + j];
   }
-  float st[DELTA_RPW][DELTA_EPL];
+  float st[RPW][DELTA_EPL];
 #pragma unroll
-  for (int j = 0; j < DELTA_RPW; ++j) {
+  for (int j = 0; j < RPW; ++j) {
     const int r = warp + j * nw;
     const float* Sr = S + (int64_t(hv) * dv + slice * RB + r) * dk;
 #pragma unroll
@@ -140,19 +145,19 @@ __global__ void __launch_bounds__(DELTA_MAX_THREADS) k_delta(const DeltaArgs a) 
     kr[e] = i < dk ? (k[i] * nrm[1]) * inv : 0.f;
   }
   const float g = gb[0], beta = gb[1];
-  float kv[DELTA_RPW];
+  float kv[RPW];
 #pragma unroll
-  for (int j = 0; j < DELTA_RPW; ++j) {
+  for (int j = 0; j < RPW; ++j) {
     float p = 0.f;
 #pragma unroll
     for (int e = 0; e < DELTA_EPL; ++e) { st[j][e] *= g; p += st[j][e] * kr[e]; }
     kv[j] = p;
   }
 #pragma unroll
-  for (int j = 0; j < DELTA_RPW; ++j) kv[j] = warp_sum(kv[j]);
-  float y[DELTA_RPW];
+  for (int j = 0; j < RPW; ++j) kv[j] = warp_sum(kv[j]);
+  float y[RPW];
 #pragma unroll
-  for (int j = 0; j < DELTA_RPW; ++j) {
+  for (int j = 0; j < RPW; ++j) {
     const int r = warp + j * nw;
     const float delta = ((r < RB ? v[r] : 0.f) - kv[j]) * beta;
     float p = 0.f;
@@ -161,9 +166,9 @@ __global__ void __launch_bounds__(DELTA_MAX_THREADS) k_delta(const DeltaArgs a) 
     y[j] = p;
   }
 #pragma unroll
-  for (int j = 0; j < DELTA_RPW; ++j) y[j] = warp_sum(y[j]);
+  for (int j = 0; j < RPW; ++j) y[j] = warp_sum(y[j]);
 #pragma unroll
-  for (int j = 0; j < DELTA_RPW; ++j) {
+  for (int j = 0; j < RPW; ++j) {
     const int r = warp + j * nw;
     if (r >= RB) continue;
     float* Sr = S + (int64_t(hv) * dv + slice * RB + r) * dk;
@@ -841,18 +846,19 @@ void launch_delta(const DeltaArgs& a, cudaStream_t st, bool pdl) {
     throw Error(ERR_UNSUPPORTED, "DeltaNet head dims outside the decode kernel's range");
   const int nch = 2 * a.dk + a.rows_per_block;
   const size_t smem = size_t(2 * a.dk + a.rows_per_block + nch * (2 * a.conv_k - 1)) * 4;
-  launch(k_delta, dim3(a.nv, a.dv / a.rows_per_block), dim3(DELTA_THREADS), smem, st, pdl, a);
+  launch(k_delta<DELTA_RPW>, dim3(a.nv, a.dv / a.rows_per_block), dim3(DELTA_THREADS), smem, st, pdl, a);
 }
 
 // Batched: up to 128 rows per CTA (a whole 128-row value head), so the q/k
 // convolution and norms of a key head are computed by fewer CTAs.
 void launch_delta_batch(const DeltaArgs& a, int T, cudaStream_t st, bool pdl) {
-  const int threads = std::max(DELTA_THREADS, 32 * ((a.rows_per_block + DELTA_RPW - 1) / DELTA_RPW));
-  if (a.dk > 32 * DELTA_EPL || threads > DELTA_MAX_THREADS || a.dv % a.rows_per_block)
+  constexpr int RPW = 2 * DELTA_RPW;
+  const int threads = std::max(DELTA_THREADS, 32 * ((a.rows_per_block + RPW - 1) / RPW));
+  if (a.dk > 32 * DELTA_EPL || threads > 256 || a.dv % a.rows_per_block)
     throw Error(ERR_UNSUPPORTED, "DeltaNet head dims outside the decode kernel's range");
   const int nch = 2 * a.dk + a.rows_per_block;
   const size_t smem = size_t(2 * a.dk + a.rows_per_block + nch * (2 * a.conv_k - 1)) * 4;
-  launch(k_delta, dim3(a.nv, a.dv / a.rows_per_block, T), dim3(threads), smem, st, pdl, a);
+  launch(k_delta<RPW>, dim3(a.nv, a.dv / a.rows_per_block, T), dim3(threads), smem, st, pdl, a);
 }
 
 void launch_delta_seq(const DeltaArgs& a, int S, cudaStream_t st, bool pdl) {
