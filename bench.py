@@ -214,7 +214,14 @@ def batched_decode(model, cfg, stream, args, rank, local, dist) -> dict:
     D2H logits of every sequence, host argmax)."""
     import numpy as np
     import torch
-    B = args.batch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    ep = bool(args.ep) and world > 1
+    B = args.batch // world if ep else args.batch
+    if ep:
+        # expert parallelism: args.batch sequences in all, B per rank; every
+        # decode step routes all ranks' tokens over the experts split by id
+        import swiftlet_b200 as swl
+        model.ep_init(rank, world, swl.ep_unique_id_broadcast(rank), B)
     steps, e2e_steps = args.batch_steps, min(args.batch_steps, 8)
     rng = np.random.default_rng(PROMPT_SEED + 1000 + rank)
     # prompt lengths: all args.batch_prompt, or uniform in [batch_prompt, batch_prompt_max] (ragged)
@@ -254,10 +261,12 @@ def batched_decode(model, cfg, stream, args, rank, local, dist) -> dict:
     ms, e2e_ms = max_over_ranks([ms, e2e_ms], dist, f"cuda:{local}")
     for s in states:
         s.free()
-    world = int(os.environ.get("WORLD_SIZE", "1"))
     bt = algorithmic_bytes_per_token(cfg, float(np.mean(lens)) + args.warmup + steps / 2)
     L = cfg.num_hidden_layers
-    uniq = expected_unique_experts(cfg.num_experts, cfg.num_experts_per_tok, B)
+    # distinct routed experts this rank reads per layer: of all E for its own
+    # B tokens, or of its E / world for every rank's tokens
+    uniq = (expected_unique_experts(cfg.num_experts, cfg.num_experts_per_tok, B * world) / world if ep else
+            expected_unique_experts(cfg.num_experts, cfg.num_experts_per_tok, B))
     per_seq = bt["delta_state"] + bt["conv_ring"] + bt["kv"] + bt["embed_row"]
     dense = bt["total"] - bt["experts"] - per_seq
     step_bytes = dense + L * (uniq + 1) * bt["expert_blob"] + B * per_seq
@@ -266,6 +275,9 @@ def batched_decode(model, cfg, stream, args, rank, local, dist) -> dict:
     step_s = ms / steps / 1000.0
     return {
         "B": B, "value": replica_rate(world, B * steps, ms), "unit": "tok/s", "steps": steps,
+        "expert_parallel": {"world": world, "sequences_per_rank": B,
+                            "collectives_per_layer": "NCCL all-gather (digits, router logits) + reduce-scatter"}
+        if ep else None,
         "ms_per_step": ms / steps, "prompt": args.batch_prompt if hi == args.batch_prompt else [args.batch_prompt, hi],
         "prefill": {"tokens": int(lens.sum()), "ms": prefill_ms,
                     "tok_s": float(lens.sum()) / (prefill_ms / 1000.0),
@@ -305,20 +317,26 @@ def run_ours(args) -> None:
     model.set_stream(stream.cuda_stream)
     if args.batch_only or args.model == "80b":
         # the batched leg alone: profiling, or the 80B-shaped ragged batch
-        # (BASELINE config 5 on each GPU; expert parallelism is not built, so
-        # several GPUs run replicas)
+        # (replicas per GPU, or with --ep the routed
+        # experts split over the GPUs)
         res = batched_decode(model, cfg, stream, args, rank, local, dist)
         model.close()
         if rank == 0:
             line = {"metric": METRIC, "batched": res, "profiling_only": True}
             if args.model == "80b":
-                line = {"metric": "80B-A3B q4 ragged batched decode tok/s (B=64 per GPU)", "value": res["value"],
+                ep = bool(args.ep) and world > 1
+                line = {"metric": "80B-A3B q4 ragged batched decode tok/s (B=%d %s)"
+                                  % (args.batch, "over all GPUs, expert-parallel" if ep else "per GPU"),
+                        "value": res["value"],
                         "unit": "tok/s", "n_gpus": world, "steps": res["steps"], "warmup": args.warmup,
-                        "ms_per_step": res["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+                        "ms_per_step": res["ms_per_step"], "higher_is_better": True,
+                        "scaling": "strong" if ep else "weak",
                         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                         "config": {"workload": "qwen3-next-80b-a3b shape (48 layers, 512 experts top-10 + shared), q4 "
-                                               "g64, 64 sequences with seeded prompts of ragged length per GPU",
-                                   "parallelism": "replica x%d (no expert parallelism)" % world},
+                                               "g64, %d sequences with seeded prompts of ragged length %s"
+                                               % (args.batch, "split over the GPUs" if ep else "per GPU"),
+                                   "parallelism": ("ep%d (routed experts by id, sequences data-parallel)" % world)
+                                   if ep else "replica x%d" % world},
                         "batched": res}
             print(json.dumps(line), flush=True)
         if dist:
@@ -447,6 +465,8 @@ def main() -> None:
                     help="ragged prompts: lengths uniform in [--batch-prompt, this]")
     ap.add_argument("--model", default="35b", choices=["35b", "80b"],
                     help="80b: the Qwen3-Next-80B-shaped batched leg alone (BASELINE config 5 per GPU)")
+    ap.add_argument("--ep", action="store_true",
+                    help="batched leg with expert parallelism over the ranks (--batch sequences in all)")
     ap.add_argument("--batch-only", action="store_true",
                     help="profiling only: run the batched leg alone and print its numbers")
     ap.add_argument("--layers", type=int, default=None,

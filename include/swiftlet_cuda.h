@@ -112,6 +112,34 @@ int swl_step_batch_device(swl_model* model, swl_state** states, int32_t nseq, co
  * `why` (may be NULL) receives the reason for 0. Negative on error. */
 int swl_batch_supported(swl_model* model, char* why, int32_t why_len);
 
+/* Expert parallelism for batched decode. The reference runs on one Metal
+ * device and has no counterpart; the sharding follows the MoE block it
+ * computes (QwenMetalModel.swift:798-873, QwenCPUModel.swift:506-566): the
+ * routed experts of every layer are split by id over `world` ranks, one
+ * process and GPU per rank, each with its own model opened from the same
+ * checkpoint. NCCL (libnccl.so.2) is loaded on first use.
+ *
+ * swl_ep_unique_id writes a communicator id (SWL_EP_ID_BYTES bytes) that one
+ * rank makes and hands to the others out of band. swl_ep_init joins the group
+ * (blocks until every rank has joined): from then on, a decode launch of
+ * swl_step_batch / swl_step_batch_device with one token for each of exactly
+ * tokens_per_rank sequences routes all ranks' tokens together. Per MoE layer
+ * the ranks all-gather the tokens' quantised inputs and router logits, rank r
+ * computes experts [r * E / world, (r + 1) * E / world) for every token and
+ * the shared expert for its own tokens, and a reduce-scatter returns each
+ * token's sum to its rank. 2 <= tokens_per_rank, tokens_per_rank * world <= 64.
+ * Every rank must make the same decode calls in the same order; a decode call
+ * with another number of sequences returns SWL_ERR_INVALID before any launch.
+ * Prompt calls (a sequence with two or more tokens) and swl_step stay on the
+ * rank, which keeps every expert resident. */
+#define SWL_EP_ID_BYTES 128
+int swl_ep_unique_id(void* out, int32_t out_len);
+int swl_ep_init(swl_model* model, int32_t rank, int32_t world, const void* id, int32_t id_len,
+                int32_t tokens_per_rank);
+/* 1 when expert parallelism is on (rank, world and the owned expert range are
+ * written; each pointer may be NULL), 0 when off (0, 1, 0, E). */
+int swl_ep_info(const swl_model* model, int32_t* rank, int32_t* world, int32_t* expert_lo, int32_t* expert_hi);
+
 /* Same as swl_step with device-resident tokens and logits (either logits
  * pointer may be NULL); `greedy_out` (device, may be NULL) receives the
  * argmax of the last logits (first index on ties, as TextGenerator.swift:90). */

@@ -78,6 +78,9 @@ _SIGNATURES = {
     "swl_step_device": (_I, [_P, _P, _P, C.c_int32, _P, _P]),
     "swl_step_batch_device": (_I, [_P, _P, C.c_int32, _P, _P, _P]),
     "swl_batch_supported": (_I, [_P, C.c_char_p, C.c_int32]),
+    "swl_ep_unique_id": (_I, [_P, C.c_int32]),
+    "swl_ep_init": (_I, [_P, C.c_int32, C.c_int32, _P, C.c_int32, C.c_int32]),
+    "swl_ep_info": (_I, [_P] * 5),
     "swl_pool_stats": (_I, [_P, C.POINTER(swl_pool_info)]),
     "swl_pool_resize": (_I, [_P, _D]),
     "swl_set_stream": (_I, [_P, _P]),
@@ -277,6 +280,23 @@ class QwenCUDAModel:
             _check(rc)
         return rc == 1, buf.value.decode()
 
+    def ep_init(self, rank: int, world: int, ep_id: bytes, tokens_per_rank: int) -> None:
+        """Joins an expert-parallel group of `world` ranks (swl_ep_init); every
+        rank passes the same id (from ep_unique_id) and tokens_per_rank."""
+        if len(ep_id) != EP_ID_BYTES:
+            raise ValueError(f"expert-parallel id must be {EP_ID_BYTES} bytes")
+        buf = C.create_string_buffer(bytes(ep_id), EP_ID_BYTES)
+        _check(lib().swl_ep_init(self._h, int(rank), int(world), C.cast(buf, C.c_void_p), EP_ID_BYTES,
+                                 int(tokens_per_rank)))
+
+    def ep_info(self) -> tuple[bool, int, int, int, int]:
+        """(on, rank, world, first owned expert, end of the owned range)."""
+        v = [C.c_int32() for _ in range(4)]
+        rc = lib().swl_ep_info(self._h, *[C.byref(x) for x in v])
+        if rc < 0:
+            _check(rc)
+        return (rc == 1, *[x.value for x in v])
+
     def step_device(self, d_tokens: int, n: int, state: DecodeState, d_logits: int = 0, d_greedy: int = 0) -> None:
         """Device-pointer form (tokens/logits already in HBM)."""
         _check(lib().swl_step_device(self._h, state._bind(self), C.c_void_p(d_tokens), int(n),
@@ -332,6 +352,25 @@ class QwenCUDAModel:
         out = np.empty((c.linear_num_value_heads, c.linear_value_head_dim, c.linear_key_head_dim), np.float32)
         _check(lib().swl_debug_delta_state(self._h, state._bind(self), layer, _ptr(out)))
         return out
+
+
+EP_ID_BYTES = 128
+
+
+def ep_unique_id() -> bytes:
+    """A fresh expert-parallel communicator id (swl_ep_unique_id)."""
+    buf = C.create_string_buffer(EP_ID_BYTES)
+    _check(lib().swl_ep_unique_id(C.cast(buf, C.c_void_p), EP_ID_BYTES))
+    return buf.raw
+
+
+def ep_unique_id_broadcast(rank: int) -> bytes:
+    """Rank 0 makes the id and torch.distributed (already initialised, any
+    backend) hands it to the other ranks."""
+    import torch.distributed as dist
+    box = [ep_unique_id() if rank == 0 else None]
+    dist.broadcast_object_list(box, src=0)
+    return box[0]
 
 
 def gemv_affine(packed, scales, biases, out_dim: int, in_dim: int, group: int, bits: int, x) -> np.ndarray:

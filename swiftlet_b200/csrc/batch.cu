@@ -678,12 +678,14 @@ __global__ void __launch_bounds__(BR_THREADS) k_broute(const BRouteArgs a) {
   __shared__ int off[BR_MAXE + 1], tb[BR_MAXE + 1];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int T = a.T, E = a.E, K = a.K;
+  const int e_lo = a.e_lo, e_hi = min(a.e_hi, E), sh_lo = min(a.sh_lo, T), sh_hi = min(a.sh_hi, T);
   pdl_wait();
   for (int e = tid; e < E; e += BR_THREADS) msk[e] = 0ull;
   for (int tok = warp; tok < T; tok += BR_THREADS / 32)
     warp_route(a.logits + int64_t(tok) * (E + 1), E, K, a.norm_topk, ids + tok * K, wts + tok * K, shs + tok);
   __syncthreads();
-  for (int p = tid; p < T * K; p += BR_THREADS) atomicOr(&msk[ids[p]], 1ull << (p / K));
+  for (int p = tid; p < T * K; p += BR_THREADS)
+    if (ids[p] >= e_lo && ids[p] < e_hi) atomicOr(&msk[ids[p]], 1ull << (p / K));
   __syncthreads();
   if (warp == 0) {
     // exclusive scans of the counts (off) and of the token tiles (tb)
@@ -707,19 +709,23 @@ __global__ void __launch_bounds__(BR_THREADS) k_broute(const BRouteArgs a) {
   pdl_launch();
   for (int p = tid; p < T * K; p += BR_THREADS) {
     const int tok = p / K, e = ids[p];
+    a.ids[p] = e;
+    a.w[p] = wts[p];
+    if (e < e_lo || e >= e_hi) {  // another rank's expert
+      a.slot_of[p] = -1;
+      continue;
+    }
     const int rank = __popcll(msk[e] & ((1ull << tok) - 1ull));
     const int slot = off[e] + rank;
     a.slot_of[p] = slot;
     a.slot_tok[slot] = tok;
-    a.ids[p] = e;
-    a.w[p] = wts[p];
   }
   for (int tok = tid; tok < T; tok += BR_THREADS) {
     a.slot_tok[T * K + tok] = tok;
     a.sh[tok] = shs[tok];
   }
   const int rbg = (a.inter + 31) / 32, rbd = (a.hidden + 63) / 64, rbs = (a.shared_inter + 31) / 32;
-  const int ntt_s = (T + BG_TOK - 1) / BG_TOK;
+  const int nsh = max(0, sh_hi - sh_lo), ntt_s = (nsh + BG_TOK - 1) / BG_TOK;
   // item i of a list belongs to the expert e with tb[e] * rb_n <= i <
   // tb[e + 1] * rb_n (binary search over the tile prefix sums); every thread
   // writes items, not one thread per expert
@@ -740,12 +746,12 @@ __global__ void __launch_bounds__(BR_THREADS) k_broute(const BRouteArgs a) {
   for (int i = tid; i < ntt_s * rbs; i += BR_THREADS) {
     const int rb = i / ntt_s, tt = i - rb * ntt_s;
     if (base_gu + i < a.max_gu)
-      a.items_gu[base_gu + i] = make_int4(E, rb * 32, T * K + tt * BG_TOK, min(BG_TOK, T - tt * BG_TOK));
+      a.items_gu[base_gu + i] = make_int4(E, rb * 32, T * K + sh_lo + tt * BG_TOK, min(BG_TOK, nsh - tt * BG_TOK));
   }
   for (int i = tid; i < ntt_s * rbd; i += BR_THREADS) {
     const int rb = i / ntt_s, tt = i - rb * ntt_s;
     if (base_dn + i < a.max_dn)
-      a.items_dn[base_dn + i] = make_int4(E, rb * 64, T * K + tt * BG_TOK, min(BG_TOK, T - tt * BG_TOK));
+      a.items_dn[base_dn + i] = make_int4(E, rb * 64, T * K + sh_lo + tt * BG_TOK, min(BG_TOK, nsh - tt * BG_TOK));
   }
   if (tid == 0) {
     a.nitems[0] = min(base_gu + ntt_s * rbs, a.max_gu);
@@ -777,6 +783,30 @@ __global__ void k_bcombine(const BCombineArgs a) {
 
 void launch_bcombine(const BCombineArgs& a, cudaStream_t st, bool pdl) {
   launch(k_bcombine, dim3((a.D + 255) / 256, a.T), dim3(256), 0, st, pdl, a);
+}
+
+// Expert-parallel form of k_bcombine (BCombineEpArgs): the partial sum of
+// this rank's experts for every token of the step, with the shared expert and
+// the residual added on the token's own rank only.
+__global__ void k_bcombine_ep(const BCombineEpArgs a) {
+  pdl_wait();
+  const int tok = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= a.D) return;
+  float acc = 0.f;
+  for (int k = 0; k < a.K; ++k) {
+    const int s = a.slot_of[tok * a.K + k];
+    if (s >= 0) acc += a.w[tok * a.K + k] * a.ydown[int64_t(s) * a.ystride + i];
+  }
+  if (tok >= a.own_lo && tok < a.own_hi) {
+    acc += a.sh[tok] * a.ydown[int64_t(a.T * a.K + tok) * a.ystride + i];
+    acc += a.h[int64_t(tok - a.own_lo) * a.D + i];
+  }
+  a.part[int64_t(tok) * a.D + i] = acc;
+  pdl_launch();
+}
+
+void launch_bcombine_ep(const BCombineEpArgs& a, cudaStream_t st, bool pdl) {
+  launch(k_bcombine_ep, dim3((a.D + 255) / 256, a.T), dim3(256), 0, st, pdl, a);
 }
 
 // Every sequence of the step has consumed its tokens.

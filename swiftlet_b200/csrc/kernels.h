@@ -276,6 +276,25 @@ struct BRouteArgs {
   int* nitems = nullptr;          // [2] gate/up, down
   int inter = 0, shared_inter = 0, hidden = 0;
   int max_gu = 0, max_dn = 0;
+  // Expert parallelism: only experts [e_lo, e_hi) get slots and items (the
+  // other picks get slot -1), and only tokens [sh_lo, sh_hi) get shared-expert
+  // items. The defaults cover every expert and token.
+  int e_lo = 0, e_hi = 1 << 30, sh_lo = 0, sh_hi = 1 << 30;
+};
+
+// Expert-parallel combine: part[t] = sum of the weighted outputs of this
+// rank's picks of token t, plus, for the rank's own tokens [own_lo, own_hi),
+// the gated shared expert and the residual h[t - own_lo]. A reduce-scatter of
+// part over the ranks then yields each rank's new residual stream.
+struct BCombineEpArgs {
+  const float* h = nullptr;       // [own_hi - own_lo][D]
+  float* part = nullptr;          // [T][D]
+  const float* ydown = nullptr;   // [slots][ystride]
+  int64_t ystride = 0;
+  const int* slot_of = nullptr;   // [T][K], -1 for another rank's expert
+  const float* w = nullptr;
+  const float* sh = nullptr;
+  int T = 0, K = 0, D = 0, own_lo = 0, own_hi = 0;
 };
 
 struct BCombineArgs {
@@ -296,6 +315,7 @@ void launch_bgemm(const BGemmArgs& a, int bits, int dt, int grid, cudaStream_t s
 int bgemm_grid(int bits, int dt, const BGLayout& L);
 void launch_broute(const BRouteArgs& a, cudaStream_t stream, bool pdl);
 void launch_bcombine(const BCombineArgs& a, cudaStream_t stream, bool pdl);
+void launch_bcombine_ep(const BCombineEpArgs& a, cudaStream_t stream, bool pdl);
 // Sequence s of the step has consumed seq_n[s] tokens (1 when seq_n is null).
 void launch_badvance(const StateDev* sds, int S, const int* seq_n, cudaStream_t stream, bool pdl);
 // Chunked steps: the DeltaNet recurrence over each sequence's tokens in order

@@ -16,6 +16,7 @@
 
 #include "../../include/swiftlet_cuda.h"
 #include "common.h"
+#include "ep_nccl.h"
 #include "host_io.h"
 #include "kernels.h"
 #include "synth.h"
@@ -148,6 +149,15 @@ struct Model {
   int h_tokens_cap = 0;
   std::vector<State*> live;  // states created on this model and not yet freed
   BatchBufs bb;              // batched decode
+  // Expert parallelism (swl_ep_init): this rank routes its ep_tokens decode
+  // tokens together with every other rank's and computes only experts
+  // [ep_rank * E / ep_world, (ep_rank + 1) * E / ep_world) for all of them.
+  EpComm* ep = nullptr;
+  int ep_rank = 0, ep_world = 1, ep_tokens = 0;
+  bool ep_decode = false;    // set by the decode entry points: launches may exchange
+  float* ep_part = nullptr;  // [ep_world * ep_tokens][hidden] partial MoE sums
+  int ep_lo() const { return int(int64_t(ep_rank) * cfg.experts / ep_world); }
+  int ep_hi() const { return int(int64_t(ep_rank + 1) * cfg.experts / ep_world); }
   int batch_ok = -1;         // -1 unchecked; 1 every module fits the batched kernels
   std::string batch_why;     // why not
   Trace trace;               // SWL_TRACE=<records>: per-block kernel timeline
@@ -194,6 +204,13 @@ struct Model {
   void run_packed(State* const* s, int nseq, const int32_t* tokens, const int* counts, float* logits_out);
   void bdense(const std::vector<std::pair<QLin, float*>>& segs, int64_t y_stride, int mode, const uint2* bt,
               const float2* meta, int T, cudaStream_t st);
+  // Decode calls of an expert-parallel model route exactly ep_tokens
+  // sequences on every rank; anything else is refused before any launch.
+  void check_ep_call(bool decode, int nseq) const {
+    if (ep && decode && nseq != ep_tokens)
+      throw Error(ERR_INVALID, "expert-parallel decode steps exactly " + std::to_string(ep_tokens) +
+                                   " sequences per rank (got " + std::to_string(nseq) + ")");
+  }
   // Throws when a kernel of the last steps reported a bounded wait that gave
   // up (its results are then unreliable); clears the word for the next step.
   void check_status(const int* host_word) {
@@ -205,9 +222,17 @@ struct Model {
   }
 };
 
+// Marks the launches of one decode call as expert-parallel ones.
+struct EpDecode {
+  Model& m;
+  EpDecode(Model& model, bool on) : m(model) { m.ep_decode = on; }
+  ~EpDecode() { m.ep_decode = false; }
+};
+
 Model::~Model() {
   drop_graphs();
   if (stream) cudaStreamSynchronize(stream);
+  ep_destroy(ep);
   for (State* s : live) {  // a caller that frees states after the model only releases the handle
     cudaFree(s->mem);
     s->mem = nullptr;
@@ -886,7 +911,6 @@ void Model::bdense(const std::vector<std::pair<QLin, float*>>& segs, int64_t y_s
 void Model::enqueue_batch(int T, int S, bool chunked, cudaStream_t st) {
   const ModelConfig& c = cfg;
   const int D = c.hidden, K = c.topk, E = c.experts, H = c.heads, hd = c.head_dim;
-  const int slots = T * (K + 1);
   const bool pdl = use_pdl;
   EmbedArgs e;
   e.table = embed; e.tokens = bb.tokens; e.cursor = nullptr; e.h = bb.h; e.vocab = c.vocab; e.err = err;
@@ -940,10 +964,29 @@ void Model::enqueue_batch(int T, int S, bool chunked, cudaStream_t st) {
     }
     bdense({{ld.out_lin, bb.h}}, D, BM_RESIDUAL, bb.bt_a, bb.meta_a, T, st);
     const int gs_r = ld.router.gs;
-    digit(bb.h, D, T, D, gs_r, PRO_RMSNORM, ld.post_norm, nullptr, 0, bb.xmoe, bb.bt_a, bb.meta_a);
-    bdense({{ld.router, bb.rlog}, {ld.sgate, bb.rlog + E}}, E + 1, BM_STORE, bb.bt_a, bb.meta_a, T, st);
+    // Expert-parallel decode: this rank's tokens are rows [own, own + T) of
+    // the Ta tokens that every rank routes; their digits and router logits
+    // are written in place and all-gathered.
+    const bool ep_on = ep && ep_decode && !chunked;
+    const int Ta = ep_on ? T * ep_world : T, own = ep_on ? ep_rank * T : 0;
+    const int64_t bt_row = D / 32 * 12, meta_row = D / gs_r;
+    uint2* bt_own = bb.bt_a + own * bt_row;
+    float2* meta_own = bb.meta_a + own * meta_row;
+    float* rlog_own = bb.rlog + int64_t(own) * (E + 1);
+    digit(bb.h, D, T, D, gs_r, PRO_RMSNORM, ld.post_norm, nullptr, 0, bb.xmoe, bt_own, meta_own);
+    bdense({{ld.router, rlog_own}, {ld.sgate, rlog_own + E}}, E + 1, BM_STORE, bt_own, meta_own, T, st);
+    if (ep_on) {
+      ep_group_start(ep);
+      ep_allgather(ep, bb.bt_a, size_t(T) * bt_row * sizeof(uint2), st);
+      ep_allgather(ep, bb.meta_a, size_t(T) * meta_row * sizeof(float2), st);
+      ep_allgather(ep, bb.rlog, size_t(T) * (E + 1) * sizeof(float), st);
+      ep_group_end(ep);
+    }
     BRouteArgs r;
-    r.logits = bb.rlog; r.T = T; r.E = E; r.K = K; r.norm_topk = c.norm_topk;
+    r.logits = bb.rlog; r.T = Ta; r.E = E; r.K = K; r.norm_topk = c.norm_topk;
+    if (ep_on) {
+      r.e_lo = ep_lo(); r.e_hi = ep_hi(); r.sh_lo = own; r.sh_hi = own + T;
+    }
     r.ids = bb.ids; r.w = bb.w; r.sh = bb.sh; r.slot_of = bb.slot_of; r.slot_tok = bb.slot_tok;
     r.items_gu = bb.items_gu; r.items_dn = bb.items_dn; r.nitems = bb.nitems;
     r.inter = c.moe_inter; r.shared_inter = c.shared_inter; r.hidden = D; r.max_gu = bb.max_gu; r.max_dn = bb.max_dn;
@@ -957,7 +1000,7 @@ void Model::enqueue_batch(int T, int S, bool chunked, cudaStream_t st) {
     gu.xbt = bb.bt_a; gu.xmeta = bb.meta_a; gu.bt_row = D / 32 * 12; gu.meta_row = D / gs_r;
     launch_bgemm(gu, ld.eg.lin.bits, ld.eg.lin.dt, bgemm_grid(ld.eg.lin.bits, ld.eg.lin.dt, gu.L), st, pdl);
     const int gs_d = ld.ed.lin.gs, I = c.moe_inter;
-    digit(bb.hmid, bb.hmid_stride, slots, I, gs_d, PRO_COPY, nullptr, nullptr, 0, nullptr, bb.bt_b, bb.meta_b);
+    digit(bb.hmid, bb.hmid_stride, Ta * (K + 1), I, gs_d, PRO_COPY, nullptr, nullptr, 0, nullptr, bb.bt_b, bb.meta_b);
     BGemmArgs dn;
     dn.mode = BM_STORE; dn.in = I;
     if (!bgemm_layout(I, ld.ed.lin.bits, ld.ed.lin.dt, gs_d, dn.L)) throw Error(ERR_UNSUPPORTED, "batched down layout");
@@ -966,10 +1009,18 @@ void Model::enqueue_batch(int T, int S, bool chunked, cudaStream_t st) {
     dn.out = bb.ydown; dn.out_stride = D;
     dn.xbt = bb.bt_b; dn.xmeta = bb.meta_b; dn.bt_row = I / 32 * 12; dn.meta_row = I / gs_d;
     launch_bgemm(dn, ld.ed.lin.bits, ld.ed.lin.dt, bgemm_grid(ld.ed.lin.bits, ld.ed.lin.dt, dn.L), st, pdl);
-    BCombineArgs cb;
-    cb.h = bb.h; cb.ydown = bb.ydown; cb.ystride = D; cb.slot_of = bb.slot_of; cb.w = bb.w; cb.sh = bb.sh;
-    cb.T = T; cb.K = K; cb.D = D;
-    launch_bcombine(cb, st, pdl);
+    if (ep_on) {
+      BCombineEpArgs ce;
+      ce.h = bb.h; ce.part = ep_part; ce.ydown = bb.ydown; ce.ystride = D; ce.slot_of = bb.slot_of; ce.w = bb.w;
+      ce.sh = bb.sh; ce.T = Ta; ce.K = K; ce.D = D; ce.own_lo = own; ce.own_hi = own + T;
+      launch_bcombine_ep(ce, st, pdl);
+      ep_reduce_scatter(ep, ep_part, bb.h, size_t(T) * D, st);
+    } else {
+      BCombineArgs cb;
+      cb.h = bb.h; cb.ydown = bb.ydown; cb.ystride = D; cb.slot_of = bb.slot_of; cb.w = bb.w; cb.sh = bb.sh;
+      cb.T = T; cb.K = K; cb.D = D;
+      launch_bcombine(cb, st, pdl);
+    }
   }
   launch_badvance(bb.sds, S, chunked ? bb.seq_n : nullptr, st, pdl);
   digit(bb.h, D, T, D, lm_head.gs, PRO_RMSNORM, final_norm, nullptr, 0, nullptr, bb.bt_a, bb.meta_a);
@@ -989,6 +1040,13 @@ void Model::run_batch(State* const* s, int S, const int* counts, int T) {
     sd[i] = s[i]->host_desc;
     chunked = chunked || counts[i] > 1;
   }
+  // the ranks of an expert-parallel group exchange ep_tokens rows each per
+  // layer; a decode launch of another size is refused before anything is
+  // enqueued (every rank must make the same calls in the same order)
+  const bool ep_step = ep && ep_decode && !chunked;
+  if (ep_step && T != ep_tokens)
+    throw Error(ERR_INVALID, "expert-parallel decode steps exactly " + std::to_string(ep_tokens) +
+                                 " sequences per rank, one token each (got " + std::to_string(T) + ")");
   SWL_CUDA(cudaMemcpyAsync(bb.sds, sd.data(), size_t(S) * sizeof(StateDev), cudaMemcpyHostToDevice, stream));
   if (chunked) {
     std::vector<int> maps(2 * size_t(T) + 2 * size_t(S));
@@ -1007,7 +1065,7 @@ void Model::run_batch(State* const* s, int S, const int* counts, int T) {
     SWL_CUDA(cudaMemcpyAsync(bb.seq_first, sfirst, size_t(S) * 4, cudaMemcpyHostToDevice, stream));
     SWL_CUDA(cudaMemcpyAsync(bb.seq_n, sn, size_t(S) * 4, cudaMemcpyHostToDevice, stream));
   }
-  if (use_graph) {
+  if (use_graph && !ep_step) {
     const int key = chunked ? (1 << 20) | (T << 8) | S : T;
     auto it = bb.graphs.find(key);
     if (it == bb.graphs.end())
@@ -1273,6 +1331,9 @@ int swl_step_batch(swl_model* model, swl_state** states, const int32_t* tokens, 
     first[i] = off;
     off += counts[i];
   }
+  bool decode = true;
+  for (int i = 0; i < nseq; ++i) decode = decode && counts[i] == 1;
+  m.check_ep_call(decode, nseq);
   if (nseq < 2 || !m.batch_supported()) {
     for (int i = 0; i < nseq; ++i) {
       int rc = swl_step(model, states[i], tokens + first[i], counts[i], logits_out + int64_t(i) * m.cfg.vocab);
@@ -1282,6 +1343,7 @@ int swl_step_batch(swl_model* model, swl_state** states, const int32_t* tokens, 
   }
   std::vector<State*> ss(nseq);
   for (int i = 0; i < nseq; ++i) ss[i] = &states[i]->s;
+  EpDecode guard(m, decode);
   m.run_packed(ss.data(), nseq, tokens, counts, logits_out);
   int status = 0;
   SWL_CUDA(cudaMemcpyAsync(&status, m.kstatus, 4, cudaMemcpyDeviceToHost, m.stream));
@@ -1303,6 +1365,7 @@ int swl_step_batch_device(swl_model* model, swl_state** states, int32_t nseq, co
     if (states[i]->s.pos + 1 > states[i]->s.max_ctx)
       throw Error(ERR_CAPACITY, "context capacity exceeded (max_ctx " + std::to_string(states[i]->s.max_ctx) + ")");
   }
+  m.check_ep_call(true, nseq);
   if (nseq < 2 || !m.batch_supported()) {
     for (int i = 0; i < nseq; ++i) {
       int rc = swl_step_device(model, states[i], d_tokens + i, 1, d_logits ? d_logits + int64_t(i) * m.cfg.vocab : nullptr,
@@ -1313,6 +1376,7 @@ int swl_step_batch_device(swl_model* model, swl_state** states, int32_t nseq, co
   }
   const int64_t V = m.cfg.vocab;
   m.ensure_batch();
+  EpDecode guard(m, true);
   for (int b0 = 0; b0 < nseq; b0 += BT_MAX) {
     const int T = std::min(BT_MAX, nseq - b0);
     std::vector<State*> ss(T);
@@ -1376,6 +1440,67 @@ int swl_pool_resize(swl_model* model, double gb) {
   if (gb > 0 && double(model->m.pool_size) > gb * 1073741824.0)
     throw Error(ERR_CAPACITY, "the HBM-resident expert pool holds every expert; it cannot shrink below " +
                                   std::to_string(double(model->m.pool_size) / 1073741824.0) + " GB");
+  API_END
+}
+
+int swl_ep_unique_id(void* out, int32_t out_len) {
+  API_BEGIN
+  if (!out || out_len < EP_ID_BYTES) throw Error(ERR_INVALID, "the id needs SWL_EP_ID_BYTES bytes");
+  ep_unique_id(out);
+  API_END
+}
+
+int swl_ep_init(swl_model* model, int32_t rank, int32_t world, const void* id, int32_t id_len,
+                int32_t tokens_per_rank) {
+  API_BEGIN
+  if (!model || !id || id_len < EP_ID_BYTES) throw Error(ERR_INVALID, "null model or short id");
+  Model& m = model->m;
+  if (m.ep) throw Error(ERR_INVALID, "expert parallelism is already initialised on this model");
+  if (world < 1 || rank < 0 || rank >= world) throw Error(ERR_INVALID, "rank outside the world");
+  if (tokens_per_rank < 2 || int64_t(tokens_per_rank) * world > BT_MAX)
+    throw Error(ERR_UNSUPPORTED, "expert-parallel decode takes 2 or more sequences per rank and at most " +
+                                     std::to_string(BT_MAX) + " over all ranks per step");
+  if (world > m.cfg.experts) throw Error(ERR_UNSUPPORTED, "more ranks than experts");
+  if (!m.batch_supported()) throw Error(ERR_UNSUPPORTED, "expert parallelism needs the batched kernels: " + m.batch_why);
+  SWL_CUDA(cudaSetDevice(m.device));
+  SWL_CUDA(cudaStreamSynchronize(m.stream));
+  m.ensure_batch();
+  float* part = reinterpret_cast<float*>(m.dmalloc(size_t(tokens_per_rank) * world * m.cfg.hidden * sizeof(float)));
+  EpComm* c = ep_init(rank, world, id);
+  // every rank must route the same number of tokens over the same experts
+  int* chk = reinterpret_cast<int*>(m.dmalloc(4 * sizeof(int)));
+  const int mine[4] = {tokens_per_rank, -tokens_per_rank, m.cfg.experts, -m.cfg.experts};
+  int got[4];
+  try {
+    SWL_CUDA(cudaMemcpyAsync(chk, mine, sizeof(mine), cudaMemcpyHostToDevice, m.stream));
+    ep_allreduce_i32_max(c, chk, 4, m.stream);
+    SWL_CUDA(cudaMemcpyAsync(got, chk, sizeof(got), cudaMemcpyDeviceToHost, m.stream));
+    SWL_CUDA(cudaStreamSynchronize(m.stream));
+  } catch (...) {
+    ep_destroy(c);
+    throw;
+  }
+  if (got[0] != -got[1] || got[2] != -got[3]) {
+    ep_destroy(c);
+    throw Error(ERR_INVALID, "ranks disagree on tokens per rank or on the expert count");
+  }
+  m.ep = c;
+  m.ep_rank = rank;
+  m.ep_world = world;
+  m.ep_tokens = tokens_per_rank;
+  m.ep_part = part;
+  API_END
+}
+
+int swl_ep_info(const swl_model* model, int32_t* rank, int32_t* world, int32_t* expert_lo, int32_t* expert_hi) {
+  API_BEGIN
+  if (!model) throw Error(ERR_INVALID, "null model");
+  const Model& m = model->m;
+  if (rank) *rank = m.ep_rank;
+  if (world) *world = m.ep_world;
+  if (expert_lo) *expert_lo = m.ep ? m.ep_lo() : 0;
+  if (expert_hi) *expert_hi = m.ep ? m.ep_hi() : m.cfg.experts;
+  return m.ep ? 1 : 0;
   API_END
 }
 
