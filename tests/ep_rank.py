@@ -34,7 +34,9 @@ def main() -> int:
     on, r, w, lo, hi = ep.ep_info()
     V = plain.config.vocab_size
     rng = np.random.default_rng(1000 + rank)
-    prompts = [rng.integers(0, V, int(n)).tolist() for n in rng.integers(1, 6, tpr)]
+    # prompts of 2+ tokens: a prompt call stays on the rank on every rank alike
+    # (a call of one token per sequence would be a decode call, which exchanges)
+    prompts = [rng.integers(0, V, int(n)).tolist() for n in rng.integers(2, 7, tpr)]
     ps = [plain.new_state(64) for _ in prompts]
     es = [ep.new_state(64) for _ in prompts]
     ref = plain.step_batch(prompts, ps)
