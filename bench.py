@@ -15,6 +15,13 @@ logits, host argmax). Weights streamed per token (~1.7 GB) exceed the
 in oracle/) on the host cores on a bounded sample of the same workload.
 With N > 1 ranks every rank runs an independent replica (batch-1 decode does
 not shard); value = tokens of all ranks / max elapsed over ranks.
+
+`--model 80b` runs BASELINE config 5 alone: 64 sequences of ragged seeded
+prompts, then batched greedy decode. Under torchrun with `--ep` the 64
+sequences are split over the ranks and the routed experts of every layer are
+split by id (swl_ep_init: NCCL all-gather + reduce-scatter per layer), so the
+total work is fixed ("scaling": "strong"); without it each rank runs its own
+64 sequences as a replica.
 """
 from __future__ import annotations
 

@@ -155,6 +155,7 @@ struct Model {
   EpComm* ep = nullptr;
   int ep_rank = 0, ep_world = 1, ep_tokens = 0;
   bool ep_decode = false;    // set by the decode entry points: launches may exchange
+  bool ep_graph = true;      // capture expert-parallel steps (SWL_EP_NO_GRAPH=1: launch directly)
   float* ep_part = nullptr;  // [ep_world * ep_tokens][hidden] partial MoE sums
   int ep_lo() const { return int(int64_t(ep_rank) * cfg.experts / ep_world); }
   int ep_hi() const { return int(int64_t(ep_rank + 1) * cfg.experts / ep_world); }
@@ -1065,8 +1066,10 @@ void Model::run_batch(State* const* s, int S, const int* counts, int T) {
     SWL_CUDA(cudaMemcpyAsync(bb.seq_first, sfirst, size_t(S) * 4, cudaMemcpyHostToDevice, stream));
     SWL_CUDA(cudaMemcpyAsync(bb.seq_n, sn, size_t(S) * 4, cudaMemcpyHostToDevice, stream));
   }
-  if (use_graph && !ep_step) {
-    const int key = chunked ? (1 << 20) | (T << 8) | S : T;
+  if (use_graph && (!ep_step || ep_graph)) {
+    // expert-parallel steps hold their NCCL calls in the graph (every rank
+    // captures the same calls in the same order)
+    const int key = (ep_step ? 1 << 30 : 0) | (chunked ? (1 << 20) | (T << 8) | S : T);
     auto it = bb.graphs.find(key);
     if (it == bb.graphs.end())
       it = bb.graphs.emplace(key, capture(stream, [&] { enqueue_batch(T, S, chunked, stream); })).first;
@@ -1485,6 +1488,7 @@ int swl_ep_init(swl_model* model, int32_t rank, int32_t world, const void* id, i
     throw Error(ERR_INVALID, "ranks disagree on tokens per rank or on the expert count");
   }
   m.ep = c;
+  m.ep_graph = !env_flag("SWL_EP_NO_GRAPH");
   m.ep_rank = rank;
   m.ep_world = world;
   m.ep_tokens = tokens_per_rank;

@@ -1,6 +1,8 @@
 """Expert parallelism (swl_ep_init): the routed experts of every layer split
 by id over two GPUs, NCCL all-gather of the tokens' quantised MoE inputs and
-router logits, reduce-scatter of the partial sums. Each rank runs as its own
+router logits, reduce-scatter of the partial sums; decode steps replayed as
+CUDA graphs that hold the NCCL calls, and launched directly
+(SWL_EP_NO_GRAPH=1). Each rank runs as its own
 process (tests/ep_rank.py) and checks its sequences' logits against the same
 checkpoint stepped by the single-GPU batched path, which the other batched
 tests pin to the CPU oracle: 2e-2 max-abs, 1e-3 relative-L2, greedy ids
@@ -25,22 +27,22 @@ def _gpus() -> int:
     return torch.cuda.device_count()
 
 
-@pytest.mark.parametrize("shape", ["tiny", "80b"])
-def test_expert_parallel_matches_single_gpu(shape, tmp_path):
+@pytest.mark.parametrize("shape,graph", [("tiny", True), ("80b", True), ("80b", False)])
+def test_expert_parallel_matches_single_gpu(shape, graph, tmp_path):
     world = 2
     if _gpus() < world:
         pytest.skip("expert parallelism needs two GPUs")
     d = TINY_BASELINE if shape == "tiny" else formats.write_synthetic(
         str(tmp_path / "80b"), with_layers(NEXT_80B, 4), seed=99)
     ep_id = swl.ep_unique_id().hex()
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", SWL_EP_NO_GRAPH="0" if graph else "1")
     outs = [str(tmp_path / f"rank{r}.json") for r in range(world)]
     procs = [subprocess.Popen([sys.executable, os.path.join(ROOT, "tests", "ep_rank.py"), d, str(r), str(world),
                                ep_id, "4", "6", outs[r]], env=env, cwd=ROOT) for r in range(world)]
     rcs = []
     try:
         for p in procs:
-            rcs.append(p.wait(timeout=600))
+            rcs.append(p.wait(timeout=300))
     finally:
         for p in procs:
             if p.poll() is None:
