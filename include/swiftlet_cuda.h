@@ -192,6 +192,28 @@ int swl_bench_expert_sweep(swl_model* model, int32_t iters, float* ms_out, doubl
  * as CSV to `path` and clears the buffer. */
 int swl_trace_dump(swl_model* model, const char* path);
 
+/* On-device sampling: SwiftletSession.sample (SwiftletSession.swift:226-273)
+ * for nseq rows of logits (device buffers, row i at d_logits + i * row_stride;
+ * not modified). Per row, as the reference: ids in d_suppress, and the ids in
+ * d_eos when the row bans EOS (d_ban_eos[i] != 0; d_ban_eos NULL bans them in
+ * every row), become -inf; with d_counts ([nseq][vocab], times each token was
+ * generated; may be NULL) every token seen n > 0 times loses
+ * presence_penalty + frequency_penalty * n; temperature <= 0 takes the first
+ * maximum; otherwise the top_k largest (top_k <= 1024 unless >= vocab; ties
+ * at the k-th value and in the ordering go to the lower id) are weighted by
+ * exp((l - l_max) / temperature), cut at the first cumulative share >= top_p,
+ * and d_uniform[i] (a [0, 1) draw per row; the caller's RNG replaces
+ * Float.random) picks the token. d_out[i] gets the id; update_counts != 0 adds
+ * it to d_counts. Queued on cuda_stream (NULL: the default stream). */
+typedef struct swl_sample_options {
+  float temperature, top_p, presence_penalty, frequency_penalty;
+  int32_t top_k;
+} swl_sample_options;
+int swl_sample_device(const float* d_logits, int32_t nseq, int32_t vocab, int64_t row_stride,
+                      const swl_sample_options* opt, const int32_t* d_suppress, int32_t n_suppress,
+                      const int32_t* d_eos, int32_t n_eos, const int32_t* d_ban_eos, int32_t* d_counts,
+                      int32_t update_counts, const float* d_uniform, int32_t* d_out, void* cuda_stream);
+
 /* Model-free kernels on host buffers, for kernel-level parity tests:
  * y = W x for one MLX-affine matrix (sdtype 0 f32, 1 bf16, 2 f16) ... */
 int swl_kernel_gemv_affine(const uint32_t* packed, const void* scales, const void* biases, int sdtype, int out_dim,

@@ -78,6 +78,8 @@ _SIGNATURES = {
     "swl_step_device": (_I, [_P, _P, _P, C.c_int32, _P, _P]),
     "swl_step_batch_device": (_I, [_P, _P, C.c_int32, _P, _P, _P]),
     "swl_batch_supported": (_I, [_P, C.c_char_p, C.c_int32]),
+    "swl_sample_device": (_I, [_P, C.c_int32, C.c_int32, _I64, _P, _P, C.c_int32, _P, C.c_int32, _P, _P,
+                               C.c_int32, _P, _P, _P]),
     "swl_ep_unique_id": (_I, [_P, C.c_int32]),
     "swl_ep_init": (_I, [_P, C.c_int32, C.c_int32, _P, C.c_int32, C.c_int32]),
     "swl_ep_info": (_I, [_P] * 5),
@@ -352,6 +354,26 @@ class QwenCUDAModel:
         out = np.empty((c.linear_num_value_heads, c.linear_value_head_dim, c.linear_key_head_dim), np.float32)
         _check(lib().swl_debug_delta_state(self._h, state._bind(self), layer, _ptr(out)))
         return out
+
+
+class swl_sample_options(C.Structure):
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("presence_penalty", C.c_float),
+                ("frequency_penalty", C.c_float), ("top_k", C.c_int32)]
+
+
+def sample_device(d_logits: int, nseq: int, vocab: int, row_stride: int, *, temperature: float = 0.7,
+                  top_k: int = 20, top_p: float = 0.8, presence_penalty: float = 0.0, frequency_penalty: float = 0.0,
+                  d_suppress: int = 0, n_suppress: int = 0, d_eos: int = 0, n_eos: int = 0, d_ban_eos: int = 0,
+                  d_counts: int = 0, update_counts: bool = False, d_uniform: int = 0, d_out: int = 0,
+                  stream: int = 0) -> None:
+    """SwiftletSession.sample on the GPU for nseq device rows (swl_sample_device);
+    the defaults are GenerationOptions' (SwiftletSession.swift:20-28) without penalties."""
+    o = swl_sample_options(float(temperature), float(top_p), float(presence_penalty), float(frequency_penalty),
+                           int(top_k))
+    v = lambda p: C.c_void_p(p or None)  # noqa: E731
+    _check(lib().swl_sample_device(v(d_logits), int(nseq), int(vocab), int(row_stride), C.byref(o), v(d_suppress),
+                                   int(n_suppress), v(d_eos), int(n_eos), v(d_ban_eos), v(d_counts),
+                                   int(bool(update_counts)), v(d_uniform), v(d_out), v(stream)))
 
 
 EP_ID_BYTES = 128

@@ -307,6 +307,27 @@ struct BCombineArgs {
   int T = 0, K = 0, D = 0;
 };
 
+// On-device sampling (SwiftletSession.sample, SwiftletSession.swift:226-273),
+// one row of logits per sequence.
+constexpr int SMP_KMAX = 1024;  // largest top_k (when below the vocabulary)
+struct SampleArgs {
+  const float* logits = nullptr;  // [nseq][row_stride]
+  int64_t row_stride = 0;
+  int nseq = 0, vocab = 0;
+  float temperature = 0.f, top_p = 1.f, presence = 0.f, frequency = 0.f;
+  int top_k = 1;
+  const int* suppress = nullptr;  // ids set to -inf in every row
+  int n_suppress = 0;
+  const int* eos = nullptr;       // ids set to -inf in rows that ban EOS
+  int n_eos = 0;
+  const int* ban_eos = nullptr;   // [nseq] nonzero: ban EOS; null: every row
+  int* counts = nullptr;          // [nseq][vocab] times each token was generated (may be null)
+  int update_counts = 0;          // add the sampled token to counts
+  const float* uniform = nullptr; // [nseq] uniform [0, 1) draws
+  int* out = nullptr;             // [nseq] sampled ids
+};
+void launch_sample(const SampleArgs& a, cudaStream_t stream);
+
 void launch_digitize(const DigitArgs& a, cudaStream_t stream, bool pdl);
 // Fills a.L for the matrices of the launch (all with these bits / scale
 // dtype / group size) and returns whether the shapes are supported.

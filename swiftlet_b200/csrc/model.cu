@@ -1763,6 +1763,27 @@ int swl_kernel_expert_swiglu(const uint32_t* gate_w, const void* gate_s, const v
   API_END
 }
 
+int swl_sample_device(const float* d_logits, int32_t nseq, int32_t vocab, int64_t row_stride,
+                      const swl_sample_options* opt, const int32_t* d_suppress, int32_t n_suppress,
+                      const int32_t* d_eos, int32_t n_eos, const int32_t* d_ban_eos, int32_t* d_counts,
+                      int32_t update_counts, const float* d_uniform, int32_t* d_out, void* cuda_stream) {
+  API_BEGIN
+  if (!d_logits || !opt || !d_out || nseq < 1 || vocab < 1 || row_stride < vocab)
+    throw Error(ERR_INVALID, "sampling: null buffer or bad shape");
+  if ((n_suppress > 0 && !d_suppress) || (n_eos > 0 && !d_eos) || n_suppress < 0 || n_eos < 0)
+    throw Error(ERR_INVALID, "sampling: id list without buffer");
+  if (opt->temperature > 0.f && !d_uniform) throw Error(ERR_INVALID, "sampling: temperature > 0 needs uniform draws");
+  if (!(opt->top_p > 0.f)) throw Error(ERR_INVALID, "sampling: top_p must be > 0");
+  SampleArgs a;
+  a.logits = d_logits; a.row_stride = row_stride; a.nseq = nseq; a.vocab = vocab;
+  a.temperature = opt->temperature; a.top_p = opt->top_p; a.presence = opt->presence_penalty;
+  a.frequency = opt->frequency_penalty; a.top_k = opt->top_k;
+  a.suppress = d_suppress; a.n_suppress = n_suppress; a.eos = n_eos > 0 ? d_eos : nullptr; a.n_eos = n_eos;
+  a.ban_eos = d_ban_eos; a.counts = d_counts; a.update_counts = update_counts; a.uniform = d_uniform; a.out = d_out;
+  launch_sample(a, reinterpret_cast<cudaStream_t>(cuda_stream));
+  API_END
+}
+
 int swl_kernel_gemv_affine(const uint32_t* packed, const void* scales, const void* biases, int sdtype, int out_dim,
                            int in_dim, int group, int bits, const float* x, float* y) {
   API_BEGIN
