@@ -5,8 +5,10 @@
 // -inf; every token seen n > 0 times loses presence + frequency * n; then
 // temperature <= 0 takes the first maximum, otherwise the k = clamp(top_k, 1,
 // V) largest logits are selected (radix select over order-preserving 32-bit
-// keys: four 8-bit histogram passes find the k-th largest key, a block scan
-// gathers the larger ones and, in index order, the ties needed), sorted by
+// keys: four 8-bit histogram passes find the k-th largest key, over the row
+// until the keys at or above the chosen bin fit SMP_CAP and then over a
+// shared-memory copy of those; the larger keys and the lowest-id ties needed
+// are gathered), sorted by
 // logit (ties: lower id first), weighted by exp((l - l_max) / temperature),
 // cut at the first cumulative share >= top_p, and sampled by walking
 // u * sum down the weights, as the reference does, in its sequential order.
@@ -19,10 +21,15 @@ namespace swl {
 namespace {
 
 constexpr int SMP_THREADS = 1024;
+constexpr int SMP_CAP = 8192;  // keys the top-k select keeps in shared memory
 
 __device__ __forceinline__ uint32_t fkey(float f) {
   const uint32_t u = __float_as_uint(f);
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__device__ __forceinline__ float fval(uint32_t key) {
+  return __uint_as_float((key & 0x80000000u) ? (key ^ 0x80000000u) : ~key);
 }
 
 __device__ __forceinline__ float adjusted(const SampleArgs& a, const float* lg, const int* cnt,
@@ -65,7 +72,7 @@ __device__ int block_scan(int v, int* ex, int* warp_sums) {
 }
 
 __global__ void __launch_bounds__(SMP_THREADS) k_sample(const SampleArgs a) {
-  extern __shared__ uint32_t ban[];  // ceil(V / 32) words
+  extern __shared__ uint32_t ban[];  // ceil(V / 32) words, then SMP_CAP keys and SMP_CAP ids
   __shared__ unsigned hist[256];
   __shared__ float cval[SMP_KMAX], prob[SMP_KMAX];
   __shared__ int cidx[SMP_KMAX];
@@ -73,7 +80,7 @@ __global__ void __launch_bounds__(SMP_THREADS) k_sample(const SampleArgs a) {
   __shared__ float bval[32];
   __shared__ int bidx[32];
   __shared__ uint32_t s_prefix;
-  __shared__ int s_remaining;
+  __shared__ int s_remaining, s_bin, s_n;
   const int s = blockIdx.x, tid = threadIdx.x, V = a.vocab;
   const float* lg = a.logits + int64_t(s) * a.row_stride;
   int* cnt = a.counts ? a.counts + int64_t(s) * V : nullptr;
@@ -118,16 +125,30 @@ __global__ void __launch_bounds__(SMP_THREADS) k_sample(const SampleArgs a) {
     }
   } else {
     const int k = max(1, min(a.top_k, V));
-    // k-th largest key, 8 bits at a time from the top
-    if (tid == 0) { s_prefix = 0u; s_remaining = k; }
+    // k-th largest key, 8 bits at a time from the top. The passes read the
+    // row until the keys at or above the chosen bin fit SMP_CAP; then one
+    // more pass copies them to shared memory and the remaining passes and
+    // the gather run there.
+    uint32_t* lkey = ban + ((V + 31) >> 5);
+    int* lidx = reinterpret_cast<int*>(lkey + SMP_CAP);
+    if (tid == 0) { s_prefix = 0u; s_remaining = k; s_n = 0; }
     uint32_t mask = 0u;
+    bool local = false;
+    int n_local = 0;
     for (int shift = 24; shift >= 0; shift -= 8) {
       for (int b = tid; b < 256; b += SMP_THREADS) hist[b] = 0u;
       __syncthreads();
       const uint32_t prefix = s_prefix;
-      for (int v = tid; v < V; v += SMP_THREADS) {
-        const uint32_t key = fkey(adjusted(a, lg, cnt, ban, v));
-        if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+      if (local) {
+        for (int i = tid; i < n_local; i += SMP_THREADS) {
+          const uint32_t key = lkey[i];
+          if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        }
+      } else {
+        for (int v = tid; v < V; v += SMP_THREADS) {
+          const uint32_t key = fkey(adjusted(a, lg, cnt, ban, v));
+          if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        }
       }
       __syncthreads();
       if (tid == 0) {
@@ -137,33 +158,67 @@ __global__ void __launch_bounds__(SMP_THREADS) k_sample(const SampleArgs a) {
           rem -= int(hist[b]);
         }
         s_prefix = prefix | (uint32_t(b) << shift);
+        s_bin = int(hist[b]);
         s_remaining = rem;
       }
       mask |= 255u << shift;
       __syncthreads();
+      if (!local && shift > 0 && (k - s_remaining) + s_bin <= SMP_CAP) {
+        // keys whose leading bits are at or above the chosen bin's
+        const uint32_t top = s_prefix >> shift;
+        for (int v = tid; v < V; v += SMP_THREADS) {
+          const uint32_t key = fkey(adjusted(a, lg, cnt, ban, v));
+          if ((key >> shift) >= top) {
+            const int at = atomicAdd(&s_n, 1);
+            lkey[at] = key;
+            lidx[at] = v;
+          }
+        }
+        __syncthreads();
+        local = true;
+        n_local = s_n;
+      }
     }
     const uint32_t thr = s_prefix;
-    const int need_eq = s_remaining;
-    // gather: thread t scans ids [t * C, (t + 1) * C) in order
-    const int C = (V + SMP_THREADS - 1) / SMP_THREADS;
-    const int v0 = min(V, tid * C), v1 = min(V, v0 + C);
-    int n_gt = 0, n_eq = 0;
-    for (int v = v0; v < v1; ++v) {
-      const uint32_t key = fkey(adjusted(a, lg, cnt, ban, v));
-      n_gt += key > thr;
-      n_eq += key == thr;
-    }
-    int gt_off, eq_off;
-    const int tot_gt = block_scan(n_gt, &gt_off, warp_sums);
-    block_scan(n_eq, &eq_off, warp_sums);
-    for (int v = v0; v < v1; ++v) {
-      const float x = adjusted(a, lg, cnt, ban, v);
-      const uint32_t key = fkey(x);
-      if (key > thr) {
-        cval[gt_off] = x; cidx[gt_off] = v; ++gt_off;
-      } else if (key == thr) {
-        if (eq_off < need_eq) { cval[tot_gt + eq_off] = x; cidx[tot_gt + eq_off] = v; }
-        ++eq_off;
+    const int need_eq = s_remaining, tot_gt = k - need_eq;
+    if (local) {
+      // larger keys in any order (the sort below fixes it); of the keys equal
+      // to the threshold, the need_eq lowest ids
+      if (tid == 0) s_n = 0;
+      __syncthreads();
+      for (int i = tid; i < n_local; i += SMP_THREADS) {
+        const uint32_t key = lkey[i];
+        if (key > thr) {
+          const int at = atomicAdd(&s_n, 1);
+          cval[at] = fval(key); cidx[at] = lidx[i];
+        } else if (key == thr) {
+          int rank = 0;
+          for (int j = 0; j < n_local; ++j) rank += lkey[j] == thr && lidx[j] < lidx[i];
+          if (rank < need_eq) { cval[tot_gt + rank] = fval(key); cidx[tot_gt + rank] = lidx[i]; }
+        }
+      }
+    } else {
+      // gather: thread t scans ids [t * C, (t + 1) * C) in order
+      const int C = (V + SMP_THREADS - 1) / SMP_THREADS;
+      const int v0 = min(V, tid * C), v1 = min(V, v0 + C);
+      int n_gt = 0, n_eq = 0;
+      for (int v = v0; v < v1; ++v) {
+        const uint32_t key = fkey(adjusted(a, lg, cnt, ban, v));
+        n_gt += key > thr;
+        n_eq += key == thr;
+      }
+      int gt_off, eq_off;
+      block_scan(n_gt, &gt_off, warp_sums);
+      block_scan(n_eq, &eq_off, warp_sums);
+      for (int v = v0; v < v1; ++v) {
+        const float x = adjusted(a, lg, cnt, ban, v);
+        const uint32_t key = fkey(x);
+        if (key > thr) {
+          cval[gt_off] = x; cidx[gt_off] = v; ++gt_off;
+        } else if (key == thr) {
+          if (eq_off < need_eq) { cval[tot_gt + eq_off] = x; cidx[tot_gt + eq_off] = v; }
+          ++eq_off;
+        }
       }
     }
     // bitonic sort of the k candidates: logit descending, id ascending
@@ -221,8 +276,8 @@ void launch_sample(const SampleArgs& a, cudaStream_t st) {
   if (a.nseq < 1 || a.vocab < 1 || a.row_stride < a.vocab) throw Error(ERR_INVALID, "sampling: bad shape");
   if (a.temperature > 0.f && a.top_k > SMP_KMAX && a.vocab > SMP_KMAX)
     throw Error(ERR_UNSUPPORTED, "sampling: top_k above " + std::to_string(SMP_KMAX));
-  const size_t smem = size_t((a.vocab + 31) / 32) * 4;
-  if (smem > 160 * 1024) throw Error(ERR_UNSUPPORTED, "sampling: vocabulary above 1.3M tokens");
+  const size_t smem = size_t((a.vocab + 31) / 32) * 4 + size_t(SMP_CAP) * 8;
+  if (smem > 200 * 1024) throw Error(ERR_UNSUPPORTED, "sampling: vocabulary above 1.1M tokens");
   SWL_CUDA(cudaFuncSetAttribute(k_sample, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
   k_sample<<<a.nseq, SMP_THREADS, smem, st>>>(a);
   SWL_CUDA(cudaGetLastError());
