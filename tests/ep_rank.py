@@ -8,7 +8,8 @@ an expert-parallel one that computes only its share of the routed experts and
 exchanges partial sums with the other ranks over NCCL. Both prefill the same
 seeded prompts, then decode `steps` greedy tokens (fed from the plain model's
 argmax so both see the same inputs); the logits of every step are compared
-within the north-star tolerances (2e-2 max-abs, 1e-3 relative-L2).
+within the logit tolerances of the batched parity tests (2e-2 max-abs, 1e-3
+relative-L2).
 """
 import json
 import os
