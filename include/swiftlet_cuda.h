@@ -173,6 +173,19 @@ int swl_debug_layer(swl_model* model, swl_state* state, int32_t layer, const flo
                     int32_t* pick_ids, float* pick_w);
 /* Delta-rule state of a DeltaNet layer ([nv][dv][dk] f32, host). */
 int swl_debug_delta_state(swl_model* model, swl_state* state, int32_t layer, float* out);
+/* Kernel family of every launch of one single-token decode step (embedding,
+ * layers, lm_head with greedy argmax), comma-separated into out (out_len
+ * bytes including the terminator; SWL_ERR_CAPACITY if too small). Families:
+ * embed, igemv / sgemv / gemv (dense projections, router, lm_head), router,
+ * delta, attn, igateup / sgateup / gateup, idown / sdown / down (the integer
+ * tensor-core, slice and register-streaming kernels). Nothing runs. */
+int swl_debug_kernel_path(swl_model* model, char* out, int32_t out_len);
+/* Runs one bounded mbarrier wait that nothing completes, with a limit of
+ * limit_us microseconds (1 .. 1e6), through the same status word the decode
+ * kernels report their timeouts in: returns SWL_ERR_CUDA once the wait has
+ * given up, the way a decode step reports a weight copy that never arrived,
+ * and leaves the model usable. */
+int swl_debug_wait_timeout(swl_model* model, int32_t limit_us);
 
 /* Expert-GEMV sweep for the roofline measurement: `iters` passes over all
  * layers of the fused routed+shared expert kernels (gate/up + SiLU, then
@@ -251,9 +264,14 @@ typedef struct swl_affine_matrix {
  * GPU (different streams without ordering) race on it. Work is queued on
  * `stream` (a cudaStream_t; NULL = legacy default stream) and not waited
  * for. The first call on a device looks up the array's device address
- * (host-side set-up); make that first call before any stream capture. */
+ * (host-side set-up); make that first call before any stream capture.
+ * d_status (device int32, may be NULL): the kernels OR bit 0 into it when a
+ * bounded wait for their weight copies gave up (about 2 s), in which case y
+ * is incomplete; the call never clears it, so the caller zeroes it once and
+ * reads it after synchronising. With NULL such a timeout goes unreported. */
 int swl_expert_swiglu_noalloc(const swl_affine_matrix* gate, const swl_affine_matrix* up,
-                              const swl_affine_matrix* down, const float* x, float* y, void* stream);
+                              const swl_affine_matrix* down, const float* x, float* y, int32_t* d_status,
+                              void* stream);
 
 #ifdef __cplusplus
 }

@@ -90,11 +90,13 @@ _SIGNATURES = {
     "swl_debug_tensor_bytes": (_I, [_P, C.c_char_p, _I64, _I64, _P, _I64]),
     "swl_debug_layer": (_I, [_P, _P, C.c_int32, _P, _P, _P, _P]),
     "swl_debug_delta_state": (_I, [_P, _P, C.c_int32, _P]),
+    "swl_debug_kernel_path": (_I, [_P, C.c_char_p, C.c_int32]),
+    "swl_debug_wait_timeout": (_I, [_P, C.c_int32]),
     "swl_bench_expert_sweep": (_I, [_P, C.c_int32, _P, _P, _P]),
     "swl_trace_dump": (_I, [_P, C.c_char_p]),
     "swl_kernel_gemv_affine": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P]),
     "swl_kernel_expert_swiglu": (_I, [_P] * 9 + [_I, _I, _I, _I, _I, _P, _P]),
-    "swl_expert_swiglu_noalloc": (_I, [C.POINTER(swl_affine_matrix)] * 3 + [_P, _P, _P]),
+    "swl_expert_swiglu_noalloc": (_I, [C.POINTER(swl_affine_matrix)] * 3 + [_P, _P, _P, _P]),
 }
 
 _lib = None
@@ -355,6 +357,18 @@ class QwenCUDAModel:
         _check(lib().swl_debug_delta_state(self._h, state._bind(self), layer, _ptr(out)))
         return out
 
+    def kernel_path(self) -> list[str]:
+        """Kernel family of every launch of one single-token decode step
+        (``swl_debug_kernel_path``): e.g. ``["embed", "igemv", "delta", ...]``."""
+        buf = C.create_string_buffer(1 << 16)
+        _check(lib().swl_debug_kernel_path(self._h, buf, len(buf)))
+        return buf.value.decode().split(",")
+
+    def debug_wait_timeout(self, limit_us: int) -> None:
+        """One bounded wait that nothing completes (``swl_debug_wait_timeout``):
+        raises SwiftletError(SWL_ERR_CUDA) once it has given up."""
+        _check(lib().swl_debug_wait_timeout(self._h, int(limit_us)))
+
 
 class swl_sample_options(C.Structure):
     _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("presence_penalty", C.c_float),
@@ -419,10 +433,13 @@ def expert_swiglu(gate, up, down, hidden: int, inter: int, group: int, bits: int
 
 
 def expert_swiglu_noalloc(gate: swl_affine_matrix, up: swl_affine_matrix, down: swl_affine_matrix, d_x: int,
-                          d_y: int, stream: int | None = None) -> None:
-    """Allocation-free expert SwiGLU on device buffers (queued on `stream`, not waited for)."""
+                          d_y: int, stream: int | None = None, d_status: int | None = None) -> None:
+    """Allocation-free expert SwiGLU on device buffers (queued on `stream`, not waited for).
+    `d_status` (device int32 address, optional) gets bit 0 set when a bounded
+    wait inside the kernels gave up."""
     _check(lib().swl_expert_swiglu_noalloc(C.byref(gate), C.byref(up), C.byref(down), C.c_void_p(d_x),
-                                           C.c_void_p(d_y), C.c_void_p(stream or None)))
+                                           C.c_void_p(d_y), C.c_void_p(d_status or None),
+                                           C.c_void_p(stream or None)))
 
 
 class TextGenerator:

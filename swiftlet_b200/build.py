@@ -38,8 +38,12 @@ def _nvcc() -> str:
     return os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 
-def _compile(src: str, verbose: bool) -> str:
+def _compile(src: str, verbose: bool, force: bool = True) -> str:
     obj = os.path.join(OBJ, os.path.basename(src) + ".o")
+    if not force and os.path.exists(obj):
+        t = os.path.getmtime(obj)
+        if all(os.path.getmtime(p) <= t for p in [src] + headers()):
+            return obj
     cmd = [_nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC,-O3",
            "-I", os.path.join(ROOT, "include"), "-c", src, "-o", obj]
     if verbose:
@@ -53,7 +57,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
         return LIB
     os.makedirs(OBJ, exist_ok=True)
     with cf.ThreadPoolExecutor(max_workers=max(1, os.cpu_count() or 1)) as ex:
-        objs = list(ex.map(lambda s: _compile(s, verbose), sources()))
+        objs = list(ex.map(lambda s: _compile(s, verbose, force), sources()))
     subprocess.run([_nvcc(), *ARCH, "-shared", "-o", LIB + ".tmp", *objs], check=True)
     os.replace(LIB + ".tmp", LIB)
     return LIB

@@ -6,6 +6,11 @@
   hidden 2048, vocab 151936, 256 experts top-8, intermediate 512, shared 512
   (qwen3_5 split DeltaNet projections).
 * ``NEXT_80B`` — Qwen3-Next-80B-A3B shape: 48 layers, 512 experts top-10.
+* ``MID`` — the 35B layout (split DeltaNet projections, 128-dim DeltaNet
+  heads, 3 DeltaNet : 1 GQA) shrunk so the CPU oracle runs 32 steps in
+  seconds: hidden 512, 4 layers, vocab 2048, 16 experts top-4. Every linear
+  module is 16-byte aligned with 8 groups of 64 per row, so decode takes the
+  same integer tensor-core kernels as the 35B shape.
 """
 
 TINY = {
@@ -43,6 +48,13 @@ NEXT_80B = {
     "shared_expert_intermediate_size": 512, "norm_topk_prob": True,
     "tie_word_embeddings": False, "full_attention_interval": 4,
 }
+
+
+MID = dict(Q35_35B)
+MID.update({"hidden_size": 512, "num_hidden_layers": 4, "vocab_size": 2048, "num_attention_heads": 4,
+            "num_key_value_heads": 2, "head_dim": 128, "linear_num_key_heads": 2, "linear_num_value_heads": 4,
+            "num_experts": 16, "num_experts_per_tok": 4})
+MID_SEED = 29  # synthetic weights; its 32 greedy steps keep a top-1 margin of 0.025 over the runner-up
 
 
 def with_layers(cfg: dict, n: int) -> dict:

@@ -11,6 +11,7 @@
 #include <cudaTypedefs.h>
 
 #include "kernels.h"
+#include "launch.h"
 #include "slice.h"
 
 namespace swl {
@@ -499,6 +500,7 @@ void launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl) {
 #define CALL(B, D) igemv_fmt<B, D>(a, ST, TM, none, ST.kpg(), sgrid, ssmem, st, pdl)
       SWL_DISPATCH_IMMA(l0.bits, l0.dt, CALL);
 #undef CALL
+      path_note("igemv");
       return;
     }
     if (plan_dense(lins, ys, a.nseg, a.in, a.prologue, a.head_dim, a.x, a.aux, a.aux2, a.x_out, a.status, ST, sR,
@@ -507,6 +509,7 @@ void launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl) {
 #define CALL(B, D) sgemv_fmt<B, D>(a, ST, none, sR, sgrid, ssmem, st, pdl)
       SWL_DISPATCH_FMT(l0.bits, l0.dt, CALL);
 #undef CALL
+      path_note("sgemv");
       return;
     }
   }
@@ -521,6 +524,7 @@ void launch_gemv(const GemvArgs& a, cudaStream_t st, bool pdl) {
 #define CALL(B, D) gemv_fmt<B, D>(a, T, R, CPL, gss, LPR, nslab, grid, smem, st, pdl)
   SWL_DISPATCH_FMT(l0.bits, l0.dt, CALL);
 #undef CALL
+  path_note("gemv");
 }
 
 void launch_router(const RouterArgs& r, int E, cudaStream_t st, bool pdl) {
@@ -551,10 +555,12 @@ void launch_router(const RouterArgs& r, int E, cudaStream_t st, bool pdl) {
 #define CALL(B, D) igemv_fmt<B, D>(a, ST, TM, rt, ST.kpg(), sgrid, ssmem, st, pdl)
         SWL_DISPATCH_IMMA(r.gate.bits, r.gate.dt, CALL);
 #undef CALL
+        path_note("igemv");
       } else {
 #define CALL(B, D) sgemv_fmt<B, D>(a, ST, rt, sR, sgrid, ssmem, st, pdl)
         SWL_DISPATCH_FMT(r.gate.bits, r.gate.dt, CALL);
 #undef CALL
+        path_note("sgemv");
       }
       return;
     }
@@ -569,6 +575,7 @@ void launch_router(const RouterArgs& r, int E, cudaStream_t st, bool pdl) {
 #define CALL(B, D) router_fmt<B, D>(r, T, E, CPL, gss, LPR, nslab, grid, smem, st, pdl)
   SWL_DISPATCH_FMT(r.gate.bits, r.gate.dt, CALL);
 #undef CALL
+  path_note("router");
 }
 
 void launch_moe_gateup(const MoeArgs& m, cudaStream_t st, bool pdl) {
@@ -586,12 +593,14 @@ void launch_moe_gateup(const MoeArgs& m, cudaStream_t st, bool pdl) {
 #define CALL(B, D) igateup_fmt<B, D>(m, ST, TM, ST.kpg(), sgrid, ssmem, st, pdl)
       SWL_DISPATCH_IMMA(g.bits, g.dt, CALL);
 #undef CALL
+      path_note("igateup");
       return;
     }
     if (plan_gateup(m, ST, sgrid, ssmem)) {
 #define CALL(B, D) sgateup_fmt<B, D>(m, ST, sgrid, ssmem, st, pdl)
       SWL_DISPATCH_FMT(g.bits, g.dt, CALL);
 #undef CALL
+      path_note("sgateup");
       return;
     }
   }
@@ -606,6 +615,7 @@ void launch_moe_gateup(const MoeArgs& m, cudaStream_t st, bool pdl) {
 #define CALL(B, D) gateup_fmt<B, D>(m, R, CPL, gss, LPR, tr, ts, nslab, grid, smem, st, pdl)
   SWL_DISPATCH_FMT(g.bits, g.dt, CALL);
 #undef CALL
+  path_note("gateup");
 }
 
 void launch_moe_down(const MoeArgs& m, cudaStream_t st, bool pdl) {
@@ -622,12 +632,14 @@ void launch_moe_down(const MoeArgs& m, cudaStream_t st, bool pdl) {
 #define CALL(B, D_) idown_fmt<B, D_>(m, ST, TM, ST.kpg(), sgrid, ssmem, st, pdl)
       SWL_DISPATCH_IMMA(d.bits, d.dt, CALL);
 #undef CALL
+      path_note("idown");
       return;
     }
     if (plan_down(m, ST, sgrid, ssmem)) {
 #define CALL(B, D_) sdown_fmt<B, D_>(m, ST, sgrid, ssmem, st, pdl)
       SWL_DISPATCH_FMT(d.bits, d.dt, CALL);
 #undef CALL
+      path_note("sdown");
       return;
     }
   }
@@ -645,6 +657,7 @@ void launch_moe_down(const MoeArgs& m, cudaStream_t st, bool pdl) {
 #define CALL(B, D_) down_fmt<B, D_>(m, ne, R, gss, LPR, nslab, grid, smem, st, pdl)
   SWL_DISPATCH_FMT(d.bits, d.dt, CALL);
 #undef CALL
+  path_note("down");
 }
 
 }  // namespace swl

@@ -85,16 +85,17 @@ __device__ __forceinline__ bool mbar_try(uint64_t* b, unsigned parity) {
 // long wait (a producer waiting for a free slot) leaves the issue slots to
 // the warps doing the work.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* b, unsigned parity, unsigned long long limit_ns) {
   if (mbar_try(b, parity)) return true;
   const unsigned long long t0 = gtimer();
   for (int i = 0; i < (1 << 26); ++i) {
     if (mbar_try(b, parity)) return true;
     if (i >= 16) __nanosleep(i < 64 ? 64 : 256);
-    if (gtimer() - t0 > kWaitLimitNs) break;
+    if (gtimer() - t0 > limit_ns) break;
   }
   return false;
 }
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, unsigned parity) { return mbar_wait_for(b, parity, kWaitLimitNs); }
 // L2 policy for weights that are read once per token: evict them first, so
 // activations, recurrent state and the KV cache stay resident.
 __device__ __forceinline__ uint64_t l2_evict_first() {

@@ -362,6 +362,9 @@ void launch_delta_batch(const DeltaArgs& a, int T, cudaStream_t stream, bool pdl
 // T > 1: T sequences of a batched step (grid.z = T).
 void launch_attn(const AttnArgs& a, cudaStream_t stream, bool pdl, int T = 1);
 void launch_embed(const EmbedArgs& a, int hidden, cudaStream_t stream, bool pdl);
+// Test helper: a bounded mbarrier wait that nothing completes gives up after
+// limit_ns and sets bit 0 of *status (the decode kernels' timeout report).
+void launch_wait_probe(int* status, unsigned long long limit_ns, cudaStream_t stream);
 // Debug/test helper: dequantise rows [r0, r1) of a module to f32.
 void launch_dequant(const QLin& l, int64_t r0, int64_t r1, float* out, cudaStream_t stream);
 

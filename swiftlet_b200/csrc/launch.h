@@ -3,9 +3,20 @@
 // cudaGetLastError, which can hold an older, unrelated error).
 #pragma once
 
+#include <string>
+#include <vector>
+
 #include "common.h"
 
 namespace swl {
+
+// While set, every launcher on this thread appends the kernel family it
+// chose ("igemv", "idown", "delta", ...), so a test can assert which kernels a
+// decode step runs (the tensor-core, slice or register-streaming ones).
+extern thread_local std::vector<std::string>* g_path_log;
+inline void path_note(const char* family) {
+  if (g_path_log) g_path_log->push_back(family);
+}
 
 template <typename Kern, typename... Args>
 void launch(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl, Args... args) {

@@ -847,6 +847,7 @@ void launch_delta(const DeltaArgs& a, cudaStream_t st, bool pdl) {
   const int nch = 2 * a.dk + a.rows_per_block;
   const size_t smem = size_t(2 * a.dk + a.rows_per_block + nch * (2 * a.conv_k - 1)) * 4;
   launch(k_delta<DELTA_RPW>, dim3(a.nv, a.dv / a.rows_per_block), dim3(DELTA_THREADS), smem, st, pdl, a);
+  path_note("delta");
 }
 
 // Batched: up to 128 rows per CTA (a whole 128-row value head), so the q/k
@@ -893,10 +894,33 @@ void launch_attn(const AttnArgs& a, cudaStream_t st, bool pdl, int T) {
     case 256: launch_cluster(k_attn<256>, grid, block, cluster, attn_smem_bytes<256>(G, a.rot), st, pdl, a); break;
     default: throw Error(ERR_UNSUPPORTED, "attention head size must be 16, 32, 64, 128 or 256");
   }
+  path_note("attn");
 }
 
 void launch_embed(const EmbedArgs& a, int hidden, cudaStream_t st, bool pdl) {
   launch(k_embed, dim3((hidden + 255) / 256), dim3(256), 0, st, pdl, a, hidden);
+  path_note("embed");
+}
+
+// A wait that nothing completes: one mbarrier expecting an arrival that never
+// comes, waited on with the streaming kernels' bounded wait and a short
+// limit. Giving up sets bit 0 of the status word exactly as those kernels do;
+// no copy is in flight, so nothing is left behind.
+__global__ void k_wait_probe(int* status, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    mbar_init_fence();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (!mbar_wait_for(&bar, 0, limit_ns)) atomicOr(status, 1);
+    asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(&bar)) : "memory");
+  }
+}
+
+void launch_wait_probe(int* status, unsigned long long limit_ns, cudaStream_t st) {
+  launch(k_wait_probe, dim3(1), dim3(32), 0, st, false, status, limit_ns);
 }
 
 void launch_bembed(const EmbedArgs& a, int hidden, int T, cudaStream_t st, bool pdl) {

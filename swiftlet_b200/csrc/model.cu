@@ -19,12 +19,14 @@
 #include "ep_nccl.h"
 #include "host_io.h"
 #include "kernels.h"
+#include "launch.h"
 #include "synth.h"
 
 namespace swl {
 
 static thread_local std::string g_error;
 void set_last_error(const std::string& message) { g_error = message; }
+thread_local std::vector<std::string>* g_path_log = nullptr;
 
 static float bf16f(uint16_t u) { uint32_t v = uint32_t(u) << 16; float f; memcpy(&f, &v, 4); return f; }
 static float f16f(uint16_t h) {
@@ -1629,6 +1631,53 @@ int swl_debug_delta_state(swl_model* model, swl_state* state, int32_t layer, flo
   SWL_CUDA(cudaSetDevice(m.device));
   SWL_CUDA(cudaStreamSynchronize(m.stream));
   SWL_CUDA(cudaMemcpy(out, state->s.dstate[layer], size_t(m.cfg.nv) * m.cfg.dv * m.cfg.dk * 4, cudaMemcpyDeviceToHost));
+  API_END
+}
+
+int swl_debug_kernel_path(swl_model* model, char* out, int32_t out_len) {
+  API_BEGIN
+  if (!model || !out || out_len < 1) throw Error(ERR_INVALID, "null argument");
+  Model& m = model->m;
+  SWL_CUDA(cudaSetDevice(m.device));
+  // Enqueue one decode token (body and greedy head) into a throwaway capture:
+  // the launchers record their choices, nothing runs.
+  std::vector<std::string> log;
+  struct Scope {
+    explicit Scope(std::vector<std::string>* p) { g_path_log = p; }
+    ~Scope() { g_path_log = nullptr; }
+  } scope(&log);
+  SWL_CUDA(cudaStreamSynchronize(m.stream));
+  cudaGraph_t graph = nullptr;
+  SWL_CUDA(cudaStreamBeginCapture(m.stream, cudaStreamCaptureModeThreadLocal));
+  try {
+    m.enqueue_body(m.stream);
+    m.enqueue_head(m.stream, true);
+  } catch (...) {
+    cudaStreamEndCapture(m.stream, &graph);
+    if (graph) cudaGraphDestroy(graph);
+    throw;
+  }
+  SWL_CUDA(cudaStreamEndCapture(m.stream, &graph));
+  if (graph) cudaGraphDestroy(graph);
+  std::string joined;
+  for (size_t i = 0; i < log.size(); ++i) joined += (i ? "," : "") + log[i];
+  if (int64_t(joined.size()) + 1 > out_len)
+    throw Error(ERR_CAPACITY, "kernel path needs " + std::to_string(joined.size() + 1) + " bytes");
+  memcpy(out, joined.c_str(), joined.size() + 1);
+  API_END
+}
+
+int swl_debug_wait_timeout(swl_model* model, int32_t limit_us) {
+  API_BEGIN
+  if (!model) throw Error(ERR_INVALID, "null model");
+  if (limit_us < 1 || limit_us > 1000000) throw Error(ERR_INVALID, "limit must be 1 us .. 1 s");
+  Model& m = model->m;
+  SWL_CUDA(cudaSetDevice(m.device));
+  launch_wait_probe(m.kstatus, (unsigned long long)limit_us * 1000ull, m.stream);
+  int word = 0;
+  SWL_CUDA(cudaMemcpyAsync(&word, m.kstatus, 4, cudaMemcpyDeviceToHost, m.stream));
+  SWL_CUDA(cudaStreamSynchronize(m.stream));
+  m.check_status(&word);  // throws ERR_CUDA (and clears the word) when the wait gave up
   API_END
 }
 

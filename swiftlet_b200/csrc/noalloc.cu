@@ -20,10 +20,16 @@ namespace swl {
 // Largest intermediate size (moe_intermediate_size) the shared scratch holds.
 constexpr int kNoAllocMaxInter = 16384;
 // [0, kNoAllocMaxInter): the intermediate vector; [kNoAllocMaxInter]: the
-// combine weight (1.0). 64 KiB + 256 B per device.
+// combine weight (1.0); [kNoAllocMaxInter + 1]: the status word the kernels
+// write when the caller passes none. 64 KiB + 256 B per device.
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocMaxInter + 64];
 
-__global__ void k_noalloc_set_weight() { g_noalloc_scratch[kNoAllocMaxInter] = 1.0f; }
+// Sets the combine weight and clears the internal status word before the
+// expert kernels of one call run.
+__global__ void k_noalloc_set_weight() {
+  g_noalloc_scratch[kNoAllocMaxInter] = 1.0f;
+  reinterpret_cast<int*>(g_noalloc_scratch)[kNoAllocMaxInter + 1] = 0;
+}
 
 // Device address of the scratch array, looked up once per device with that
 // device current. In host code the array's name is only a host-side stand-in.
@@ -68,12 +74,13 @@ static QLin affine_of(const swl_affine_matrix* m, const char* what) {
 using namespace swl;
 
 extern "C" int swl_expert_swiglu_noalloc(const swl_affine_matrix* gate, const swl_affine_matrix* up,
-                                         const swl_affine_matrix* down, const float* d_x, float* d_y, void* stream) {
+                                         const swl_affine_matrix* down, const float* d_x, float* d_y,
+                                         int32_t* d_status, void* stream) {
   try {
-    cudaGetLastError();  // an unrelated earlier failure must not be reported as this call's
     const QLin g = affine_of(gate, "gate"), u = affine_of(up, "up"), d = affine_of(down, "down");
     if (!d_x || !d_y) throw Error(ERR_INVALID, "null input or output");
     if (reinterpret_cast<uintptr_t>(d_x) % 16) throw Error(ERR_INVALID, "x must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(d_status) % 4) throw Error(ERR_INVALID, "status word must be 4-byte aligned");
     if (u.out != g.out || u.in != g.in || d.in != g.out || d.out != g.in)
       throw Error(ERR_INVALID, "gate/up must be [inter, hidden] and down [hidden, inter]");
     if (g.bits != u.bits || g.bits != d.bits || g.dt != u.dt || g.dt != d.dt || g.gs != u.gs || g.gs != d.gs)
@@ -95,6 +102,9 @@ extern "C" int swl_expert_swiglu_noalloc(const swl_affine_matrix* gate, const sw
     m.x = d_x;
     m.h = d_y;  // the down kernel accumulates: start from zero
     m.pick_ids = nullptr; m.pick_w = nullptr; m.advance_sd = nullptr; m.advance_cursor = nullptr;
+    // bit 0 of the status word: a bounded wait for weight copies gave up and
+    // y is incomplete; the caller's word if given, else the scratch's own
+    m.status = d_status ? d_status : reinterpret_cast<int*>(scratch + kNoAllocMaxInter + 1);
     SWL_CUDA(cudaMemsetAsync(d_y, 0, size_t(d.out) * sizeof(float), st));
     launch(k_noalloc_set_weight, dim3(1), dim3(1), 0, st, false);
     launch_moe_gateup(m, st, false);
