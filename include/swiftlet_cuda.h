@@ -82,6 +82,23 @@ int swl_state_free(swl_state* state);
 /* DecodeState.position (QwenCPUModel.swift:185). */
 int32_t swl_state_position(const swl_state* state);
 
+/* Conversation-state reuse (SwiftletSession.swift:114-132 keeps one
+ * DecodeState across turns; :193-213 decides when a follow-up extends it).
+ * swl_state_reset replaces SwiftletSession.resetConversation (a fresh
+ * DecodeState): position 0, zeroed recurrent state. swl_state_copy forks a
+ * sequence: dst (same model, max_ctx >= src position) gets src's position,
+ * conv rings, delta states and KV rows. swl_state_save writes a host snapshot
+ * of the whole decode state (NULL out: *written = bytes needed;
+ * SWL_ERR_CAPACITY if out_bytes is short); swl_state_load restores one into
+ * any state of a model with the same shape (SWL_ERR_FORMAT otherwise;
+ * SWL_ERR_CAPACITY when the state's max_ctx is below the snapshot's
+ * position). Decoding from a restored or copied state gives the same logits
+ * as continuing the original. */
+int swl_state_reset(swl_state* state);
+int swl_state_copy(swl_state* dst, const swl_state* src);
+int swl_state_save(const swl_state* state, void* out, int64_t out_bytes, int64_t* written);
+int swl_state_load(swl_state* state, const void* in, int64_t in_bytes);
+
 /* Replaces InferenceModel.step(_:state:) (TextGenerator.swift:7;
  * QwenMetalModel.swift:359-366): consumes n >= 1 tokens, advances the
  * state's position by n and writes the LAST position's logits (vocab_size
@@ -153,6 +170,25 @@ int swl_pool_stats(const swl_model* model, swl_pool_info* out);
  * HBM pool holds the full expert set; a budget below it returns
  * SWL_ERR_CAPACITY and leaves the pool untouched. */
 int swl_pool_resize(swl_model* model, double gb);
+
+/* Container verification (scripts/verify_container.py; manifest fields
+ * Qpack.swift:38-46). Every file named in `hashes_json` (NULL:
+ * <dir>/hashes.json, {"files": {relative path: sha256 hex}}) is hashed (host
+ * threads in parallel) and compared; a file whose size differs from the
+ * size manifest.json lists for it counts as corrupt. Returns SWL_OK when all
+ * match, SWL_ERR_FORMAT when any file is corrupt or missing (SWL_ERR_IO when
+ * the hash list cannot be read). With delete_corrupt != 0 the corrupt files
+ * and manifest.json are deleted, as the script does, so the installer reads
+ * the container as incomplete and fetches just those files again. `out` (may
+ * be NULL) receives the counts either way. No GPU is used. */
+typedef struct swl_verify_report {
+  int64_t checked, ok, corrupt, missing;
+  char first_bad[256]; /* relative path of the first bad file ("" if none) */
+} swl_verify_report;
+int swl_qpack_verify(const char* dir, const char* hashes_json, int32_t delete_corrupt, swl_verify_report* out);
+/* SHA-256 of a file as 64 lowercase hex digits plus a terminator (hex_out
+ * holds 65 bytes). */
+int swl_sha256_file(const char* path, char* hex_out);
 
 /* Runs all work of `model` on this CUDA stream (cudaStream_t); NULL selects
  * the model's own stream. Graphs are re-captured on the new stream. */

@@ -52,6 +52,11 @@ class swl_config(C.Structure):
         ("rope_theta", C.c_double), ("partial_rotary_factor", C.c_double), ("rms_norm_eps", C.c_double)]
 
 
+class swl_verify_report(C.Structure):
+    _fields_ = [("checked", C.c_int64), ("ok", C.c_int64), ("corrupt", C.c_int64), ("missing", C.c_int64),
+                ("first_bad", C.c_char * 256)]
+
+
 class swl_affine_matrix(C.Structure):
     """A device-resident MLX-affine matrix (see include/swiftlet_cuda.h)."""
     _fields_ = [("weight", C.c_void_p), ("scales", C.c_void_p), ("biases", C.c_void_p), ("rows", C.c_int32),
@@ -91,6 +96,12 @@ _SIGNATURES = {
     "swl_debug_layer": (_I, [_P, _P, C.c_int32, _P, _P, _P, _P]),
     "swl_debug_delta_state": (_I, [_P, _P, C.c_int32, _P]),
     "swl_debug_kernel_path": (_I, [_P, C.c_char_p, C.c_int32]),
+    "swl_state_reset": (_I, [_P]),
+    "swl_qpack_verify": (_I, [C.c_char_p, C.c_char_p, C.c_int32, C.POINTER(swl_verify_report)]),
+    "swl_sha256_file": (_I, [C.c_char_p, C.c_char_p]),
+    "swl_state_copy": (_I, [_P, _P]),
+    "swl_state_save": (_I, [_P, _P, C.c_int64, C.POINTER(C.c_int64)]),
+    "swl_state_load": (_I, [_P, _P, C.c_int64]),
     "swl_debug_wait_timeout": (_I, [_P, C.c_int32]),
     "swl_bench_expert_sweep": (_I, [_P, C.c_int32, _P, _P, _P]),
     "swl_trace_dump": (_I, [_P, C.c_char_p]),
@@ -357,6 +368,28 @@ class QwenCUDAModel:
         _check(lib().swl_debug_delta_state(self._h, state._bind(self), layer, _ptr(out)))
         return out
 
+    # ---- conversation-state reuse (SwiftletSession.swift:114-132, 193-213) ----
+    def reset_state(self, state: DecodeState) -> None:
+        """SwiftletSession.resetConversation: position 0, zeroed recurrent state."""
+        _check(lib().swl_state_reset(state._bind(self)))
+
+    def copy_state(self, dst: DecodeState, src: DecodeState) -> None:
+        """Forks `src` into `dst` (position, conv rings, delta states, KV rows)."""
+        _check(lib().swl_state_copy(dst._bind(self), src._bind(self)))
+
+    def save_state(self, state: DecodeState) -> bytes:
+        """Host snapshot of the state's whole decode state."""
+        h = state._bind(self)
+        n = C.c_int64()
+        _check(lib().swl_state_save(h, None, 0, C.byref(n)))
+        buf = C.create_string_buffer(n.value)
+        _check(lib().swl_state_save(h, buf, n.value, C.byref(n)))
+        return buf.raw[:n.value]
+
+    def load_state(self, state: DecodeState, data: bytes) -> None:
+        """Restores a snapshot taken by save_state on a model of the same shape."""
+        _check(lib().swl_state_load(state._bind(self), data, len(data)))
+
     def kernel_path(self) -> list[str]:
         """Kernel family of every launch of one single-token decode step
         (``swl_debug_kernel_path``): e.g. ``["embed", "igemv", "delta", ...]``."""
@@ -430,6 +463,28 @@ def expert_swiglu(gate, up, down, hidden: int, inter: int, group: int, bits: int
     y = np.empty(hidden, np.float32)
     _check(lib().swl_kernel_expert_swiglu(*[_ptr(a) for a in arrs], sd, bits, group, hidden, inter, _ptr(x), _ptr(y)))
     return y
+
+
+def verify_container(container: str, hashes_json: str | None = None, delete_corrupt: bool = False) -> dict:
+    """SHA-256 check of a .qpack container against its hashes.json
+    (scripts/verify_container.py). Returns the counts; raises SwiftletError
+    (SWL_ERR_FORMAT) when a file is corrupt or missing, after filling them."""
+    r = swl_verify_report()
+    rc = lib().swl_qpack_verify(os.fsencode(container), os.fsencode(hashes_json) if hashes_json else None,
+                                int(bool(delete_corrupt)), C.byref(r))
+    rep = {"checked": r.checked, "ok": r.ok, "corrupt": r.corrupt, "missing": r.missing,
+           "first_bad": r.first_bad.decode()}
+    if rc != SWL_OK:
+        err = SwiftletError(rc, lib().swl_last_error().decode())
+        err.report = rep
+        raise err
+    return rep
+
+
+def sha256_file(path: str) -> str:
+    out = C.create_string_buffer(65)
+    _check(lib().swl_sha256_file(os.fsencode(path), out))
+    return out.value.decode()
 
 
 def expert_swiglu_noalloc(gate: swl_affine_matrix, up: swl_affine_matrix, down: swl_affine_matrix, d_x: int,

@@ -1275,6 +1275,152 @@ int swl_state_free(swl_state* state) {
 
 int32_t swl_state_position(const swl_state* state) { return state ? state->s.pos : -1; }
 
+// ---- conversation-state reuse (SwiftletSession.swift:114-132, 193-213) ----
+// A snapshot is the sequence's whole decode state: a 64-byte header (magic,
+// the shape fields it depends on, the position), then layer by layer the
+// DeltaNet conv ring [conv_k][conv_dim] and delta state [nv][dv][dk], or the
+// attention K then V rows [kv_heads][pos][head_dim], all f32.
+namespace {
+constexpr uint64_t kSnapMagic = 0x31504e534c5753ull;  // "SWLSNP1\0"
+struct SnapHeader {
+  uint64_t magic;
+  int32_t layers, hidden, conv_k, conv_dim, nv, dv, dk, kv_heads, head_dim, interval, pos, reserved[3];
+};
+static_assert(sizeof(SnapHeader) == 64, "snapshot header is 64 bytes");
+
+SnapHeader snap_header(const ModelConfig& c, int pos) {
+  SnapHeader h{};
+  h.magic = kSnapMagic;
+  h.layers = c.layers; h.hidden = c.hidden; h.conv_k = c.conv_k; h.conv_dim = c.conv_dim();
+  h.nv = c.nv; h.dv = c.dv; h.dk = c.dk; h.kv_heads = c.kv_heads; h.head_dim = c.head_dim;
+  h.interval = c.full_attn_interval; h.pos = pos;
+  return h;
+}
+int64_t snap_bytes(const ModelConfig& c, int pos) {
+  int64_t n = sizeof(SnapHeader);
+  for (int l = 0; l < c.layers; ++l)
+    n += c.is_linear(l) ? (int64_t(c.conv_k) * c.conv_dim() + int64_t(c.nv) * c.dv * c.dk) * 4
+                        : 2 * int64_t(c.kv_heads) * pos * c.head_dim * 4;
+  return n;
+}
+// Copies one state's contents to or from a flat buffer (device or host) or
+// another state; `kv_rows` rows of every K/V head.
+void copy_state_parts(const Model& m, const State& st, uint8_t* flat, bool to_flat, int kv_rows, cudaStream_t stream) {
+  const ModelConfig& c = m.cfg;
+  const size_t conv_b = size_t(c.conv_k) * c.conv_dim() * 4, ds_b = size_t(c.nv) * c.dv * c.dk * 4;
+  const size_t row_b = size_t(c.head_dim) * 4, pitch = size_t(st.max_ctx) * row_b, head_b = size_t(kv_rows) * row_b;
+  size_t off = sizeof(SnapHeader);
+  auto cp = [&](void* dev, size_t bytes) {
+    if (to_flat) SWL_CUDA(cudaMemcpyAsync(flat + off, dev, bytes, cudaMemcpyDefault, stream));
+    else SWL_CUDA(cudaMemcpyAsync(dev, flat + off, bytes, cudaMemcpyDefault, stream));
+    off += bytes;
+  };
+  auto cp_kv = [&](float* dev) {
+    if (head_b == 0) return;
+    if (to_flat)
+      SWL_CUDA(cudaMemcpy2DAsync(flat + off, head_b, dev, pitch, head_b, c.kv_heads, cudaMemcpyDefault, stream));
+    else
+      SWL_CUDA(cudaMemcpy2DAsync(dev, pitch, flat + off, head_b, head_b, c.kv_heads, cudaMemcpyDefault, stream));
+    off += head_b * c.kv_heads;
+  };
+  for (int l = 0; l < c.layers; ++l) {
+    if (c.is_linear(l)) { cp(st.conv[l], conv_b); cp(st.dstate[l], ds_b); }
+    else { cp_kv(st.kc[l]); cp_kv(st.vc[l]); }
+  }
+}
+void set_position(Model& m, State& st, int pos) {
+  st.pos = pos;
+  SWL_CUDA(cudaMemcpyAsync(st.d_pos, &st.pos, 4, cudaMemcpyHostToDevice, m.stream));
+}
+Model& state_model(swl_state* s) {
+  if (!s || !s->s.model) throw Error(ERR_INVALID, "null state or its model was closed");
+  return *s->s.model;
+}
+}  // namespace
+
+int swl_state_reset(swl_state* state) {
+  API_BEGIN
+  Model& m = state_model(state);
+  SWL_CUDA(cudaSetDevice(m.device));
+  State& st = state->s;
+  const ModelConfig& c = m.cfg;
+  for (int l = 0; l < c.layers; ++l) {
+    if (!c.is_linear(l)) continue;  // attention rows past the position are never read
+    SWL_CUDA(cudaMemsetAsync(st.conv[l], 0, size_t(c.conv_k) * c.conv_dim() * 4, m.stream));
+    SWL_CUDA(cudaMemsetAsync(st.dstate[l], 0, size_t(c.nv) * c.dv * c.dk * 4, m.stream));
+  }
+  set_position(m, st, 0);
+  SWL_CUDA(cudaStreamSynchronize(m.stream));
+  API_END
+}
+
+int swl_state_copy(swl_state* dst, const swl_state* src) {
+  API_BEGIN
+  Model& m = state_model(dst);
+  if (!src || src->s.model != &m) throw Error(ERR_INVALID, "both states must belong to the same open model");
+  if (dst == src) return SWL_OK;
+  const State& a = src->s;
+  State& b = dst->s;
+  if (a.pos > b.max_ctx)
+    throw Error(ERR_CAPACITY, "destination max_ctx " + std::to_string(b.max_ctx) + " below the source position " +
+                                  std::to_string(a.pos));
+  SWL_CUDA(cudaSetDevice(m.device));
+  const ModelConfig& c = m.cfg;
+  const size_t row_b = size_t(c.head_dim) * 4;
+  for (int l = 0; l < c.layers; ++l) {
+    if (c.is_linear(l)) {
+      SWL_CUDA(cudaMemcpyAsync(b.conv[l], a.conv[l], size_t(c.conv_k) * c.conv_dim() * 4, cudaMemcpyDeviceToDevice, m.stream));
+      SWL_CUDA(cudaMemcpyAsync(b.dstate[l], a.dstate[l], size_t(c.nv) * c.dv * c.dk * 4, cudaMemcpyDeviceToDevice, m.stream));
+    } else if (a.pos > 0) {
+      for (float* const* kv : {&a.kc[l], &a.vc[l]}) {
+        float* d = kv == &a.kc[l] ? b.kc[l] : b.vc[l];
+        SWL_CUDA(cudaMemcpy2DAsync(d, size_t(b.max_ctx) * row_b, *kv, size_t(a.max_ctx) * row_b, size_t(a.pos) * row_b,
+                                   c.kv_heads, cudaMemcpyDeviceToDevice, m.stream));
+      }
+    }
+  }
+  set_position(m, b, a.pos);
+  SWL_CUDA(cudaStreamSynchronize(m.stream));
+  API_END
+}
+
+int swl_state_save(const swl_state* state, void* out, int64_t out_bytes, int64_t* written) {
+  API_BEGIN
+  Model& m = state_model(const_cast<swl_state*>(state));
+  const State& st = state->s;
+  const int64_t need = snap_bytes(m.cfg, st.pos);
+  if (written) *written = need;
+  if (!out) return SWL_OK;  // size query
+  if (out_bytes < need) throw Error(ERR_CAPACITY, "snapshot needs " + std::to_string(need) + " bytes");
+  SWL_CUDA(cudaSetDevice(m.device));
+  const SnapHeader h = snap_header(m.cfg, st.pos);
+  memcpy(out, &h, sizeof h);
+  copy_state_parts(m, st, static_cast<uint8_t*>(out), true, st.pos, m.stream);
+  SWL_CUDA(cudaStreamSynchronize(m.stream));
+  API_END
+}
+
+int swl_state_load(swl_state* state, const void* in, int64_t in_bytes) {
+  API_BEGIN
+  Model& m = state_model(state);
+  if (!in || in_bytes < int64_t(sizeof(SnapHeader))) throw Error(ERR_FORMAT, "snapshot shorter than its header");
+  SnapHeader h;
+  memcpy(&h, in, sizeof h);
+  const SnapHeader want = snap_header(m.cfg, h.pos);
+  if (h.magic != kSnapMagic || memcmp(&h, &want, sizeof h) != 0 || h.pos < 0)
+    throw Error(ERR_FORMAT, "snapshot was not taken from a model of this shape");
+  if (in_bytes != snap_bytes(m.cfg, h.pos)) throw Error(ERR_FORMAT, "snapshot size does not match its header");
+  State& st = state->s;
+  if (h.pos > st.max_ctx)
+    throw Error(ERR_CAPACITY, "state max_ctx " + std::to_string(st.max_ctx) + " below the snapshot position " +
+                                  std::to_string(h.pos));
+  SWL_CUDA(cudaSetDevice(m.device));
+  copy_state_parts(m, st, const_cast<uint8_t*>(static_cast<const uint8_t*>(in)), false, h.pos, m.stream);
+  set_position(m, st, h.pos);
+  SWL_CUDA(cudaStreamSynchronize(m.stream));
+  API_END
+}
+
 static void check_tokens(const Model& m, const int32_t* t, int n) {
   if (!t || n < 1) throw Error(ERR_INVALID, "step needs at least one token");
   for (int i = 0; i < n; ++i)

@@ -160,3 +160,23 @@ def write_synthetic(out_dir: str, config: dict, seed: int, bits: int = 4, group_
     with open(os.path.join(out_dir, "config.json"), "w") as f:
         json.dump(cfg, f, indent=2)
     return out_dir
+
+
+def write_hashes(container: str) -> dict:
+    """hashes.json for a container (verify_container.py --write-hashes): the
+    SHA-256 of every file except dot-files and hashes.json itself."""
+    import hashlib
+    out = {}
+    for r, _, files in os.walk(container):
+        for f in files:
+            rel = os.path.relpath(os.path.join(r, f), container)
+            if rel.startswith(".") or rel == "hashes.json":
+                continue
+            h = hashlib.sha256()
+            with open(os.path.join(container, rel), "rb") as fh:
+                for chunk in iter(lambda: fh.read(1 << 22), b""):
+                    h.update(chunk)
+            out[rel] = h.hexdigest()
+    with open(os.path.join(container, "hashes.json"), "w") as f:
+        json.dump({"files": dict(sorted(out.items()))}, f, indent=1)
+    return out

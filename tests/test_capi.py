@@ -13,7 +13,7 @@ from conftest import ROOT, REF_FIXTURES
 def declared_symbols():
     text = open(os.path.join(ROOT, "include", "swiftlet_cuda.h")).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(swl_[a-z_]+)\s*\(", text)))
+    return sorted(set(re.findall(r"\b(swl_[a-z0-9_]+)\s*\(", text)))
 
 
 def test_header_declares_the_boundary():

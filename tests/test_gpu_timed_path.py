@@ -100,3 +100,33 @@ def test_bounded_wait_timeout_is_reported_and_model_stays_usable(mid, golden):
     ref = np.array(golden["prompt_logits"], np.float32)
     assert np.abs(logits - ref).max() < 2e-2
     assert int(np.argmax(logits)) == golden["greedy_32"][0]
+
+
+def test_state_snapshot_copy_and_reset(mid, golden):
+    """Conversation-state reuse (SwiftletSession.swift:114-132): a saved and
+    restored state, and a forked one, continue exactly as the original; a
+    reset state starts over; a snapshot refuses a smaller context."""
+    _, gpu = mid
+    st = swl.DecodeState(64)
+    gpu.step(golden["prompt"], st)
+    snap = gpu.save_state(st)
+    fork = swl.DecodeState(48)
+    gpu.copy_state(fork, st)
+    toks = golden["greedy_32"][:6]
+    ref = [gpu.step([t], st) for t in toks]
+    back = swl.DecodeState(32)
+    gpu.load_state(back, snap)
+    assert back.position == len(golden["prompt"])
+    for t, r in zip(toks, ref):
+        assert np.array_equal(gpu.step([t], back), r)
+        assert np.array_equal(gpu.step([t], fork), r)
+    gpu.reset_state(fork)
+    assert fork.position == 0
+    logits = gpu.step(golden["prompt"], fork)
+    assert np.abs(logits - np.array(golden["prompt_logits"], np.float32)).max() < 2e-2
+    with pytest.raises(swl.SwiftletError) as err:
+        gpu.load_state(swl.DecodeState(4), snap)
+    assert err.value.code == swl.SWL_ERR_CAPACITY
+    with pytest.raises(swl.SwiftletError) as err:
+        gpu.load_state(swl.DecodeState(64), snap[:-4])
+    assert err.value.code == swl.SWL_ERR_FORMAT
