@@ -1,27 +1,33 @@
 #!/usr/bin/env python
-"""Decode benchmark of the Qwen3.6-35B-A3B-shaped q4 model on B200.
+"""Decode benchmark of the Qwen3.6-35B-A3B / Qwen3-Next-80B-A3B-shaped q4 models on B200.
 
-Workload: 40 layers (3 gated-DeltaNet : 1 gated GQA),
-hidden 2048, vocab 151936, 256 experts top-8 + 1 shared (intermediate 512),
-every linear MLX-affine 4-bit group-64 with bf16 scales/biases, random-init
+One GPU (the default): the line's `value` is single-stream greedy decode
+(B=1) of the 35B shape: 40 layers (3 gated-DeltaNet : 1 gated GQA), hidden
+2048, vocab 151936, 256 experts top-8 + 1 shared (intermediate 512), every
+linear MLX-affine 4-bit group-64 with bf16 scales/biases, random-init
 weights generated on the device from a seed (synthetic checkpoint), a
-512-token seeded prompt, then greedy single-stream decode (B=1). One "step"
-is one decoded token; `value` is tokens/s with the token feedback kept in
-HBM, `e2e` is the same through the host API (swl_step: H2D token, D2H
-logits, host argmax). Weights streamed per token (~1.7 GB) exceed the
-126 MB L2, so no flush is needed between steps.
+512-token seeded prompt. One "step" is one decoded token; `value` is tokens/s
+with the token feedback kept in HBM, `e2e` is the same through the host API
+(swl_step: H2D token, D2H logits, host argmax). Weights streamed per token
+(~1.7 GB) exceed the 126 MB L2, so no flush is needed between steps. The same
+line carries the other measurements of the metric:
+  * `b64`: 64 sequences of the 35B shape decoding together (batched kernels);
+  * `expert_gemv`: the expert GEMV/GEMM sweeps over all 40 layers at B = 1, 8
+    and 64, for 4-bit and 8-bit experts, against their algorithmic bytes;
+  * `deltanet`: the DeltaNet decode step of the 80B shape at B = 1 and 64;
+  * `batched`: the 80B shape with 64 sequences of seeded ragged prompts
+    (lengths uniform in [128, 8192]), batched greedy decode, world 1.
+
+Several GPUs (torchrun, one rank per GPU): the line is that last workload
+split over the ranks by expert parallelism: the 64 sequences (the same
+prompt lengths whatever the rank count) are divided among the ranks and the
+routed experts of every layer are split by id (swl_ep_init: NCCL all-gather
++ reduce-scatter per MoE layer); `value` is all ranks' tokens over the
+slowest rank's time and `batched.expert_parallel.world` is the rank count,
+so `batched.value` compares across rank counts ("scaling": "strong").
 
 `--impl reference` times the reference's CPU algorithm (the C++ restatement
 in oracle/) on the host cores on a bounded sample of the same workload.
-With N > 1 ranks every rank runs an independent replica (batch-1 decode does
-not shard); value = tokens of all ranks / max elapsed over ranks.
-
-`--model 80b` runs BASELINE config 5 alone: 64 sequences of ragged seeded
-prompts, then batched greedy decode. Under torchrun with `--ep` the 64
-sequences are split over the ranks and the routed experts of every layer are
-split by id (swl_ep_init: NCCL all-gather + reduce-scatter per layer), so the
-total work is fixed ("scaling": "strong"); without it each rank runs its own
-64 sequences as a replica.
 """
 from __future__ import annotations
 
@@ -43,12 +49,12 @@ PROMPT_SEED = 4242
 MODEL_SEED = 35
 
 
-def model_dir(tmp: str, layers: int | None = None, model: str = "35b") -> str:
+def model_dir(tmp: str, layers: int | None = None, model: str = "35b", bits: int = 4) -> str:
     from swiftlet_b200 import formats
     from swiftlet_b200.configs import NEXT_80B, Q35_35B, with_layers
     base = NEXT_80B if model == "80b" else Q35_35B
     cfg = with_layers(base, layers) if layers else base
-    return formats.write_synthetic(os.path.join(tmp, f"synth-{model}"), cfg, seed=MODEL_SEED)
+    return formats.write_synthetic(os.path.join(tmp, f"synth-{model}-q{bits}"), cfg, seed=MODEL_SEED, bits=bits)
 
 
 def algorithmic_bytes_per_token(cfg, ctx: float) -> dict:
@@ -152,7 +158,7 @@ def profile_traffic() -> dict:
     return json.load(open(p)) if os.path.exists(p) else {}
 
 
-def cpu_decode_sample(mdir: str, n_steps: int, warm: int = 1) -> dict:
+def cpu_decode_sample(mdir: str, n_steps: int, warm: int = 1, label: str = "35B") -> dict:
     """The oracle (C++ restatement of QwenCPUModel) decoding on all host threads."""
     import numpy as np
     import oracle
@@ -167,26 +173,36 @@ def cpu_decode_sample(mdir: str, n_steps: int, warm: int = 1) -> dict:
         logits = cpu.step([int(np.argmax(logits))], st)
     dt = time.perf_counter() - t0
     return {"value": n_steps / dt, "unit": "tok/s", "cores": oracle.max_threads(), "kind": "port",
-            "sample": f"{n_steps} greedy decode steps after a 1-token prompt and {warm} warm-up step(s), same 35B-shaped "
-                      "synthetic model; dense weights retained as f32, experts dequantised per call "
-                      "(QwenCPUModel with retainAllLayers=true)",
+            "sample": f"{n_steps} greedy decode steps of one sequence after a 1-token prompt and {warm} warm-up "
+                      f"step(s), same {label}-shaped synthetic model; dense weights retained as f32, experts "
+                      "dequantised per call (QwenCPUModel with retainAllLayers=true; the reference steps "
+                      "sequences one at a time, so this is also its batched rate)",
             "seconds": dt}
 
 
 def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     if rank != 0:
         return
-    steps = min(args.steps, 6)
+    multi = world > 1
+    steps = min(args.steps, 4 if multi else 6)
     warm = min(args.warmup, 1)
     with tempfile.TemporaryDirectory() as tmp:
-        cb = cpu_decode_sample(model_dir(tmp), steps, warm)
-    line = {"metric": METRIC, "value": cb["value"], "unit": "tok/s", "n_gpus": args.gpus, "steps": steps,
+        cb = cpu_decode_sample(model_dir(tmp, None, "80b" if multi else "35b"), steps, warm,
+                               "80B" if multi else "35B")
+    if multi:
+        metric = "80B-A3B q4 ragged batched decode tok/s (%d sequences over all GPUs, expert-parallel)" % args.batch
+        config = {"workload": "qwen3-next-80b-a3b shape, q4 g64 bf16, batched decode (CPU sample: the reference "
+                              "steps one sequence at a time)", "parallelism": "none (host cores)"}
+    else:
+        metric = METRIC
+        config = {"workload": "qwen3.6-35b-a3b shape, q4 g64 bf16, B=1 greedy decode (CPU sample)",
+                  "global_batch": 1, "parallelism": "none (host cores)"}
+    line = {"metric": metric, "value": cb["value"], "unit": "tok/s", "n_gpus": args.gpus, "steps": steps,
             "warmup": warm, "requested_steps": args.steps, "ms_per_step": 1000.0 / cb["value"],
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "impl": "reference",
-            "config": {"workload": "qwen3.6-35b-a3b shape, q4 g64 bf16, B=1 greedy decode (CPU sample)",
-                       "global_batch": 1, "parallelism": "none (host cores)"},
+            "higher_is_better": True, "scaling": "strong" if multi else "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "impl": "reference", "config": config,
             "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": cb["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -214,29 +230,39 @@ def expected_unique_experts(E: int, K: int, B: int) -> float:
     return E * (1.0 - (1.0 - K / E) ** B)
 
 
-def batched_decode(model, cfg, stream, args, rank, local, dist) -> dict:
-    """B sequences, each with its own seeded prompt of args.batch_prompt
-    tokens (run through the batched rounds), then greedy decode with the
-    tokens fed back on the device; e2e through swl_step_batch (H2D tokens,
-    D2H logits of every sequence, host argmax)."""
+def prompt_lengths(args) -> "np.ndarray":
+    """The batched workload's prompt lengths: all args.batch_prompt, or seeded
+    uniform in [batch_prompt, batch_prompt_max]; the same list whatever the
+    number of ranks (rank r of N takes sequences [r * B / N, (r + 1) * B / N))."""
+    import numpy as np
+    hi = max(args.batch_prompt, args.batch_prompt_max or 0)
+    if hi == args.batch_prompt:
+        return np.full(args.batch, args.batch_prompt)
+    return np.random.default_rng(PROMPT_SEED + 1000).integers(args.batch_prompt, hi + 1, args.batch)
+
+
+def batched_decode(model, cfg, stream, args, rank, local, dist, ep: bool, steps: int, deltanet: bool = False) -> dict:
+    """args.batch sequences with seeded prompts (run through packed batched
+    launches), then greedy decode with the tokens fed back on the device; e2e
+    through swl_step_batch (H2D tokens, D2H logits of every sequence, host
+    argmax). With `ep` the sequences are split over the ranks and the routed
+    experts by id (every decode step routes all ranks' tokens)."""
     import numpy as np
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
-    ep = bool(args.ep) and world > 1
+    ep = ep and world > 1
     B = args.batch // world if ep else args.batch
     if ep:
-        # expert parallelism: args.batch sequences in all, B per rank; every
-        # decode step routes all ranks' tokens over the experts split by id
         import swiftlet_b200 as swl
         model.ep_init(rank, world, swl.ep_unique_id_broadcast(rank), B)
-    steps, e2e_steps = args.batch_steps, min(args.batch_steps, 8)
-    rng = np.random.default_rng(PROMPT_SEED + 1000 + rank)
-    # prompt lengths: all args.batch_prompt, or uniform in [batch_prompt, batch_prompt_max] (ragged)
-    hi = max(args.batch_prompt, args.batch_prompt_max or 0)
-    lens = rng.integers(args.batch_prompt, hi + 1, B) if hi > args.batch_prompt else np.full(B, args.batch_prompt)
+    e2e_steps = min(steps, 8)
+    all_lens = prompt_lengths(args)
+    first = rank * B if ep else 0
+    lens = all_lens[first:first + B]
     extra = args.warmup + steps + e2e_steps + 8
     states = [model.new_state(max_ctx=int(n) + extra) for n in lens]
-    prompts = [rng.integers(0, cfg.vocab_size, int(n)).astype(np.int32) for n in lens]
+    prompts = [np.random.default_rng(PROMPT_SEED + 2000 + first + i).integers(0, cfg.vocab_size, int(n)).astype(np.int32)
+               for i, n in enumerate(lens)]
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
     ev[0].record(stream)
     logits = model.step_batch(prompts, states)
@@ -265,7 +291,8 @@ def batched_decode(model, cfg, stream, args, rank, local, dist) -> dict:
     ev[5].record(stream)
     torch.cuda.synchronize()
     e2e_ms = ev[4].elapsed_time(ev[5])
-    ms, e2e_ms = max_over_ranks([ms, e2e_ms], dist, f"cuda:{local}")
+    ms, e2e_ms, prefill_ms = max_over_ranks([ms, e2e_ms, prefill_ms], dist, f"cuda:{local}")
+    delta = deltanet_sweeps(model, cfg, states) if deltanet else None
     for s in states:
         s.free()
     bt = algorithmic_bytes_per_token(cfg, float(np.mean(lens)) + args.warmup + steps / 2)
@@ -280,25 +307,110 @@ def batched_decode(model, cfg, stream, args, rank, local, dist) -> dict:
     peaks, peak_kind = measured_peaks()
     hbm = float(peaks["hbm_gbs"])
     step_s = ms / steps / 1000.0
-    return {
-        "B": B, "value": replica_rate(world, B * steps, ms), "unit": "tok/s", "steps": steps,
-        "expert_parallel": {"world": world, "sequences_per_rank": B,
-                            "collectives_per_layer": "NCCL all-gather (digits, router logits) + reduce-scatter"}
-        if ep else None,
-        "ms_per_step": ms / steps, "prompt": args.batch_prompt if hi == args.batch_prompt else [args.batch_prompt, hi],
-        "prefill": {"tokens": int(lens.sum()), "ms": prefill_ms,
-                    "tok_s": float(lens.sum()) / (prefill_ms / 1000.0),
-                    "mode": "packed launches of up to 64 tokens, an equal share per sequence"},
-        "step_roofline": {"bound": "hbm", "bytes_per_step": step_bytes, "achieved": step_bytes / step_s / 1e9,
-                          "peak": hbm, "unit": "GB/s", "frac": step_bytes / step_s / 1e9 / hbm,
-                          "peak_kind": peak_kind,
+    hi = int(all_lens.max())
+    res = {
+        "B": B * (world if ep else 1), "sequences_per_rank": B, "value": replica_rate(world if ep else 1, B * steps, ms),
+        "unit": "tok/s", "steps": steps, "warmup": args.warmup,
+        "expert_parallel": {"world": world if ep else 1, "sequences_per_rank": B,
+                            "experts_per_rank": cfg.num_experts // (world if ep else 1),
+                            "collectives_per_layer": "NCCL all-gather (digits, router logits) + reduce-scatter"
+                            if ep else "none (one rank holds every expert)"},
+        "ms_per_step": ms / steps,
+        "prompt": args.batch_prompt if hi == args.batch_prompt else [args.batch_prompt, args.batch_prompt_max],
+        "prefill": {"tokens": int(all_lens.sum()) if ep else int(lens.sum()), "ms": prefill_ms,
+                    "tok_s": float(all_lens.sum() if ep else lens.sum()) / (prefill_ms / 1000.0),
+                    "mode": "packed launches of up to 64 tokens, an equal share per sequence; each rank prefills "
+                            "its own sequences"},
+        "step_roofline": {"bound": "hbm", "bytes_per_step_per_rank": step_bytes,
+                          "achieved": step_bytes / step_s / 1e9, "peak": hbm, "unit": "GB/s",
+                          "frac": step_bytes / step_s / 1e9 / hbm, "peak_kind": peak_kind,
                           "bytes": "dense weights once + (expected distinct routed experts %.1f + shared) blobs per "
                                    "layer + per-sequence delta state r/w, conv ring and f32 KV" % uniq},
-        "e2e": {"value": replica_rate(world, B * e2e_steps, e2e_ms), "unit": "tok/s",
+        "e2e": {"value": replica_rate(world if ep else 1, B * e2e_steps, e2e_ms), "unit": "tok/s",
                 "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B * cfg.vocab_size},
         "gpu_launches_per_step": 3 + 11 * L + 3,
         "clocks": clk.summary(),
     }
+    if delta:
+        res["deltanet"] = delta
+    return res
+
+
+def deltanet_sweeps(model, cfg, states) -> dict:
+    """DeltaNet decode step of every DeltaNet layer of this model's shape:
+    B = len(states) from the last batched step,
+    and B = 1 on one state after one swl_step; bytes are the f32 state read
+    and written plus the small per-token vectors."""
+    import numpy as np
+    peaks, peak_kind = measured_peaks()
+    hbm = float(peaks["hbm_gbs"])
+    out = {}
+    iters = 8
+    ms, byts, launches = model.bench_delta_sweep(len(states), iters)
+    per_launch = ms / launches
+    out["B%d" % len(states)] = {"us_per_layer": per_launch * 1000.0, "bytes_per_layer": byts * iters / launches,
+                                "achieved": byts * iters / (ms / 1000.0) / 1e9, "peak": hbm,
+                                "frac": byts * iters / (ms / 1000.0) / 1e9 / hbm, "unit": "GB/s",
+                                "peak_kind": peak_kind}
+    st = model.new_state(max_ctx=64)
+    model.step([7, 8], st)
+    model.step([9], st)
+    ms, byts, launches = model.bench_delta_sweep(1, iters * 8)
+    per_launch = ms / launches
+    out["B1"] = {"us_per_layer": per_launch * 1000.0, "bytes_per_layer": byts * iters * 8 / launches,
+                 "achieved": byts * iters * 8 / (ms / 1000.0) / 1e9, "peak": hbm,
+                 "frac": byts * iters * 8 / (ms / 1000.0) / 1e9 / hbm, "unit": "GB/s", "peak_kind": peak_kind}
+    st.free()
+    out["note"] = ("graph of the decode recurrence (conv, norms, gating, delta rule) over all %d DeltaNet layers, "
+                   "timed with CUDA events; state [%d, %d, %d] f32 per sequence and layer"
+                   % (sum(1 for i in range(cfg.num_hidden_layers) if cfg.is_linear_layer(i)),
+                      cfg.linear_num_value_heads, cfg.linear_value_head_dim, cfg.linear_key_head_dim))
+    return out
+
+
+def expert_gemv_leg(tmp, local, bits: int, stream, model=None) -> dict:
+    """Expert GEMV/GEMM sweeps over all 40 layers of the 35B shape (distinct
+    weights per layer, so nothing stays in L2): B = 1 through the single-token
+    expert kernels, B = 8 and 64 through the batched grouped GEMMs; bytes are
+    the distinct routed experts the routing picked plus the shared expert (and
+    router for the batched block)."""
+    import numpy as np
+    import swiftlet_b200 as swl
+    own = model is None
+    if own:
+        model = swl.QwenCUDAModel(model_dir(tmp, None, "35b", bits), device=local)
+        model.set_stream(stream.cuda_stream)
+    cfg = model.config
+    peaks, peak_kind = measured_peaks()
+    hbm = float(peaks["hbm_gbs"])
+    out = {}
+    st = model.new_state(max_ctx=64)
+    model.step([11, 12, 13], st)
+    model.step([14], st)
+    iters = 4
+    ms, bytes_layer, _ = model.bench_expert_sweep(iters)
+    per_s = ms / 1000.0 / (iters * cfg.num_hidden_layers)
+    out["B1"] = {"achieved": bytes_layer / per_s / 1e9, "peak": hbm, "frac": bytes_layer / per_s / 1e9 / hbm,
+                 "unit": "GB/s", "us_per_layer": per_s * 1e6, "distinct_experts_per_layer": cfg.num_experts_per_tok + 1,
+                 "kernels": "k_igateup + k_idown (integer tensor-core GEMV)"}
+    st.free()
+    rng = np.random.default_rng(PROMPT_SEED + 77)
+    for B in (8, 64):
+        states = [model.new_state(max_ctx=16) for _ in range(B)]
+        model.step_batch([[int(t)] for t in rng.integers(0, cfg.vocab_size, B)], states)
+        model.step_batch([[int(t)] for t in rng.integers(0, cfg.vocab_size, B)], states)
+        ms, byts, uniq, _ = model.bench_moe_sweep(B, iters)
+        sec = ms / 1000.0 / iters
+        out["B%d" % B] = {"achieved": byts / sec / 1e9, "peak": hbm, "frac": byts / sec / 1e9 / hbm, "unit": "GB/s",
+                          "us_per_layer": sec * 1e6 / cfg.num_hidden_layers,
+                          "distinct_experts_per_layer": uniq / cfg.num_hidden_layers + 1,
+                          "kernels": "k_broute + k_bgemm gate/up and down + k_bcombine (grouped GEMMs)"}
+        for s in states:
+            s.free()
+    if own:
+        model.close()
+    out["weights"] = "q%d g64, bf16 scales/biases; expert blob %d B" % (bits, 1769472 if bits == 4 else 3342336)
+    return out
 
 
 def run_ours(args) -> None:
@@ -317,38 +429,38 @@ def run_ours(args) -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
     tmp = tempfile.mkdtemp()
-    mdir = model_dir(tmp, args.layers, args.model)
-    model = swl.QwenCUDAModel(mdir, device=local)
-    cfg = model.config
     stream = torch.cuda.Stream()
-    model.set_stream(stream.cuda_stream)
-    if args.batch_only or args.model == "80b":
-        # the batched leg alone: profiling, or the 80B-shaped ragged batch
-        # (replicas per GPU, or with --ep the routed
-        # experts split over the GPUs)
-        res = batched_decode(model, cfg, stream, args, rank, local, dist)
+    if world > 1 or args.model == "80b" or args.batch_only:
+        # the 80B-shaped ragged batch (expert-parallel over the ranks), or
+        # the batched leg alone (profiling)
+        model = swl.QwenCUDAModel(model_dir(tmp, args.layers, args.model if args.batch_only else "80b"), device=local)
+        model.set_stream(stream.cuda_stream)
+        cfg = model.config
+        res = batched_decode(model, cfg, stream, args, rank, local, dist, ep=world > 1, steps=args.steps)
         model.close()
         if rank == 0:
-            line = {"metric": METRIC, "batched": res, "profiling_only": True}
-            if args.model == "80b":
-                ep = bool(args.ep) and world > 1
-                line = {"metric": "80B-A3B q4 ragged batched decode tok/s (B=%d %s)"
-                                  % (args.batch, "over all GPUs, expert-parallel" if ep else "per GPU"),
-                        "value": res["value"],
-                        "unit": "tok/s", "n_gpus": world, "steps": res["steps"], "warmup": args.warmup,
-                        "ms_per_step": res["ms_per_step"], "higher_is_better": True,
-                        "scaling": "strong" if ep else "weak",
-                        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-                        "config": {"workload": "qwen3-next-80b-a3b shape (48 layers, 512 experts top-10 + shared), q4 "
-                                               "g64, %d sequences with seeded prompts of ragged length %s"
-                                               % (args.batch, "split over the GPUs" if ep else "per GPU"),
-                                   "parallelism": ("ep%d (routed experts by id, sequences data-parallel)" % world)
-                                   if ep else "replica x%d" % world},
-                        "batched": res}
+            line = {"metric": "80B-A3B q4 ragged batched decode tok/s (%d sequences over all GPUs, expert-parallel)"
+                              % args.batch,
+                    "value": res["value"], "unit": "tok/s", "n_gpus": world, "steps": res["steps"],
+                    "warmup": args.warmup, "ms_per_step": res["ms_per_step"], "higher_is_better": True,
+                    "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                    "config": {"workload": "qwen3-next-80b-a3b shape (48 layers, 512 experts top-10 + shared), q4 "
+                                           "g64, %d sequences with seeded prompts of ragged length, split over the "
+                                           "GPUs" % args.batch,
+                               "parallelism": "ep%d (routed experts by id, sequences data-parallel)" % world,
+                               "l2": "no flush: each step streams tens of GB of weights, state and KV"},
+                    "e2e": res["e2e"], "gpu_launches": res["gpu_launches_per_step"] * res["steps"],
+                    "clocks": res["clocks"], "batched": res}
+            if args.batch_only:
+                line["profiling_only"] = True
             print(json.dumps(line), flush=True)
         if dist:
             dist.destroy_process_group()
         return
+    mdir = model_dir(tmp, args.layers, "35b")
+    model = swl.QwenCUDAModel(mdir, device=local)
+    cfg = model.config
+    model.set_stream(stream.cuda_stream)
     rng = np.random.default_rng(PROMPT_SEED + rank)
     prompt = rng.integers(0, cfg.vocab_size, args.prompt).astype(np.int32)
     e2e_steps = min(args.steps, 32)
@@ -374,17 +486,12 @@ def run_ours(args) -> None:
     for _ in range(args.warmup):
         dev_step(i); i += 1
     torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    torch.cuda.synchronize()
     with ClockSampler(local) as clk:
         ev[2].record(stream)
         for _ in range(args.steps):
             dev_step(i); i += 1
         ev[3].record(stream)
         torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
     ms = ev[2].elapsed_time(ev[3])
 
     # end to end through the public host API
@@ -397,27 +504,26 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     e2e_ms = ev[4].elapsed_time(ev[5])
 
-    # batched decode: args.batch sequences advancing together through the
-    # batched kernels (one weight stream per step for all of them)
-    bres = None
-    if args.batch > 1:
-        bres = batched_decode(model, cfg, stream, args, rank, local, dist)
-
     # roofline of the dominant kernels: the fused expert GEMV pair, swept over all layers
     sweep_iters = 4
     sweep_ms, bytes_layer, sweep_launches = model.bench_expert_sweep(sweep_iters)
-    ms, e2e_ms, sweep_ms = max_over_ranks([ms, e2e_ms, sweep_ms], dist, f"cuda:{local}")
-    if rank != 0:
-        model.close()
-        if dist:
-            dist.destroy_process_group()
-        return
+
+    # 64 sequences of the 35B shape advancing together (one weight stream per step)
+    b64 = None
+    if args.batch > 1:
+        b64_args = argparse.Namespace(**vars(args))
+        b64_args.batch_prompt, b64_args.batch_prompt_max = 128, None
+        b64 = batched_decode(model, cfg, stream, b64_args, rank, local, None, ep=False, steps=args.batch_steps)
+    gemv = {"q4": expert_gemv_leg(tmp, local, 4, stream, model)} if not args.no_gemv else None
+    model.close()
+    if gemv is not None:
+        gemv["q8"] = expert_gemv_leg(tmp, local, 8, stream)
 
     peaks, peak_kind = measured_peaks()
     hbm = float(peaks["hbm_gbs"])
     ctx_mean = args.prompt + args.warmup + args.steps / 2
     bt = algorithmic_bytes_per_token(cfg, ctx_mean)
-    value = replica_rate(world, args.steps, ms)
+    value = args.steps / (ms / 1000.0)
     per_launch_s = sweep_ms / 1000.0 / (sweep_iters * cfg.num_hidden_layers)
     achieved = bytes_layer / per_launch_s / 1e9
     traffic = profile_traffic().get("moe_expert_pair_bytes_per_layer")
@@ -429,32 +535,43 @@ def run_ours(args) -> None:
         "config": {"workload": "qwen3.6-35b-a3b shape (%d layers, hidden 2048, 256 experts top-8 + shared, "
                                "vocab 151936), q4 g64, B=1 greedy decode after a %d-token prompt"
                                % (cfg.num_hidden_layers, args.prompt),
-                   "model": "Q35_35B synthetic seed %d" % MODEL_SEED, "global_batch": world, "seq_len": args.prompt,
-                   "parallelism": "replica x%d" % world if world > 1 else "single GPU",
+                   "model": "Q35_35B synthetic seed %d" % MODEL_SEED, "global_batch": 1, "seq_len": args.prompt,
+                   "parallelism": "single GPU",
                    "l2": "no flush: each token streams ~1.7 GB of weights, far above the 126 MB L2"},
         "prefill": {"tokens": args.prompt, "ms": prefill_ms, "tok_s": args.prompt / (prefill_ms / 1000.0),
                     "mode": "chunked: launches of up to 64 prompt tokens through the batched kernels"},
-        "step_roofline": {"bound": "hbm", "bytes_per_token": bt["total"], "achieved": bt["total"] * value / world / 1e9,
-                          "peak": hbm, "unit": "GB/s", "frac": bt["total"] * value / world / 1e9 / hbm,
+        "step_roofline": {"bound": "hbm", "bytes_per_token": bt["total"], "achieved": bt["total"] * value / 1e9,
+                          "peak": hbm, "unit": "GB/s", "frac": bt["total"] * value / 1e9 / hbm,
                           "peak_kind": peak_kind},
         "roofline": {"kernel": "k_igateup + k_idown (8 routed + 1 shared expert, one layer)", "bound": "hbm",
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "bytes_per_launch_pair": bytes_layer, "avg_pair_us": per_launch_s * 1e6,
-                     "traffic": traffic, "peak_kind": peak_kind},
-        "e2e": {"value": replica_rate(world, e2e_steps, e2e_ms), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                     "traffic": traffic, "traffic_source": "ncu capture committed in profiles/traffic.json "
+                                                          "(per launch pair; not re-measured in this run)",
+                     "peak_kind": peak_kind},
+        "e2e": {"value": e2e_steps / (e2e_ms / 1000.0), "unit": "tok/s", "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": 4 * cfg.vocab_size},
         "gpu_launches": launches_per_token * args.steps,
         "clocks": clk.summary(),
     }
-    if bres is not None:
-        line["batched"] = bres
-    if world == 1 and not args.no_cpu_baseline:
+    if b64 is not None:
+        line["b64"] = b64
+    if gemv is not None:
+        line["expert_gemv"] = gemv
+    if not args.no_80b:
+        # the 80B-shaped ragged batch on this one GPU (the multi-GPU runs
+        # split the same workload by expert parallelism), with the DeltaNet
+        # step sweeps of that shape
+        m80 = swl.QwenCUDAModel(model_dir(tmp, args.layers, "80b"), device=local)
+        m80.set_stream(stream.cuda_stream)
+        line["batched"] = batched_decode(m80, m80.config, stream, args, rank, local, None, ep=False,
+                                         steps=args.batch_steps, deltanet=True)
+        line["deltanet"] = line["batched"].pop("deltanet")
+        m80.close()
+    if not args.no_cpu_baseline:
         cb = cpu_decode_sample(mdir, 2, 1)
         line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
-    model.close()
     print(json.dumps(line), flush=True)
-    if dist:
-        dist.destroy_process_group()
 
 
 def main() -> None:
@@ -468,12 +585,14 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=64, help="sequences of the batched-decode leg (<= 1: skip it)")
     ap.add_argument("--batch-prompt", type=int, default=128)
     ap.add_argument("--batch-steps", type=int, default=32)
-    ap.add_argument("--batch-prompt-max", type=int, default=None,
-                    help="ragged prompts: lengths uniform in [--batch-prompt, this]")
+    ap.add_argument("--batch-prompt-max", type=int, default=8192,
+                    help="80B batch: prompt lengths uniform in [--batch-prompt, this]")
     ap.add_argument("--model", default="35b", choices=["35b", "80b"],
-                    help="80b: the Qwen3-Next-80B-shaped batched leg alone (BASELINE config 5 per GPU)")
-    ap.add_argument("--ep", action="store_true",
-                    help="batched leg with expert parallelism over the ranks (--batch sequences in all)")
+                    help="80b: the Qwen3-Next-80B-shaped ragged batch alone")
+    ap.add_argument("--ep", action="store_true", help="accepted for compatibility: several ranks always split "
+                                                      "the 80B batch by expert parallelism")
+    ap.add_argument("--no-gemv", action="store_true", help="skip the expert GEMV/GEMM sweeps")
+    ap.add_argument("--no-80b", action="store_true", help="skip the 80B-shaped ragged batch on one GPU")
     ap.add_argument("--batch-only", action="store_true",
                     help="profiling only: run the batched leg alone and print its numbers")
     ap.add_argument("--layers", type=int, default=None,

@@ -233,6 +233,24 @@ int swl_debug_wait_timeout(swl_model* model, int32_t limit_us);
 int swl_bench_expert_sweep(swl_model* model, int32_t iters, float* ms_out, double* bytes_per_layer,
                            int32_t* launches_out);
 
+/* Batched expert sweep for the expert-GEMM roofline at B = T (2..64): the
+ * MoE block of the batched path (router, routing, grouped gate/up and down
+ * GEMMs, combine) over every layer for the T tokens the last batched decode
+ * step left in the model's scratch, `iters` times, timed with CUDA events.
+ * Outputs the elapsed ms, the algorithmic bytes of one sweep (the distinct
+ * routed experts each layer's routing picked, counted on the host from one
+ * untimed pass, plus the shared expert and router of every layer), that
+ * distinct-expert count and the launches. Modifies only model scratch. */
+int swl_bench_moe_sweep(swl_model* model, int32_t T, int32_t iters, float* ms_out, double* bytes_out,
+                        int32_t* unique_experts_out, int32_t* launches_out);
+/* DeltaNet step sweep: the decode recurrence of every DeltaNet layer for one
+ * token (T = 1, the state of the last swl_step) or for the T sequences of the
+ * last batched decode step, `iters` times, timed with CUDA events; bytes =
+ * state read + written, conv taps, projections in, y and z out, per sequence
+ * and layer. Benchmark only: it advances those states' recurrences. */
+int swl_bench_delta_sweep(swl_model* model, int32_t T, int32_t iters, float* ms_out, double* bytes_out,
+                          int32_t* launches_out);
+
 /* Kernel timeline: with SWL_TRACE=<records> set when the model was opened,
  * every CTA of every decode kernel appends {tag, block, start, after the
  * dependency wait, end} (ns, %globaltimer); tag = kind + 16 * (layer + 1)

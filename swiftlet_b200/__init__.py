@@ -97,6 +97,10 @@ _SIGNATURES = {
     "swl_debug_delta_state": (_I, [_P, _P, C.c_int32, _P]),
     "swl_debug_kernel_path": (_I, [_P, C.c_char_p, C.c_int32]),
     "swl_state_reset": (_I, [_P]),
+    "swl_bench_moe_sweep": (_I, [_P, C.c_int32, C.c_int32, C.POINTER(C.c_float), C.POINTER(C.c_double),
+                                 C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
+    "swl_bench_delta_sweep": (_I, [_P, C.c_int32, C.c_int32, C.POINTER(C.c_float), C.POINTER(C.c_double),
+                                   C.POINTER(C.c_int32)]),
     "swl_qpack_verify": (_I, [C.c_char_p, C.c_char_p, C.c_int32, C.POINTER(swl_verify_report)]),
     "swl_sha256_file": (_I, [C.c_char_p, C.c_char_p]),
     "swl_state_copy": (_I, [_P, _P]),
@@ -356,6 +360,19 @@ class QwenCUDAModel:
         b = C.c_double()
         n = C.c_int32()
         _check(lib().swl_bench_expert_sweep(self._h, int(iters), C.byref(ms), C.byref(b), C.byref(n)))
+        return ms.value, b.value, n.value
+
+    def bench_moe_sweep(self, T: int, iters: int):
+        """(ms, bytes per sweep, distinct experts per sweep, launches) of the batched MoE block."""
+        ms, b, u, n = C.c_float(), C.c_double(), C.c_int32(), C.c_int32()
+        _check(lib().swl_bench_moe_sweep(self._h, int(T), int(iters), C.byref(ms), C.byref(b), C.byref(u),
+                                         C.byref(n)))
+        return ms.value, b.value, u.value, n.value
+
+    def bench_delta_sweep(self, T: int, iters: int):
+        """(ms, bytes per sweep, launches) of the DeltaNet decode step over every DeltaNet layer."""
+        ms, b, n = C.c_float(), C.c_double(), C.c_int32()
+        _check(lib().swl_bench_delta_sweep(self._h, int(T), int(iters), C.byref(ms), C.byref(b), C.byref(n)))
         return ms.value, b.value, n.value
 
     def trace_dump(self, path: str) -> None:

@@ -182,6 +182,130 @@ __global__ void __launch_bounds__(RPW == 8 ? DELTA_MAX_THREADS : 256, RPW == 8 ?
   trc.end(a.trace);
 }
 
+// The same step for 128-dim key heads, spread over many small CTAs so that
+// every SM streams state: CTA = (v-head, slice of RB = NW * RPW rows[, sequence
+// of a batched step]); warp w owns rows w * RPW .. w * RPW + RPW - 1 of the
+// slice and each lane holds four consecutive elements of a row, so a row is
+// one 16-byte load (and store) per lane. The rows are loaded, and the conv
+// history and weights staged, before the dependency wait.
+constexpr int DELTA4_DK = 128;
+template <int RPW, int NW>
+__global__ void __launch_bounds__(NW * 32) k_delta4(const DeltaArgs a) {
+  constexpr int RB = RPW * NW, DK = DELTA4_DK;
+  extern __shared__ __align__(16) float sm[];
+  __shared__ __align__(16) float q[DK];
+  __shared__ __align__(16) float k[DK];
+  __shared__ float v[RB], gb[2], nrm[2];
+  const int K = a.conv_k;
+  const int hv = blockIdx.x, slice = blockIdx.y, rep = a.nv / a.nk, hk = hv / rep;
+  const int keyDim = a.nk * DK, dv = a.dv;
+  constexpr int nch = 2 * DK + RB;
+  float* taps = sm;                  // [nch][K-1] older conv inputs
+  float* cw = taps + nch * (K - 1);  // [nch][K] conv weights
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const StateDev* sd = a.sd + blockIdx.z;
+  const float* proj = a.proj + blockIdx.z * a.proj_stride;
+  float* yout = a.y + int64_t(blockIdx.z) * a.nv * dv;
+  float* zout = a.z + int64_t(blockIdx.z) * a.nv * dv;
+  TraceRec trc;
+  trc.start(a.trace);
+  // ---- before the wait: everything written by earlier tokens ----
+  const int pos = *sd->pos;
+  const float* ring = sd->conv[a.layer];
+  float* S = sd->dstate[a.layer];
+  const int row0 = slice * RB + warp * RPW;  // first row of this warp within the head
+  float4* S4 = reinterpret_cast<float4*>(S + (int64_t(hv) * dv + row0) * DK) + lane;
+  float4 st[RPW];
+#pragma unroll
+  for (int j = 0; j < RPW; ++j) st[j] = S4[j * (DK / 4)];
+  auto chan = [&](int t) {
+    if (t < DK) return hk * DK + t;
+    if (t < 2 * DK) return keyDim + hk * DK + (t - DK);
+    return 2 * keyDim + hv * dv + slice * RB + (t - 2 * DK);
+  };
+  for (int t = threadIdx.x; t < nch; t += blockDim.x) {
+    const int c = chan(t);
+    for (int j = 0; j < K - 1; ++j) {
+      const int rs = ((pos - (K - 1) + j) % K + K) % K;
+      taps[t * (K - 1) + j] = ring[int64_t(rs) * a.conv_dim + c];
+    }
+    for (int j = 0; j < K; ++j) cw[t * K + j] = a.conv_w[c * K + j];
+  }
+  const float alog = a.a_log[hv], dtb = a.dt_bias[hv];
+  pdl_wait();
+  trc.waited(a.trace);
+  // ---- the current token's projections ----
+  float* ring_w = sd->conv[a.layer];
+  const int slot = pos % K;
+  const bool own_qk = (hv % rep) == 0 && slice == 0;
+  for (int t = threadIdx.x; t < nch; t += blockDim.x) {
+    const int c = chan(t);
+    const float xn = proj[delta_src(a, c)];
+    float acc = 0.f;
+    for (int j = 0; j < K - 1; ++j) acc += cw[t * K + j] * taps[t * (K - 1) + j];
+    acc += cw[t * K + K - 1] * xn;
+    const float o = silu_ref(acc);
+    if (t < DK) q[t] = o; else if (t < 2 * DK) k[t - DK] = o; else v[t - 2 * DK] = o;
+    if (t >= 2 * DK || own_qk) ring_w[int64_t(slot) * a.conv_dim + c] = xn;
+  }
+  if (threadIdx.x == 0) {
+    int bi, ai;
+    delta_ba(a, hv, bi, ai);
+    gb[0] = expf(-expf(alog) * softplus_ref(proj[ai] + dtb));
+    gb[1] = sigmoid_ref(proj[bi]);
+  }
+  for (int i = threadIdx.x; i < RB; i += blockDim.x) {
+    const int d = slice * RB + i;
+    zout[hv * dv + d] = silu_ref(proj[delta_z(a, hv, d)]);  // the output gate's activation
+  }
+  __syncthreads();
+  pdl_launch();
+  // q/k RMSNorm: warp 0 reduces q, warp 1 reduces k
+  if (warp < 2) {
+    const float4 x4 = reinterpret_cast<const float4*>(warp == 0 ? q : k)[lane];
+    float ss = x4.x * x4.x + x4.y * x4.y + x4.z * x4.z + x4.w * x4.w;
+    ss = warp_sum(ss);
+    if (lane == 0) nrm[warp] = 1.f / sqrtf(ss / float(DK) + 1e-6f);
+  }
+  __syncthreads();
+  const float inv = 1.f / sqrtf(float(DK));
+  const float qs = nrm[0] * (inv * inv), ks = nrm[1] * inv;
+  float4 qr = reinterpret_cast<const float4*>(q)[lane], kr = reinterpret_cast<const float4*>(k)[lane];
+  qr.x *= qs; qr.y *= qs; qr.z *= qs; qr.w *= qs;
+  kr.x *= ks; kr.y *= ks; kr.z *= ks; kr.w *= ks;
+  const float g = gb[0], beta = gb[1];
+  float kv[RPW];
+#pragma unroll
+  for (int j = 0; j < RPW; ++j) {
+    st[j].x *= g; st[j].y *= g; st[j].z *= g; st[j].w *= g;
+    kv[j] = st[j].x * kr.x + st[j].y * kr.y + st[j].z * kr.z + st[j].w * kr.w;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1)
+#pragma unroll
+    for (int j = 0; j < RPW; ++j) kv[j] += __shfl_xor_sync(0xffffffffu, kv[j], o);
+  float y[RPW];
+#pragma unroll
+  for (int j = 0; j < RPW; ++j) {
+    const float delta = (v[warp * RPW + j] - kv[j]) * beta;
+    st[j].x += kr.x * delta; st[j].y += kr.y * delta; st[j].z += kr.z * delta; st[j].w += kr.w * delta;
+    y[j] = st[j].x * qr.x + st[j].y * qr.y + st[j].z * qr.z + st[j].w * qr.w;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1)
+#pragma unroll
+    for (int j = 0; j < RPW; ++j) y[j] += __shfl_xor_sync(0xffffffffu, y[j], o);
+#pragma unroll
+  for (int j = 0; j < RPW; ++j) S4[j * (DK / 4)] = st[j];
+  if (lane < RPW) {
+    float yl = y[0];
+#pragma unroll
+    for (int j = 1; j < RPW; ++j) if (lane == j) yl = y[j];
+    yout[hv * dv + row0 + lane] = yl;
+  }
+  trc.end(a.trace);
+}
+
 // Chunked step: the recurrence of k_delta over a sequence's consecutive
 // tokens in order, the state rows in registers throughout (one CTA per
 // (v-head, sequence), the whole head's dv rows). The conv window of each
@@ -841,7 +965,19 @@ __global__ void k_dequant(const QLin L, int64_t r0, int64_t r1, float* out) {
 }
 
 // ------------------------------------------------------------- launches --
+// 128-dim key heads: RB = NW * RPW rows per CTA.
+template <int RPW, int NW>
+static bool launch_delta4(const DeltaArgs& a, int T, cudaStream_t st, bool pdl) {
+  constexpr int RB = RPW * NW;
+  if (a.dk != DELTA4_DK || a.dv % RB || a.conv_k < 1 || a.conv_k > 8) return false;
+  const size_t smem = size_t(2 * DELTA4_DK + RB) * (2 * a.conv_k - 1) * 4;
+  launch(k_delta4<RPW, NW>, dim3(a.nv, a.dv / RB, T), dim3(NW * 32), smem, st, pdl, a);
+  return true;
+}
+
 void launch_delta(const DeltaArgs& a, cudaStream_t st, bool pdl) {
+  // one token: 8 rows per CTA (512 CTAs of 128 threads at 32 heads x 128 rows)
+  if (launch_delta4<2, 4>(a, 1, st, pdl)) { path_note("delta"); return; }
   if (a.dk > 32 * DELTA_EPL || a.rows_per_block > DELTA_RPW * (DELTA_THREADS / 32) || a.dv % a.rows_per_block)
     throw Error(ERR_UNSUPPORTED, "DeltaNet head dims outside the decode kernel's range");
   const int nch = 2 * a.dk + a.rows_per_block;
@@ -853,6 +989,8 @@ void launch_delta(const DeltaArgs& a, cudaStream_t st, bool pdl) {
 // Batched: up to 128 rows per CTA (a whole 128-row value head), so the q/k
 // convolution and norms of a key head are computed by fewer CTAs.
 void launch_delta_batch(const DeltaArgs& a, int T, cudaStream_t st, bool pdl) {
+  // 32 rows per CTA: 4 CTAs per head and sequence
+  if (launch_delta4<4, 8>(a, T, st, pdl)) return;
   constexpr int RPW = 2 * DELTA_RPW;
   const int threads = std::max(DELTA_THREADS, 32 * ((a.rows_per_block + RPW - 1) / RPW));
   if (a.dk > 32 * DELTA_EPL || threads > 256 || a.dv % a.rows_per_block)

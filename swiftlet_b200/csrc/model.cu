@@ -198,6 +198,7 @@ struct Model {
   bool batch_supported();
   void ensure_batch();
   void enqueue_batch(int T, int S, bool chunked, cudaStream_t st);
+  void enqueue_batch_moe(int l, int T, bool chunked, cudaStream_t st);
   // S sequences consume counts[i] tokens each (T in total, already in
   // bb.tokens, sequence-major)
   void run_batch(State* const* s, int S, const int* counts, int T);
@@ -913,7 +914,7 @@ void Model::bdense(const std::vector<std::pair<QLin, float*>>& segs, int64_t y_s
 
 void Model::enqueue_batch(int T, int S, bool chunked, cudaStream_t st) {
   const ModelConfig& c = cfg;
-  const int D = c.hidden, K = c.topk, E = c.experts, H = c.heads, hd = c.head_dim;
+  const int D = c.hidden, H = c.heads, hd = c.head_dim;
   const bool pdl = use_pdl;
   EmbedArgs e;
   e.table = embed; e.tokens = bb.tokens; e.cursor = nullptr; e.h = bb.h; e.vocab = c.vocab; e.err = err;
@@ -966,69 +967,88 @@ void Model::enqueue_batch(int T, int S, bool chunked, cudaStream_t st) {
             bb.meta_a);
     }
     bdense({{ld.out_lin, bb.h}}, D, BM_RESIDUAL, bb.bt_a, bb.meta_a, T, st);
-    const int gs_r = ld.router.gs;
-    // Expert-parallel decode: this rank's tokens are rows [own, own + T) of
-    // the Ta tokens that every rank routes; their digits and router logits
-    // are written in place and all-gathered.
-    const bool ep_on = ep && ep_decode && !chunked;
-    const int Ta = ep_on ? T * ep_world : T, own = ep_on ? ep_rank * T : 0;
-    const int64_t bt_row = D / 32 * 12, meta_row = D / gs_r;
-    uint2* bt_own = bb.bt_a + own * bt_row;
-    float2* meta_own = bb.meta_a + own * meta_row;
-    float* rlog_own = bb.rlog + int64_t(own) * (E + 1);
-    digit(bb.h, D, T, D, gs_r, PRO_RMSNORM, ld.post_norm, nullptr, 0, bb.xmoe, bt_own, meta_own);
-    bdense({{ld.router, rlog_own}, {ld.sgate, rlog_own + E}}, E + 1, BM_STORE, bt_own, meta_own, T, st);
-    if (ep_on) {
-      ep_group_start(ep);
-      ep_allgather(ep, bb.bt_a, size_t(T) * bt_row * sizeof(uint2), st);
-      ep_allgather(ep, bb.meta_a, size_t(T) * meta_row * sizeof(float2), st);
-      ep_allgather(ep, bb.rlog, size_t(T) * (E + 1) * sizeof(float), st);
-      ep_group_end(ep);
-    }
-    BRouteArgs r;
-    r.logits = bb.rlog; r.T = Ta; r.E = E; r.K = K; r.norm_topk = c.norm_topk;
-    if (ep_on) {
-      r.e_lo = ep_lo(); r.e_hi = ep_hi(); r.sh_lo = own; r.sh_hi = own + T;
-    }
-    r.ids = bb.ids; r.w = bb.w; r.sh = bb.sh; r.slot_of = bb.slot_of; r.slot_tok = bb.slot_tok;
-    r.items_gu = bb.items_gu; r.items_dn = bb.items_dn; r.nitems = bb.nitems;
-    r.inter = c.moe_inter; r.shared_inter = c.shared_inter; r.hidden = D; r.max_gu = bb.max_gu; r.max_dn = bb.max_dn;
-    launch_broute(r, st, pdl);
-    BGemmArgs gu;
-    gu.mode = BM_SWIGLU; gu.in = D;
-    if (!bgemm_layout(D, ld.eg.lin.bits, ld.eg.lin.dt, gs_r, gu.L)) throw Error(ERR_UNSUPPORTED, "batched gate/up layout");
-    gu.expert_mode = 1; gu.eg = bmat(ld.eg); gu.eu = bmat(ld.eu); gu.sg = bmat(ld.sh_g); gu.su = bmat(ld.sh_u);
-    gu.experts = E; gu.items = bb.items_gu; gu.nitems = bb.nitems; gu.max_items = bb.max_gu; gu.in_map = bb.slot_tok;
-    gu.out = bb.hmid; gu.out_stride = bb.hmid_stride;
-    gu.xbt = bb.bt_a; gu.xmeta = bb.meta_a; gu.bt_row = D / 32 * 12; gu.meta_row = D / gs_r;
-    launch_bgemm(gu, ld.eg.lin.bits, ld.eg.lin.dt, bgemm_grid(ld.eg.lin.bits, ld.eg.lin.dt, gu.L), st, pdl);
-    const int gs_d = ld.ed.lin.gs, I = c.moe_inter;
-    digit(bb.hmid, bb.hmid_stride, Ta * (K + 1), I, gs_d, PRO_COPY, nullptr, nullptr, 0, nullptr, bb.bt_b, bb.meta_b);
-    BGemmArgs dn;
-    dn.mode = BM_STORE; dn.in = I;
-    if (!bgemm_layout(I, ld.ed.lin.bits, ld.ed.lin.dt, gs_d, dn.L)) throw Error(ERR_UNSUPPORTED, "batched down layout");
-    dn.expert_mode = 1; dn.eg = bmat(ld.ed); dn.sg = bmat(ld.sh_d);
-    dn.experts = E; dn.items = bb.items_dn; dn.nitems = bb.nitems + 1; dn.max_items = bb.max_dn; dn.in_map = nullptr;
-    dn.out = bb.ydown; dn.out_stride = D;
-    dn.xbt = bb.bt_b; dn.xmeta = bb.meta_b; dn.bt_row = I / 32 * 12; dn.meta_row = I / gs_d;
-    launch_bgemm(dn, ld.ed.lin.bits, ld.ed.lin.dt, bgemm_grid(ld.ed.lin.bits, ld.ed.lin.dt, dn.L), st, pdl);
-    if (ep_on) {
-      BCombineEpArgs ce;
-      ce.h = bb.h; ce.part = ep_part; ce.ydown = bb.ydown; ce.ystride = D; ce.slot_of = bb.slot_of; ce.w = bb.w;
-      ce.sh = bb.sh; ce.T = Ta; ce.K = K; ce.D = D; ce.own_lo = own; ce.own_hi = own + T;
-      launch_bcombine_ep(ce, st, pdl);
-      ep_reduce_scatter(ep, ep_part, bb.h, size_t(T) * D, st);
-    } else {
-      BCombineArgs cb;
-      cb.h = bb.h; cb.ydown = bb.ydown; cb.ystride = D; cb.slot_of = bb.slot_of; cb.w = bb.w; cb.sh = bb.sh;
-      cb.T = T; cb.K = K; cb.D = D;
-      launch_bcombine(cb, st, pdl);
-    }
+    enqueue_batch_moe(l, T, chunked, st);
   }
   launch_badvance(bb.sds, S, chunked ? bb.seq_n : nullptr, st, pdl);
   digit(bb.h, D, T, D, lm_head.gs, PRO_RMSNORM, final_norm, nullptr, 0, nullptr, bb.bt_a, bb.meta_a);
   bdense({{lm_head, bb.logits}}, c.vocab, BM_STORE, bb.bt_a, bb.meta_a, T, st);
   launch_bargmax(bb.logits, T, c.vocab, bb.greedy, st, pdl);
+}
+
+// MoE block of layer l for the T tokens of a batched step (rows of bb.h):
+// router, routing, grouped expert GEMMs, combine (QwenCPUModel.swift:500-569);
+// with expert parallelism, the exchange around them.
+void Model::enqueue_batch_moe(int l, int T, bool chunked, cudaStream_t st) {
+  const ModelConfig& c = cfg;
+  const int D = c.hidden, K = c.topk, E = c.experts;
+  const bool pdl = use_pdl;
+  const LayerDev& ld = L[l];
+  auto digit = [&](const float* x, int64_t xs, int rows, int in, int gs, int pro, const float* aux, const float* aux2,
+                   int head_dim, float* x_out, uint2* bt, float2* meta) {
+    DigitArgs d;
+    d.x = x; d.x_stride = xs; d.rows = rows; d.in = in; d.gs = gs; d.prologue = pro;
+    d.aux = aux; d.aux2 = aux2; d.head_dim = head_dim; d.eps = float(c.eps); d.x_out = x_out;
+    d.bt = bt; d.meta = meta; d.bt_row = in / 32 * 12; d.meta_row = in / gs;
+    launch_digitize(d, st, pdl);
+  };
+  const int gs_r = ld.router.gs;
+  // Expert-parallel decode: this rank's tokens are rows [own, own + T) of
+  // the Ta tokens that every rank routes; their digits and router logits
+  // are written in place and all-gathered.
+  const bool ep_on = ep && ep_decode && !chunked;
+  const int Ta = ep_on ? T * ep_world : T, own = ep_on ? ep_rank * T : 0;
+  const int64_t bt_row = D / 32 * 12, meta_row = D / gs_r;
+  uint2* bt_own = bb.bt_a + own * bt_row;
+  float2* meta_own = bb.meta_a + own * meta_row;
+  float* rlog_own = bb.rlog + int64_t(own) * (E + 1);
+  digit(bb.h, D, T, D, gs_r, PRO_RMSNORM, ld.post_norm, nullptr, 0, bb.xmoe, bt_own, meta_own);
+  bdense({{ld.router, rlog_own}, {ld.sgate, rlog_own + E}}, E + 1, BM_STORE, bt_own, meta_own, T, st);
+  if (ep_on) {
+    ep_group_start(ep);
+    ep_allgather(ep, bb.bt_a, size_t(T) * bt_row * sizeof(uint2), st);
+    ep_allgather(ep, bb.meta_a, size_t(T) * meta_row * sizeof(float2), st);
+    ep_allgather(ep, bb.rlog, size_t(T) * (E + 1) * sizeof(float), st);
+    ep_group_end(ep);
+  }
+  BRouteArgs r;
+  r.logits = bb.rlog; r.T = Ta; r.E = E; r.K = K; r.norm_topk = c.norm_topk;
+  if (ep_on) {
+    r.e_lo = ep_lo(); r.e_hi = ep_hi(); r.sh_lo = own; r.sh_hi = own + T;
+  }
+  r.ids = bb.ids; r.w = bb.w; r.sh = bb.sh; r.slot_of = bb.slot_of; r.slot_tok = bb.slot_tok;
+  r.items_gu = bb.items_gu; r.items_dn = bb.items_dn; r.nitems = bb.nitems;
+  r.inter = c.moe_inter; r.shared_inter = c.shared_inter; r.hidden = D; r.max_gu = bb.max_gu; r.max_dn = bb.max_dn;
+  launch_broute(r, st, pdl);
+  BGemmArgs gu;
+  gu.mode = BM_SWIGLU; gu.in = D;
+  if (!bgemm_layout(D, ld.eg.lin.bits, ld.eg.lin.dt, gs_r, gu.L)) throw Error(ERR_UNSUPPORTED, "batched gate/up layout");
+  gu.expert_mode = 1; gu.eg = bmat(ld.eg); gu.eu = bmat(ld.eu); gu.sg = bmat(ld.sh_g); gu.su = bmat(ld.sh_u);
+  gu.experts = E; gu.items = bb.items_gu; gu.nitems = bb.nitems; gu.max_items = bb.max_gu; gu.in_map = bb.slot_tok;
+  gu.out = bb.hmid; gu.out_stride = bb.hmid_stride;
+  gu.xbt = bb.bt_a; gu.xmeta = bb.meta_a; gu.bt_row = D / 32 * 12; gu.meta_row = D / gs_r;
+  launch_bgemm(gu, ld.eg.lin.bits, ld.eg.lin.dt, bgemm_grid(ld.eg.lin.bits, ld.eg.lin.dt, gu.L), st, pdl);
+  const int gs_d = ld.ed.lin.gs, I = c.moe_inter;
+  digit(bb.hmid, bb.hmid_stride, Ta * (K + 1), I, gs_d, PRO_COPY, nullptr, nullptr, 0, nullptr, bb.bt_b, bb.meta_b);
+  BGemmArgs dn;
+  dn.mode = BM_STORE; dn.in = I;
+  if (!bgemm_layout(I, ld.ed.lin.bits, ld.ed.lin.dt, gs_d, dn.L)) throw Error(ERR_UNSUPPORTED, "batched down layout");
+  dn.expert_mode = 1; dn.eg = bmat(ld.ed); dn.sg = bmat(ld.sh_d);
+  dn.experts = E; dn.items = bb.items_dn; dn.nitems = bb.nitems + 1; dn.max_items = bb.max_dn; dn.in_map = nullptr;
+  dn.out = bb.ydown; dn.out_stride = D;
+  dn.xbt = bb.bt_b; dn.xmeta = bb.meta_b; dn.bt_row = I / 32 * 12; dn.meta_row = I / gs_d;
+  launch_bgemm(dn, ld.ed.lin.bits, ld.ed.lin.dt, bgemm_grid(ld.ed.lin.bits, ld.ed.lin.dt, dn.L), st, pdl);
+  if (ep_on) {
+    BCombineEpArgs ce;
+    ce.h = bb.h; ce.part = ep_part; ce.ydown = bb.ydown; ce.ystride = D; ce.slot_of = bb.slot_of; ce.w = bb.w;
+    ce.sh = bb.sh; ce.T = Ta; ce.K = K; ce.D = D; ce.own_lo = own; ce.own_hi = own + T;
+    launch_bcombine_ep(ce, st, pdl);
+    ep_reduce_scatter(ep, ep_part, bb.h, size_t(T) * D, st);
+  } else {
+    BCombineArgs cb;
+    cb.h = bb.h; cb.ydown = bb.ydown; cb.ystride = D; cb.slot_of = bb.slot_of; cb.w = bb.w; cb.sh = bb.sh;
+    cb.T = T; cb.K = K; cb.D = D;
+    launch_bcombine(cb, st, pdl);
+  }
 }
 
 // S sequences consume counts[i] tokens each (T in total, in bb.tokens,
@@ -1869,6 +1889,105 @@ int swl_bench_expert_sweep(swl_model* model, int32_t iters, float* ms_out, doubl
     *bytes_per_layer = double(m.cfg.topk) * double(qlin_bytes(l0.eg.lin) + qlin_bytes(l0.eu.lin) + qlin_bytes(l0.ed.lin)) +
                        double(qlin_bytes(l0.sh_g) + qlin_bytes(l0.sh_u) + qlin_bytes(l0.sh_d));
   if (launches) *launches = 2 * iters * m.cfg.layers;
+  API_END
+}
+
+namespace {
+// Times `iters` replays of a graph holding `body` (after one untimed replay).
+float time_graph(Model& m, const std::function<void()>& body, int iters) {
+  cudaGraphExec_t g = capture(m.stream, body);
+  cudaEvent_t e0, e1;
+  SWL_CUDA(cudaEventCreate(&e0));
+  SWL_CUDA(cudaEventCreate(&e1));
+  float ms = 0.f;
+  try {
+    SWL_CUDA(cudaGraphLaunch(g, m.stream));
+    SWL_CUDA(cudaEventRecord(e0, m.stream));
+    for (int it = 0; it < iters; ++it) SWL_CUDA(cudaGraphLaunch(g, m.stream));
+    SWL_CUDA(cudaEventRecord(e1, m.stream));
+    SWL_CUDA(cudaEventSynchronize(e1));
+    SWL_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+  } catch (...) {
+    cudaEventDestroy(e0); cudaEventDestroy(e1); cudaGraphExecDestroy(g);
+    throw;
+  }
+  cudaEventDestroy(e0); cudaEventDestroy(e1); cudaGraphExecDestroy(g);
+  return ms;
+}
+}  // namespace
+
+int swl_bench_moe_sweep(swl_model* model, int32_t T, int32_t iters, float* ms_out, double* bytes_out,
+                        int32_t* unique_out, int32_t* launches) {
+  API_BEGIN
+  if (!model || !ms_out || iters < 1) throw Error(ERR_INVALID, "bad argument");
+  Model& m = model->m;
+  if (!m.bb.ready || T < 2 || T > BT_MAX || m.ep) throw Error(ERR_INVALID, "needs a prior batched decode step of T tokens");
+  SWL_CUDA(cudaSetDevice(m.device));
+  const ModelConfig& c = m.cfg;
+  // One direct pass records each layer's routing: the distinct experts the
+  // grouped GEMMs read are the bytes that count.
+  std::vector<int> ids(size_t(c.layers) * T * c.topk);
+  for (int l = 0; l < c.layers; ++l) {
+    m.enqueue_batch_moe(l, T, false, m.stream);
+    SWL_CUDA(cudaMemcpyAsync(ids.data() + size_t(l) * T * c.topk, m.bb.ids, size_t(T) * c.topk * 4,
+                             cudaMemcpyDeviceToHost, m.stream));
+  }
+  SWL_CUDA(cudaStreamSynchronize(m.stream));
+  int64_t uniq = 0;
+  for (int l = 0; l < c.layers; ++l) {
+    std::vector<char> seen(c.experts, 0);
+    for (int i = 0; i < T * c.topk; ++i) {
+      const int e = ids[size_t(l) * T * c.topk + i];
+      if (e >= 0 && e < c.experts && !seen[e]) { seen[e] = 1; ++uniq; }
+    }
+  }
+  *ms_out = time_graph(m, [&] { for (int l = 0; l < c.layers; ++l) m.enqueue_batch_moe(l, T, false, m.stream); }, iters);
+  const LayerDev& l0 = m.L[0];
+  const double blob = double(qlin_bytes(l0.eg.lin) + qlin_bytes(l0.eu.lin) + qlin_bytes(l0.ed.lin));
+  const double shared = double(qlin_bytes(l0.sh_g) + qlin_bytes(l0.sh_u) + qlin_bytes(l0.sh_d));
+  const double router = double(qlin_bytes(l0.router) + qlin_bytes(l0.sgate));
+  if (bytes_out) *bytes_out = double(uniq) * blob + double(c.layers) * (shared + router);
+  if (unique_out) *unique_out = int32_t(uniq);
+  if (launches) *launches = iters * c.layers * 8;
+  API_END
+}
+
+int swl_bench_delta_sweep(swl_model* model, int32_t T, int32_t iters, float* ms_out, double* bytes_out,
+                          int32_t* launches) {
+  API_BEGIN
+  if (!model || !ms_out || iters < 1) throw Error(ERR_INVALID, "bad argument");
+  Model& m = model->m;
+  const ModelConfig& c = m.cfg;
+  if (T == 1 ? !m.stepped : (!m.bb.ready || T < 2 || T > BT_MAX)) throw Error(ERR_INVALID, "needs a prior step of T tokens");
+  SWL_CUDA(cudaSetDevice(m.device));
+  int nl = 0;
+  auto body = [&] {
+    nl = 0;
+    for (int l = 0; l < c.layers; ++l) {
+      if (!c.is_linear(l)) continue;
+      const LayerDev& ld = m.L[l];
+      DeltaArgs d;
+      d.split = c.split_layout; d.nk = c.nk; d.nv = c.nv; d.dk = c.dk; d.dv = c.dv; d.conv_k = c.conv_k;
+      d.conv_dim = c.conv_dim(); d.conv_w = ld.conv_w; d.a_log = ld.a_log; d.dt_bias = ld.dt_bias; d.layer = l;
+      if (T == 1) {
+        d.proj = m.proj; d.sd = m.cur; d.rows_per_block = std::min(c.dv, 32); d.y = m.yv; d.z = m.zv;
+        launch_delta(d, m.stream, m.use_pdl);
+      } else {
+        d.proj = m.bb.proj; d.proj_stride = m.bb.projn; d.sd = m.bb.sds; d.rows_per_block = c.dv <= 128 ? c.dv : 32;
+        d.y = m.bb.yv; d.z = m.bb.zv;
+        launch_delta_batch(d, T, m.stream, m.use_pdl);
+      }
+      ++nl;
+    }
+  };
+  *ms_out = time_graph(m, body, iters);
+  // per sequence and layer: the f32 state read and written, the conv taps
+  // read and the new conv input written, the token's projections read, y
+  // and silu(z) written
+  const double per = 2.0 * c.nv * c.dv * c.dk * 4 + double(c.conv_k) * c.conv_dim() * 4 +
+                     double(c.conv_dim() + c.value_dim() + 2 * c.nv) * 4 + 2.0 * c.value_dim() * 4;
+  if (bytes_out) *bytes_out = per * T * nl;
+  if (launches) *launches = iters * nl;
   API_END
 }
 
