@@ -757,6 +757,28 @@ __global__ void __launch_bounds__(BR_THREADS) k_broute(const BRouteArgs a) {
     a.nitems[0] = min(base_gu + ntt_s * rbs, a.max_gu);
     a.nitems[1] = min(base_dn + ntt_s * rbd, a.max_dn);
   }
+  if (a.items_tgu) {
+    // the tensor-core GEMM's lists: 64 intermediate rows of gate and up, 128 hidden rows
+    const int tg = (a.inter + 63) / 64, td = (a.hidden + 127) / 128, ts = (a.shared_inter + 63) / 64;
+    for (int i = tid; i < min(tb[E] * tg, a.max_tgu); i += BR_THREADS) a.items_tgu[i] = routed_item(i, tg, 64);
+    for (int i = tid; i < min(tb[E] * td, a.max_tdn); i += BR_THREADS) a.items_tdn[i] = routed_item(i, td, 128);
+    const int bg = tb[E] * tg, bd = tb[E] * td;
+    for (int i = tid; i < ntt_s * ts; i += BR_THREADS) {
+      const int rb = i / ntt_s, tt = i - rb * ntt_s;
+      if (bg + i < a.max_tgu)
+        a.items_tgu[bg + i] = make_int4(E, rb * 64, T * K + sh_lo + tt * BG_TOK, min(BG_TOK, nsh - tt * BG_TOK));
+    }
+    for (int i = tid; i < ntt_s * td; i += BR_THREADS) {
+      const int rb = i / ntt_s, tt = i - rb * ntt_s;
+      if (bd + i < a.max_tdn)
+        a.items_tdn[bd + i] = make_int4(E, rb * 128, T * K + sh_lo + tt * BG_TOK, min(BG_TOK, nsh - tt * BG_TOK));
+    }
+    for (int sl = off[E] + tid; sl < T * K; sl += BR_THREADS) a.slot_tok[sl] = 0;
+    if (tid == 0) {
+      a.ntitems[0] = min(bg + ntt_s * ts, a.max_tgu);
+      a.ntitems[1] = min(bd + ntt_s * td, a.max_tdn);
+    }
+  }
 }
 
 void launch_broute(const BRouteArgs& a, cudaStream_t st, bool pdl) {

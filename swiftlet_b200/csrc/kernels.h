@@ -259,6 +259,50 @@ struct BGemmArgs {
   int64_t bt_row = 0, meta_row = 0;
 };
 
+// Grouped GEMM on the tcgen05 tensor cores (tgemm.cu): the operations of
+// BGemmArgs with 128-row items (dense: 128 rows of a segment; expert gate/up:
+// 64 intermediate rows of gate and of up; expert down: 128 hidden rows) and
+// tiles of up to 16 tokens, reading the activations as a digit matrix from
+// launch_tdigit (three rows of base-254 digits per token or slot).
+struct TGemmArgs {
+  int mode = BM_STORE;
+  int in = 0, gs = 64;
+  int scale_f32 = 0;            // scales/biases f32 (else bf16)
+  // dense launches: up to four segments over one input
+  BMat seg[4];
+  float* y[4] = {nullptr, nullptr, nullptr, nullptr};
+  int nseg = 0;
+  int seg_rb[5] = {0, 0, 0, 0, 0};  // cumulative 128-row blocks
+  int64_t y_stride = 0;
+  int ntok = 0;
+  // expert launches: items {expert, first row, first slot, slots} from
+  // k_broute's tensor-core lists (expert == experts: the shared expert)
+  int expert_mode = 0;
+  BMat eg, eu, sg, su;
+  int experts = 0;
+  const int4* items = nullptr;
+  const int* nitems = nullptr;
+  int max_items = 0;
+  float* out = nullptr;         // expert outputs, slot-major
+  int64_t out_stride = 0;
+  // digitised inputs (launch_tdigit)
+  const int8_t* dg = nullptr;   // [dg_rows][in]
+  int64_t dg_rows = 0;
+  const float2* meta = nullptr; // [rows][meta_row] (1 / digit scale, sum) per group
+  int64_t meta_row = 0;
+  int* status = nullptr;        // bit 0: a bounded wait inside the kernel gave up
+};
+// Whether the tensor-core GEMM takes matrices of this format; false also
+// when SWL_NO_TCGEN05 is set.
+bool tgemm_supported(int in, int bits, int dt, int gs);
+// Launches it (grid = persistent CTAs); false, with nothing launched, when
+// the shapes or tensor maps do not fit it.
+bool launch_tgemm(const TGemmArgs& a, int bits, int grid, cudaStream_t stream, bool pdl);
+// Digits of `rows` rows in the tensor-core layout: row i reads source row
+// in_map[i] (or i) of a.x, applies a.prologue, and writes dg[(3i + d) * in + k]
+// and a.meta[i * a.meta_row + g]; a.bt is unused.
+void launch_tdigit(const DigitArgs& a, const int* in_map, int8_t* dg, cudaStream_t stream, bool pdl);
+
 // Routing and grouping of a batch: per token the softmax top-k of the router
 // logits (QwenCPUModel.swift:506-521), then picks sorted by expert into
 // slots (expert-major, tokens ascending within an expert; the shared expert
@@ -280,6 +324,14 @@ struct BRouteArgs {
   // other picks get slot -1), and only tokens [sh_lo, sh_hi) get shared-expert
   // items. The defaults cover every expert and token.
   int e_lo = 0, e_hi = 1 << 30, sh_lo = 0, sh_hi = 1 << 30;
+  // Optional item lists of the tensor-core GEMM: gate/up items of 64
+  // intermediate rows, down items of 128 hidden rows; counts in ntitems[2].
+  // Slots past the routed ones get slot_tok 0 so digit rows can be made for
+  // every slot index.
+  int4* items_tgu = nullptr;
+  int4* items_tdn = nullptr;
+  int* ntitems = nullptr;
+  int max_tgu = 0, max_tdn = 0;
 };
 
 // Expert-parallel combine: part[t] = sum of the weighted outputs of this

@@ -93,6 +93,13 @@ struct BatchBufs {
   int *ids = nullptr, *slot_of = nullptr, *slot_tok = nullptr, *nitems = nullptr, *tokens = nullptr, *greedy = nullptr;
   int4 *items_gu = nullptr, *items_dn = nullptr;
   int max_gu = 0, max_dn = 0;
+  // tensor-core expert GEMMs: 64 / 128-row item lists, digit matrices and
+  // group metadata of the expert inputs (per slot)
+  int4 *items_tgu = nullptr, *items_tdn = nullptr;
+  int max_tgu = 0, max_tdn = 0;
+  int* ntitems = nullptr;
+  int8_t *dg_x = nullptr, *dg_mid = nullptr;
+  float2 *tmeta_x = nullptr, *tmeta_mid = nullptr;
   uint2 *bt_a = nullptr, *bt_b = nullptr;
   float2 *meta_a = nullptr, *meta_b = nullptr;
   StateDev* sds = nullptr;
@@ -199,6 +206,7 @@ struct Model {
   void ensure_batch();
   void enqueue_batch(int T, int S, bool chunked, cudaStream_t st);
   void enqueue_batch_moe(int l, int T, bool chunked, cudaStream_t st);
+  void enqueue_batch_combine(int T, int Ta, int own, bool ep_on, cudaStream_t st);
   // S sequences consume counts[i] tokens each (T in total, already in
   // bb.tokens, sequence-major)
   void run_batch(State* const* s, int S, const int* counts, int T);
@@ -873,6 +881,18 @@ void Model::ensure_batch() {
   bb.max_dn = tiles * ((D + 63) / 64);
   bb.items_gu = reinterpret_cast<int4*>(dmalloc(size_t(bb.max_gu) * sizeof(int4)));
   bb.items_dn = reinterpret_cast<int4*>(dmalloc(size_t(bb.max_dn) * sizeof(int4)));
+  bb.max_tgu = tiles * ((std::max(c.moe_inter, c.shared_inter) + 63) / 64);
+  bb.max_tdn = tiles * ((D + 127) / 128);
+  bb.items_tgu = reinterpret_cast<int4*>(dmalloc(size_t(bb.max_tgu) * sizeof(int4)));
+  bb.items_tdn = reinterpret_cast<int4*>(dmalloc(size_t(bb.max_tdn) * sizeof(int4)));
+  bb.ntitems = i4(2);
+  {
+    const int mi = std::max(c.moe_inter, c.shared_inter);
+    bb.dg_x = reinterpret_cast<int8_t*>(dmalloc(size_t(slots) * 3 * D));
+    bb.dg_mid = reinterpret_cast<int8_t*>(dmalloc(size_t(slots) * 3 * ((mi + 255) / 256 * 256)));
+    bb.tmeta_x = reinterpret_cast<float2*>(dmalloc(size_t(slots) * (D / 32 + 1) * sizeof(float2)));
+    bb.tmeta_mid = reinterpret_cast<float2*>(dmalloc(size_t(slots) * (mi / 32 + 1) * sizeof(float2)));
+  }
   bb.bt_a = reinterpret_cast<uint2*>(dmalloc(size_t(T) * (max_in / 32) * 12 * sizeof(uint2)));
   bb.meta_a = reinterpret_cast<float2*>(dmalloc(size_t(T) * (max_in / 32) * sizeof(float2)));
   bb.bt_b = reinterpret_cast<uint2*>(dmalloc(size_t(slots) * (c.moe_inter / 32 + 1) * 12 * sizeof(uint2)));
@@ -1018,7 +1038,49 @@ void Model::enqueue_batch_moe(int l, int T, bool chunked, cudaStream_t st) {
   r.ids = bb.ids; r.w = bb.w; r.sh = bb.sh; r.slot_of = bb.slot_of; r.slot_tok = bb.slot_tok;
   r.items_gu = bb.items_gu; r.items_dn = bb.items_dn; r.nitems = bb.nitems;
   r.inter = c.moe_inter; r.shared_inter = c.shared_inter; r.hidden = D; r.max_gu = bb.max_gu; r.max_dn = bb.max_dn;
+  const int gs_d = ld.ed.lin.gs, I = c.moe_inter;
+  // the tensor-core grouped GEMMs take the experts when their formats allow
+  // (expert-parallel steps exchange digits, not the MoE input rows the
+  // tensor-core layout is made from: they keep the mma.sync GEMMs)
+  const bool tc = !ep_on && tgemm_supported(D, ld.eg.lin.bits, ld.eg.lin.dt, gs_r) && ld.eg.lin.gs == gs_r &&
+                  tgemm_supported(I, ld.ed.lin.bits, ld.ed.lin.dt, gs_d) && c.shared_inter == I &&
+                  ld.sh_g.bits == ld.eg.lin.bits && ld.sh_g.dt == ld.eg.lin.dt && ld.sh_g.gs == gs_r &&
+                  ld.sh_d.gs == gs_d && ld.ed.lin.bits == ld.eg.lin.bits;
+  if (tc) {
+    r.items_tgu = bb.items_tgu; r.items_tdn = bb.items_tdn; r.ntitems = bb.ntitems;
+    r.max_tgu = bb.max_tgu; r.max_tdn = bb.max_tdn;
+  }
   launch_broute(r, st, pdl);
+  if (tc) {
+    const int slots = Ta * (K + 1), bits = ld.eg.lin.bits;
+    DigitArgs dx;
+    dx.x = bb.xmoe; dx.x_stride = D; dx.rows = slots; dx.in = D; dx.gs = gs_r; dx.prologue = PRO_COPY;
+    dx.meta = bb.tmeta_x; dx.meta_row = D / gs_r;
+    launch_tdigit(dx, bb.slot_tok, bb.dg_x, st, pdl);
+    TGemmArgs gu;
+    gu.mode = BM_SWIGLU; gu.in = D; gu.gs = gs_r; gu.scale_f32 = ld.eg.lin.dt == DT_F32;
+    gu.expert_mode = 1; gu.eg = bmat(ld.eg); gu.eu = bmat(ld.eu); gu.sg = bmat(ld.sh_g); gu.su = bmat(ld.sh_u);
+    gu.experts = E; gu.items = bb.items_tgu; gu.nitems = bb.ntitems; gu.max_items = bb.max_tgu;
+    gu.out = bb.hmid; gu.out_stride = bb.hmid_stride;
+    gu.dg = bb.dg_x; gu.dg_rows = int64_t(3) * slots; gu.meta = bb.tmeta_x; gu.meta_row = D / gs_r;
+    gu.status = kstatus;
+    const bool ok_gu = launch_tgemm(gu, bits, sm_count(), st, pdl);
+    DigitArgs dm;
+    dm.x = bb.hmid; dm.x_stride = bb.hmid_stride; dm.rows = slots; dm.in = I; dm.gs = gs_d; dm.prologue = PRO_COPY;
+    dm.meta = bb.tmeta_mid; dm.meta_row = I / gs_d;
+    if (ok_gu) launch_tdigit(dm, nullptr, bb.dg_mid, st, pdl);
+    TGemmArgs dn;
+    dn.mode = BM_STORE; dn.in = I; dn.gs = gs_d; dn.scale_f32 = ld.ed.lin.dt == DT_F32;
+    dn.expert_mode = 1; dn.eg = bmat(ld.ed); dn.sg = bmat(ld.sh_d);
+    dn.experts = E; dn.items = bb.items_tdn; dn.nitems = bb.ntitems + 1; dn.max_items = bb.max_tdn;
+    dn.out = bb.ydown; dn.out_stride = D;
+    dn.dg = bb.dg_mid; dn.dg_rows = int64_t(3) * slots; dn.meta = bb.tmeta_mid; dn.meta_row = I / gs_d;
+    dn.status = kstatus;
+    if (!ok_gu || !launch_tgemm(dn, bits, sm_count(), st, pdl))
+      throw Error(ERR_UNSUPPORTED, "tensor-core expert GEMM: tensor maps do not fit these experts");
+    enqueue_batch_combine(T, Ta, own, ep_on, st);
+    return;
+  }
   BGemmArgs gu;
   gu.mode = BM_SWIGLU; gu.in = D;
   if (!bgemm_layout(D, ld.eg.lin.bits, ld.eg.lin.dt, gs_r, gu.L)) throw Error(ERR_UNSUPPORTED, "batched gate/up layout");
@@ -1027,7 +1089,6 @@ void Model::enqueue_batch_moe(int l, int T, bool chunked, cudaStream_t st) {
   gu.out = bb.hmid; gu.out_stride = bb.hmid_stride;
   gu.xbt = bb.bt_a; gu.xmeta = bb.meta_a; gu.bt_row = D / 32 * 12; gu.meta_row = D / gs_r;
   launch_bgemm(gu, ld.eg.lin.bits, ld.eg.lin.dt, bgemm_grid(ld.eg.lin.bits, ld.eg.lin.dt, gu.L), st, pdl);
-  const int gs_d = ld.ed.lin.gs, I = c.moe_inter;
   digit(bb.hmid, bb.hmid_stride, Ta * (K + 1), I, gs_d, PRO_COPY, nullptr, nullptr, 0, nullptr, bb.bt_b, bb.meta_b);
   BGemmArgs dn;
   dn.mode = BM_STORE; dn.in = I;
@@ -1037,6 +1098,16 @@ void Model::enqueue_batch_moe(int l, int T, bool chunked, cudaStream_t st) {
   dn.out = bb.ydown; dn.out_stride = D;
   dn.xbt = bb.bt_b; dn.xmeta = bb.meta_b; dn.bt_row = I / 32 * 12; dn.meta_row = I / gs_d;
   launch_bgemm(dn, ld.ed.lin.bits, ld.ed.lin.dt, bgemm_grid(ld.ed.lin.bits, ld.ed.lin.dt, dn.L), st, pdl);
+  enqueue_batch_combine(T, Ta, own, ep_on, st);
+}
+
+// Expert outputs back into the residual stream: the weighted routed sums
+// and the gated shared expert (QwenCPUModel.swift:552-566), or with expert
+// parallelism this rank's partial sums and their reduce-scatter.
+void Model::enqueue_batch_combine(int T, int Ta, int own, bool ep_on, cudaStream_t st) {
+  const ModelConfig& c = cfg;
+  const int D = c.hidden, K = c.topk;
+  const bool pdl = use_pdl;
   if (ep_on) {
     BCombineEpArgs ce;
     ce.h = bb.h; ce.part = ep_part; ce.ydown = bb.ydown; ce.ystride = D; ce.slot_of = bb.slot_of; ce.w = bb.w;
