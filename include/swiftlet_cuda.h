@@ -293,6 +293,14 @@ int swl_kernel_expert_swiglu(const uint32_t* gate_w, const void* gate_s, const v
                              const void* down_b, int sdtype, int bits, int group, int hidden, int inter, const float* x,
                              float* y);
 
+/* ... and the gated delta rule over T tokens (the recurrence of
+ * QwenCPUModel.swift:459-488 on given inputs, as MetalKernelTests.swift:
+ * 194-220 constructs it) through the chunked-parallel prompt kernel:
+ * q, k [T][Hk][Dk], v [T][Hv][Dv], g, beta [T][Hv], state [Hv][Dv][Dk]
+ * (updated in place), y [T][Hv][Dv]. Needs Dk = 128 and Dv a multiple of 32. */
+int swl_kernel_gated_delta(const float* q, const float* k, const float* v, const float* g, const float* beta,
+                           float* state, float* y, int32_t T, int32_t Hk, int32_t Hv, int32_t Dk, int32_t Dv);
+
 /* ---- allocation-free entry point (no counterpart in the reference) ----- */
 
 /* A device-resident MLX-affine matrix: uint32 words packed low bits first,

@@ -97,6 +97,7 @@ _SIGNATURES = {
     "swl_debug_delta_state": (_I, [_P, _P, C.c_int32, _P]),
     "swl_debug_kernel_path": (_I, [_P, C.c_char_p, C.c_int32]),
     "swl_state_reset": (_I, [_P]),
+    "swl_kernel_gated_delta": (_I, [_P] * 7 + [C.c_int32] * 5),
     "swl_bench_moe_sweep": (_I, [_P, C.c_int32, C.c_int32, C.POINTER(C.c_float), C.POINTER(C.c_double),
                                  C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
     "swl_bench_delta_sweep": (_I, [_P, C.c_int32, C.c_int32, C.POINTER(C.c_float), C.POINTER(C.c_double),
@@ -480,6 +481,15 @@ def expert_swiglu(gate, up, down, hidden: int, inter: int, group: int, bits: int
     y = np.empty(hidden, np.float32)
     _check(lib().swl_kernel_expert_swiglu(*[_ptr(a) for a in arrs], sd, bits, group, hidden, inter, _ptr(x), _ptr(y)))
     return y
+
+
+def gated_delta(q, k, v, g, beta, state, T, Hk, Hv, Dk, Dv):
+    """Gated delta rule over T steps on the GPU's chunked prompt kernel. Returns (y, state)."""
+    arrs = [np.ascontiguousarray(a, dtype=np.float32) for a in (q, k, v, g, beta)]
+    st = np.array(state, dtype=np.float32, copy=True)
+    y = np.zeros(T * Hv * Dv, np.float32)
+    _check(lib().swl_kernel_gated_delta(*[_ptr(a) for a in arrs], _ptr(st), _ptr(y), T, Hk, Hv, Dk, Dv))
+    return y, st
 
 
 def verify_container(container: str, hashes_json: str | None = None, delete_corrupt: bool = False) -> dict:

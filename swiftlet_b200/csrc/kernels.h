@@ -135,6 +135,33 @@ struct DeltaArgs {
   Trace trace;
 };
 
+// Chunked-parallel delta rule (delta_wy.cu) of a prompt launch: per token the
+// normalised q / k rows, v rows and (log g, beta) pairs that k_delta_prep
+// writes, per sequence (blockIdx.z) its token range; the state is each
+// sequence's own (sd) or, for the kernel-level entry point, one direct state.
+struct WyArgs {
+  const float* q = nullptr;   // [tokens][q_stride], key head h at h * dk
+  const float* k = nullptr;
+  const float* v = nullptr;   // [tokens][v_stride], value head h at h * dv
+  const float* lg = nullptr;  // [tokens][gb_stride]: (log g, beta) of value head h at 2h, 2h + 1
+  float *qw = nullptr, *kw = nullptr, *vw = nullptr, *lgw = nullptr;  // the same buffers, written by the prep
+  int64_t q_stride = 0, k_stride = 0, v_stride = 0, gb_stride = 0;
+  int nk = 0, nv = 0, dk = 0, dv = 0;
+  const StateDev* sd = nullptr;
+  int layer = 0;
+  float* state = nullptr;     // direct state [nv][dv][dk] (kernel-level entry; sd unused)
+  const int* seq_first = nullptr;  // token range of sequence blockIdx.z (null: tokens [0, ntok))
+  const int* seq_n = nullptr;
+  const int* tok_seq = nullptr;    // prep: sequence and offset of each token
+  const int* tok_off = nullptr;
+  int ntok = 0;
+  float* y = nullptr;         // [tokens][y_stride] recurrence output
+  int64_t y_stride = 0;
+};
+bool delta_wy_supported(int dk, int dv, int nk, int nv, int conv_dim);
+void launch_delta_prep(const DeltaArgs& a, const WyArgs& w, int T, cudaStream_t stream, bool pdl);
+void launch_delta_wy(const WyArgs& a, int S, cudaStream_t stream, bool pdl);
+
 struct AttnArgs {
   const float* qout;       // [H * 2 * hd] (per head: q | gate)
   const float* knew;       // [Hkv * hd]

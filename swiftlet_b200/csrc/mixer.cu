@@ -18,28 +18,6 @@ namespace swl {
 // (QwenCPUModel.swift:423-488). Block = (v-head, slice of RB dv rows); a
 // warp owns rows r = warp, warp + 4, ...; the state rows are loaded into
 // registers before the dependency wait (they were written one token ago).
-__device__ __forceinline__ int delta_src(const DeltaArgs& a, int c) {
-  // Index into `proj` of mixed-qkv channel c.
-  if (a.split) return c;
-  const int keyDim = a.nk * a.dk, rep = a.nv / a.nk, chunk = 2 * a.dk + 2 * rep * a.dv;
-  if (c < keyDim) { const int hk = c / a.dk; return hk * chunk + (c - hk * a.dk); }
-  if (c < 2 * keyDim) { const int cc = c - keyDim, hk = cc / a.dk; return hk * chunk + a.dk + (cc - hk * a.dk); }
-  const int cv = c - 2 * keyDim, hv = cv / a.dv, i = cv - hv * a.dv, hk = hv / rep, ri = hv - hk * rep;
-  return hk * chunk + 2 * a.dk + ri * a.dv + i;
-}
-__device__ __forceinline__ int delta_z(const DeltaArgs& a, int hv, int i) {
-  if (a.split) return a.conv_dim + hv * a.dv + i;
-  const int rep = a.nv / a.nk, chunk = 2 * a.dk + 2 * rep * a.dv, hk = hv / rep, ri = hv - hk * rep;
-  return hk * chunk + 2 * a.dk + rep * a.dv + ri * a.dv + i;
-}
-__device__ __forceinline__ void delta_ba(const DeltaArgs& a, int hv, int& bi, int& ai) {
-  const int valueDim = a.nv * a.dv;
-  if (a.split) { bi = a.conv_dim + valueDim + hv; ai = a.conv_dim + valueDim + a.nv + hv; return; }
-  const int keyDim = a.nk * a.dk, rep = a.nv / a.nk, hk = hv / rep, ri = hv - hk * rep;
-  const int base = 2 * keyDim + 2 * valueDim + hk * 2 * rep;
-  bi = base + ri; ai = base + rep + ri;
-}
-
 constexpr int DELTA_THREADS = 128;     // single-sequence launches
 constexpr int DELTA_MAX_THREADS = 512; // batched launches: one CTA per (v-head, sequence), 8 rows per warp
 constexpr int DELTA_RPW = 8;  // rows per warp (RB <= 32)

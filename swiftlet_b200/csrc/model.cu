@@ -100,6 +100,9 @@ struct BatchBufs {
   int* ntitems = nullptr;
   int8_t *dg_x = nullptr, *dg_mid = nullptr;
   float2 *tmeta_x = nullptr, *tmeta_mid = nullptr;
+  // chunked-parallel delta rule of prompt launches: per token normalised q,
+  // k, v and (log g, beta)
+  float *wy_q = nullptr, *wy_k = nullptr, *wy_v = nullptr, *wy_gb = nullptr;
   uint2 *bt_a = nullptr, *bt_b = nullptr;
   float2 *meta_a = nullptr, *meta_b = nullptr;
   StateDev* sds = nullptr;
@@ -893,6 +896,10 @@ void Model::ensure_batch() {
     bb.tmeta_x = reinterpret_cast<float2*>(dmalloc(size_t(slots) * (D / 32 + 1) * sizeof(float2)));
     bb.tmeta_mid = reinterpret_cast<float2*>(dmalloc(size_t(slots) * (mi / 32 + 1) * sizeof(float2)));
   }
+  if (c.nv > 0) {
+    bb.wy_q = f(size_t(T) * c.key_dim()); bb.wy_k = f(size_t(T) * c.key_dim());
+    bb.wy_v = f(size_t(T) * c.value_dim()); bb.wy_gb = f(size_t(T) * 2 * c.nv);
+  }
   bb.bt_a = reinterpret_cast<uint2*>(dmalloc(size_t(T) * (max_in / 32) * 12 * sizeof(uint2)));
   bb.meta_a = reinterpret_cast<float2*>(dmalloc(size_t(T) * (max_in / 32) * sizeof(float2)));
   bb.bt_b = reinterpret_cast<uint2*>(dmalloc(size_t(slots) * (c.moe_inter / 32 + 1) * 12 * sizeof(uint2)));
@@ -963,7 +970,19 @@ void Model::enqueue_batch(int T, int S, bool chunked, cudaStream_t st) {
       d.trace = tagged(16u * unsigned(l + 1) + 3);
       if (chunked) {
         d.seq_first = bb.seq_first; d.seq_n = bb.seq_n;
-        launch_delta_seq(d, S, st, pdl);
+        if (delta_wy_supported(c.dk, c.dv, c.nk, c.nv, c.conv_dim())) {
+          // chunk-parallel form: per-token inputs, then each sequence's tokens as one chunk
+          WyArgs w;
+          w.q = w.qw = bb.wy_q; w.k = w.kw = bb.wy_k; w.v = w.vw = bb.wy_v; w.lg = w.lgw = bb.wy_gb;
+          w.q_stride = w.k_stride = c.key_dim(); w.v_stride = c.value_dim(); w.gb_stride = 2 * c.nv;
+          w.nk = c.nk; w.nv = c.nv; w.dk = c.dk; w.dv = c.dv; w.sd = bb.sds; w.layer = l;
+          w.seq_first = bb.seq_first; w.seq_n = bb.seq_n; w.tok_seq = bb.tok_seq; w.tok_off = bb.tok_off;
+          w.y = bb.yv; w.y_stride = c.value_dim();
+          launch_delta_prep(d, w, T, st, pdl);
+          launch_delta_wy(w, S, st, pdl);
+        } else {
+          launch_delta_seq(d, S, st, pdl);
+        }
         launch_conv_ring(d, S, st, pdl);
       } else {
         launch_delta_batch(d, T, st, pdl);
@@ -2140,6 +2159,41 @@ int swl_kernel_expert_swiglu(const uint32_t* gate_w, const void* gate_s, const v
     launch_moe_down(m, 0, false);
     SWL_CUDA(cudaDeviceSynchronize());
     SWL_CUDA(cudaMemcpy(y, dy, size_t(hidden) * 4, cudaMemcpyDeviceToHost));
+  } catch (...) {
+    for (void* p : bufs) cudaFree(p);
+    throw;
+  }
+  for (void* p : bufs) cudaFree(p);
+  API_END
+}
+
+int swl_kernel_gated_delta(const float* q, const float* k, const float* v, const float* g, const float* beta,
+                           float* state, float* y, int32_t T, int32_t Hk, int32_t Hv, int32_t Dk, int32_t Dv) {
+  API_BEGIN
+  if (!q || !k || !v || !g || !beta || !state || !y || T < 1) throw Error(ERR_INVALID, "null argument");
+  if (Hk < 1 || Hv % Hk || !delta_wy_supported(Dk, Dv, Hk, Hv, 0))
+    throw Error(ERR_UNSUPPORTED, "chunked delta rule: needs 128-dim key heads and value heads in multiples of 32");
+  std::vector<void*> bufs;
+  auto dm = [&](size_t n) { void* p = nullptr; SWL_CUDA(cudaMalloc(&p, std::max<size_t>(n, 16))); bufs.push_back(p); return p; };
+  try {
+    const size_t nq = size_t(T) * Hk * Dk, nvv = size_t(T) * Hv * Dv, ns = size_t(Hv) * Dv * Dk;
+    std::vector<float> gb(size_t(T) * 2 * Hv);
+    for (size_t i = 0; i < size_t(T) * Hv; ++i) { gb[2 * i] = logf(g[i]); gb[2 * i + 1] = beta[i]; }
+    float* dq = (float*)dm(nq * 4); float* dk = (float*)dm(nq * 4); float* dv = (float*)dm(nvv * 4);
+    float* dgb = (float*)dm(gb.size() * 4); float* dst = (float*)dm(ns * 4); float* dy = (float*)dm(nvv * 4);
+    SWL_CUDA(cudaMemcpy(dq, q, nq * 4, cudaMemcpyHostToDevice));
+    SWL_CUDA(cudaMemcpy(dk, k, nq * 4, cudaMemcpyHostToDevice));
+    SWL_CUDA(cudaMemcpy(dv, v, nvv * 4, cudaMemcpyHostToDevice));
+    SWL_CUDA(cudaMemcpy(dgb, gb.data(), gb.size() * 4, cudaMemcpyHostToDevice));
+    SWL_CUDA(cudaMemcpy(dst, state, ns * 4, cudaMemcpyHostToDevice));
+    WyArgs w;
+    w.q = dq; w.k = dk; w.v = dv; w.lg = dgb;
+    w.q_stride = w.k_stride = int64_t(Hk) * Dk; w.v_stride = int64_t(Hv) * Dv; w.gb_stride = 2 * Hv;
+    w.nk = Hk; w.nv = Hv; w.dk = Dk; w.dv = Dv; w.state = dst; w.ntok = T; w.y = dy; w.y_stride = int64_t(Hv) * Dv;
+    launch_delta_wy(w, 1, 0, false);
+    SWL_CUDA(cudaDeviceSynchronize());
+    SWL_CUDA(cudaMemcpy(y, dy, nvv * 4, cudaMemcpyDeviceToHost));
+    SWL_CUDA(cudaMemcpy(state, dst, ns * 4, cudaMemcpyDeviceToHost));
   } catch (...) {
     for (void* p : bufs) cudaFree(p);
     throw;

@@ -64,3 +64,32 @@ def test_expert_swiglu_matches_oracle(bits, hidden, inter, group, sdtype):
     ref = oracle.expert_swiglu(gate, up, down, hidden, inter, group, bits, x)
     y = swl.expert_swiglu(gate, up, down, hidden, inter, group, bits, x)
     assert np.abs(y - ref).max() / (np.abs(ref).max() + 1e-6) < 1e-5
+
+
+def _delta_inputs(rng, T, Hk, Hv, Dk, Dv):
+    """Inputs as the decode path forms them: k unit-norm, q of norm 1/sqrt(dk)
+    (RMSNorm scaled 1/sqrt(dk) and 1/dk), g = exp(-exp(A) softplus(a)),
+    beta = sigmoid(b) (QwenCPUModel.swift:423-458)."""
+    q = rng.normal(0, 1, (T, Hk, Dk)).astype(np.float32)
+    k = rng.normal(0, 1, (T, Hk, Dk)).astype(np.float32)
+    q /= np.linalg.norm(q, axis=-1, keepdims=True) * np.sqrt(Dk)
+    k /= np.linalg.norm(k, axis=-1, keepdims=True)
+    v = rng.normal(0, 1, (T, Hv, Dv)).astype(np.float32)
+    a_log = rng.uniform(0, 1, Hv)
+    g = np.exp(-np.exp(a_log) * np.log1p(np.exp(rng.normal(0, 1, (T, Hv))))).astype(np.float32)
+    beta = (1 / (1 + np.exp(-rng.normal(0, 1, (T, Hv))))).astype(np.float32)
+    state = rng.normal(0, 0.1, (Hv, Dv, Dk)).astype(np.float32)
+    return q, k, v, g, beta, state
+
+
+@pytest.mark.parametrize("T", [1, 64, 65, 130, 4096])
+def test_chunked_delta_rule_matches_sequential_oracle(T):
+    """The chunk-parallel prompt kernel (64-token chunks, triangular solve)
+    against the oracle's token-by-token recurrence (MetalKernelTests.swift:
+    194-220 construction): outputs and final state within 1e-4 relative."""
+    Hk, Hv, Dk, Dv = 2, 4, 128, 128
+    q, k, v, g, beta, state = _delta_inputs(np.random.default_rng(T), T, Hk, Hv, Dk, Dv)
+    y_ref, s_ref = oracle.gated_delta(q, k, v, g, beta, state, T, Hk, Hv, Dk, Dv)
+    y, s = swl.gated_delta(q, k, v, g, beta, state, T, Hk, Hv, Dk, Dv)
+    assert np.abs(y - y_ref).max() / (np.abs(y_ref).max() + 1e-6) < 1e-4
+    assert np.abs(s - s_ref).max() / (np.abs(s_ref).max() + 1e-6) < 1e-4
