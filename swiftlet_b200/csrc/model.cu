@@ -9,7 +9,12 @@
 #include <cstdlib>
 #include <cstring>
 #include <functional>
+#include <fcntl.h>
+#include <unistd.h>
+
 #include <map>
+#include <set>
+#include <unordered_map>
 #include <memory>
 #include <string>
 #include <vector>
@@ -171,6 +176,24 @@ struct Model {
   float* ep_part = nullptr;  // [ep_world * ep_tokens][hidden] partial MoE sums
   int ep_lo() const { return int(int64_t(ep_rank) * cfg.experts / ep_world); }
   int ep_hi() const { return int(int64_t(ep_rank + 1) * cfg.experts / ep_world); }
+  // Expert streaming: a .qpack model whose experts exceed the HBM budget
+  // keeps a pool of max_slots expert slots, filled from the layer files on a
+  // miss (ExpertCache.swift:9-102): slots are taken lazily up to max_slots,
+  // then free ones, then the least frequently used with the oldest last use
+  // (a layer's own picks are never evicted for each other). Use counts live
+  // per (layer, expert) for the model's lifetime, as the reference's.
+  bool streaming = false;
+  int max_slots = 0, used_slots = 0;
+  std::vector<int64_t> slot_key, slot_tick;  // key occupying each slot (-1 free), its last use
+  std::unordered_map<int64_t, int> key_slot;
+  std::unordered_map<int64_t, int64_t> key_freq;
+  int64_t tick = 0;
+  std::vector<int> layer_fd;
+  uint8_t* h_stage = nullptr;  // pinned staging of a layer's missing blobs [topk][stride]
+  int* h_picks = nullptr;      // pinned: router picks [topk], then their slots [topk]
+  int* d_pick_slots = nullptr; // slots of the current layer's picks (the expert kernels' pick ids)
+  void stream_alloc(double gb);
+  void stream_resolve(int l, cudaStream_t st);
   int batch_ok = -1;         // -1 unchecked; 1 every module fits the batched kernels
   std::string batch_why;     // why not
   Trace trace;               // SWL_TRACE=<records>: per-block kernel timeline
@@ -254,6 +277,9 @@ Model::~Model() {
     s->model = nullptr;
   }
   for (void* p : allocs) cudaFree(p);
+  for (int fd : layer_fd) if (fd >= 0) close(fd);
+  if (h_stage) cudaFreeHost(h_stage);
+  if (h_picks) cudaFreeHost(h_picks);
   if (h_logits) cudaFreeHost(h_logits);
   if (h_tokens) cudaFreeHost(h_tokens);
   if (own) cudaStreamDestroy(own);
@@ -652,25 +678,47 @@ void Model::open(const std::string& d, double pool_gb, int dev) {
   chunk_cap = std::max((max_ctx_cap + attn_chunks - 1) / attn_chunks, attn_chunks);
   plan_sections();
   pool_size = size_t(cfg.layers) * cfg.experts * stride;
-  if (pool_gb > 0 && double(pool_size) > pool_gb * 1073741824.0)
-    throw Error(ERR_CAPACITY, "expert pool needs " + std::to_string(double(pool_size) / 1073741824.0) +
-                                  " GB of HBM, above the budget; the HBM-resident pool does not stream experts");
+  if (pool_gb > 0 && double(pool_size) > pool_gb * 1073741824.0) {
+    if (mode != QPACK)
+      throw Error(ERR_CAPACITY, "expert pool needs " + std::to_string(double(pool_size) / 1073741824.0) +
+                                    " GB of HBM, above the budget; experts stream only from a .qpack container");
+    streaming = true;
+    use_graph = false;  // every MoE layer waits for its routing on the host
+  }
   // pass 1: plan the dense arena, pass 2: allocate and fill
   planning = true; dense_used = 0;
   build_weights();
   dense_size = dense_used;
   dense = reinterpret_cast<uint8_t*>(dmalloc(dense_size));
-  pool = reinterpret_cast<uint8_t*>(dmalloc(pool_size));
+  if (!streaming) pool = reinterpret_cast<uint8_t*>(dmalloc(pool_size));
   planning = false; dense_used = 0;
   build_weights();
-  for (int l = 0; l < cfg.layers; ++l) {
-    LayerDev& ld = L[l];
-    ld.pool = pool + size_t(l) * cfg.experts * stride;
-    ld.eg = expert_proj(ld.pool, "gate_proj", cfg.moe_inter, cfg.hidden);
-    ld.eu = expert_proj(ld.pool, "up_proj", cfg.moe_inter, cfg.hidden);
-    ld.ed = expert_proj(ld.pool, "down_proj", cfg.hidden, cfg.moe_inter);
+  if (streaming) {
+    payload = 0;
+    for (auto& sec : sections) payload = std::max(payload, sec.offset + sec.size);
+    for (int l = 0; l < cfg.layers; ++l) {
+      char name[64];
+      snprintf(name, sizeof name, "/packed_experts/layer_%02d.bin", l);
+      const int fd = ::open((dir + name).c_str(), O_RDONLY);
+      if (fd < 0) throw Error(ERR_IO, std::string("cannot open ") + dir + name);
+      layer_fd.push_back(fd);
+      const off_t size = lseek(fd, 0, SEEK_END);
+      if (size < off_t(int64_t(cfg.experts) * stride)) throw Error(ERR_FORMAT, std::string("short layer file: ") + name);
+    }
+    SWL_CUDA(cudaMallocHost(&h_stage, size_t(cfg.topk) * stride));
+    SWL_CUDA(cudaMallocHost(&h_picks, size_t(2 * cfg.topk) * 4));
+    d_pick_slots = reinterpret_cast<int*>(dmalloc(size_t(cfg.topk) * 4));
+    stream_alloc(pool_gb);
+  } else {
+    for (int l = 0; l < cfg.layers; ++l) {
+      LayerDev& ld = L[l];
+      ld.pool = pool + size_t(l) * cfg.experts * stride;
+      ld.eg = expert_proj(ld.pool, "gate_proj", cfg.moe_inter, cfg.hidden);
+      ld.eu = expert_proj(ld.pool, "up_proj", cfg.moe_inter, cfg.hidden);
+      ld.ed = expert_proj(ld.pool, "down_proj", cfg.hidden, cfg.moe_inter);
+    }
+    upload_experts();
   }
-  upload_experts();
   alloc_scratch();
   SWL_CUDA(cudaStreamSynchronize(stream));
   ck.reset();  // weights are resident; drop the file mappings
@@ -723,7 +771,7 @@ void Model::enqueue_layer(int l, cudaStream_t st, bool advance) {
   m.hmid = hmid; m.hmid_stride = hmid_stride; m.topk = c.topk; m.h = h;
   m.advance_sd = advance ? cur : nullptr; m.advance_cursor = cursor; m.status = kstatus;
   m.smem_kb = 136;  // gate/up sits between the router and down kernels
-  const bool route_in_moe = moe_routes_from_logits(m, c.experts);
+  const bool route_in_moe = !streaming && moe_routes_from_logits(m, c.experts);
   if (route_in_moe) { m.logits = rlogits; m.experts = c.experts; m.norm_topk = c.norm_topk; }
   RouterArgs r;
   r.gate = ld.router; r.sgate = ld.sgate; r.h = h; r.norm_w = ld.post_norm; r.eps = float(c.eps);
@@ -732,10 +780,103 @@ void Model::enqueue_layer(int l, cudaStream_t st, bool advance) {
   r.pool = nullptr; r.pool_stride = stride; r.prefetch_bytes = 0; r.status = kstatus; r.skip_topk = route_in_moe;
   r.trace = tagged(lt + 5);
   launch_router(r, c.experts, st, pdl);
+  if (streaming) {
+    // the picks go to the host, missing blobs come in, and the expert
+    // kernels address the slots
+    stream_resolve(l, st);
+    m.pick_ids = d_pick_slots;
+  }
   m.trace = tagged(lt + 6);
   launch_moe_gateup(m, st, pdl);
   m.trace = tagged(lt + 7);
   launch_moe_down(m, st, pdl);
+}
+
+// (Re)allocates the slot pool for a budget of gb (at least 16 slots, at most
+// every expert, ExpertCache.swift:30-33) and forgets every resident blob.
+void Model::stream_alloc(double gb) {
+  const int64_t total = int64_t(cfg.layers) * cfg.experts;
+  const int64_t want = std::min<int64_t>(std::max<int64_t>(int64_t(gb * 1073741824.0 / double(stride)), 16), total);
+  if (want < cfg.topk) throw Error(ERR_CAPACITY, "expert pool below one layer's picks");
+  SWL_CUDA(cudaStreamSynchronize(stream));
+  if (pool) {
+    cudaFree(pool);
+    allocs.erase(std::remove(allocs.begin(), allocs.end(), static_cast<void*>(pool)), allocs.end());
+    pool = nullptr;
+  }
+  max_slots = int(want);
+  pool_size = size_t(max_slots) * stride;
+  pool = reinterpret_cast<uint8_t*>(dmalloc(pool_size));
+  used_slots = 0;
+  slot_key.assign(max_slots, -1);
+  slot_tick.assign(max_slots, 0);
+  key_slot.clear();
+  for (int l = 0; l < cfg.layers; ++l) {
+    LayerDev& ld = L[l];
+    ld.pool = pool;
+    ld.eg = expert_proj(pool, "gate_proj", cfg.moe_inter, cfg.hidden);
+    ld.eu = expert_proj(pool, "up_proj", cfg.moe_inter, cfg.hidden);
+    ld.ed = expert_proj(pool, "down_proj", cfg.hidden, cfg.moe_inter);
+    ld.eg.count = ld.eu.count = ld.ed.count = max_slots;
+  }
+}
+
+// Slots of layer l's router picks: hits refresh their slot, misses are read
+// from the layer file into pinned staging and copied to a slot on `st`.
+void Model::stream_resolve(int l, cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  SWL_CUDA(cudaStreamIsCapturing(st, &cs));
+  if (cs != cudaStreamCaptureStatusNone) throw Error(ERR_UNSUPPORTED, "a streaming model's steps cannot be captured");
+  const int K = cfg.topk;
+  SWL_CUDA(cudaMemcpyAsync(h_picks, pick_ids, size_t(K) * 4, cudaMemcpyDeviceToHost, st));
+  SWL_CUDA(cudaStreamSynchronize(st));  // also retires the previous layer's copies out of h_stage
+  ++tick;
+  std::set<int> held;  // this layer's slots: never evicted for another of its picks
+  for (int i = 0; i < K; ++i) {
+    const int e = h_picks[i];
+    if (e < 0 || e >= cfg.experts) throw Error(ERR_CUDA, "router produced an expert id out of range");
+    const int64_t key = (int64_t(l) << 32) | e;
+    ++key_freq[key];
+    auto it = key_slot.find(key);
+    int s;
+    if (it != key_slot.end()) {
+      ++hits;
+      s = it->second;
+    } else {
+      ++misses;
+      if (used_slots < max_slots) {
+        s = used_slots++;
+      } else {
+        s = -1;
+        for (int j = 0; j < used_slots && s < 0; ++j) if (slot_key[j] < 0) s = j;
+        if (s < 0) {
+          // least frequently used, then least recently used
+          int64_t bf = INT64_MAX, bt = INT64_MAX;
+          for (int j = 0; j < used_slots; ++j) {
+            if (held.count(j)) continue;
+            const int64_t f = key_freq[slot_key[j]], t = slot_tick[j];
+            if (f < bf || (f == bf && t < bt)) { bf = f; bt = t; s = j; }
+          }
+        }
+        if (s < 0) throw Error(ERR_CAPACITY, "expert pool too small for one layer's picks");
+        if (slot_key[s] >= 0) key_slot.erase(slot_key[s]);
+      }
+      uint8_t* stage = h_stage + size_t(i) * stride;
+      int64_t got = 0;
+      while (got < stride) {
+        const ssize_t r = pread(layer_fd[l], stage + got, size_t(stride - got), off_t(int64_t(e) * stride + got));
+        if (r <= 0) throw Error(ERR_IO, "short read of an expert blob (layer " + std::to_string(l) + ")");
+        got += r;
+      }
+      SWL_CUDA(cudaMemcpyAsync(pool + size_t(s) * stride, stage, size_t(stride), cudaMemcpyHostToDevice, st));
+      slot_key[s] = key;
+      key_slot[key] = s;
+    }
+    slot_tick[s] = tick;
+    held.insert(s);
+    h_picks[K + i] = s;
+  }
+  SWL_CUDA(cudaMemcpyAsync(d_pick_slots, h_picks + K, size_t(K) * 4, cudaMemcpyHostToDevice, st));
 }
 
 void Model::enqueue_body(cudaStream_t st) {
@@ -797,7 +938,7 @@ void Model::run(State* s, int n, bool amax) {
   else enqueue_head(stream, amax);
   s->pos += n;
   stepped = true;
-  hits += int64_t(n) * cfg.topk * cfg.layers;
+  if (!streaming) hits += int64_t(n) * cfg.topk * cfg.layers;
 }
 
 // ------------------------------------------------------- batched decode --
@@ -823,6 +964,7 @@ bool Model::batch_supported() {
   if (batch_ok >= 0) return batch_ok == 1;
   const ModelConfig& c = cfg;
   auto no = [&](const std::string& why) { batch_why = why; batch_ok = 0; return false; };
+  if (streaming) return no("experts stream from the container: sequences step one at a time");
   auto fits = [&](const QLin& q, int gs, int in) {
     BGLayout L;
     return q.bits && q.gs == gs && q.in == in && bgemm_layout(q.in, q.bits, q.dt, q.gs, L) && aligned16(q.w) &&
@@ -1687,8 +1829,8 @@ int swl_pool_stats(const swl_model* model, swl_pool_info* o) {
   if (!model || !o) throw Error(ERR_INVALID, "null argument");
   const Model& m = model->m;
   o->expert_stride = m.stride;
-  o->slot_count = int64_t(m.cfg.layers) * m.cfg.experts;
-  o->allocated_slots = o->slot_count;
+  o->slot_count = m.streaming ? m.max_slots : int64_t(m.cfg.layers) * m.cfg.experts;
+  o->allocated_slots = m.streaming ? m.used_slots : o->slot_count;
   o->hits = m.hits;
   o->misses = m.misses;
   o->resident_bytes = int64_t(m.pool_size);
@@ -1698,9 +1840,17 @@ int swl_pool_stats(const swl_model* model, swl_pool_info* o) {
 int swl_pool_resize(swl_model* model, double gb) {
   API_BEGIN
   if (!model) throw Error(ERR_INVALID, "null model");
-  if (gb > 0 && double(model->m.pool_size) > gb * 1073741824.0)
+  Model& m = model->m;
+  if (m.streaming) {
+    // QwenMetalModel.shrinkCache(toGB:): a fresh pool for the new budget
+    SWL_CUDA(cudaSetDevice(m.device));
+    m.stream_alloc(gb > 0 ? gb : double(int64_t(m.cfg.layers) * m.cfg.experts) * double(m.stride) / 1073741824.0);
+    return SWL_OK;
+  }
+  if (gb > 0 && double(m.pool_size) > gb * 1073741824.0)
     throw Error(ERR_CAPACITY, "the HBM-resident expert pool holds every expert; it cannot shrink below " +
-                                  std::to_string(double(model->m.pool_size) / 1073741824.0) + " GB");
+                                  std::to_string(double(m.pool_size) / 1073741824.0) + " GB (open a .qpack "
+                                  "container with a smaller budget to stream experts)");
   API_END
 }
 
@@ -1947,6 +2097,7 @@ int swl_bench_expert_sweep(swl_model* model, int32_t iters, float* ms_out, doubl
   if (!model || !ms_out || iters < 1) throw Error(ERR_INVALID, "bad argument");
   Model& m = model->m;
   if (!m.stepped) throw Error(ERR_INVALID, "run one step before the expert sweep");
+  if (m.streaming) throw Error(ERR_UNSUPPORTED, "the expert sweep needs every expert resident");
   SWL_CUDA(cudaSetDevice(m.device));
   // One sweep over every layer's expert pair (routing as the last step left
   // it), captured once as a graph so the timing is device time only.
