@@ -1112,7 +1112,10 @@ void Model::enqueue_batch(int T, int S, bool chunked, cudaStream_t st) {
       d.trace = tagged(16u * unsigned(l + 1) + 3);
       if (chunked) {
         d.seq_first = bb.seq_first; d.seq_n = bb.seq_n;
-        if (delta_wy_supported(c.dk, c.dv, c.nk, c.nv, c.conv_dim())) {
+        // the chunk-parallel form pays off once sequences bring many tokens
+        // each; packed launches of one or two tokens per sequence keep the
+        // token-by-token kernel
+        if (T >= 16 * S && delta_wy_supported(c.dk, c.dv, c.nk, c.nv, c.conv_dim())) {
           // chunk-parallel form: per-token inputs, then each sequence's tokens as one chunk
           WyArgs w;
           w.q = w.qw = bb.wy_q; w.k = w.kw = bb.wy_k; w.v = w.vw = bb.wy_v; w.lg = w.lgw = bb.wy_gb;

@@ -31,14 +31,18 @@ def test_streamed_pool_matches_resident_pool(container):
     small = swl.QwenCUDAModel(container, cache_budget_gb=budget)
     st_f, st_s = swl.DecodeState(64), swl.DecodeState(64)
     prompt = [1, 5, 9, 42, 7, 99, 3, 17, 64, 2]
+    # the resident model prefills through the batched kernels, the streaming
+    # one token by token (its routing goes to the host layer by layer): the
+    # logits agree to f32 reassociation, the greedy tokens exactly
     a = full.step(prompt, st_f)
     b = small.step(prompt, st_s)
-    assert np.array_equal(a, b)
+    assert np.abs(a - b).max() < 1e-4
     for _ in range(12):
         t = int(np.argmax(a))
+        assert t == int(np.argmax(b))
         a = full.step([t], st_f)
         b = small.step([t], st_s)
-        assert np.array_equal(a, b)
+        assert np.abs(a - b).max() < 1e-4
     s = small.expert_cache
     assert s.slot_count == 20 and s.allocated_slots <= 20
     assert s.misses > 20 and s.hits > 0          # evictions happened, some picks hit
@@ -48,5 +52,5 @@ def test_streamed_pool_matches_resident_pool(container):
     small.shrink_cache(16 * stride / 2**30)
     assert small.expert_cache.slot_count == 16
     t = int(np.argmax(a))
-    assert np.array_equal(full.step([t], st_f), small.step([t], st_s))
+    assert np.abs(full.step([t], st_f) - small.step([t], st_s)).max() < 1e-4
     assert total > 20
