@@ -57,7 +57,7 @@ constexpr int TG_KC = 256;               // codes per chunk
 constexpr int TG_A_BYTES = TG_ROWS * TG_KC;        // unpacked 8-bit tile: two 128-byte atoms of 128 rows
 constexpr int TG_P_BYTES = TG_ROWS * TG_KC / 2;    // packed 4-bit tile: one atom
 constexpr int TG_B_BYTES = TG_N * TG_KC;           // digit tile: two atoms of 48 rows
-constexpr int TG_XCHG = 64 * TG_TOK;               // SwiGLU: up-row sums handed to the gate rows
+constexpr int TG_XCHG = 64 * (TG_TOK + 1);         // SwiGLU: up-row sums handed to the gate rows (padded rows)
 
 struct TGemmMaps {
   CUtensorMap a[4];  // dense: segments; experts: routed gate (or down), routed up, shared gate (or down), shared up
@@ -72,7 +72,8 @@ struct TgLayout {
   static constexpr int A_OFF = S * P_SIZE;
   static constexpr int B_OFF = A_OFF + S * TG_A_BYTES;
   static constexpr int X_OFF = B_OFF + S * TG_B_BYTES;
-  static constexpr int BAR_OFF = X_OFF + TG_XCHG * 4;
+  static constexpr int M_OFF = X_OFF + TG_XCHG * 4;           // group metadata of two items [2][TG_TOK][32] float2
+  static constexpr int BAR_OFF = M_OFF + 2 * TG_TOK * 32 * 8;
   // full[S], unpacked[S], empty[S], tfull[2], tempty[2], drain, tmem address, abort flag, producer/mma step counts
   static constexpr int TOTAL = BAR_OFF + (3 * S + 5) * 8 + 16;
 };
@@ -352,19 +353,67 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
     }
   } else {
     // ---------------------------------------------------- epilogue ------
+    // Per item, each thread holds its weight row's scales and biases (bf16,
+    // up to 32 groups) in registers and the item's group metadata sits in a
+    // shared-memory slot; both are fetched for the next item while this one
+    // runs, so the per-chunk loop reads only TMEM, registers and shared memory.
     const int r = threadIdx.x;  // TMEM lane = tile row
     const uint32_t lane_base = tmem + (uint32_t(32 * warp) << 16);
-    const int sb = a.scale_f32 ? 4 : 2;
-    int j = 0;
-    for (int it = blockIdx.x; it < nit && !*abort_flag; it += gridDim.x) {
-      const TgItem d = tg_item(a, it);
+    const int ng = in / a.gs;   // groups per row (<= 32)
+    float2* meta_s = reinterpret_cast<float2*>(sm + Lay::M_OFF);  // [2][TG_TOK][32]
+    uint4 sc_cur[4], bi_cur[4], sc_nxt[4], bi_nxt[4];
+    auto fetch_rows = [&](const TgItem& d, uint4 (&sc)[4], uint4 (&bi)[4]) {
+      const bool swg = a.expert_mode && a.mode == BM_SWIGLU;
+      const bool upr = swg && r >= 64;
+      const int mrow = swg ? (r & 63) : r;
+      const bool ok = mrow < d.rows;
+      const uint4* sp = reinterpret_cast<const uint4*>((upr ? d.s2 : d.s) + int64_t(mrow) * d.srow);
+      const uint4* bp = reinterpret_cast<const uint4*>((upr ? d.b2 : d.b) + int64_t(mrow) * d.srow);
+      const int nq = (ng * 2 + 15) / 16;  // 16-byte pieces of a row
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        sc[q] = (ok && q < nq) ? __ldg(sp + q) : make_uint4(0, 0, 0, 0);
+        bi[q] = (ok && q < nq) ? __ldg(bp + q) : make_uint4(0, 0, 0, 0);
+      }
+    };
+    auto fetch_meta = [&](const TgItem& d, int slot) {
+      float2* dst = meta_s + slot * (TG_TOK * 32);
+      for (int i = r; i < d.nt * ng; i += 128) {
+        const int t = i / ng, g = i - t * ng;
+        dst[t * 32 + g] = __ldg(a.meta + int64_t(d.s0 + t) * a.meta_row + g);
+      }
+    };
+    auto bf = [](const uint4 (&v)[4], int g) -> float {
+      // selects, not an indexed load: the arrays stay in registers
+      const int qi = g >> 3, wi = (g >> 1) & 3;
+      const uint4 q = qi == 0 ? v[0] : qi == 1 ? v[1] : qi == 2 ? v[2] : v[3];
+      const uint32_t w = wi == 0 ? q.x : wi == 1 ? q.y : wi == 2 ? q.z : q.w;
+      return __uint_as_float((g & 1) ? (w & 0xFFFF0000u) : (w << 16));
+    };
+    int j = 0, nslot = 0;
+    int it = blockIdx.x;
+    TgItem d;
+    if (it < nit) {
+      d = tg_item(a, it);
+      fetch_rows(d, sc_cur, bi_cur);
+      fetch_meta(d, 0);
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    for (; it < nit && !*abort_flag; it += gridDim.x) {
       const bool swiglu = a.expert_mode && a.mode == BM_SWIGLU;
-      // this thread's weight row: SwiGLU rows 64..127 are up's rows
       const bool up = swiglu && r >= 64;
       const int mrow = swiglu ? (r & 63) : r;
       const bool valid = mrow < d.rows;
-      const uint8_t* sp = (up ? d.s2 : d.s) + int64_t(mrow) * d.srow;
-      const uint8_t* bp = (up ? d.b2 : d.b) + int64_t(mrow) * d.srow;
+      // the next item's descriptor, scales and metadata, in flight meanwhile
+      const int itn = it + gridDim.x;
+      TgItem dn = d;
+      if (itn < nit) {
+        dn = tg_item(a, itn);
+        fetch_rows(dn, sc_nxt, bi_nxt);
+        fetch_meta(dn, nslot ^ 1);
+      }
+      const float2* mcur = meta_s + nslot * (TG_TOK * 32);
+      const int nld = (3 * d.nt + 15) / 16;  // TMEM column groups of 16 that hold this item's tokens
       float acc_t[TG_TOK];
 #pragma unroll
       for (int t = 0; t < TG_TOK; ++t) acc_t[t] = 0.f;
@@ -372,16 +421,6 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
       for (int kc = 0; kc < nkc; ++kc, ++j) {
         const int acc = j & 1;
         const unsigned aph = (j >> 1) & 1;
-        float sc[4], bi[4];
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const int gi = kc * gpc + g;
-          const bool ok = valid && g < gpc;
-          sc[g] = ok ? (sb == 2 ? bf16_to_f32(__ldg(reinterpret_cast<const unsigned short*>(sp) + gi))
-                                : __ldg(reinterpret_cast<const float*>(sp) + gi)) : 0.f;
-          bi[g] = ok ? (sb == 2 ? bf16_to_f32(__ldg(reinterpret_cast<const unsigned short*>(bp) + gi))
-                                : __ldg(reinterpret_cast<const float*>(bp) + gi)) : 0.f;
-        }
         // warp-uniform outcome: the TMEM loads below are warp-collective
         if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], aph) ? 1 : 0)) { fail(); bad = true; break; }
         tg_fence_after();
@@ -391,23 +430,20 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
           uint32_t v0[16], v1[16], v2[16];
           const uint32_t col = lane_base + uint32_t(acc * gpc * TG_N + g * TG_N);
           tg_ld16(col, v0);
-          tg_ld16(col + 16, v1);
-          tg_ld16(col + 32, v2);
+          if (nld > 1) tg_ld16(col + 16, v1);
+          if (nld > 2) tg_ld16(col + 32, v2);
           tg_ld_wait();
-          const float2* mt = a.meta + int64_t(d.s0) * a.meta_row + kc * gpc + g;
+          const int gi = kc * gpc + g;
+          const float s_rg = bf(sc_cur, gi), b_rg = bf(bi_cur, gi);
 #pragma unroll
           for (int t = 0; t < TG_TOK; ++t) {
-            if (t < d.nt) {
-              // digit columns 3t, 3t + 1, 3t + 2 of this token
-              const int c0 = 3 * t;
-              auto pick = [&](int c) -> uint32_t {
-                return c < 16 ? v0[c] : (c < 32 ? v1[c - 16] : v2[c - 32]);
-              };
-              const float p0 = tg_i2f(pick(c0)), p1 = tg_i2f(pick(c0 + 1)), p2 = tg_i2f(pick(c0 + 2));
-              const float vv = p0 + (p1 + p2 * (1.f / 254.f)) * (1.f / 254.f);
-              const float2 m = __ldg(mt + int64_t(t) * a.meta_row);
-              acc_t[t] = fmaf(sc[g] * m.x, vv, fmaf(bi[g], m.y, acc_t[t]));
-            }
+            if (t >= d.nt) break;
+            const int c0 = 3 * t;
+            auto pick = [&](int c) -> uint32_t { return c < 16 ? v0[c] : (c < 32 ? v1[c - 16] : v2[c - 32]); };
+            const float p0 = tg_i2f(pick(c0)), p1 = tg_i2f(pick(c0 + 1)), p2 = tg_i2f(pick(c0 + 2));
+            const float vv = p0 + (p1 + p2 * (1.f / 254.f)) * (1.f / 254.f);
+            const float2 m = mcur[t * 32 + gi];
+            acc_t[t] = fmaf(s_rg * m.x, vv, fmaf(b_rg, m.y, acc_t[t]));
           }
         }
         tg_fence_before();
@@ -441,17 +477,22 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
         // up rows hand their sums to the gate rows through shared memory
         if (up)
 #pragma unroll
-          for (int t = 0; t < TG_TOK; ++t) xchg[(r - 64) * TG_TOK + t] = acc_t[t];
+          for (int t = 0; t < TG_TOK; ++t) xchg[(r - 64) * (TG_TOK + 1) + t] = acc_t[t];
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (!up && valid)
 #pragma unroll
           for (int t = 0; t < TG_TOK; ++t) {
             if (t >= d.nt) break;
-            const float g = acc_t[t], u = xchg[r * TG_TOK + t];
+            const float g = acc_t[t], u = xchg[r * (TG_TOK + 1) + t];
             a.out[int64_t(d.s0 + t) * a.out_stride + d.row0 + r] = (g / (1.f + expf(-g))) * u;
           }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
       }
+      // the next item's metadata slot is complete; this item's may be reused
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      d = dn;
+      nslot ^= 1;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) { sc_cur[q] = sc_nxt[q]; bi_cur[q] = bi_nxt[q]; }
     }
   }
   // ---- tear-down: nothing of this CTA may still be in flight ----
@@ -507,12 +548,16 @@ static bool tg_disabled() {
 }
 
 bool tgemm_supported(int in, int bits, int dt, int gs) {
-  return !tg_disabled() && (bits == 4 || bits == 8) && (dt == DT_BF16 || dt == DT_F32) && (gs == 64 || gs == 128) &&
-         in % TG_KC == 0 && in <= 16384;
+  return !tg_disabled() && (bits == 4 || bits == 8) && dt == DT_BF16 && (gs == 64 || gs == 128) && in % TG_KC == 0 &&
+         in / gs <= 32 && (in / gs) % 8 == 0;
 }
 
+// Weight rows whole 128-byte segments; scale and bias rows 16-byte pieces
+// at 16-byte aligned addresses (the epilogue reads them as such).
 static bool tg_mat_ok(const BMat& m, int in, int bits) {
-  return m.w && m.wrow == int64_t(in) * bits / 8 && m.wrow % 128 == 0;
+  auto al = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  return m.w && m.wrow == int64_t(in) * bits / 8 && m.wrow % 128 == 0 && al(m.s) && al(m.b) && m.srow % 16 == 0 &&
+         m.es % 16 == 0 && m.eb % 16 == 0;
 }
 
 bool launch_tgemm(const TGemmArgs& a, int bits, int grid, cudaStream_t st, bool pdl) {
