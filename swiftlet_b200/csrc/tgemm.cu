@@ -129,6 +129,18 @@ __device__ __forceinline__ uint32_t tg_prmt(uint32_t a, uint32_t b, uint32_t sel
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
   return r;
 }
+// Pipeline wait: polls without sleeping for the first ~4k tries (hand-offs
+// between the roles are short), then backs off; gives up after about 2 s.
+__device__ __forceinline__ bool tg_wait(uint64_t* b, unsigned parity) {
+  if (mbar_try(b, parity)) return true;
+  const unsigned long long t0 = gtimer();
+  for (int i = 0; i < (1 << 26); ++i) {
+    if (mbar_try(b, parity)) return true;
+    if (i >= 4096) __nanosleep(128);
+    if ((i & 255) == 0 && gtimer() - t0 > kWaitLimitNs) break;
+  }
+  return false;
+}
 // Exact float of an int32 partial sum (|v| < 2^22): magic-number conversion.
 __device__ __forceinline__ float tg_i2f(uint32_t v) {
   return __int_as_float(int(v) + 0x4B400000) - 12582912.f;
@@ -255,7 +267,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
         for (int kc = 0; kc < nkc; ++kc, ++j) {
           const int s = j % S;
           const unsigned ph = (j / S) & 1;
-          if (!mbar_wait(&empty[s], ph ^ 1)) { fail(); break; }
+          if (!tg_wait(&empty[s], ph ^ 1)) { fail(); break; }
           if (*abort_flag) break;
           uint8_t* A = sm + Lay::A_OFF + s * TG_A_BYTES;
           uint8_t* B = sm + Lay::B_OFF + s * TG_B_BYTES;
@@ -295,8 +307,8 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
         for (int kc = 0; kc < nkc; ++kc, ++j) {
           const int s = j % S, acc = j & 1;
           const unsigned ph = (j / S) & 1, aph = (j >> 1) & 1;
-          if (!mbar_wait(&full[s], ph) || (BITS == 4 && !mbar_wait(&unpacked[s], ph))) { fail(); break; }
-          if (!mbar_wait(&tempty[acc], aph ^ 1)) { fail(); break; }
+          if (!tg_wait(&full[s], ph) || (BITS == 4 && !tg_wait(&unpacked[s], ph))) { fail(); break; }
+          if (!tg_wait(&tempty[acc], aph ^ 1)) { fail(); break; }
           if (*abort_flag) break;
           tg_fence_after();
           const uint32_t A = smem_u32(sm + Lay::A_OFF + s * TG_A_BYTES);
@@ -314,7 +326,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
       }
       // every MMA issued above has completed once this commit arrives
       tg_commit(drain);
-      if (!mbar_wait(drain, 0)) fail();
+      if (!tg_wait(drain, 0)) fail();
     }
   } else if (warp >= 6) {
     // ---------------------------------------------------- 4-bit unpack --
@@ -325,12 +337,14 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
         for (int kc = 0; kc < nkc; ++kc, ++j) {
           const int s = j % S;
           const unsigned ph = (j / S) & 1;
-          if (!mbar_wait(&full[s], ph)) { fail(); break; }
+          if (!tg_wait(&full[s], ph)) { fail(); break; }
           const uint8_t* P = sm + Lay::P_OFF + s * TG_P_BYTES;
           uint8_t* A = sm + Lay::A_OFF + s * TG_A_BYTES;
           // unit u = (row, packed chunk c): 32 codes -> 32 bytes of atom c / 4
           for (int u = ut; u < TG_ROWS * 8; u += 64) {
-            const int r = u >> 3, c = u & 7, sw = r & 7;
+            // rows fastest: the eight lanes of a quarter-warp touch eight
+            // different swizzled 16-byte columns (no bank conflicts)
+            const int r = u & (TG_ROWS - 1), c = u >> 7, sw = r & 7;
             const uint4 w = *reinterpret_cast<const uint4*>(P + r * 128 + ((c ^ sw) << 4));
             uint32_t o[8];
             const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
@@ -422,7 +436,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
         const int acc = j & 1;
         const unsigned aph = (j >> 1) & 1;
         // warp-uniform outcome: the TMEM loads below are warp-collective
-        if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], aph) ? 1 : 0)) { fail(); bad = true; break; }
+        if (!__all_sync(0xffffffffu, tg_wait(&tfull[acc], aph) ? 1 : 0)) { fail(); bad = true; break; }
         tg_fence_after();
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
