@@ -675,7 +675,7 @@ __global__ void __launch_bounds__(BR_THREADS) k_broute(const BRouteArgs a) {
   __shared__ float wts[BT_MAX * 32];
   __shared__ float shs[BT_MAX];
   __shared__ unsigned long long msk[BR_MAXE];
-  __shared__ int off[BR_MAXE + 1], tb[BR_MAXE + 1];
+  __shared__ int off[BR_MAXE + 1], tb[BR_MAXE + 1], tb5[BR_MAXE + 1];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int T = a.T, E = a.E, K = a.K;
   const int e_lo = a.e_lo, e_hi = min(a.e_hi, E), sh_lo = min(a.sh_lo, T), sh_hi = min(a.sh_hi, T);
@@ -689,21 +689,23 @@ __global__ void __launch_bounds__(BR_THREADS) k_broute(const BRouteArgs a) {
   __syncthreads();
   if (warp == 0) {
     // exclusive scans of the counts (off) and of the token tiles (tb)
-    int run_c = 0, run_t = 0;
+    int run_c = 0, run_t = 0, run_5 = 0;
     for (int e0 = 0; e0 < E; e0 += 32) {
       const int e = e0 + lane;
-      const int c = e < E ? __popcll(msk[e]) : 0, tt = (c + BG_TOK - 1) / BG_TOK;
-      int ic = c, it = tt;
+      const int c = e < E ? __popcll(msk[e]) : 0, tt = (c + BG_TOK - 1) / BG_TOK, t5 = (c + 4) / 5;
+      int ic = c, it = tt, i5 = t5;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int vc = __shfl_up_sync(0xffffffffu, ic, o), vt = __shfl_up_sync(0xffffffffu, it, o);
-        if (lane >= o) { ic += vc; it += vt; }
+        const int v5 = __shfl_up_sync(0xffffffffu, i5, o);
+        if (lane >= o) { ic += vc; it += vt; i5 += v5; }
       }
-      if (e < E) { off[e] = run_c + ic - c; tb[e] = run_t + it - tt; }
+      if (e < E) { off[e] = run_c + ic - c; tb[e] = run_t + it - tt; tb5[e] = run_5 + i5 - t5; }
       run_c += __shfl_sync(0xffffffffu, ic, 31);
       run_t += __shfl_sync(0xffffffffu, it, 31);
+      run_5 += __shfl_sync(0xffffffffu, i5, 31);
     }
-    if (lane == 0) { off[E] = run_c; tb[E] = run_t; }
+    if (lane == 0) { off[E] = run_c; tb[E] = run_t; tb5[E] = run_5; }
   }
   __syncthreads();
   pdl_launch();
@@ -758,25 +760,39 @@ __global__ void __launch_bounds__(BR_THREADS) k_broute(const BRouteArgs a) {
     a.nitems[1] = min(base_dn + ntt_s * rbd, a.max_dn);
   }
   if (a.items_tgu) {
-    // the tensor-core GEMM's lists: 64 intermediate rows of gate and up, 128 hidden rows
+    // the tensor-core GEMM's lists: 64 intermediate rows of gate and up, 128
+    // hidden rows; tiles of at most 5 slots (its narrow N = 16 items)
+    constexpr int TT = 5;
+    auto routed5 = [&](int i, int rb_n, int rows) {
+      int lo = 0, hi = E;
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (tb5[mid] * rb_n <= i) lo = mid;
+        else hi = mid;
+      }
+      const int e = lo, c = __popcll(msk[e]), ntt = (c + TT - 1) / TT;
+      const int r = i - tb5[e] * rb_n, rb = r / ntt, tt = r - rb * ntt;
+      return make_int4(e, rb * rows, off[e] + tt * TT, min(TT, c - tt * TT));
+    };
     const int tg = (a.inter + 63) / 64, td = (a.hidden + 127) / 128, ts = (a.shared_inter + 63) / 64;
-    for (int i = tid; i < min(tb[E] * tg, a.max_tgu); i += BR_THREADS) a.items_tgu[i] = routed_item(i, tg, 64);
-    for (int i = tid; i < min(tb[E] * td, a.max_tdn); i += BR_THREADS) a.items_tdn[i] = routed_item(i, td, 128);
-    const int bg = tb[E] * tg, bd = tb[E] * td;
-    for (int i = tid; i < ntt_s * ts; i += BR_THREADS) {
-      const int rb = i / ntt_s, tt = i - rb * ntt_s;
+    const int nt5 = (nsh + TT - 1) / TT;
+    for (int i = tid; i < min(tb5[E] * tg, a.max_tgu); i += BR_THREADS) a.items_tgu[i] = routed5(i, tg, 64);
+    for (int i = tid; i < min(tb5[E] * td, a.max_tdn); i += BR_THREADS) a.items_tdn[i] = routed5(i, td, 128);
+    const int bg = tb5[E] * tg, bd = tb5[E] * td;
+    for (int i = tid; i < nt5 * ts; i += BR_THREADS) {
+      const int rb = i / nt5, tt = i - rb * nt5;
       if (bg + i < a.max_tgu)
-        a.items_tgu[bg + i] = make_int4(E, rb * 64, T * K + sh_lo + tt * BG_TOK, min(BG_TOK, nsh - tt * BG_TOK));
+        a.items_tgu[bg + i] = make_int4(E, rb * 64, T * K + sh_lo + tt * TT, min(TT, nsh - tt * TT));
     }
-    for (int i = tid; i < ntt_s * td; i += BR_THREADS) {
-      const int rb = i / ntt_s, tt = i - rb * ntt_s;
+    for (int i = tid; i < nt5 * td; i += BR_THREADS) {
+      const int rb = i / nt5, tt = i - rb * nt5;
       if (bd + i < a.max_tdn)
-        a.items_tdn[bd + i] = make_int4(E, rb * 128, T * K + sh_lo + tt * BG_TOK, min(BG_TOK, nsh - tt * BG_TOK));
+        a.items_tdn[bd + i] = make_int4(E, rb * 128, T * K + sh_lo + tt * TT, min(TT, nsh - tt * TT));
     }
     for (int sl = off[E] + tid; sl < T * K; sl += BR_THREADS) a.slot_tok[sl] = 0;
     if (tid == 0) {
-      a.ntitems[0] = min(bg + ntt_s * ts, a.max_tgu);
-      a.ntitems[1] = min(bd + ntt_s * td, a.max_tdn);
+      a.ntitems[0] = min(bg + nt5 * ts, a.max_tgu);
+      a.ntitems[1] = min(bd + nt5 * td, a.max_tdn);
     }
   }
 }

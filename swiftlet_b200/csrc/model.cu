@@ -1026,8 +1026,10 @@ void Model::ensure_batch() {
   bb.max_dn = tiles * ((D + 63) / 64);
   bb.items_gu = reinterpret_cast<int4*>(dmalloc(size_t(bb.max_gu) * sizeof(int4)));
   bb.items_dn = reinterpret_cast<int4*>(dmalloc(size_t(bb.max_dn) * sizeof(int4)));
-  bb.max_tgu = tiles * ((std::max(c.moe_inter, c.shared_inter) + 63) / 64);
-  bb.max_tdn = tiles * ((D + 127) / 128);
+  // tensor-core lists: tiles of at most 5 slots
+  const int tiles5 = std::min(c.experts, T * K) + (T * K) / 5 + 1 + (T + 4) / 5;
+  bb.max_tgu = tiles5 * ((std::max(c.moe_inter, c.shared_inter) + 63) / 64);
+  bb.max_tdn = tiles5 * ((D + 127) / 128);
   bb.items_tgu = reinterpret_cast<int4*>(dmalloc(size_t(bb.max_tgu) * sizeof(int4)));
   bb.items_tdn = reinterpret_cast<int4*>(dmalloc(size_t(bb.max_tdn) * sizeof(int4)));
   bb.ntitems = i4(2);

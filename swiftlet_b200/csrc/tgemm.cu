@@ -51,31 +51,44 @@ namespace swl {
 
 constexpr int TG_THREADS = 256;
 constexpr int TG_ROWS = 128;             // MMA M
-constexpr int TG_TOK = 16;               // tokens (slots) per item
-constexpr int TG_N = 3 * TG_TOK;         // MMA N: three digit columns per token
 constexpr int TG_KC = 256;               // codes per chunk
 constexpr int TG_A_BYTES = TG_ROWS * TG_KC;        // unpacked 8-bit tile: two 128-byte atoms of 128 rows
 constexpr int TG_P_BYTES = TG_ROWS * TG_KC / 2;    // packed 4-bit tile: one atom
-constexpr int TG_B_BYTES = TG_N * TG_KC;           // digit tile: two atoms of 48 rows
-constexpr int TG_XCHG = 64 * (TG_TOK + 1);         // SwiGLU: up-row sums handed to the gate rows (padded rows)
+constexpr int TG_DENSE_TOK = 16;                   // tokens per dense item (N = 48)
+constexpr int TG_EXPERT_TOK = 5;                   // slots per expert item (N = 16)
+
+// Item width: N digit columns (three per token or slot); expert items are
+// narrow (a routed expert sees a few tokens per step), so their MMAs, digit
+// tiles and accumulators are a third the size and four accumulator sets fit.
+template <int TN>
+struct TgShape {
+  static constexpr int N = TN;
+  static constexpr int TOK = TN / 3;                 // 16 -> 5, 48 -> 16
+  static constexpr int NACC = TN == 16 ? 4 : 2;      // accumulator sets in TMEM
+  static constexpr int B_BYTES = TN * TG_KC;         // digit tile: two atoms of N rows
+  static constexpr int XCHG = 64 * (TOK + 1);        // SwiGLU: up-row sums handed to the gate rows (padded rows)
+  // kind::i8, D s32, A u8 (weight codes), B s8 (digits), both K-major, M 128
+  static constexpr uint32_t IDESC = (2u << 4) | (0u << 7) | (1u << 10) | (uint32_t(TN >> 3) << 17) | (uint32_t(TG_ROWS >> 4) << 24);
+};
 
 struct TGemmMaps {
   CUtensorMap a[4];  // dense: segments; experts: routed gate (or down), routed up, shared gate (or down), shared up
   CUtensorMap b;     // digit matrix [rows][in] s8 as {128 B, rows, in / 128}
 };
 
-template <int BITS>
+template <int BITS, int TN>
 struct TgLayout {
-  static constexpr int S = BITS == 4 ? 3 : 4;  // stages
+  using Sh = TgShape<TN>;
+  static constexpr int S = BITS == 4 ? (TN == 16 ? 4 : 3) : (TN == 16 ? 5 : 4);  // stages
   static constexpr int P_OFF = 0;
   static constexpr int P_SIZE = BITS == 4 ? TG_P_BYTES : 0;
   static constexpr int A_OFF = S * P_SIZE;
   static constexpr int B_OFF = A_OFF + S * TG_A_BYTES;
-  static constexpr int X_OFF = B_OFF + S * TG_B_BYTES;
-  static constexpr int M_OFF = X_OFF + TG_XCHG * 4;           // group metadata of two items [2][TG_TOK][32] float2
-  static constexpr int BAR_OFF = M_OFF + 2 * TG_TOK * 32 * 8;
-  // full[S], unpacked[S], empty[S], tfull[2], tempty[2], drain, tmem address, abort flag, producer/mma step counts
-  static constexpr int TOTAL = BAR_OFF + (3 * S + 5) * 8 + 16;
+  static constexpr int X_OFF = B_OFF + S * Sh::B_BYTES;
+  static constexpr int M_OFF = X_OFF + Sh::XCHG * 4;          // group metadata of two items [2][TOK][32] float2
+  static constexpr int BAR_OFF = M_OFF + 2 * Sh::TOK * 32 * 8;
+  // full[S], unpacked[S], empty[S], tfull[NACC], tempty[NACC], drain, tmem address, abort flag, step count
+  static constexpr int TOTAL = BAR_OFF + (3 * S + 2 * Sh::NACC + 1) * 8 + 16;
 };
 
 // ---- tcgen05 / TMA primitives --------------------------------------------
@@ -85,14 +98,11 @@ __device__ __forceinline__ uint64_t tg_desc(uint32_t saddr) {
   return uint64_t((saddr >> 4) & 0x3FFFu) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) | (uint64_t(1) << 46) |
          (uint64_t(2) << 61);
 }
-// kind::i8, D s32, A u8 (weight codes), B s8 (digits), both K-major, M 128, N 48
-constexpr uint32_t kTgIdesc = (2u << 4) | (0u << 7) | (1u << 10) | (uint32_t(TG_N >> 3) << 17) | (uint32_t(TG_ROWS >> 4) << 24);
-
-__device__ __forceinline__ void tg_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, bool accumulate) {
+__device__ __forceinline__ void tg_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, bool accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(kTgIdesc), "r"(uint32_t(accumulate))
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(uint32_t(accumulate))
       : "memory");
 }
 __device__ __forceinline__ void tg_commit(uint64_t* bar) {
@@ -163,7 +173,7 @@ struct TgItem {
 __device__ __forceinline__ TgItem tg_item(const TGemmArgs& a, int it) {
   TgItem d;
   if (!a.expert_mode) {
-    const int ntt = (a.ntok + TG_TOK - 1) / TG_TOK;
+    const int ntt = (a.ntok + TG_DENSE_TOK - 1) / TG_DENSE_TOK;
     const int rb = it / ntt, tt = it - rb * ntt;
     int sg = 0;
     while (sg + 1 < a.nseg && rb >= a.seg_rb[sg + 1]) ++sg;
@@ -172,8 +182,8 @@ __device__ __forceinline__ TgItem tg_item(const TGemmArgs& a, int it) {
     d.expert = -1;
     d.row0 = (rb - a.seg_rb[sg]) * TG_ROWS;
     d.rows = min(TG_ROWS, m.rows - d.row0);
-    d.s0 = tt * TG_TOK;
-    d.nt = min(TG_TOK, a.ntok - d.s0);
+    d.s0 = tt * TG_DENSE_TOK;
+    d.nt = min(TG_DENSE_TOK, a.ntok - d.s0);
     d.srow = m.srow;
     d.s = m.s + d.row0 * m.srow;
     d.b = m.b + d.row0 * m.srow;
@@ -204,22 +214,23 @@ __device__ __forceinline__ TgItem tg_item(const TGemmArgs& a, int it) {
 }
 
 __device__ __forceinline__ int tg_nitems(const TGemmArgs& a) {
-  if (!a.expert_mode) return a.seg_rb[a.nseg] * ((a.ntok + TG_TOK - 1) / TG_TOK);
+  if (!a.expert_mode) return a.seg_rb[a.nseg] * ((a.ntok + TG_DENSE_TOK - 1) / TG_DENSE_TOK);
   return min(*a.nitems, a.max_items);
 }
 
-template <int BITS>
+template <int BITS, int TN>
 __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, const __grid_constant__ TGemmMaps M) {
-  using Lay = TgLayout<BITS>;
-  constexpr int S = Lay::S;
+  using Lay = TgLayout<BITS, TN>;
+  using Sh = TgShape<TN>;
+  constexpr int S = Lay::S, NACC = Sh::NACC, TOK = Sh::TOK, TG_N = Sh::N;
   extern __shared__ __align__(1024) uint8_t tg_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tg_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + Lay::BAR_OFF);
   uint64_t* unpacked = full + S;
   uint64_t* empty = unpacked + S;
   uint64_t* tfull = empty + S;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
+  uint64_t* tempty = tfull + NACC;
+  uint64_t* drain = tempty + NACC;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* issued_ctr = const_cast<int*>(abort_flag) + 1;
@@ -233,7 +244,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
       mbar_init(&unpacked[s], 64);
       mbar_init(&empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < NACC; ++i) {
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], 128);
     }
@@ -270,10 +281,10 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
           if (!tg_wait(&empty[s], ph ^ 1)) { fail(); break; }
           if (*abort_flag) break;
           uint8_t* A = sm + Lay::A_OFF + s * TG_A_BYTES;
-          uint8_t* B = sm + Lay::B_OFF + s * TG_B_BYTES;
+          uint8_t* B = sm + Lay::B_OFF + s * Sh::B_BYTES;
           const bool two = a.expert_mode && a.mode == BM_SWIGLU;  // gate rows 0-63, up rows 64-127
           const unsigned abytes = BITS == 4 ? TG_P_BYTES : TG_A_BYTES;
-          mbar_expect_tx(&full[s], abytes + TG_B_BYTES);
+          mbar_expect_tx(&full[s], abytes + Sh::B_BYTES);
           const int nseg_k = BITS == 4 ? 1 : 2;  // 128-byte K segments of weights per chunk
           for (int q = 0; q < nseg_k; ++q) {
             uint8_t* dst = BITS == 4 ? sm + Lay::P_OFF + s * TG_P_BYTES : A + q * (TG_ROWS * 128);
@@ -305,19 +316,19 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
       int j = 0;
       for (int it = blockIdx.x; it < nit && !*abort_flag; it += gridDim.x) {
         for (int kc = 0; kc < nkc; ++kc, ++j) {
-          const int s = j % S, acc = j & 1;
-          const unsigned ph = (j / S) & 1, aph = (j >> 1) & 1;
+          const int s = j % S, acc = j % NACC;
+          const unsigned ph = (j / S) & 1, aph = (j / NACC) & 1;
           if (!tg_wait(&full[s], ph) || (BITS == 4 && !tg_wait(&unpacked[s], ph))) { fail(); break; }
           if (!tg_wait(&tempty[acc], aph ^ 1)) { fail(); break; }
           if (*abort_flag) break;
           tg_fence_after();
           const uint32_t A = smem_u32(sm + Lay::A_OFF + s * TG_A_BYTES);
-          const uint32_t B = smem_u32(sm + Lay::B_OFF + s * TG_B_BYTES);
+          const uint32_t B = smem_u32(sm + Lay::B_OFF + s * Sh::B_BYTES);
           for (int g = 0; g < gpc; ++g)
             for (int kk = 0; kk < kpg; ++kk) {
               const int koff = g * a.gs + kk * 32, atom = koff >> 7, off = koff & 127;
               tg_mma(tmem + uint32_t(acc * gpc * TG_N + g * TG_N), tg_desc(A + atom * (TG_ROWS * 128) + off),
-                     tg_desc(B + atom * (TG_N * 128) + off), kk > 0);
+                     tg_desc(B + atom * (TG_N * 128) + off), Sh::IDESC, kk > 0);
             }
           tg_commit(&empty[s]);
           tg_commit(&tfull[acc]);
@@ -374,7 +385,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
     const int r = threadIdx.x;  // TMEM lane = tile row
     const uint32_t lane_base = tmem + (uint32_t(32 * warp) << 16);
     const int ng = in / a.gs;   // groups per row (<= 32)
-    float2* meta_s = reinterpret_cast<float2*>(sm + Lay::M_OFF);  // [2][TG_TOK][32]
+    float2* meta_s = reinterpret_cast<float2*>(sm + Lay::M_OFF);  // [2][TOK][32]
     uint4 sc_cur[4], bi_cur[4], sc_nxt[4], bi_nxt[4];
     auto fetch_rows = [&](const TgItem& d, uint4 (&sc)[4], uint4 (&bi)[4]) {
       const bool swg = a.expert_mode && a.mode == BM_SWIGLU;
@@ -391,7 +402,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
       }
     };
     auto fetch_meta = [&](const TgItem& d, int slot) {
-      float2* dst = meta_s + slot * (TG_TOK * 32);
+      float2* dst = meta_s + slot * (TOK * 32);
       for (int i = r; i < d.nt * ng; i += 128) {
         const int t = i / ng, g = i - t * ng;
         dst[t * 32 + g] = __ldg(a.meta + int64_t(d.s0 + t) * a.meta_row + g);
@@ -426,31 +437,44 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
         fetch_rows(dn, sc_nxt, bi_nxt);
         fetch_meta(dn, nslot ^ 1);
       }
-      const float2* mcur = meta_s + nslot * (TG_TOK * 32);
+      const float2* mcur = meta_s + nslot * (TOK * 32);
       const int nld = (3 * d.nt + 15) / 16;  // TMEM column groups of 16 that hold this item's tokens
-      float acc_t[TG_TOK];
+      float acc_t[TOK];
 #pragma unroll
-      for (int t = 0; t < TG_TOK; ++t) acc_t[t] = 0.f;
+      for (int t = 0; t < TOK; ++t) acc_t[t] = 0.f;
       bool bad = false;
       for (int kc = 0; kc < nkc; ++kc, ++j) {
-        const int acc = j & 1;
-        const unsigned aph = (j >> 1) & 1;
+        const int acc = j % NACC;
+        const unsigned aph = (j / NACC) & 1;
         // warp-uniform outcome: the TMEM loads below are warp-collective
         if (!__all_sync(0xffffffffu, tg_wait(&tfull[acc], aph) ? 1 : 0)) { fail(); bad = true; break; }
         tg_fence_after();
+        // narrow items: every group's 16 columns in flight before one wait
+        uint32_t w4[4][16];
+        if constexpr (TN == 16) {
+#pragma unroll
+          for (int g = 0; g < 4; ++g)
+            if (g < gpc) tg_ld16(lane_base + uint32_t(acc * gpc * TG_N + g * TG_N), w4[g]);
+          tg_ld_wait();
+        }
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
           if (g >= gpc) break;
           uint32_t v0[16], v1[16], v2[16];
-          const uint32_t col = lane_base + uint32_t(acc * gpc * TG_N + g * TG_N);
-          tg_ld16(col, v0);
-          if (nld > 1) tg_ld16(col + 16, v1);
-          if (nld > 2) tg_ld16(col + 32, v2);
-          tg_ld_wait();
+          if constexpr (TN == 16) {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) v0[q] = w4[g][q];
+          } else {
+            const uint32_t col = lane_base + uint32_t(acc * gpc * TG_N + g * TG_N);
+            tg_ld16(col, v0);
+            if (nld > 1) tg_ld16(col + 16, v1);
+            if (nld > 2) tg_ld16(col + 32, v2);
+            tg_ld_wait();
+          }
           const int gi = kc * gpc + g;
           const float s_rg = bf(sc_cur, gi), b_rg = bf(bi_cur, gi);
 #pragma unroll
-          for (int t = 0; t < TG_TOK; ++t) {
+          for (int t = 0; t < TOK; ++t) {
             if (t >= d.nt) break;
             const int c0 = 3 * t;
             auto pick = [&](int c) -> uint32_t { return c < 16 ? v0[c] : (c < 32 ? v1[c - 16] : v2[c - 32]); };
@@ -474,7 +498,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
         float* y = a.y[d.mat];
         if (valid)
 #pragma unroll
-          for (int t = 0; t < TG_TOK; ++t) {
+          for (int t = 0; t < TOK; ++t) {
             if (t >= d.nt) break;
             float* o = y + int64_t(d.s0 + t) * a.y_stride + d.row0 + r;
             if (a.mode == BM_RESIDUAL) *o += acc_t[t];
@@ -483,7 +507,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
       } else if (!swiglu) {
         if (valid)
 #pragma unroll
-          for (int t = 0; t < TG_TOK; ++t) {
+          for (int t = 0; t < TOK; ++t) {
             if (t >= d.nt) break;
             a.out[int64_t(d.s0 + t) * a.out_stride + d.row0 + r] = acc_t[t];
           }
@@ -491,13 +515,13 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
         // up rows hand their sums to the gate rows through shared memory
         if (up)
 #pragma unroll
-          for (int t = 0; t < TG_TOK; ++t) xchg[(r - 64) * (TG_TOK + 1) + t] = acc_t[t];
+          for (int t = 0; t < TOK; ++t) xchg[(r - 64) * (TOK + 1) + t] = acc_t[t];
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (!up && valid)
 #pragma unroll
-          for (int t = 0; t < TG_TOK; ++t) {
+          for (int t = 0; t < TOK; ++t) {
             if (t >= d.nt) break;
-            const float g = acc_t[t], u = xchg[r * (TG_TOK + 1) + t];
+            const float g = acc_t[t], u = xchg[r * (TOK + 1) + t];
             a.out[int64_t(d.s0 + t) * a.out_stride + d.row0 + r] = (g / (1.f + expf(-g))) * u;
           }
       }
@@ -598,10 +622,16 @@ bool launch_tgemm(const TGemmArgs& a, int bits, int grid, cudaStream_t st, bool 
         return false;
     }
   }
-  if (!tg_map(&M.b, a.dg, a.dg_rows, a.in, TG_N, 0, 0)) return false;
-  const size_t smem = size_t(bits == 4 ? TgLayout<4>::TOTAL : TgLayout<8>::TOTAL) + 1024;
-  if (bits == 4) launch(k_tgemm<4>, dim3(grid), dim3(TG_THREADS), smem, st, pdl, a, M);
-  else launch(k_tgemm<8>, dim3(grid), dim3(TG_THREADS), smem, st, pdl, a, M);
+  // expert items: at most TG_EXPERT_TOK slots (N = 16); dense items: 16 tokens (N = 48)
+  const int tn = a.expert_mode ? 16 : 48;
+  if (!tg_map(&M.b, a.dg, a.dg_rows, a.in, tn, 0, 0)) return false;
+  if (a.expert_mode) {
+    if (bits == 4) launch(k_tgemm<4, 16>, dim3(grid), dim3(TG_THREADS), size_t(TgLayout<4, 16>::TOTAL) + 1024, st, pdl, a, M);
+    else launch(k_tgemm<8, 16>, dim3(grid), dim3(TG_THREADS), size_t(TgLayout<8, 16>::TOTAL) + 1024, st, pdl, a, M);
+  } else {
+    if (bits == 4) launch(k_tgemm<4, 48>, dim3(grid), dim3(TG_THREADS), size_t(TgLayout<4, 48>::TOTAL) + 1024, st, pdl, a, M);
+    else launch(k_tgemm<8, 48>, dim3(grid), dim3(TG_THREADS), size_t(TgLayout<8, 48>::TOTAL) + 1024, st, pdl, a, M);
+  }
   path_note("tgemm");
   return true;
 }
