@@ -55,7 +55,6 @@ constexpr int TG_KC = 256;               // codes per chunk
 constexpr int TG_A_BYTES = TG_ROWS * TG_KC;        // unpacked 8-bit tile: two 128-byte atoms of 128 rows
 constexpr int TG_P_BYTES = TG_ROWS * TG_KC / 2;    // packed 4-bit tile: one atom
 constexpr int TG_DENSE_TOK = 16;                   // tokens per dense item (N = 48)
-constexpr int TG_EXPERT_TOK = 5;                   // slots per expert item (N = 16)
 
 // Item width: N digit columns (three per token or slot); expert items are
 // narrow (a routed expert sees a few tokens per step), so their MMAs, digit
