@@ -18,7 +18,7 @@
 // epilogue can apply the per-(row, group) scales. Two accumulator sets
 // alternate, so the MMAs of chunk j + 1 run while the epilogue reads chunk j.
 //
-// Warp roles of a CTA (256 threads, one CTA per SM, persistent over items
+// Warp roles of a CTA (320 threads, one CTA per SM, persistent over items
 // c, c + grid, ...):
 //   warps 0-3  epilogue: warp w reads TMEM lanes 32w..32w+31 (one weight row
 //              per thread), accumulates each token in registers and writes
@@ -29,7 +29,7 @@
 //              stages, completion on one mbarrier per stage;
 //   warp 5     TMEM allocation and MMA issue (one thread), tcgen05.commit to
 //              free a stage and to publish an accumulator set;
-//   warps 6-7  4-bit weights only: unpack the packed tile into the 8-bit,
+//   warps 6-9  4-bit weights only: unpack the packed tile into the 8-bit,
 //              128-byte swizzled K-major layout the MMA reads (two LOP3 and
 //              two PRMT per 8 codes), then fence the writes to the async
 //              proxy.
@@ -42,6 +42,7 @@
 
 #include <algorithm>
 #include <mutex>
+#include <type_traits>
 
 #include "imma_impl.cuh"
 #include "kernels.h"
@@ -49,7 +50,8 @@
 
 namespace swl {
 
-constexpr int TG_THREADS = 256;
+constexpr int TG_THREADS = 320;   // 4 epilogue, producer, MMA, 4 unpack warps
+constexpr int TG_UNPACK = 128;    // unpack threads (warps 6-9)
 constexpr int TG_ROWS = 128;             // MMA M
 constexpr int TG_KC = 256;               // codes per chunk
 constexpr int TG_A_BYTES = TG_ROWS * TG_KC;        // unpacked 8-bit tile: two 128-byte atoms of 128 rows
@@ -240,7 +242,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&unpacked[s], 64);
+      mbar_init(&unpacked[s], TG_UNPACK);
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < NACC; ++i) {
@@ -345,7 +347,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
   } else if (warp >= 6) {
     // ---------------------------------------------------- 4-bit unpack --
     if constexpr (BITS == 4) {
-      const int ut = threadIdx.x - 192;  // 0..63
+      const int ut = threadIdx.x - 192;  // 0 .. TG_UNPACK - 1
       int j = 0;
       for (int it = blockIdx.x; it < nit && !*abort_flag; it += gridDim.x) {
         for (int kc = 0; kc < nkc; ++kc, ++j) {
@@ -355,8 +357,8 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
           const uint8_t* P = sm + Lay::P_OFF + s * TG_P_BYTES;
           uint8_t* A = sm + Lay::A_OFF + s * TG_A_BYTES;
           // unit u = (row, packed chunk c): 32 codes -> 32 bytes of atom c / 4
-#pragma unroll 4
-          for (int u = ut; u < TG_ROWS * 8; u += 64) {
+#pragma unroll 2
+          for (int u = ut; u < TG_ROWS * 8; u += TG_UNPACK) {
             // rows fastest: the eight lanes of a quarter-warp touch eight
             // different swizzled 16-byte columns (no bank conflicts)
             const int r = u & (TG_ROWS - 1), c = u >> 7, sw = r & 7;
@@ -478,15 +480,24 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
           const int gi = kc * gpc + g;
           const float s_rg = bf(sc_cur, gi), b_rg = bf(bi_cur, gi);
           if constexpr (TN == 16) {
-            // every token slot, branch-free (slots past the item's get zero
-            // weight): independent chains across tokens
+            // the item's token slots, unrolled for each count (independent
+            // chains across tokens, no work for empty slots)
+            auto tok = [&](auto NT) {
 #pragma unroll
-            for (int t = 0; t < TOK; ++t) {
-              const float2 m = t < d.nt ? mcur[t * 32 + gi] : make_float2(0.f, 0.f);
-              // v = P0 + P1 / 254 + P2 / 254^2 as (254 P0 + P1 + P2 / 254) / 254
-              const int q = int(v0[3 * t]) * 254 + int(v0[3 * t + 1]);
-              const float vv = fmaf(float(int(v0[3 * t + 2])), 1.f / 254.f, float(q));
-              acc_t[t] = fmaf(s_rg * m.x * (1.f / 254.f), vv, fmaf(b_rg, m.y, acc_t[t]));
+              for (int t = 0; t < decltype(NT)::value; ++t) {
+                const float2 m = mcur[t * 32 + gi];
+                // v = P0 + P1 / 254 + P2 / 254^2 as (254 P0 + P1 + P2 / 254) / 254
+                const int q = int(v0[3 * t]) * 254 + int(v0[3 * t + 1]);
+                const float vv = fmaf(float(int(v0[3 * t + 2])), 1.f / 254.f, float(q));
+                acc_t[t] = fmaf(s_rg * m.x * (1.f / 254.f), vv, fmaf(b_rg, m.y, acc_t[t]));
+              }
+            };
+            switch (d.nt) {
+              case 1: tok(std::integral_constant<int, 1>{}); break;
+              case 2: tok(std::integral_constant<int, 2>{}); break;
+              case 3: tok(std::integral_constant<int, 3>{}); break;
+              case 4: tok(std::integral_constant<int, 4>{}); break;
+              default: tok(std::integral_constant<int, 5>{}); break;
             }
           } else {
 #pragma unroll
