@@ -18,7 +18,7 @@
 // epilogue can apply the per-(row, group) scales. Two accumulator sets
 // alternate, so the MMAs of chunk j + 1 run while the epilogue reads chunk j.
 //
-// Warp roles of a CTA (320 threads, one CTA per SM, persistent over items
+// Warp roles of a CTA (256 threads, one CTA per SM, persistent over items
 // c, c + grid, ...):
 //   warps 0-3  epilogue: warp w reads TMEM lanes 32w..32w+31 (one weight row
 //              per thread), accumulates each token in registers and writes
@@ -29,7 +29,7 @@
 //              stages, completion on one mbarrier per stage;
 //   warp 5     TMEM allocation and MMA issue (one thread), tcgen05.commit to
 //              free a stage and to publish an accumulator set;
-//   warps 6-9  4-bit weights only: unpack the packed tile into the 8-bit,
+//   warps 6-7  4-bit weights only: unpack the packed tile into the 8-bit,
 //              128-byte swizzled K-major layout the MMA reads (two LOP3 and
 //              two PRMT per 8 codes), then fence the writes to the async
 //              proxy.
@@ -42,7 +42,6 @@
 
 #include <algorithm>
 #include <mutex>
-#include <type_traits>
 
 #include "imma_impl.cuh"
 #include "kernels.h"
@@ -50,8 +49,7 @@
 
 namespace swl {
 
-constexpr int TG_THREADS = 320;   // 4 epilogue, producer, MMA, 4 unpack warps
-constexpr int TG_UNPACK = 128;    // unpack threads (warps 6-9)
+constexpr int TG_THREADS = 256;
 constexpr int TG_ROWS = 128;             // MMA M
 constexpr int TG_KC = 256;               // codes per chunk
 constexpr int TG_A_BYTES = TG_ROWS * TG_KC;        // unpacked 8-bit tile: two 128-byte atoms of 128 rows
@@ -242,7 +240,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&unpacked[s], TG_UNPACK);
+      mbar_init(&unpacked[s], 64);
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < NACC; ++i) {
@@ -323,18 +321,14 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
           if (!tg_wait(&tempty[acc], aph ^ 1)) { fail(); break; }
           if (*abort_flag) break;
           tg_fence_after();
-          // descriptors of the stage's tiles; a K step adds its byte offset
-          // (>> 4) to the start-address field
-          const uint64_t ad = tg_desc(smem_u32(sm + Lay::A_OFF + s * TG_A_BYTES));
-          const uint64_t bd = tg_desc(smem_u32(sm + Lay::B_OFF + s * Sh::B_BYTES));
-          const uint32_t dacc = tmem + uint32_t(acc * gpc * TG_N);
-#pragma unroll
-          for (int i = 0; i < TG_KC / 32; ++i) {  // eight K = 32 steps: group i / kpg
-            const int atom = i >> 2, off = (i & 3) * 32;
-            const int g = i / kpg;
-            tg_mma(dacc + uint32_t(g * TG_N), ad + uint64_t((atom * (TG_ROWS * 128) + off) >> 4),
-                   bd + uint64_t((atom * (TG_N * 128) + off) >> 4), Sh::IDESC, (i % kpg) != 0);
-          }
+          const uint32_t A = smem_u32(sm + Lay::A_OFF + s * TG_A_BYTES);
+          const uint32_t B = smem_u32(sm + Lay::B_OFF + s * Sh::B_BYTES);
+          for (int g = 0; g < gpc; ++g)
+            for (int kk = 0; kk < kpg; ++kk) {
+              const int koff = g * a.gs + kk * 32, atom = koff >> 7, off = koff & 127;
+              tg_mma(tmem + uint32_t(acc * gpc * TG_N + g * TG_N), tg_desc(A + atom * (TG_ROWS * 128) + off),
+                     tg_desc(B + atom * (TG_N * 128) + off), Sh::IDESC, kk > 0);
+            }
           tg_commit(&empty[s]);
           tg_commit(&tfull[acc]);
         }
@@ -347,7 +341,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
   } else if (warp >= 6) {
     // ---------------------------------------------------- 4-bit unpack --
     if constexpr (BITS == 4) {
-      const int ut = threadIdx.x - 192;  // 0 .. TG_UNPACK - 1
+      const int ut = threadIdx.x - 192;  // 0..63
       int j = 0;
       for (int it = blockIdx.x; it < nit && !*abort_flag; it += gridDim.x) {
         for (int kc = 0; kc < nkc; ++kc, ++j) {
@@ -357,8 +351,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
           const uint8_t* P = sm + Lay::P_OFF + s * TG_P_BYTES;
           uint8_t* A = sm + Lay::A_OFF + s * TG_A_BYTES;
           // unit u = (row, packed chunk c): 32 codes -> 32 bytes of atom c / 4
-#pragma unroll 2
-          for (int u = ut; u < TG_ROWS * 8; u += TG_UNPACK) {
+          for (int u = ut; u < TG_ROWS * 8; u += 64) {
             // rows fastest: the eight lanes of a quarter-warp touch eight
             // different swizzled 16-byte columns (no bank conflicts)
             const int r = u & (TG_ROWS - 1), c = u >> 7, sw = r & 7;
@@ -479,37 +472,15 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
           }
           const int gi = kc * gpc + g;
           const float s_rg = bf(sc_cur, gi), b_rg = bf(bi_cur, gi);
-          if constexpr (TN == 16) {
-            // the item's token slots, unrolled for each count (independent
-            // chains across tokens, no work for empty slots)
-            auto tok = [&](auto NT) {
 #pragma unroll
-              for (int t = 0; t < decltype(NT)::value; ++t) {
-                const float2 m = mcur[t * 32 + gi];
-                // v = P0 + P1 / 254 + P2 / 254^2 as (254 P0 + P1 + P2 / 254) / 254
-                const int q = int(v0[3 * t]) * 254 + int(v0[3 * t + 1]);
-                const float vv = fmaf(float(int(v0[3 * t + 2])), 1.f / 254.f, float(q));
-                acc_t[t] = fmaf(s_rg * m.x * (1.f / 254.f), vv, fmaf(b_rg, m.y, acc_t[t]));
-              }
-            };
-            switch (d.nt) {
-              case 1: tok(std::integral_constant<int, 1>{}); break;
-              case 2: tok(std::integral_constant<int, 2>{}); break;
-              case 3: tok(std::integral_constant<int, 3>{}); break;
-              case 4: tok(std::integral_constant<int, 4>{}); break;
-              default: tok(std::integral_constant<int, 5>{}); break;
-            }
-          } else {
-#pragma unroll
-            for (int t = 0; t < TOK; ++t) {
-              if (t >= d.nt) break;
-              const int c0 = 3 * t;
-              auto pick = [&](int c) -> uint32_t { return c < 16 ? v0[c] : (c < 32 ? v1[c - 16] : v2[c - 32]); };
-              const float p0 = tg_i2f(pick(c0)), p1 = tg_i2f(pick(c0 + 1)), p2 = tg_i2f(pick(c0 + 2));
-              const float vv = p0 + (p1 + p2 * (1.f / 254.f)) * (1.f / 254.f);
-              const float2 m = mcur[t * 32 + gi];
-              acc_t[t] = fmaf(s_rg * m.x, vv, fmaf(b_rg, m.y, acc_t[t]));
-            }
+          for (int t = 0; t < TOK; ++t) {
+            if (t >= d.nt) break;
+            const int c0 = 3 * t;
+            auto pick = [&](int c) -> uint32_t { return c < 16 ? v0[c] : (c < 32 ? v1[c - 16] : v2[c - 32]); };
+            const float p0 = tg_i2f(pick(c0)), p1 = tg_i2f(pick(c0 + 1)), p2 = tg_i2f(pick(c0 + 2));
+            const float vv = p0 + (p1 + p2 * (1.f / 254.f)) * (1.f / 254.f);
+            const float2 m = mcur[t * 32 + gi];
+            acc_t[t] = fmaf(s_rg * m.x, vv, fmaf(b_rg, m.y, acc_t[t]));
           }
         }
         tg_fence_before();
