@@ -321,14 +321,18 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
           if (!tg_wait(&tempty[acc], aph ^ 1)) { fail(); break; }
           if (*abort_flag) break;
           tg_fence_after();
-          const uint32_t A = smem_u32(sm + Lay::A_OFF + s * TG_A_BYTES);
-          const uint32_t B = smem_u32(sm + Lay::B_OFF + s * Sh::B_BYTES);
-          for (int g = 0; g < gpc; ++g)
-            for (int kk = 0; kk < kpg; ++kk) {
-              const int koff = g * a.gs + kk * 32, atom = koff >> 7, off = koff & 127;
-              tg_mma(tmem + uint32_t(acc * gpc * TG_N + g * TG_N), tg_desc(A + atom * (TG_ROWS * 128) + off),
-                     tg_desc(B + atom * (TG_N * 128) + off), Sh::IDESC, kk > 0);
-            }
+          // descriptors of the stage's tiles; a K step adds its byte offset
+          // (>> 4) to the start-address field
+          const uint64_t ad = tg_desc(smem_u32(sm + Lay::A_OFF + s * TG_A_BYTES));
+          const uint64_t bd = tg_desc(smem_u32(sm + Lay::B_OFF + s * Sh::B_BYTES));
+          const uint32_t dacc = tmem + uint32_t(acc * gpc * TG_N);
+#pragma unroll
+          for (int i = 0; i < TG_KC / 32; ++i) {  // eight K = 32 steps: group i / kpg
+            const int atom = i >> 2, off = (i & 3) * 32;
+            const int g = i / kpg;
+            tg_mma(dacc + uint32_t(g * TG_N), ad + uint64_t((atom * (TG_ROWS * 128) + off) >> 4),
+                   bd + uint64_t((atom * (TG_N * 128) + off) >> 4), Sh::IDESC, (i % kpg) != 0);
+          }
           tg_commit(&empty[s]);
           tg_commit(&tfull[acc]);
         }
@@ -351,6 +355,7 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
           const uint8_t* P = sm + Lay::P_OFF + s * TG_P_BYTES;
           uint8_t* A = sm + Lay::A_OFF + s * TG_A_BYTES;
           // unit u = (row, packed chunk c): 32 codes -> 32 bytes of atom c / 4
+#pragma unroll 4
           for (int u = ut; u < TG_ROWS * 8; u += 64) {
             // rows fastest: the eight lanes of a quarter-warp touch eight
             // different swizzled 16-byte columns (no bank conflicts)
@@ -472,15 +477,28 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
           }
           const int gi = kc * gpc + g;
           const float s_rg = bf(sc_cur, gi), b_rg = bf(bi_cur, gi);
+          if constexpr (TN == 16) {
+            // every token slot, branch-free (slots past the item's get zero
+            // weight): independent chains across tokens
 #pragma unroll
-          for (int t = 0; t < TOK; ++t) {
-            if (t >= d.nt) break;
-            const int c0 = 3 * t;
-            auto pick = [&](int c) -> uint32_t { return c < 16 ? v0[c] : (c < 32 ? v1[c - 16] : v2[c - 32]); };
-            const float p0 = tg_i2f(pick(c0)), p1 = tg_i2f(pick(c0 + 1)), p2 = tg_i2f(pick(c0 + 2));
-            const float vv = p0 + (p1 + p2 * (1.f / 254.f)) * (1.f / 254.f);
-            const float2 m = mcur[t * 32 + gi];
-            acc_t[t] = fmaf(s_rg * m.x, vv, fmaf(b_rg, m.y, acc_t[t]));
+            for (int t = 0; t < TOK; ++t) {
+              const float2 m = t < d.nt ? mcur[t * 32 + gi] : make_float2(0.f, 0.f);
+              // v = P0 + P1 / 254 + P2 / 254^2 as (254 P0 + P1 + P2 / 254) / 254
+              const int q = int(v0[3 * t]) * 254 + int(v0[3 * t + 1]);
+              const float vv = fmaf(float(int(v0[3 * t + 2])), 1.f / 254.f, float(q));
+              acc_t[t] = fmaf(s_rg * m.x * (1.f / 254.f), vv, fmaf(b_rg, m.y, acc_t[t]));
+            }
+          } else {
+#pragma unroll
+            for (int t = 0; t < TOK; ++t) {
+              if (t >= d.nt) break;
+              const int c0 = 3 * t;
+              auto pick = [&](int c) -> uint32_t { return c < 16 ? v0[c] : (c < 32 ? v1[c - 16] : v2[c - 32]); };
+              const float p0 = tg_i2f(pick(c0)), p1 = tg_i2f(pick(c0 + 1)), p2 = tg_i2f(pick(c0 + 2));
+              const float vv = p0 + (p1 + p2 * (1.f / 254.f)) * (1.f / 254.f);
+              const float2 m = mcur[t * 32 + gi];
+              acc_t[t] = fmaf(s_rg * m.x, vv, fmaf(b_rg, m.y, acc_t[t]));
+            }
           }
         }
         tg_fence_before();
