@@ -361,6 +361,17 @@ def deltanet_sweeps(model, cfg, states) -> dict:
                  "achieved": byts * iters * 8 / (ms / 1000.0) / 1e9, "peak": hbm,
                  "frac": byts * iters * 8 / (ms / 1000.0) / 1e9 / hbm, "unit": "GB/s", "peak_kind": peak_kind}
     st.free()
+    # chunked-parallel prompt recurrence: one sequence of 4096 tokens
+    import swiftlet_b200 as swl
+    T = 4096
+    ms, fl = swl.bench_gated_delta(T, cfg.linear_num_key_heads, cfg.linear_num_value_heads,
+                                   cfg.linear_key_head_dim, cfg.linear_value_head_dim, 10)
+    tf = fl / (ms / 1000.0) / 1e12
+    out["prefill_4096"] = {"us_per_layer": ms * 100.0, "tflops": tf,
+                           "tok_s_per_layer": T * 10 / (ms / 1000.0),
+                           "kernel": "k_delta_wy (64-token chunks, f32 CUDA cores)",
+                           "of_bf16_peak": tf / (float(peaks["bf16_tflops"])),
+                           "flops": "per chunk and value head 2 x (2 C^2 dk + 2 C dk dv + 2 C^2 dv + C dk dv), C = 64"}
     out["note"] = ("graph of the decode recurrence (conv, norms, gating, delta rule) over all %d DeltaNet layers, "
                    "timed with CUDA events; state [%d, %d, %d] f32 per sequence and layer"
                    % (sum(1 for i in range(cfg.num_hidden_layers) if cfg.is_linear_layer(i)),

@@ -301,6 +301,13 @@ int swl_kernel_expert_swiglu(const uint32_t* gate_w, const void* gate_s, const v
 int swl_kernel_gated_delta(const float* q, const float* k, const float* v, const float* g, const float* beta,
                            float* state, float* y, int32_t T, int32_t Hk, int32_t Hv, int32_t Dk, int32_t Dv);
 
+/* Timing of that chunked prompt kernel on device-resident inputs of T tokens
+ * (a fixed input pattern shaped like the prompt path's), `iters` launches
+ * timed with CUDA events; flops_out = the chunked algorithm's multiply-add
+ * work x 2 over all launches. */
+int swl_bench_gated_delta(int32_t T, int32_t Hk, int32_t Hv, int32_t Dk, int32_t Dv, int32_t iters, float* ms_out,
+                          double* flops_out);
+
 /* ---- allocation-free entry point (no counterpart in the reference) ----- */
 
 /* A device-resident MLX-affine matrix: uint32 words packed low bits first,

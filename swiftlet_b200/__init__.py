@@ -98,6 +98,7 @@ _SIGNATURES = {
     "swl_debug_kernel_path": (_I, [_P, C.c_char_p, C.c_int32]),
     "swl_state_reset": (_I, [_P]),
     "swl_kernel_gated_delta": (_I, [_P] * 7 + [C.c_int32] * 5),
+    "swl_bench_gated_delta": (_I, [C.c_int32] * 6 + [C.POINTER(C.c_float), C.POINTER(C.c_double)]),
     "swl_bench_moe_sweep": (_I, [_P, C.c_int32, C.c_int32, C.POINTER(C.c_float), C.POINTER(C.c_double),
                                  C.POINTER(C.c_int32), C.POINTER(C.c_int32)]),
     "swl_bench_delta_sweep": (_I, [_P, C.c_int32, C.c_int32, C.POINTER(C.c_float), C.POINTER(C.c_double),
@@ -490,6 +491,13 @@ def gated_delta(q, k, v, g, beta, state, T, Hk, Hv, Dk, Dv):
     y = np.zeros(T * Hv * Dv, np.float32)
     _check(lib().swl_kernel_gated_delta(*[_ptr(a) for a in arrs], _ptr(st), _ptr(y), T, Hk, Hv, Dk, Dv))
     return y, st
+
+
+def bench_gated_delta(T, Hk, Hv, Dk, Dv, iters):
+    """(ms, flops) of `iters` launches of the chunked prompt delta-rule kernel over T tokens."""
+    ms, fl = C.c_float(), C.c_double()
+    _check(lib().swl_bench_gated_delta(T, Hk, Hv, Dk, Dv, iters, C.byref(ms), C.byref(fl)))
+    return ms.value, fl.value
 
 
 def verify_container(container: str, hashes_json: str | None = None, delete_corrupt: bool = False) -> dict:

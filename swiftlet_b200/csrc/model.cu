@@ -2358,6 +2358,64 @@ int swl_kernel_gated_delta(const float* q, const float* k, const float* v, const
   API_END
 }
 
+int swl_bench_gated_delta(int32_t T, int32_t Hk, int32_t Hv, int32_t Dk, int32_t Dv, int32_t iters, float* ms_out,
+                          double* flops_out) {
+  API_BEGIN
+  if (!ms_out || T < 1 || iters < 1 || Hk < 1 || Hv % Hk || !delta_wy_supported(Dk, Dv, Hk, Hv, 0))
+    throw Error(ERR_INVALID, "bad argument");
+  std::vector<void*> bufs;
+  auto dm = [&](size_t n) { void* p = nullptr; SWL_CUDA(cudaMalloc(&p, std::max<size_t>(n, 16))); bufs.push_back(p); return p; };
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  try {
+    // inputs as the prompt path forms them, from a fixed pattern: unit keys,
+    // queries of norm 1 / sqrt(dk), log-decays around -0.7, beta 0.5
+    const size_t nq = size_t(T) * Hk * Dk, nvv = size_t(T) * Hv * Dv, ns = size_t(Hv) * Dv * Dk;
+    std::vector<float> hq(nq), hk(nq), hv(nvv), hg(size_t(T) * 2 * Hv);
+    uint64_t x = 0x9E3779B97F4A7C15ull;
+    auto rnd = [&]() { x ^= x << 13; x ^= x >> 7; x ^= x << 17; return float((x >> 40) & 0xFFFFFF) / 16777216.f - 0.5f; };
+    for (size_t r = 0; r < size_t(T) * Hk; ++r) {
+      double a = 0, b = 0;
+      for (int i = 0; i < Dk; ++i) { hq[r * Dk + i] = rnd(); hk[r * Dk + i] = rnd(); a += hq[r * Dk + i] * hq[r * Dk + i]; b += hk[r * Dk + i] * hk[r * Dk + i]; }
+      for (int i = 0; i < Dk; ++i) { hq[r * Dk + i] /= float(std::sqrt(a * Dk)); hk[r * Dk + i] /= float(std::sqrt(b)); }
+    }
+    for (auto& v : hv) v = rnd();
+    for (size_t i = 0; i < size_t(T) * Hv; ++i) { hg[2 * i] = -0.7f + 0.5f * rnd(); hg[2 * i + 1] = 0.5f + 0.5f * rnd(); }
+    float* dq = (float*)dm(nq * 4); float* dk = (float*)dm(nq * 4); float* dv = (float*)dm(nvv * 4);
+    float* dgb = (float*)dm(hg.size() * 4); float* dst = (float*)dm(ns * 4); float* dy = (float*)dm(nvv * 4);
+    SWL_CUDA(cudaMemcpy(dq, hq.data(), nq * 4, cudaMemcpyHostToDevice));
+    SWL_CUDA(cudaMemcpy(dk, hk.data(), nq * 4, cudaMemcpyHostToDevice));
+    SWL_CUDA(cudaMemcpy(dv, hv.data(), nvv * 4, cudaMemcpyHostToDevice));
+    SWL_CUDA(cudaMemcpy(dgb, hg.data(), hg.size() * 4, cudaMemcpyHostToDevice));
+    SWL_CUDA(cudaMemset(dst, 0, ns * 4));
+    WyArgs w;
+    w.q = dq; w.k = dk; w.v = dv; w.lg = dgb;
+    w.q_stride = w.k_stride = int64_t(Hk) * Dk; w.v_stride = int64_t(Hv) * Dv; w.gb_stride = 2 * Hv;
+    w.nk = Hk; w.nv = Hv; w.dk = Dk; w.dv = Dv; w.state = dst; w.ntok = T; w.y = dy; w.y_stride = int64_t(Hv) * Dv;
+    SWL_CUDA(cudaEventCreate(&e0));
+    SWL_CUDA(cudaEventCreate(&e1));
+    launch_delta_wy(w, 1, 0, false);  // warm-up
+    SWL_CUDA(cudaEventRecord(e0, 0));
+    for (int i = 0; i < iters; ++i) launch_delta_wy(w, 1, 0, false);
+    SWL_CUDA(cudaEventRecord(e1, 0));
+    SWL_CUDA(cudaEventSynchronize(e1));
+    SWL_CUDA(cudaEventElapsedTime(ms_out, e0, e1));
+    // per 64-token chunk and value head (C = 64): C^2 dk (K K^T, Q K^T) x 2
+    // + 2 C dk dv (S_0 k, S_0 q) + C^2 dv (solve) + C^2 dv (y) + C dk dv (state),
+    // two flops per multiply-add
+    const double C = 64, chunks = std::ceil(double(T) / C);
+    if (flops_out)
+      *flops_out = 2.0 * chunks * Hv * (2 * C * C * Dk + 2 * C * Dk * Dv + 2 * C * C * Dv + C * Dk * Dv) * iters;
+  } catch (...) {
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    for (void* p : bufs) cudaFree(p);
+    throw;
+  }
+  cudaEventDestroy(e0); cudaEventDestroy(e1);
+  for (void* p : bufs) cudaFree(p);
+  API_END
+}
+
 int swl_sample_device(const float* d_logits, int32_t nseq, int32_t vocab, int64_t row_stride,
                       const swl_sample_options* opt, const int32_t* d_suppress, int32_t n_suppress,
                       const int32_t* d_eos, int32_t n_eos, const int32_t* d_ban_eos, int32_t* d_counts,
