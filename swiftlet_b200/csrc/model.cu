@@ -108,6 +108,9 @@ struct BatchBufs {
   // chunked-parallel delta rule of prompt launches: per token normalised q,
   // k, v and (log g, beta)
   float *wy_q = nullptr, *wy_k = nullptr, *wy_v = nullptr, *wy_gb = nullptr;
+  // tensor-core dense GEMMs (lm_head): digit matrix and metadata of the T rows
+  int8_t* dg_dense = nullptr;
+  float2* tmeta_dense = nullptr;
   uint2 *bt_a = nullptr, *bt_b = nullptr;
   float2 *meta_a = nullptr, *meta_b = nullptr;
   StateDev* sds = nullptr;
@@ -1040,6 +1043,8 @@ void Model::ensure_batch() {
     bb.tmeta_x = reinterpret_cast<float2*>(dmalloc(size_t(slots) * (D / 32 + 1) * sizeof(float2)));
     bb.tmeta_mid = reinterpret_cast<float2*>(dmalloc(size_t(slots) * (mi / 32 + 1) * sizeof(float2)));
   }
+  bb.dg_dense = reinterpret_cast<int8_t*>(dmalloc(size_t(T) * 3 * max_in));
+  bb.tmeta_dense = reinterpret_cast<float2*>(dmalloc(size_t(T) * (max_in / 32 + 1) * sizeof(float2)));
   if (c.nv > 0) {
     bb.wy_q = f(size_t(T) * c.key_dim()); bb.wy_k = f(size_t(T) * c.key_dim());
     bb.wy_v = f(size_t(T) * c.value_dim()); bb.wy_gb = f(size_t(T) * 2 * c.nv);
@@ -1156,8 +1161,27 @@ void Model::enqueue_batch(int T, int S, bool chunked, cudaStream_t st) {
     enqueue_batch_moe(l, T, chunked, st);
   }
   launch_badvance(bb.sds, S, chunked ? bb.seq_n : nullptr, st, pdl);
-  digit(bb.h, D, T, D, lm_head.gs, PRO_RMSNORM, final_norm, nullptr, 0, nullptr, bb.bt_a, bb.meta_a);
-  bdense({{lm_head, bb.logits}}, c.vocab, BM_STORE, bb.bt_a, bb.meta_a, T, st);
+  bool head_tc = false;
+  if (tgemm_supported(D, lm_head.bits, lm_head.dt, lm_head.gs)) {
+    // lm_head on the tensor cores: final norm into the digit matrix, then
+    // 128-row items x 16-token tiles
+    DigitArgs dd;
+    dd.x = bb.h; dd.x_stride = D; dd.rows = T; dd.in = D; dd.gs = lm_head.gs; dd.prologue = PRO_RMSNORM;
+    dd.aux = final_norm; dd.eps = float(c.eps); dd.meta = bb.tmeta_dense; dd.meta_row = D / lm_head.gs;
+    TGemmArgs hg;
+    hg.mode = BM_STORE; hg.in = D; hg.gs = lm_head.gs;
+    hg.seg[0] = bmat(lm_head); hg.y[0] = bb.logits; hg.nseg = 1;
+    hg.seg_rb[0] = 0; hg.seg_rb[1] = (c.vocab + 127) / 128;
+    hg.y_stride = c.vocab; hg.ntok = T;
+    hg.dg = bb.dg_dense; hg.dg_rows = int64_t(3) * T; hg.meta = bb.tmeta_dense; hg.meta_row = D / lm_head.gs;
+    hg.status = kstatus;
+    launch_tdigit(dd, nullptr, bb.dg_dense, st, pdl);
+    head_tc = launch_tgemm(hg, lm_head.bits, sm_count(), st, pdl);
+  }
+  if (!head_tc) {
+    digit(bb.h, D, T, D, lm_head.gs, PRO_RMSNORM, final_norm, nullptr, 0, nullptr, bb.bt_a, bb.meta_a);
+    bdense({{lm_head, bb.logits}}, c.vocab, BM_STORE, bb.bt_a, bb.meta_a, T, st);
+  }
   launch_bargmax(bb.logits, T, c.vocab, bb.greedy, st, pdl);
 }
 
