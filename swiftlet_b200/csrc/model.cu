@@ -1211,12 +1211,24 @@ void Model::enqueue_batch_moe(int l, int T, bool chunked, cudaStream_t st) {
   uint2* bt_own = bb.bt_a + own * bt_row;
   float2* meta_own = bb.meta_a + own * meta_row;
   float* rlog_own = bb.rlog + int64_t(own) * (E + 1);
-  digit(bb.h, D, T, D, gs_r, PRO_RMSNORM, ld.post_norm, nullptr, 0, bb.xmoe, bt_own, meta_own);
+  const int gs_d = ld.ed.lin.gs, I = c.moe_inter;
+  // the tensor-core grouped GEMMs take the experts when their formats allow
+  const bool tc = tgemm_supported(D, ld.eg.lin.bits, ld.eg.lin.dt, gs_r) && ld.eg.lin.gs == gs_r &&
+                  tgemm_supported(I, ld.ed.lin.bits, ld.ed.lin.dt, gs_d) && c.shared_inter == I &&
+                  ld.sh_g.bits == ld.eg.lin.bits && ld.sh_g.dt == ld.eg.lin.dt && ld.sh_g.gs == gs_r &&
+                  ld.sh_d.gs == gs_d && ld.ed.lin.bits == ld.eg.lin.bits;
+  digit(bb.h, D, T, D, gs_r, PRO_RMSNORM, ld.post_norm, nullptr, 0, bb.xmoe + int64_t(own) * D, bt_own, meta_own);
   bdense({{ld.router, rlog_own}, {ld.sgate, rlog_own + E}}, E + 1, BM_STORE, bt_own, meta_own, T, st);
   if (ep_on) {
+    // every rank's MoE inputs (the normalised rows for the tensor-core
+    // experts, or their digit tables for the mma.sync ones) and router logits
     ep_group_start(ep);
-    ep_allgather(ep, bb.bt_a, size_t(T) * bt_row * sizeof(uint2), st);
-    ep_allgather(ep, bb.meta_a, size_t(T) * meta_row * sizeof(float2), st);
+    if (tc) {
+      ep_allgather(ep, bb.xmoe, size_t(T) * D * sizeof(float), st);
+    } else {
+      ep_allgather(ep, bb.bt_a, size_t(T) * bt_row * sizeof(uint2), st);
+      ep_allgather(ep, bb.meta_a, size_t(T) * meta_row * sizeof(float2), st);
+    }
     ep_allgather(ep, bb.rlog, size_t(T) * (E + 1) * sizeof(float), st);
     ep_group_end(ep);
   }
@@ -1228,14 +1240,6 @@ void Model::enqueue_batch_moe(int l, int T, bool chunked, cudaStream_t st) {
   r.ids = bb.ids; r.w = bb.w; r.sh = bb.sh; r.slot_of = bb.slot_of; r.slot_tok = bb.slot_tok;
   r.items_gu = bb.items_gu; r.items_dn = bb.items_dn; r.nitems = bb.nitems;
   r.inter = c.moe_inter; r.shared_inter = c.shared_inter; r.hidden = D; r.max_gu = bb.max_gu; r.max_dn = bb.max_dn;
-  const int gs_d = ld.ed.lin.gs, I = c.moe_inter;
-  // the tensor-core grouped GEMMs take the experts when their formats allow
-  // (expert-parallel steps exchange digits, not the MoE input rows the
-  // tensor-core layout is made from: they keep the mma.sync GEMMs)
-  const bool tc = !ep_on && tgemm_supported(D, ld.eg.lin.bits, ld.eg.lin.dt, gs_r) && ld.eg.lin.gs == gs_r &&
-                  tgemm_supported(I, ld.ed.lin.bits, ld.ed.lin.dt, gs_d) && c.shared_inter == I &&
-                  ld.sh_g.bits == ld.eg.lin.bits && ld.sh_g.dt == ld.eg.lin.dt && ld.sh_g.gs == gs_r &&
-                  ld.sh_d.gs == gs_d && ld.ed.lin.bits == ld.eg.lin.bits;
   if (tc) {
     r.items_tgu = bb.items_tgu; r.items_tdn = bb.items_tdn; r.ntitems = bb.ntitems;
     r.max_tgu = bb.max_tgu; r.max_tdn = bb.max_tdn;
