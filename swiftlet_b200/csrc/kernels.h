@@ -327,8 +327,10 @@ bool tgemm_supported(int in, int bits, int dt, int gs);
 bool launch_tgemm(const TGemmArgs& a, int bits, int grid, cudaStream_t stream, bool pdl);
 // Digits of `rows` rows in the tensor-core layout: row i reads source row
 // in_map[i] (or i) of a.x, applies a.prologue, and writes dg[(3i + d) * in + k]
-// and a.meta[i * a.meta_row + g]; a.bt is unused.
-void launch_tdigit(const DigitArgs& a, const int* in_map, int8_t* dg, cudaStream_t stream, bool pdl);
+// and a.meta[i * a.meta_row + g]; a.bt is unused. For 4-bit weights (bits 4)
+// the values of each block of 8 are stored in the order 0, 2, 4, 6, 1, 3, 5, 7,
+// the order the GEMM's unpack leaves the weight codes in.
+void launch_tdigit(const DigitArgs& a, const int* in_map, int8_t* dg, int bits, cudaStream_t stream, bool pdl);
 
 // Routing and grouping of a batch: per token the softmax top-k of the router
 // logits (QwenCPUModel.swift:506-521), then picks sorted by expert into

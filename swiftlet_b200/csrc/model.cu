@@ -1175,7 +1175,7 @@ void Model::enqueue_batch(int T, int S, bool chunked, cudaStream_t st) {
     hg.y_stride = c.vocab; hg.ntok = T;
     hg.dg = bb.dg_dense; hg.dg_rows = int64_t(3) * T; hg.meta = bb.tmeta_dense; hg.meta_row = D / lm_head.gs;
     hg.status = kstatus;
-    launch_tdigit(dd, nullptr, bb.dg_dense, st, pdl);
+    launch_tdigit(dd, nullptr, bb.dg_dense, lm_head.bits, st, pdl);
     head_tc = launch_tgemm(hg, lm_head.bits, sm_count(), st, pdl);
   }
   if (!head_tc) {
@@ -1250,7 +1250,7 @@ void Model::enqueue_batch_moe(int l, int T, bool chunked, cudaStream_t st) {
     DigitArgs dx;
     dx.x = bb.xmoe; dx.x_stride = D; dx.rows = slots; dx.in = D; dx.gs = gs_r; dx.prologue = PRO_COPY;
     dx.meta = bb.tmeta_x; dx.meta_row = D / gs_r;
-    launch_tdigit(dx, bb.slot_tok, bb.dg_x, st, pdl);
+    launch_tdigit(dx, bb.slot_tok, bb.dg_x, bits, st, pdl);
     TGemmArgs gu;
     gu.mode = BM_SWIGLU; gu.in = D; gu.gs = gs_r; gu.scale_f32 = ld.eg.lin.dt == DT_F32;
     gu.expert_mode = 1; gu.eg = bmat(ld.eg); gu.eu = bmat(ld.eu); gu.sg = bmat(ld.sh_g); gu.su = bmat(ld.sh_u);
@@ -1262,7 +1262,7 @@ void Model::enqueue_batch_moe(int l, int T, bool chunked, cudaStream_t st) {
     DigitArgs dm;
     dm.x = bb.hmid; dm.x_stride = bb.hmid_stride; dm.rows = slots; dm.in = I; dm.gs = gs_d; dm.prologue = PRO_COPY;
     dm.meta = bb.tmeta_mid; dm.meta_row = I / gs_d;
-    if (ok_gu) launch_tdigit(dm, nullptr, bb.dg_mid, st, pdl);
+    if (ok_gu) launch_tdigit(dm, nullptr, bb.dg_mid, ld.ed.lin.bits, st, pdl);
     TGemmArgs dn;
     dn.mode = BM_STORE; dn.in = I; dn.gs = gs_d; dn.scale_f32 = ld.ed.lin.dt == DT_F32;
     dn.expert_mode = 1; dn.eg = bmat(ld.ed); dn.sg = bmat(ld.sh_d);

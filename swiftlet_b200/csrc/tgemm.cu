@@ -365,9 +365,10 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
             const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-              const uint32_t lo = wv[q] & 0x0F0F0F0Fu, hi = (wv[q] >> 4) & 0x0F0F0F0Fu;
-              o[2 * q] = tg_prmt(lo, hi, 0x5140);
-              o[2 * q + 1] = tg_prmt(lo, hi, 0x7362);
+              // codes 0, 2, 4, 6 of the word, then 1, 3, 5, 7: the digit
+              // matrix of 4-bit launches holds its values in that order
+              o[2 * q] = wv[q] & 0x0F0F0F0Fu;
+              o[2 * q + 1] = (wv[q] >> 4) & 0x0F0F0F0Fu;
             }
             uint8_t* atom = A + (c >> 2) * (TG_ROWS * 128) + r * 128;
             const int ch = 2 * (c & 3);
@@ -659,7 +660,7 @@ bool launch_tgemm(const TGemmArgs& a, int bits, int grid, cudaStream_t st, bool 
 // scale 127 / max|x| and the three base-254 digits of every value in natural
 // order: digit d of value k at dg[(3 i + d) * in + k]; meta[i][g] = (1 / scale,
 // sum of the group).
-__global__ void __launch_bounds__(256) k_tdigit(const DigitArgs a, const int* in_map, int8_t* dg) {
+__global__ void __launch_bounds__(256) k_tdigit(const DigitArgs a, const int* in_map, int8_t* dg, int perm4) {
   extern __shared__ __align__(16) float xs[];
   __shared__ float red[64];
   pdl_wait();
@@ -709,12 +710,24 @@ __global__ void __launch_bounds__(256) k_tdigit(const DigitArgs a, const int* in
     }
     float inv, rs;
     digit_scale(m, inv, rs);
+    uint32_t b[3] = {0u, 0u, 0u};
+    put_digits(v.x * inv, 0, b);
+    put_digits(v.y * inv, 1, b);
+    put_digits(v.z * inv, 2, b);
+    put_digits(v.w * inv, 3, b);
+    if (perm4) {
+      // 4-bit weights: within each block of 8 values the order is
+      // 0, 2, 4, 6, 1, 3, 5, 7 (the tensor-core unpack's nibble order); the
+      // thread of values 0-3 writes the first word, its neighbour the second
+      const bool first = (tid & 1) == 0;
+#pragma unroll
+      for (int dd = 0; dd < 3; ++dd) {
+        const uint32_t other = __shfl_xor_sync(0xffffffffu, b[dd], 1);
+        const uint32_t lo = first ? b[dd] : other, hi = first ? other : b[dd];  // values 0-3 | 4-7
+        b[dd] = first ? __byte_perm(lo, hi, 0x6420) : __byte_perm(lo, hi, 0x7531);
+      }
+    }
     if (ok) {
-      uint32_t b[3] = {0u, 0u, 0u};
-      put_digits(v.x * inv, 0, b);
-      put_digits(v.y * inv, 1, b);
-      put_digits(v.z * inv, 2, b);
-      put_digits(v.w * inv, 3, b);
 #pragma unroll
       for (int dd = 0; dd < 3; ++dd) *reinterpret_cast<uint32_t*>(d0 + int64_t(dd) * in + k) = b[dd];
       if ((tid & (gl - 1)) == 0) a.meta[int64_t(row) * a.meta_row + k / a.gs] = make_float2(rs, sum);
@@ -722,11 +735,11 @@ __global__ void __launch_bounds__(256) k_tdigit(const DigitArgs a, const int* in
   }
 }
 
-void launch_tdigit(const DigitArgs& a, const int* in_map, int8_t* dg, cudaStream_t st, bool pdl) {
+void launch_tdigit(const DigitArgs& a, const int* in_map, int8_t* dg, int bits, cudaStream_t st, bool pdl) {
   if (a.rows <= 0) return;
   if (a.in % 256 || (a.gs != 64 && a.gs != 128) || a.in > 16384)
     throw Error(ERR_UNSUPPORTED, "tensor-core digits: unsupported input size or group");
-  launch(k_tdigit, dim3(a.rows), dim3(256), size_t(a.in) * 4, st, pdl, a, in_map, dg);
+  launch(k_tdigit, dim3(a.rows), dim3(256), size_t(a.in) * 4, st, pdl, a, in_map, dg, bits == 4 ? 1 : 0);
 }
 
 }  // namespace swl
