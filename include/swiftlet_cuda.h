@@ -153,6 +153,18 @@ int swl_batch_supported(swl_model* model, char* why, int32_t why_len);
 int swl_ep_unique_id(void* out, int32_t out_len);
 int swl_ep_init(swl_model* model, int32_t rank, int32_t world, const void* id, int32_t id_len,
                 int32_t tokens_per_rank);
+/* Failure path of expert parallelism. Every rank's decode step waits in
+ * NCCL for the others, so a rank that leaves would leave its peers waiting:
+ * the host tells the library instead. Before each expert-parallel decode
+ * step the library calls fn(ctx, step) (step = expert-parallel steps this
+ * model has made); the callback confirms, out of band (a store, a heartbeat),
+ * that every peer is alive and at this step, and returns 0, or nonzero when a
+ * peer is gone. A nonzero answer, or an error NCCL reports for the
+ * communicator, ends expert parallelism on the model before anything is
+ * launched: that call and every later decode call return SWL_ERR_CUDA. NULL
+ * removes the callback. */
+typedef int (*swl_ep_liveness_fn)(void* ctx, int32_t step);
+int swl_ep_set_liveness(swl_model* model, swl_ep_liveness_fn fn, void* ctx);
 /* 1 when expert parallelism is on (rank, world and the owned expert range are
  * written; each pointer may be NULL), 0 when off (0, 1, 0, E). */
 int swl_ep_info(const swl_model* model, int32_t* rank, int32_t* world, int32_t* expert_lo, int32_t* expert_hi);

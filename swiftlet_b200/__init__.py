@@ -97,6 +97,7 @@ _SIGNATURES = {
     "swl_debug_delta_state": (_I, [_P, _P, C.c_int32, _P]),
     "swl_debug_kernel_path": (_I, [_P, C.c_char_p, C.c_int32]),
     "swl_state_reset": (_I, [_P]),
+    "swl_ep_set_liveness": (_I, [_P, _P, _P]),
     "swl_kernel_gated_delta": (_I, [_P] * 7 + [C.c_int32] * 5),
     "swl_bench_gated_delta": (_I, [C.c_int32] * 6 + [C.POINTER(C.c_float), C.POINTER(C.c_double)]),
     "swl_bench_moe_sweep": (_I, [_P, C.c_int32, C.c_int32, C.POINTER(C.c_float), C.POINTER(C.c_double),
@@ -323,6 +324,17 @@ class QwenCUDAModel:
         _check(lib().swl_step_device(self._h, state._bind(self), C.c_void_p(d_tokens), int(n),
                                      C.c_void_p(d_logits or None), C.c_void_p(d_greedy or None)))
 
+    def ep_set_liveness(self, callback) -> None:
+        """swl_ep_set_liveness: callback(step) -> True while every peer is
+        alive and at `step` (None removes it)."""
+        if callback is None:
+            self._liveness = None
+            _check(lib().swl_ep_set_liveness(self._h, None, None))
+            return
+        fn = _LIVENESS_FN(lambda ctx, step: 0 if callback(int(step)) else 1)
+        self._liveness = fn  # keep the C callback alive
+        _check(lib().swl_ep_set_liveness(self._h, C.cast(fn, C.c_void_p), None))
+
     def set_stream(self, cuda_stream: int | None) -> None:
         _check(lib().swl_set_stream(self._h, C.c_void_p(cuda_stream or None)))
 
@@ -498,6 +510,37 @@ def bench_gated_delta(T, Hk, Hv, Dk, Dv, iters):
     ms, fl = C.c_float(), C.c_double()
     _check(lib().swl_bench_gated_delta(T, Hk, Hv, Dk, Dv, iters, C.byref(ms), C.byref(fl)))
     return ms.value, fl.value
+
+
+_LIVENESS_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int32)
+
+
+def ep_store_liveness(store, rank: int, world: int, timeout_s: float = 30.0):
+    """A liveness callback for ep_set_liveness over a torch.distributed store:
+    at each step a rank publishes the step it is entering, then waits (up to
+    timeout_s) until every peer has published it too; False when one does
+    not, i.e. it left or stopped."""
+    import time
+
+    def alive(step: int) -> bool:
+        store.set(f"swl_ep/{rank}", str(step))
+        deadline = time.monotonic() + timeout_s
+        for p in range(world):
+            if p == rank:
+                continue
+            while True:
+                try:
+                    seen = int(store.get(f"swl_ep/{p}"))
+                except Exception:
+                    seen = -1
+                if seen >= step:
+                    break
+                if time.monotonic() > deadline:
+                    return False
+                time.sleep(0.002)
+        return True
+
+    return alive
 
 
 def verify_container(container: str, hashes_json: str | None = None, delete_corrupt: bool = False) -> dict:

@@ -26,7 +26,6 @@ struct Nccl {
                              cudaStream_t) = nullptr;
   ncclResult_t (*group_start)() = nullptr;
   ncclResult_t (*group_end)() = nullptr;
-  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
   ncclResult_t (*async_error)(ncclComm_t, ncclResult_t*) = nullptr;
   const char* (*error_string)(ncclResult_t) = nullptr;
   std::string why;
@@ -57,7 +56,6 @@ Nccl& nccl() {
     sym(n.group_start, "ncclGroupStart");
     sym(n.group_end, "ncclGroupEnd");
     sym(n.error_string, "ncclGetErrorString");
-    sym(n.comm_abort, "ncclCommAbort");
     sym(n.async_error, "ncclCommGetAsyncError");
     n.ok = n.why.empty();
   });
@@ -103,12 +101,6 @@ void ep_destroy(EpComm* c) {
   if (!c) return;
   if (c->comm) nccl().comm_destroy(c->comm);
   delete c;
-}
-
-void ep_abort(EpComm* c) {
-  if (!c || !c->comm) return;
-  nccl().comm_abort(c->comm);  // in-flight NCCL kernels of this communicator exit
-  c->comm = nullptr;
 }
 
 bool ep_async_error(EpComm* c, std::string* why) {

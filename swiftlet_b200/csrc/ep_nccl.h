@@ -23,10 +23,6 @@ void ep_unique_id(void* out);
 // device is the rank's device. Blocks until every rank has joined.
 EpComm* ep_init(int rank, int world, const void* id);
 void ep_destroy(EpComm* c);
-// Aborts the communicator (ncclCommAbort): NCCL kernels of it still in flight
-// exit; the handle is then unusable except for ep_destroy. Safe from another
-// thread while the owner's stream is stuck in a collective.
-void ep_abort(EpComm* c);
 // True (with NCCL's message) when the communicator reported an asynchronous
 // error, e.g. a peer that went away.
 bool ep_async_error(EpComm* c, std::string* why);

@@ -181,28 +181,28 @@ struct Model {
   bool ep_decode = false;    // set by the decode entry points: launches may exchange
   bool ep_graph = true;      // capture expert-parallel steps (SWL_EP_NO_GRAPH=1: launch directly)
   float* ep_part = nullptr;  // [ep_world * ep_tokens][hidden] partial MoE sums
-  // Failure path: a watchdog thread follows the completion event of the
-  // latest expert-parallel step; a step that has not completed after
-  // ep_timeout_ms (SWL_EP_TIMEOUT_MS, default 120 s: a peer left or hung)
-  // aborts the communicator (its NCCL kernels exit) and every later call on
-  // the model fails with SWL_ERR_CUDA instead of waiting forever.
-  struct EpWatch {
-    std::thread th;
-    std::mutex mu;
-    cudaEvent_t ev = nullptr;
-    bool pending = false;
-    std::chrono::steady_clock::time_point since;
-    std::atomic<bool> stop{false}, aborted{false};
-    std::string why;
-  };
-  EpWatch* ep_watch = nullptr;
-  int ep_timeout_ms = 120000;
-  void ep_watch_start();
-  void ep_watch_stop();
-  void ep_step_enqueued(cudaStream_t st);
-  void ep_check_alive() const {
-    if (ep_watch && ep_watch->aborted)
-      throw Error(ERR_CUDA, "expert-parallel group aborted: " + ep_watch->why);
+  // Failure path: before every expert-parallel decode step the host's
+  // liveness callback (swl_ep_set_liveness) confirms that every peer is alive
+  // and at this step; a refusal, or an error NCCL reports for the
+  // communicator, ends expert parallelism on this model before anything is
+  // launched, and every later decode call fails with SWL_ERR_CUDA.
+  swl_ep_liveness_fn ep_alive_fn = nullptr;
+  void* ep_alive_ctx = nullptr;
+  int64_t ep_steps = 0;
+  bool ep_failed = false;
+  std::string ep_fail_why;
+  void ep_check_alive() {
+    if (!ep_failed) {
+      std::string why;
+      if (ep_async_error(ep, &why)) {
+        ep_failed = true;
+        ep_fail_why = "NCCL reported " + why;
+      } else if (ep_alive_fn && ep_alive_fn(ep_alive_ctx, int32_t(ep_steps)) != 0) {
+        ep_failed = true;
+        ep_fail_why = "a peer left or stopped before step " + std::to_string(ep_steps);
+      }
+    }
+    if (ep_failed) throw Error(ERR_CUDA, "expert-parallel group failed: " + ep_fail_why);
   }
   int ep_lo() const { return int(int64_t(ep_rank) * cfg.experts / ep_world); }
   int ep_hi() const { return int(int64_t(ep_rank + 1) * cfg.experts / ep_world); }
@@ -274,8 +274,8 @@ struct Model {
               const float2* meta, int T, cudaStream_t st);
   // Decode calls of an expert-parallel model route exactly ep_tokens
   // sequences on every rank; anything else is refused before any launch.
-  void check_ep_call(bool decode, int nseq) const {
-    if (ep && decode) ep_check_alive();
+  void check_ep_call(bool decode, int nseq) {
+    if (ep && decode && ep_failed) throw Error(ERR_CUDA, "expert-parallel group failed: " + ep_fail_why);
     if (ep && decode && nseq != ep_tokens)
       throw Error(ERR_INVALID, "expert-parallel decode steps exactly " + std::to_string(ep_tokens) +
                                    " sequences per rank (got " + std::to_string(nseq) + ")");
@@ -299,7 +299,6 @@ struct EpDecode {
 };
 
 Model::~Model() {
-  ep_watch_stop();
   drop_graphs();
   if (stream) cudaStreamSynchronize(stream);
   ep_destroy(ep);
@@ -315,52 +314,6 @@ Model::~Model() {
   if (h_logits) cudaFreeHost(h_logits);
   if (h_tokens) cudaFreeHost(h_tokens);
   if (own) cudaStreamDestroy(own);
-}
-
-void Model::ep_watch_start() {
-  if (const char* t = getenv("SWL_EP_TIMEOUT_MS")) ep_timeout_ms = std::max(100, atoi(t));
-  ep_watch = new EpWatch();
-  SWL_CUDA(cudaEventCreateWithFlags(&ep_watch->ev, cudaEventDisableTiming));
-  EpWatch* w = ep_watch;
-  const int dev = device, limit = ep_timeout_ms;
-  EpComm* comm = ep;
-  w->th = std::thread([w, dev, limit, comm] {
-    cudaSetDevice(dev);
-    while (!w->stop) {
-      std::this_thread::sleep_for(std::chrono::milliseconds(20));
-      std::lock_guard<std::mutex> lock(w->mu);
-      if (!w->pending || w->aborted) continue;
-      std::string why;
-      if (cudaEventQuery(w->ev) == cudaSuccess) {
-        w->pending = false;
-      } else if (ep_async_error(comm, &why)) {
-        w->why = "NCCL reported " + why;
-        w->aborted = true;  // before the abort: a caller woken by it must see the flag
-        ep_abort(comm);
-      } else if (std::chrono::steady_clock::now() - w->since > std::chrono::milliseconds(limit)) {
-        w->why = "a step did not complete within " + std::to_string(limit) + " ms (a peer left or stopped)";
-        w->aborted = true;
-        ep_abort(comm);
-      }
-    }
-  });
-}
-
-void Model::ep_watch_stop() {
-  if (!ep_watch) return;
-  ep_watch->stop = true;
-  if (ep_watch->th.joinable()) ep_watch->th.join();
-  if (ep_watch->ev) cudaEventDestroy(ep_watch->ev);
-  delete ep_watch;
-  ep_watch = nullptr;
-}
-
-void Model::ep_step_enqueued(cudaStream_t st) {
-  if (!ep_watch) return;
-  std::lock_guard<std::mutex> lock(ep_watch->mu);
-  SWL_CUDA(cudaEventRecord(ep_watch->ev, st));
-  if (!ep_watch->pending) ep_watch->since = std::chrono::steady_clock::now();
-  ep_watch->pending = true;
 }
 
 void Model::drop_graphs() {
@@ -1440,7 +1393,7 @@ void Model::run_batch(State* const* s, int S, const int* counts, int T) {
   } else {
     enqueue_batch(T, S, chunked, stream);
   }
-  if (ep_step) ep_step_enqueued(stream);
+  if (ep_step) ++ep_steps;
   for (int i = 0; i < S; ++i) s[i]->pos += counts[i];
   stepped = true;
   hits += int64_t(T) * cfg.topk * cfg.layers;
@@ -1861,7 +1814,6 @@ int swl_step_batch(swl_model* model, swl_state** states, const int32_t* tokens, 
   int status = 0;
   SWL_CUDA(cudaMemcpyAsync(&status, m.kstatus, 4, cudaMemcpyDeviceToHost, m.stream));
   SWL_CUDA(cudaStreamSynchronize(m.stream));
-  if (m.ep && decode) m.ep_check_alive();  // the wait above may have ended by the watchdog's abort
   m.check_status(&status);
   API_END
 }
@@ -2007,12 +1959,19 @@ int swl_ep_init(swl_model* model, int32_t rank, int32_t world, const void* id, i
     throw Error(ERR_INVALID, "ranks disagree on tokens per rank or on the expert count");
   }
   m.ep = c;
-  m.ep_watch_start();
   m.ep_graph = !env_flag("SWL_EP_NO_GRAPH");
   m.ep_rank = rank;
   m.ep_world = world;
   m.ep_tokens = tokens_per_rank;
   m.ep_part = part;
+  API_END
+}
+
+int swl_ep_set_liveness(swl_model* model, swl_ep_liveness_fn fn, void* ctx) {
+  API_BEGIN
+  if (!model) throw Error(ERR_INVALID, "null model");
+  model->m.ep_alive_fn = fn;
+  model->m.ep_alive_ctx = ctx;
   API_END
 }
 

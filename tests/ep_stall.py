@@ -1,14 +1,14 @@
 """One rank of the expert-parallel failure-path check (run by tests/test_gpu_ep.py).
 
-Usage: python tests/ep_stall.py <model_dir> <rank> <world> <id_hex> <flag_dir> <out_json>
+Usage: python tests/ep_stall.py <model_dir> <rank> <world> <id_hex> <flag_dir> <store_port> <out_json>
 
-Both ranks join the group (SWL_EP_TIMEOUT_MS set by the test), prefill and
-run two decode steps together. Then rank 1 stops taking part: it stays alive
-(its memory stays valid) but makes no further call until rank 0 has written
-`done` to flag_dir. Rank 0 makes a third decode step, whose exchange has no
-partner: the library's watchdog must abort the communicator after the
-timeout, that call and the next must fail with SWL_ERR_CUDA instead of
-waiting forever, and the model must still close.
+Both ranks join the group with a liveness callback on a shared
+torch.distributed TCPStore (a heartbeat per step, 5 s limit), prefill and run
+two decode steps together. Then rank 1 stops taking part: it stays alive but
+makes no further call until rank 0 has written `done` to flag_dir. Rank 0
+makes a third decode step: its liveness check finds rank 1 missing, so the
+library must refuse that step with SWL_ERR_CUDA before launching anything,
+refuse the next one at once, and still close the model.
 """
 import json
 import os
@@ -23,11 +23,15 @@ import swiftlet_b200 as swl  # noqa: E402
 
 
 def main() -> int:
-    d, rank, world, id_hex, flags, out = sys.argv[1:7]
+    d, rank, world, id_hex, flags, port, out = sys.argv[1:8]
     rank, world = int(rank), int(world)
+    import datetime
+    import torch.distributed as dist
+    store = dist.TCPStore("127.0.0.1", int(port), world, rank == 0, timeout=datetime.timedelta(seconds=60))
     tpr = 2
     m = swl.QwenCUDAModel(d, device=rank)
     m.ep_init(rank, world, bytes.fromhex(id_hex), tpr)
+    m.ep_set_liveness(swl.ep_store_liveness(store, rank, world, timeout_s=5.0))
     V = m.config.vocab_size
     rng = np.random.default_rng(7 + rank)
     states = [m.new_state(64) for _ in range(tpr)]
@@ -60,6 +64,8 @@ def main() -> int:
     res["closed"] = True
     with open(out, "w") as f:
         json.dump(res, f)
+    if rank == 0:  # the store's host leaves last
+        time.sleep(1.0)
     return 0
 
 

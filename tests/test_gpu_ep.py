@@ -57,18 +57,23 @@ def test_expert_parallel_matches_single_gpu(shape, graph, tmp_path):
 
 def test_a_peer_that_stops_answering_is_reported_not_waited_for(tmp_path):
     """The failure path: rank 1 stops making calls after two steps (alive,
-    nothing of it in flight); rank 0's next exchange has no partner, so the
-    library's watchdog aborts the communicator after SWL_EP_TIMEOUT_MS and
-    rank 0's calls fail with SWL_ERR_CUDA within seconds, and both ranks still
+    nothing of it in flight); rank 0's liveness callback (a heartbeat on a
+    TCPStore) finds it missing before the next exchange, so rank 0's calls
+    fail with SWL_ERR_CUDA without launching anything, and both ranks still
     close their models (NVLS off, plain peer transfers)."""
+    import socket
     world = 2
     if _gpus() < world:
         pytest.skip("expert parallelism needs two GPUs")
+    with socket.socket() as s_:
+        s_.bind(("127.0.0.1", 0))
+        port = s_.getsockname()[1]
     ep_id = swl.ep_unique_id().hex()
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", SWL_EP_TIMEOUT_MS="3000")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     outs = [str(tmp_path / f"rank{r}.json") for r in range(world)]
     procs = [subprocess.Popen([sys.executable, os.path.join(ROOT, "tests", "ep_stall.py"), TINY_BASELINE, str(r),
-                               str(world), ep_id, str(tmp_path), outs[r]], env=env, cwd=ROOT) for r in range(world)]
+                               str(world), ep_id, str(tmp_path), str(port), outs[r]], env=env, cwd=ROOT)
+             for r in range(world)]
     rcs = []
     try:
         for p in procs:
@@ -82,6 +87,6 @@ def test_a_peer_that_stops_answering_is_reported_not_waited_for(tmp_path):
     assert rcs == [0] * world, (rcs, res)
     r0 = res[0]
     assert r0["codes"] == [swl.SWL_ERR_CUDA, swl.SWL_ERR_CUDA], r0
-    assert "aborted" in r0["message"]
-    assert r0["elapsed_s"] < 60, r0
+    assert "peer left or stopped" in r0["message"]
+    assert r0["elapsed_s"] < 30, r0
     assert r0["closed"] and res[1]["closed"]
