@@ -272,6 +272,12 @@ struct Model {
   void run_packed(State* const* s, int nseq, const int32_t* tokens, const int* counts, float* logits_out);
   void bdense(const std::vector<std::pair<QLin, float*>>& segs, int64_t y_stride, int mode, const uint2* bt,
               const float2* meta, int T, cudaStream_t st);
+  // The same on the tcgen05 GEMM: the T input rows (x, x_stride apart) go
+  // through `pro` into the tensor-core digit matrix (x_out: optional copy of
+  // the prepared rows), then every segment's 128-row items. False, with
+  // nothing launched, when a segment's format does not fit it.
+  bool tdense(const std::vector<std::pair<QLin, float*>>& segs, int64_t y_stride, int mode, const float* x,
+              int64_t x_stride, int T, int pro, const float* aux, float* x_out, cudaStream_t st);
   // Decode calls of an expert-parallel model route exactly ep_tokens
   // sequences on every rank; anything else is refused before any launch.
   void check_ep_call(bool decode, int nseq) {
@@ -1086,6 +1092,34 @@ void Model::ensure_batch() {
   bb.ready = true;
 }
 
+bool Model::tdense(const std::vector<std::pair<QLin, float*>>& segs, int64_t y_stride, int mode, const float* x,
+                   int64_t x_stride, int T, int pro, const float* aux, float* x_out, cudaStream_t st) {
+  if (segs.empty() || segs.size() > 4) return false;
+  const QLin& q0 = segs[0].first;
+  if (!tgemm_supported(q0.in, q0.bits, q0.dt, q0.gs)) return false;
+  for (auto& sg : segs)
+    if (sg.first.bits != q0.bits || sg.first.dt != q0.dt || sg.first.gs != q0.gs || sg.first.in != q0.in) return false;
+  TGemmArgs g;
+  g.mode = mode; g.in = q0.in; g.gs = q0.gs;
+  g.nseg = int(segs.size());
+  g.seg_rb[0] = 0;
+  for (int i = 0; i < g.nseg; ++i) {
+    g.seg[i] = bmat(segs[i].first);
+    g.y[i] = segs[i].second;
+    g.seg_rb[i + 1] = g.seg_rb[i] + (segs[i].first.out + 127) / 128;
+  }
+  g.y_stride = y_stride; g.ntok = T;
+  g.dg = bb.dg_dense; g.dg_rows = int64_t(3) * T; g.meta = bb.tmeta_dense; g.meta_row = q0.in / q0.gs;
+  g.status = kstatus;
+  // digits first: launch_tgemm checks the maps before launching anything,
+  // so a refusal leaves only a harmless digit pass behind
+  DigitArgs d;
+  d.x = x; d.x_stride = x_stride; d.rows = T; d.in = q0.in; d.gs = q0.gs; d.prologue = pro; d.aux = aux;
+  d.eps = float(cfg.eps); d.x_out = x_out; d.meta = bb.tmeta_dense; d.meta_row = q0.in / q0.gs;
+  launch_tdigit(d, nullptr, bb.dg_dense, q0.bits, st, use_pdl);
+  return launch_tgemm(g, q0.bits, sm_count(), st, use_pdl);
+}
+
 // Segments over one digitised input, launched in groups of one weight format.
 void Model::bdense(const std::vector<std::pair<QLin, float*>>& segs, int64_t y_stride, int mode, const uint2* bt,
                    const float2* meta, int T, cudaStream_t st) {
@@ -1134,10 +1168,12 @@ void Model::enqueue_batch(int T, int S, bool chunked, cudaStream_t st) {
   };
   for (int l = 0; l < c.layers; ++l) {
     const LayerDev& ld = L[l];
-    digit(bb.h, D, T, D, ld.in_lin[0].gs, PRO_RMSNORM, ld.in_norm, nullptr, 0, nullptr, bb.bt_a, bb.meta_a);
     std::vector<std::pair<QLin, float*>> segs;
     for (int s = 0; s < ld.n_in; ++s) segs.push_back({ld.in_lin[s], bb.proj + (ld.in_y[s] - proj)});
-    bdense(segs, bb.projn, BM_STORE, bb.bt_a, bb.meta_a, T, st);
+    if (!tdense(segs, bb.projn, BM_STORE, bb.h, D, T, PRO_RMSNORM, ld.in_norm, nullptr, st)) {
+      digit(bb.h, D, T, D, ld.in_lin[0].gs, PRO_RMSNORM, ld.in_norm, nullptr, 0, nullptr, bb.bt_a, bb.meta_a);
+      bdense(segs, bb.projn, BM_STORE, bb.bt_a, bb.meta_a, T, st);
+    }
     if (ld.delta) {
       DeltaArgs d;
       d.proj = bb.proj; d.proj_stride = bb.projn; d.split = c.split_layout; d.nk = c.nk; d.nv = c.nv; d.dk = c.dk;
@@ -1189,24 +1225,7 @@ void Model::enqueue_batch(int T, int S, bool chunked, cudaStream_t st) {
     enqueue_batch_moe(l, T, chunked, st);
   }
   launch_badvance(bb.sds, S, chunked ? bb.seq_n : nullptr, st, pdl);
-  bool head_tc = false;
-  if (tgemm_supported(D, lm_head.bits, lm_head.dt, lm_head.gs)) {
-    // lm_head on the tensor cores: final norm into the digit matrix, then
-    // 128-row items x 16-token tiles
-    DigitArgs dd;
-    dd.x = bb.h; dd.x_stride = D; dd.rows = T; dd.in = D; dd.gs = lm_head.gs; dd.prologue = PRO_RMSNORM;
-    dd.aux = final_norm; dd.eps = float(c.eps); dd.meta = bb.tmeta_dense; dd.meta_row = D / lm_head.gs;
-    TGemmArgs hg;
-    hg.mode = BM_STORE; hg.in = D; hg.gs = lm_head.gs;
-    hg.seg[0] = bmat(lm_head); hg.y[0] = bb.logits; hg.nseg = 1;
-    hg.seg_rb[0] = 0; hg.seg_rb[1] = (c.vocab + 127) / 128;
-    hg.y_stride = c.vocab; hg.ntok = T;
-    hg.dg = bb.dg_dense; hg.dg_rows = int64_t(3) * T; hg.meta = bb.tmeta_dense; hg.meta_row = D / lm_head.gs;
-    hg.status = kstatus;
-    launch_tdigit(dd, nullptr, bb.dg_dense, lm_head.bits, st, pdl);
-    head_tc = launch_tgemm(hg, lm_head.bits, sm_count(), st, pdl);
-  }
-  if (!head_tc) {
+  if (!tdense({{lm_head, bb.logits}}, c.vocab, BM_STORE, bb.h, D, T, PRO_RMSNORM, final_norm, nullptr, st)) {
     digit(bb.h, D, T, D, lm_head.gs, PRO_RMSNORM, final_norm, nullptr, 0, nullptr, bb.bt_a, bb.meta_a);
     bdense({{lm_head, bb.logits}}, c.vocab, BM_STORE, bb.bt_a, bb.meta_a, T, st);
   }
@@ -1245,8 +1264,11 @@ void Model::enqueue_batch_moe(int l, int T, bool chunked, cudaStream_t st) {
                   tgemm_supported(I, ld.ed.lin.bits, ld.ed.lin.dt, gs_d) && c.shared_inter == I &&
                   ld.sh_g.bits == ld.eg.lin.bits && ld.sh_g.dt == ld.eg.lin.dt && ld.sh_g.gs == gs_r &&
                   ld.sh_d.gs == gs_d && ld.ed.lin.bits == ld.eg.lin.bits;
-  digit(bb.h, D, T, D, gs_r, PRO_RMSNORM, ld.post_norm, nullptr, 0, bb.xmoe + int64_t(own) * D, bt_own, meta_own);
-  bdense({{ld.router, rlog_own}, {ld.sgate, rlog_own + E}}, E + 1, BM_STORE, bt_own, meta_own, T, st);
+  if (!(tc && tdense({{ld.router, rlog_own}, {ld.sgate, rlog_own + E}}, E + 1, BM_STORE, bb.h, D, T, PRO_RMSNORM,
+                     ld.post_norm, bb.xmoe + int64_t(own) * D, st))) {
+    digit(bb.h, D, T, D, gs_r, PRO_RMSNORM, ld.post_norm, nullptr, 0, bb.xmoe + int64_t(own) * D, bt_own, meta_own);
+    bdense({{ld.router, rlog_own}, {ld.sgate, rlog_own + E}}, E + 1, BM_STORE, bt_own, meta_own, T, st);
+  }
   if (ep_on) {
     // every rank's MoE inputs (the normalised rows for the tensor-core
     // experts, or their digit tables for the mma.sync ones) and router logits

@@ -443,7 +443,6 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
         fetch_meta(dn, nslot ^ 1);
       }
       const float2* mcur = meta_s + nslot * (TOK * 32);
-      const int nld = (3 * d.nt + 15) / 16;  // TMEM column groups of 16 that hold this item's tokens
       float acc_t[TOK];
 #pragma unroll
       for (int t = 0; t < TOK; ++t) acc_t[t] = 0.f;
@@ -472,8 +471,8 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
           } else {
             const uint32_t col = lane_base + uint32_t(acc * gpc * TG_N + g * TG_N);
             tg_ld16(col, v0);
-            if (nld > 1) tg_ld16(col + 16, v1);
-            if (nld > 2) tg_ld16(col + 32, v2);
+            tg_ld16(col + 16, v1);
+            tg_ld16(col + 32, v2);
             tg_ld_wait();
           }
           const int gi = kc * gpc + g;
@@ -490,15 +489,18 @@ __global__ void __launch_bounds__(TG_THREADS, 1) k_tgemm(const TGemmArgs a, cons
               acc_t[t] = fmaf(s_rg * m.x * (1.f / 254.f), vv, fmaf(b_rg, m.y, acc_t[t]));
             }
           } else {
+            // wide items: every token slot, branch-free (slots past the
+            // item's read zero metadata), the digit columns merged in
+            // integers as for narrow items
+            const float sr = s_rg * (1.f / 254.f);
 #pragma unroll
             for (int t = 0; t < TOK; ++t) {
-              if (t >= d.nt) break;
               const int c0 = 3 * t;
               auto pick = [&](int c) -> uint32_t { return c < 16 ? v0[c] : (c < 32 ? v1[c - 16] : v2[c - 32]); };
-              const float p0 = tg_i2f(pick(c0)), p1 = tg_i2f(pick(c0 + 1)), p2 = tg_i2f(pick(c0 + 2));
-              const float vv = p0 + (p1 + p2 * (1.f / 254.f)) * (1.f / 254.f);
-              const float2 m = mcur[t * 32 + gi];
-              acc_t[t] = fmaf(s_rg * m.x, vv, fmaf(b_rg, m.y, acc_t[t]));
+              const float2 m = t < d.nt ? mcur[t * 32 + gi] : make_float2(0.f, 0.f);
+              const int q = int(pick(c0)) * 254 + int(pick(c0 + 1));
+              const float vv = fmaf(float(int(pick(c0 + 2))), 1.f / 254.f, float(q));
+              acc_t[t] = fmaf(sr * m.x, vv, fmaf(b_rg, m.y, acc_t[t]));
             }
           }
         }
