@@ -50,6 +50,8 @@ def lib():
         L.orc_state_advance.argtypes = [P, I]
         L.orc_state_delta.argtypes = [P, P, I, fp]
         L.orc_step.argtypes = [P, P, ip, I, fp]
+        L.orc_route_gap.restype = C.c_double
+        L.orc_route_gap.argtypes = [P, I]
         L.orc_dequant.argtypes = [P, C.c_char_p, C.c_int64, C.c_int64, fp]
         L.orc_tensor_bytes.argtypes = [P, C.c_char_p, C.c_int64, C.c_int64, P]
         L.orc_tensor_info.argtypes = [P, C.c_char_p, C.c_char_p, C.POINTER(C.c_int64)]
@@ -175,6 +177,13 @@ class OracleModel:
         logits = np.zeros(self.V, np.float32)
         _check(lib().orc_step(self._h, state._h, _i(t), len(t), _f(logits)))
         return logits
+
+    def route_gap(self, reset: bool = False) -> float:
+        """Smallest relative gap (p_k - p_k+1) / p_k between the k-th and
+        (k+1)-th router probability of any row routed since the last reset:
+        below the float noise of the router logits, another implementation's
+        top-k may legitimately pick the other expert."""
+        return float(lib().orc_route_gap(self._h, int(reset)))
 
     def tensor_info(self, name: str):
         dt = C.create_string_buffer(8)

@@ -694,6 +694,12 @@ struct Model {
   std::pair<int, std::shared_ptr<LayerW>> cache{-1, nullptr};
   std::mutex mu;
   vector<vector<Pick>>* pickLog = nullptr;   // when set, moeForward appends each row's picks
+  // Smallest relative gap between the k-th and (k+1)-th router probability
+  // routed since the last orc_route_gap(reset): a test-side measure of how
+  // close an input comes to a top-k tie, where float summation order alone
+  // can change the picks of any other implementation.
+  double minRouteGap = INFINITY;
+  std::mutex gapMu;
 
   explicit Model(const string& dir) {
     string text;
@@ -956,6 +962,18 @@ struct Model {
         if ((int)picks.size() < topK) { picks.push_back({e, p}); std::stable_sort(picks.begin(), picks.end(), byProb); }
         else if (p > picks[topK - 1].p) { picks[topK - 1] = {e, p}; std::stable_sort(picks.begin(), picks.end(), byProb); }
       }
+      if (E > topK) {
+        float next = -INFINITY;
+        for (int e = 0; e < E; ++e) {
+          bool picked = false;
+          for (const Pick& pk : picks) picked |= pk.id == e;
+          if (!picked) next = std::max(next, router[(size_t)s * E + e]);
+        }
+        const double kth = picks[topK - 1].p;
+        const double gap = kth > 0 ? (kth - next) / kth : 0.0;
+        std::lock_guard<std::mutex> g(gapMu);
+        minRouteGap = std::min(minRouteGap, gap);
+      }
       rows.push_back(picks);
     }
     if (probsOut) *probsOut = router;
@@ -1171,6 +1189,15 @@ int orc_state_delta(void* mp, void* s, int layer, float* out) {
 }
 
 // Incremental step (QwenCPUModel.step :238-255): last position's logits.
+// Smallest relative top-k router gap since the last reset (+inf if none).
+double orc_route_gap(void* mp, int reset) {
+  Model& m = *(Model*)mp;
+  std::lock_guard<std::mutex> g(m.gapMu);
+  const double v = m.minRouteGap;
+  if (reset) m.minRouteGap = INFINITY;
+  return v;
+}
+
 int orc_step(void* mp, void* state, const int32_t* tokens, int n, float* logits) {
   ORC_TRY({
     Model& m = *(Model*)mp;

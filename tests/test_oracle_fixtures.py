@@ -163,3 +163,19 @@ def test_gated_delta_oracle_on_reference_lcg_case():
             Y[t, hv] = S[hv] @ qa[t, hk]
     assert np.abs(y - Y.reshape(-1)).max() < 1e-4
     assert np.abs(st - S.reshape(-1)).max() < 1e-4
+
+
+def test_route_gap_is_smallest_topk_margin():
+    # The oracle's near-tie measure used to screen parity inputs: the smallest
+    # (p_k - p_k+1) / p_k over every routed row since the last reset.
+    m = oracle.OracleModel(os.path.join(REF_FIXTURES, "tiny-model"))
+    m.route_gap(reset=True)
+    assert m.route_gap() == float("inf")
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((6, m.D)).astype(np.float32)
+    _, ids, pp, probs = m.moe_forward(x, 0)
+    s = -np.sort(-probs, axis=1)
+    want = ((s[:, m.K - 1] - s[:, m.K]) / s[:, m.K - 1]).min()
+    got = m.route_gap(reset=True)
+    assert abs(got - want) <= 1e-6 * max(1.0, abs(want)), (got, want)
+    assert m.route_gap() == float("inf")
