@@ -306,7 +306,11 @@ static bool settle_ks(SliceTab& T, int tiles, int max_tiles, int ngroups, int xs
     int S = T.S;
     if (max_tiles > S) S = S / ng * ng;
     if (S < 1) continue;
-    const double cost = double((tiles + ng - 1) / ng) * (1.0 / ks + (ks > 1 ? 0.08 : 0.0));
+    // a combine (named barrier, partials through shared memory) costs about
+    // 0.3 of a whole tile's reduction on B200: measured as the decode step's
+    // time with this weight swept from 0.08 to 2 (best at 0.3; at 0.08 the
+    // 6-tile in-projections split 4 ways over 3 rounds)
+    const double cost = double((tiles + ng - 1) / ng) * (1.0 / ks + (ks > 1 ? 0.3 : 0.0));
     if (cost < best_cost - 1e-9) { best_cost = cost; best = ks; best_s = S; }
   }
   if (!best) return false;
