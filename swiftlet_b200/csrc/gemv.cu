@@ -389,35 +389,67 @@ static bool plan_gateup(const MoeArgs& m, SliceTab& T, int& grid, size_t& smem) 
   return slice_ring(T, max_tiles, g.in, g.in / wpc + 4, 0, g.in, smem);
 }
 
+// Gate/up: one item of BR rows of one gate/up pair per CTA (the shared
+// expert's items first, then K routed slots of ipe items each). BR is the
+// smallest multiple of 8 (>= 16) whose items fit one CTA per SM, else two
+// CTAs per SM (shared memory permitting), within the shared-memory budget;
+// the item's BR / 8 MMA tiles are split over warp groups (KS warps each).
 static bool plan_igateup(const MoeArgs& m, SliceTab& T, TileMaps& M, int& grid, size_t& smem) {
   if (!slice_enabled() || !imma_enabled()) return false;
   const QLin& g = m.g.lin;
   if (!imma_fmt_ok(g) || !imma_fmt_ok(m.u.lin) || !imma_fmt_ok(m.sg) || !imma_fmt_ok(m.su)) return false;
   if (!expert_strides_ok(m.g) || !expert_strides_ok(m.u) || m.su.out != m.sg.out || m.sg.in != g.in) return false;
-  if (!aligned16(m.x) || g.in > 4096) return false;
+  if (!aligned16(m.x) || g.in > 4096 || m.topk > 16 || m.sg.out < 8 || (m.topk > 0 && g.out < 8)) return false;
   T = SliceTab{};
   T.rb = int(g.row_bytes);
   T.srow = int(g.srow);
   T.gs_shift = gs_shift_of(g);
-  T.TR = 8;
-  const int sh = m.sg.out, nq = m.topk * g.out, n = sm_count();
-  T.sh_rpc = std::max(1, (sh + n - 1) / n);
-  T.rt_rpc = nq > 0 ? std::max(1, (nq + n - 1) / n) : 0;
-  grid = std::max(1, std::max((sh + T.sh_rpc - 1) / T.sh_rpc, nq > 0 ? (nq + T.rt_rpc - 1) / T.rt_rpc : 0));
-  if (!encode_rows(&M.m[0], m.sg.w, m.sg.out, m.sg.row_bytes, 8, 0, 0) ||
-      !encode_rows(&M.m[1], m.su.w, m.su.out, m.su.row_bytes, 8, 0, 0))
-    return false;
-  if (m.topk > 0 && (m.g.count < 1 || m.u.count < 1 ||
-                     !encode_rows(&M.m[2], g.w, g.out, g.row_bytes, 8, m.g.count, m.g.wstride) ||
-                     !encode_rows(&M.m[3], m.u.lin.w, m.u.lin.out, m.u.lin.row_bytes, 8, m.u.count, m.u.wstride)))
-    return false;
-  T.slot = 2 * imma_block_bytes(g, 8);
-  const int max_tiles = (T.sh_rpc + 7) / 8 + (nq > 0 ? (T.rt_rpc + 7) / 8 + (T.rt_rpc + g.out - 1) / g.out + 1 : 0);
   T.status = m.status;
-  const int xs_f = 3 * g.in / 4, cs_f = 2 * (((g.in >> T.gs_shift) + 3) & ~3) + 4, part_f = 2 * kImmaWarps * 16;
-  return slice_ring(T, max_tiles, xs_f, cs_f, part_f, g.in, smem) &&
-         settle_ks(T, (T.sh_rpc + 7) / 8 + (T.rt_rpc + 7) / 8, max_tiles, g.in >> T.gs_shift, xs_f, cs_f, part_f,
-                   g.in, smem);
+  const int sh = m.sg.out, inter = g.out, K = m.topk, sms = sm_count(), ngroups = g.in >> T.gs_shift;
+  const int xs_f = 3 * g.in / 4, cs_f = 2 * ((ngroups + 3) & ~3) + 4, part_f = 2 * kImmaWarps * 16;
+  const int max_br = std::min(256, (std::min(sh, K > 0 ? inter : sh) / 8) * 8);
+  int br = 0;
+  size_t br_smem = 0;
+  for (int pass = 0; pass < 2 && !br; ++pass) {
+    for (int c = 16; c <= max_br && !br; c += 8) {
+      const int items = (sh + c - 1) / c + K * ((inter + c - 1) / c);
+      T.TR = c;
+      T.S = 1;
+      T.slot = 2 * imma_block_bytes(g, c);
+      const size_t need = slice_layout(T, xs_f, cs_f, part_f, g.in) + 1024;  // + the ring's 1024-byte alignment
+      if (need > g_budget) break;  // larger items only need more
+      if (pass == 0 ? items <= sms : (items <= 2 * sms && need <= 113 * 1024)) {
+        br = c;
+        br_smem = need;
+      }
+    }
+  }
+  if (!br) return false;
+  T.TR = br;
+  T.S = 1;
+  T.slot = 2 * imma_block_bytes(g, br);
+  smem = br_smem;
+  slice_layout(T, xs_f, cs_f, part_f, g.in);
+  grid = (sh + br - 1) / br + K * ((inter + br - 1) / br);
+  if (!encode_rows(&M.m[0], m.sg.w, m.sg.out, m.sg.row_bytes, br, 0, 0) ||
+      !encode_rows(&M.m[1], m.su.w, m.su.out, m.su.row_bytes, br, 0, 0))
+    return false;
+  if (K > 0 && (m.g.count < 1 || m.u.count < 1 ||
+                !encode_rows(&M.m[2], g.w, g.out, g.row_bytes, br, m.g.count, m.g.wstride) ||
+                !encode_rows(&M.m[3], m.u.lin.w, m.u.lin.out, m.u.lin.row_bytes, br, m.u.count, m.u.wstride)))
+    return false;
+  // warp groups per item: the fewest rounds of tile work, a combine costing
+  // 0.3 of a tile (as settle_ks)
+  const int tiles = br / 8;
+  double best_cost = 1e30;
+  T.W = 0;
+  for (int ks : {1, 2, 4, 8}) {
+    if (ngroups % (4 * ks)) continue;
+    const int ng = kImmaWarps / ks;
+    const double cost = double((tiles + ng - 1) / ng) * (1.0 / ks + (ks > 1 ? 0.3 : 0.0));
+    if (cost < best_cost - 1e-9) { best_cost = cost; T.W = ks; }
+  }
+  return T.W > 0;
 }
 
 static bool plan_idown(const MoeArgs& m, SliceTab& T, TileMaps& M, int& grid, size_t& smem) {

@@ -532,9 +532,16 @@ __global__ void __launch_bounds__(IM_T, 2) k_igemv(const GemvArgs a, const Slice
 }
 
 // ---------------------------------------------------------------- MoE ----
-// Gate/up of the shared and routed experts (tiles and producer as k_sgateup,
-// 8 row pairs per tile): the 16-row MMA tile is 8 gate rows over the same 8
-// up rows, so the lane holding gate row p also holds up row p.
+// Gate/up of the shared and routed experts with SiLU * up fused. CTA b owns
+// one item of up to BR = T.TR rows of one gate/up pair: items [0, nsh) cover
+// the shared expert's rows, item nsh + q routed expert slot k = q / ipe, rows
+// ((q % ipe) * BR, ...) (ipe items per expert). An item's gate rows and its up
+// rows arrive as one tensor-TMA box each plus their scale and bias rows, so a
+// CTA issues six copies: the shared items at kernel entry, the routed ones as
+// soon as consumer warp 0 has routed from the router's logits (the producer
+// waits for it on an mbarrier). The 16-row MMA tile is 8 gate rows over the
+// same 8 up rows, so the lane holding gate row p also holds up row p; the
+// item's BR / 8 tiles are split over warp groups as in the dense kernel.
 template <int BITS, int DT, int KPG>
 __global__ void __launch_bounds__(IM_T, 2) k_igateup(const MoeArgs m, const SliceTab T,
                                                    const __grid_constant__ TileMaps M) {
@@ -548,64 +555,56 @@ __global__ void __launch_bounds__(IM_T, 2) k_igateup(const MoeArgs m, const Slic
   float* gsum = reinterpret_cast<float*>(sm + T.off_cs);
   uint2* bt = reinterpret_cast<uint2*>(sm + T.off_xs);
   uint64_t* full = reinterpret_cast<uint64_t*>(sm + T.off_bar);
-  uint64_t* empty = full + T.S;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int K = m.topk, inter = m.g.lin.out, sh = m.sg.out, nq = K * inter;
-  const int s0 = min(sh, int(blockIdx.x) * T.sh_rpc), s1 = min(sh, s0 + T.sh_rpc);
-  const int q0 = min(nq, int(blockIdx.x) * T.rt_rpc), q1 = min(nq, q0 + T.rt_rpc);
-  const int ss = T.srow * SB, half = T.slot / 2, segb = 8 * 128;
-  auto tiles = [&](auto&& f) {  // f(tile, slot (K = shared), row, n)
-    int idx = 0;
-    for (int r = s0; r < s1; r += 8) f(idx++, K, r, min(8, s1 - r));
-    for (int q = q0; q < q1;) {
-      const int k = q / inter, row = q - k * inter;
-      const int n = min(8, min(q1 - q, inter - row));
-      f(idx++, k, row, n);
-      q += n;
-    }
-  };
+  const int K = m.topk, inter = m.g.lin.out, sh = m.sg.out, BR = T.TR;
+  const int nsh = (sh + BR - 1) / BR, ipe = (inter + BR - 1) / BR, b = blockIdx.x;
+  const bool shared_item = b < nsh;
+  const int k = shared_item ? K : (b - nsh) / ipe;
+  const int row0 = shared_item ? b * BR : (b - nsh - k * ipe) * BR;
+  const int n = min(BR, (shared_item ? sh : inter) - row0);
+  const int ss = T.srow * SB, half = T.slot / 2, segb = BR * 128;
+  const bool route_here = !shared_item && m.logits != nullptr;
   __shared__ int r_ids[16];
   __shared__ float r_w[16], r_sh;
-  imma_init_barriers(full, empty, T.S);
+  __shared__ __align__(8) uint64_t routed;
+  if (tid == 0) {
+    mbar_init(full, 1);
+    mbar_init(&routed, 1);
+    mbar_init_fence();
+  }
+  __syncthreads();
   if (warp == IW) {  // producer
-    const uint64_t pol = l2_evict_first();
-    int issued = 0;
-    bool ok = true;
-    auto issue = [&](int i, int k, int row, int n, int id) {
-      if (!ok) return;
-      const int s = i % T.S;
-      if (i >= T.S && !mbar_wait(empty + s, unsigned(i / T.S - 1) & 1u)) { ok = false; return; }
-      QLin G = m.sg, U = m.su;
-      if (k < K) {
-        G = expert_lin(m.g, id);
-        U = expert_lin(m.u, id);
-      }
-      uint8_t* d = ring + size_t(s) * T.slot;
-      mbar_expect_tx(full + s, 2u * tile_bytes(T, SB, 8, n));
-      tile_copy(T, SB, 8, d, full + s, &M.m[k < K ? 2 : 0], k < K ? id : -1, G.s, G.b, row, n, pol);
-      tile_copy(T, SB, 8, d + half, full + s, &M.m[k < K ? 3 : 1], k < K ? id : -1, U.s, U.b, row, n, pol);
-      issued = i + 1;
-    };
-    // shared-expert tiles first: their weights do not depend on the routing
-    if (lane == 0) tiles([&](int i, int k, int row, int n) { if (k == K) issue(i, k, row, n, 0); });
-    pdl_wait();  // the routing comes from the previous (router) grid
-    if (m.logits) {
-      warp_route(m.logits, m.experts, K, m.norm_topk, r_ids, r_w, &r_sh);
-      if (blockIdx.x == 0 && lane < K) {
-        m.pick_ids[lane] = r_ids[lane];
-        m.pick_w[lane] = r_w[lane];
-      }
-      if (blockIdx.x == 0 && lane == 0) *m.shared_scale = r_sh;
-    }
     if (lane == 0) {
-      tiles([&](int i, int k, int row, int n) {
-        if (k < K) issue(i, k, row, n, m.logits ? r_ids[k] : __ldcg(m.pick_ids + k));
-      });
+      const uint64_t pol = l2_evict_first();
+      bool ok = true, issued = false;
+      auto issue = [&](int id) {
+        QLin G = m.sg, U = m.su;
+        if (!shared_item) {
+          G = expert_lin(m.g, id);
+          U = expert_lin(m.u, id);
+        }
+        mbar_expect_tx(full, 2u * tile_bytes(T, SB, BR, n));
+        tile_copy(T, SB, BR, ring, full, &M.m[shared_item ? 0 : 2], shared_item ? -1 : id, G.s, G.b, row0, n, pol);
+        tile_copy(T, SB, BR, ring + half, full, &M.m[shared_item ? 1 : 3], shared_item ? -1 : id, U.s, U.b, row0, n,
+                  pol);
+        issued = true;
+      };
+      // the shared expert's weights do not depend on the routing
+      if (shared_item) issue(0);
+      pdl_wait();  // the routing comes from the previous (router) grid
+      if (!shared_item) {
+        if (route_here) {
+          ok = mbar_wait(&routed, 0u);
+          if (ok) issue(r_ids[k]);
+        } else {
+          issue(__ldcg(m.pick_ids + k));
+        }
+      }
       if (!ok) sl_fail(T);
       // Dependents are released only after the router grid is complete: the
       // down kernel reads the router's output before its own dependency wait.
       pdl_launch();
-      sl_drain(full, T.S, issued);
+      sl_drain(full, 1, issued ? 1 : 0);
     }
     return;
   }
@@ -613,6 +612,19 @@ __global__ void __launch_bounds__(IM_T, 2) k_igateup(const MoeArgs m, const Slic
   trc.start(m.trace);
   pdl_wait();
   trc.waited(m.trace);
+  if (route_here && warp == 0) {
+    warp_route(m.logits, m.experts, K, m.norm_topk, r_ids, r_w, &r_sh);
+    __threadfence_block();
+    if (lane == 0) mbar_arrive(&routed);
+    // the first routed item also stores the routing for observers
+    if (b == nsh) {
+      if (lane < K) {
+        m.pick_ids[lane] = r_ids[lane];
+        m.pick_w[lane] = r_w[lane];
+      }
+      if (lane == 0) *m.shared_scale = r_sh;
+    }
+  }
   GemvArgs a;
   a.in = m.g.lin.in; a.prologue = PRO_COPY; a.x = m.x;
   sl_stage_plain<IM_NT>(a, red, plain);
@@ -626,27 +638,24 @@ __global__ void __launch_bounds__(IM_T, 2) k_igateup(const MoeArgs m, const Slic
   float* kp = reinterpret_cast<float*>(sm + T.off_part);
   int g0, g1;
   ksp.range(ngroups, g0, g1);
+  const int so = BR * T.rb, bo = BR * T.rb + BR * ss;  // scale and bias rows after each weight box
   bool dead = false;
-  tiles([&](int i, int k, int row, int n) {
-    if (!ksp.mine(i)) return;
-    const int s = i % T.S;
-    const bool ok = !dead && __all_sync(0xffffffffu, mbar_wait(full + s, unsigned(i / T.S) & 1u));
+  for (int j = 0; j < (n + 7) / 8; ++j) {
+    if (!ksp.mine(j)) continue;
+    const bool ok = !dead && __all_sync(0xffffffffu, mbar_wait(full, 0u));
     dead = !ok;
     float gv = 0.f, uv = 0.f;
+    const int r = 8 * j + gi;
     if (ok) {
-      const uint8_t* gt = ring + size_t(s) * T.slot;
-      const uint8_t* ut = gt + half;
-      const int so = 8 * T.rb, bo = 8 * T.rb + 8 * ss;
-      imma_rows<BITS, DT, KPG>(gt, ut, gi, gi, segb, gt + so + gi * ss, ut + so + gi * ss, gt + bo + gi * ss,
-                               ut + bo + gi * ss, bt, gsum, grs, g0, g1, gv, uv);
+      const uint8_t* gt = ring;
+      const uint8_t* ut = ring + half;
+      imma_rows<BITS, DT, KPG>(gt, ut, r, r, segb, gt + so + r * ss, ut + so + r * ss, gt + bo + r * ss,
+                               ut + bo + r * ss, bt, gsum, grs, g0, g1, gv, uv);
     }
-    ksp.combine(kp, ksp.round(i), gi, t, gv, uv);
+    ksp.combine(kp, ksp.round(j), gi, t, gv, uv);
     __syncwarp();
-    if (ksp.kw == 0 && ok) {
-      if (lane == 0) mbar_arrive(empty + s);
-      if (t == 0 && gi < n) m.hmid[k * m.hmid_stride + row + gi] = silu_ref(gv) * uv;
-    }
-  });
+    if (ksp.kw == 0 && ok && t == 0 && r < n) m.hmid[k * m.hmid_stride + row0 + r] = silu_ref(gv) * uv;
+  }
   trc.looped(m.trace);
   if (dead) sl_fail(T);
   trc.end(m.trace);
