@@ -174,11 +174,13 @@ __device__ __forceinline__ float key_f(unsigned k) {
 // the logits, whose order the softmax preserves, with ties to the lower
 // expert id (the reference's insertion scan with a strict `>`): each round is
 // one warp max of order-preserving keys and one warp min over the ids that
-// hold it. Only the K picked probabilities are divided out. ids / w / sh are
-// shared memory.
-__device__ __forceinline__ void warp_route(const float* lg, int E, int K, int norm_topk, int* ids, float* w,
-                                           float* sh) {
-  constexpr int PL = 16;
+// hold it. Lane l holds experts l, l + 32, ... and keeps its own three best
+// (key, slot) pairs, so a round costs the winning lane a shift; only a lane
+// picked a third time rescans its unpicked slots. Only the K picked
+// probabilities are divided out. ids / w / sh are shared memory.
+template <int PL>
+__device__ __forceinline__ void warp_route_pl(const float* lg, int E, int K, int norm_topk, int* ids, float* w,
+                                              float* sh) {
   const int lane = threadIdx.x & 31;
   float lv[PL];
   unsigned key[PL];
@@ -189,33 +191,39 @@ __device__ __forceinline__ void warp_route(const float* lg, int E, int K, int no
     key[i] = e < E ? f_key(lv[i]) : 0u;
   }
   const float shared_logit = __ldcg(lg + E);
-  // this lane's best (first index wins among equal keys)
-  auto local_best = [&](unsigned& bk, int& bi) {
-    bk = 0u;
-    bi = 0x7fffffff;
+  // this lane's three best (ascending slots and a strict `>`: the lower
+  // expert id first among equal keys); slot PL = none
+  unsigned k1 = 0u, k2 = 0u, k3 = 0u;
+  int s1 = PL, s2 = PL, s3 = PL;
+  unsigned picked = 0u;
+  auto best3 = [&]() {
+    k1 = k2 = k3 = 0u;
+    s1 = s2 = s3 = PL;
 #pragma unroll
-    for (int i = 0; i < PL; ++i)
-      if (key[i] > bk) { bk = key[i]; bi = i * 32 + lane; }
+    for (int i = 0; i < PL; ++i) {
+      const unsigned kk = (picked >> i) & 1u ? 0u : key[i];
+      if (kk > k1) { k3 = k2; s3 = s2; k2 = k1; s2 = s1; k1 = kk; s1 = i; }
+      else if (kk > k2) { k3 = k2; s3 = s2; k2 = kk; s2 = i; }
+      else if (kk > k3) { k3 = kk; s3 = i; }
+    }
   };
-  unsigned bk;
-  int bi;
-  local_best(bk, bi);
+  best3();
   float mine = 0.f;  // lane k: the logit of pick k
   float top = 0.f;   // the largest logit (softmax shift)
   for (int k = 0; k < K; ++k) {
-    const unsigned mx = __reduce_max_sync(0xffffffffu, bk);
-    int id = int(__reduce_min_sync(0xffffffffu, bk == mx ? unsigned(bi) : 0x7fffffffu));
+    const unsigned mx = __reduce_max_sync(0xffffffffu, k1);
+    const unsigned bi = k1 ? unsigned(s1 * 32 + lane) : 0x7fffffffu;
+    int id = int(__reduce_min_sync(0xffffffffu, k1 == mx ? bi : 0x7fffffffu));
+    if (mx && (id & 31) == lane) {
+      picked |= 1u << s1;
+      k1 = k2; s1 = s2; k2 = k3; s2 = s3; k3 = 0u; s3 = PL;
+      if (!k1) best3();  // all three consumed: rescan the unpicked slots
+    }
     if (id >= E) id = 0;  // fewer valid logits than K: keep indices in range
     const float val = key_f(mx);
     if (k == 0) top = val;
     if (lane == k) mine = val;
     if (lane == 0) ids[k] = id;
-    if ((id & 31) == lane) {
-#pragma unroll
-      for (int i = 0; i < PL; ++i)
-        if (i * 32 + lane == id) key[i] = 0u;
-      local_best(bk, bi);
-    }
   }
   float sum = 0.f;
 #pragma unroll
@@ -223,16 +231,18 @@ __device__ __forceinline__ void warp_route(const float* lg, int E, int K, int no
     if (i * 32 + lane < E) sum += expf(lv[i] - top);
   sum = warp_sum(sum);
   const float p = lane < K ? expf(mine - top) / sum : 0.f;
-  if (lane < K) w[lane] = p;
+  // renormalisation: the picks' sum in pick order (as the reference adds
+  // them), gathered by shuffles rather than through shared memory
+  float score_sum = 0.f;
+  for (int k = 0; k < K; ++k) score_sum += __shfl_sync(0xffffffffu, p, k);
+  if (lane < K) w[lane] = norm_topk ? p / score_sum : p;
+  if (lane == 0) *sh = sigmoid_ref(shared_logit);
   __syncwarp();
-  if (lane == 0) {
-    float score_sum = 0.f;
-    for (int k = 0; k < K; ++k) score_sum += w[k];
-    if (norm_topk)
-      for (int k = 0; k < K; ++k) w[k] = w[k] / score_sum;
-    *sh = sigmoid_ref(shared_logit);
-  }
-  __syncwarp();
+}
+__device__ __forceinline__ void warp_route(const float* lg, int E, int K, int norm_topk, int* ids, float* w,
+                                           float* sh) {
+  if (E <= 256) warp_route_pl<8>(lg, E, K, norm_topk, ids, w, sh);
+  else warp_route_pl<16>(lg, E, K, norm_topk, ids, w, sh);
 }
 
 // Four consecutive scale (or bias) entries g..g+3 of a row in shared memory
@@ -538,8 +548,8 @@ __global__ void __launch_bounds__(IM_T, 2) k_igemv(const GemvArgs a, const Slice
 // ((q % ipe) * BR, ...) (ipe items per expert). An item's gate rows and its up
 // rows arrive as one tensor-TMA box each plus their scale and bias rows, so a
 // CTA issues six copies: the shared items at kernel entry, the routed ones as
-// soon as consumer warp 0 has routed from the router's logits (the producer
-// waits for it on an mbarrier). The 16-row MMA tile is 8 gate rows over the
+// soon as the producer warp has routed from the router's logits (while the
+// consumers stage the input). The 16-row MMA tile is 8 gate rows over the
 // same 8 up rows, so the lane holding gate row p also holds up row p; the
 // item's BR / 8 tiles are split over warp groups as in the dense kernel.
 template <int BITS, int DT, int KPG>
@@ -566,17 +576,30 @@ __global__ void __launch_bounds__(IM_T, 2) k_igateup(const MoeArgs m, const Slic
   const bool route_here = !shared_item && m.logits != nullptr;
   __shared__ int r_ids[16];
   __shared__ float r_w[16], r_sh;
-  __shared__ __align__(8) uint64_t routed;
   if (tid == 0) {
     mbar_init(full, 1);
-    mbar_init(&routed, 1);
     mbar_init_fence();
   }
   __syncthreads();
   if (warp == IW) {  // producer
+    if (route_here) {
+      // the routing comes from the previous (router) grid; the consumers
+      // stage the input meanwhile and never need it (the item's slot k is
+      // known), so it costs only the copies' start
+      pdl_wait();
+      warp_route(m.logits, m.experts, K, m.norm_topk, r_ids, r_w, &r_sh);
+      // the first routed item also stores the routing for observers
+      if (b == nsh) {
+        if (lane < K) {
+          m.pick_ids[lane] = r_ids[lane];
+          m.pick_w[lane] = r_w[lane];
+        }
+        if (lane == 0) *m.shared_scale = r_sh;
+      }
+    }
     if (lane == 0) {
       const uint64_t pol = l2_evict_first();
-      bool ok = true, issued = false;
+      bool issued = false;
       auto issue = [&](int id) {
         QLin G = m.sg, U = m.su;
         if (!shared_item) {
@@ -592,15 +615,7 @@ __global__ void __launch_bounds__(IM_T, 2) k_igateup(const MoeArgs m, const Slic
       // the shared expert's weights do not depend on the routing
       if (shared_item) issue(0);
       pdl_wait();  // the routing comes from the previous (router) grid
-      if (!shared_item) {
-        if (route_here) {
-          ok = mbar_wait(&routed, 0u);
-          if (ok) issue(r_ids[k]);
-        } else {
-          issue(__ldcg(m.pick_ids + k));
-        }
-      }
-      if (!ok) sl_fail(T);
+      if (!shared_item) issue(route_here ? r_ids[k] : __ldcg(m.pick_ids + k));
       // Dependents are released only after the router grid is complete: the
       // down kernel reads the router's output before its own dependency wait.
       pdl_launch();
@@ -612,19 +627,6 @@ __global__ void __launch_bounds__(IM_T, 2) k_igateup(const MoeArgs m, const Slic
   trc.start(m.trace);
   pdl_wait();
   trc.waited(m.trace);
-  if (route_here && warp == 0) {
-    warp_route(m.logits, m.experts, K, m.norm_topk, r_ids, r_w, &r_sh);
-    __threadfence_block();
-    if (lane == 0) mbar_arrive(&routed);
-    // the first routed item also stores the routing for observers
-    if (b == nsh) {
-      if (lane < K) {
-        m.pick_ids[lane] = r_ids[lane];
-        m.pick_w[lane] = r_w[lane];
-      }
-      if (lane == 0) *m.shared_scale = r_sh;
-    }
-  }
   GemvArgs a;
   a.in = m.g.lin.in; a.prologue = PRO_COPY; a.x = m.x;
   sl_stage_plain<IM_NT>(a, red, plain);
