@@ -276,6 +276,8 @@ def batched_decode(model, cfg, stream, args, rank, local, dist, ep: bool, steps:
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
+    if ep:
+        model.ep_timing(reset=True)
     with ClockSampler(local) as clk:
         ev[2].record(stream)
         for _ in range(steps):
@@ -283,6 +285,9 @@ def batched_decode(model, cfg, stream, args, rank, local, dist, ep: bool, steps:
         ev[3].record(stream)
         torch.cuda.synchronize()
     ms = ev[2].elapsed_time(ev[3])
+    # with SWL_EP_TIMING=1 and SWL_EP_NO_GRAPH=1: this rank's collective time
+    # (CUDA events around each exchange, waits for peers included)
+    ep_t = model.ep_timing() if ep else None
     host = tok.cpu().numpy().tolist()
     ev[4].record(stream)
     for _ in range(e2e_steps):
@@ -331,6 +336,12 @@ def batched_decode(model, cfg, stream, args, rank, local, dist, ep: bool, steps:
         "gpu_launches_per_step": 3 + 11 * L + 3,
         "clocks": clk.summary(),
     }
+    if ep_t:
+        coll = max_over_ranks([ep_t["collective_ms"] / max(1, ep_t["steps"])], dist, f"cuda:{local}")[0]
+        res["ep_timing"] = {"collective_ms_per_step_max_over_ranks": coll,
+                            "collectives_per_step": ep_t["collectives"] / max(1, ep_t["steps"]),
+                            "rank0_step_ms": ep_t["step_ms"] / max(1, ep_t["steps"]),
+                            "mode": "SWL_EP_NO_GRAPH=1 (steps launched directly, CUDA events around each exchange)"}
     if delta:
         res["deltanet"] = delta
     return res

@@ -165,6 +165,16 @@ int swl_ep_init(swl_model* model, int32_t rank, int32_t world, const void* id, i
  * removes the callback. */
 typedef int (*swl_ep_liveness_fn)(void* ctx, int32_t step);
 int swl_ep_set_liveness(swl_model* model, swl_ep_liveness_fn fn, void* ctx);
+/* Collective timing of expert parallelism, for finding where a step's time
+ * goes (no counterpart in the reference, whose decode runs on one device).
+ * Active only when the model's expert parallelism was initialised with the
+ * environment variables SWL_EP_TIMING=1 and SWL_EP_NO_GRAPH=1 (steps launched
+ * directly, CUDA events around every exchange). Writes out[0] = timed steps,
+ * out[1] = their total ms, out[2] = collectives (grouped all-gathers and
+ * reduce-scatters), out[3] = their total ms (each including its wait for the
+ * slowest peer); synchronises the model's stream; reset != 0 starts the
+ * counts again. Returns 1 when timing is active, 0 when not (out all 0). */
+int swl_ep_timing(swl_model* model, int32_t reset, double* out);
 /* 1 when expert parallelism is on (rank, world and the owned expert range are
  * written; each pointer may be NULL), 0 when off (0, 1, 0, E). */
 int swl_ep_info(const swl_model* model, int32_t* rank, int32_t* world, int32_t* expert_lo, int32_t* expert_hi);

@@ -88,6 +88,7 @@ _SIGNATURES = {
     "swl_ep_unique_id": (_I, [_P, C.c_int32]),
     "swl_ep_init": (_I, [_P, C.c_int32, C.c_int32, _P, C.c_int32, C.c_int32]),
     "swl_ep_info": (_I, [_P] * 5),
+    "swl_ep_timing": (_I, [_P, C.c_int32, C.POINTER(C.c_double)]),
     "swl_pool_stats": (_I, [_P, C.POINTER(swl_pool_info)]),
     "swl_pool_resize": (_I, [_P, _D]),
     "swl_set_stream": (_I, [_P, _P]),
@@ -318,6 +319,18 @@ class QwenCUDAModel:
         if rc < 0:
             _check(rc)
         return (rc == 1, *[x.value for x in v])
+
+    def ep_timing(self, reset: bool = False) -> dict | None:
+        """Collective timing of expert-parallel steps (swl_ep_timing), or None
+        when inactive (it needs SWL_EP_TIMING=1 and SWL_EP_NO_GRAPH=1 set
+        before ep_init)."""
+        out = (C.c_double * 4)()
+        rc = lib().swl_ep_timing(self._h, int(reset), out)
+        if rc < 0:
+            _check(rc)
+        if rc != 1:
+            return None
+        return {"steps": int(out[0]), "step_ms": out[1], "collectives": int(out[2]), "collective_ms": out[3]}
 
     def step_device(self, d_tokens: int, n: int, state: DecodeState, d_logits: int = 0, d_greedy: int = 0) -> None:
         """Device-pointer form (tokens/logits already in HBM)."""

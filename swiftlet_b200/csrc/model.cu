@@ -204,6 +204,43 @@ struct Model {
     }
     if (ep_failed) throw Error(ERR_CUDA, "expert-parallel group failed: " + ep_fail_why);
   }
+  // Collective timing (SWL_EP_TIMING=1 with SWL_EP_NO_GRAPH=1; swl_ep_timing):
+  // CUDA events on the stream around every exchange (the grouped all-gather,
+  // the reduce-scatter) and around every expert-parallel step, collected when
+  // queried (or when many are pending). An exchange's time includes its wait
+  // for the slowest peer to reach it.
+  bool ep_timing = false;
+  std::vector<cudaEvent_t> ep_ev_pool;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ep_coll_ev, ep_step_ev;
+  double ep_coll_ms = 0.0, ep_step_ms = 0.0;
+  int64_t ep_coll_n = 0, ep_step_n = 0;
+  cudaEvent_t ep_mark(cudaStream_t st) {
+    cudaEvent_t e;
+    if (ep_ev_pool.empty()) {
+      SWL_CUDA(cudaEventCreate(&e));
+    } else {
+      e = ep_ev_pool.back();
+      ep_ev_pool.pop_back();
+    }
+    SWL_CUDA(cudaEventRecord(e, st));
+    return e;
+  }
+  void ep_collect() {
+    auto drain = [&](std::vector<std::pair<cudaEvent_t, cudaEvent_t>>& v, double& ms, int64_t& n) {
+      for (auto& pr : v) {
+        SWL_CUDA(cudaEventSynchronize(pr.second));
+        float t = 0.f;
+        SWL_CUDA(cudaEventElapsedTime(&t, pr.first, pr.second));
+        ms += t;
+        ++n;
+        ep_ev_pool.push_back(pr.first);
+        ep_ev_pool.push_back(pr.second);
+      }
+      v.clear();
+    };
+    drain(ep_coll_ev, ep_coll_ms, ep_coll_n);
+    drain(ep_step_ev, ep_step_ms, ep_step_n);
+  }
   int ep_lo() const { return int(int64_t(ep_rank) * cfg.experts / ep_world); }
   int ep_hi() const { return int(int64_t(ep_rank + 1) * cfg.experts / ep_world); }
   // Expert streaming: a .qpack model whose experts exceed the HBM budget
@@ -307,6 +344,9 @@ struct EpDecode {
 Model::~Model() {
   drop_graphs();
   if (stream) cudaStreamSynchronize(stream);
+  for (auto& pr : ep_coll_ev) ep_ev_pool.insert(ep_ev_pool.end(), {pr.first, pr.second});
+  for (auto& pr : ep_step_ev) ep_ev_pool.insert(ep_ev_pool.end(), {pr.first, pr.second});
+  for (cudaEvent_t e : ep_ev_pool) cudaEventDestroy(e);
   ep_destroy(ep);
   for (State* s : live) {  // a caller that frees states after the model only releases the handle
     cudaFree(s->mem);
@@ -1272,6 +1312,7 @@ void Model::enqueue_batch_moe(int l, int T, bool chunked, cudaStream_t st) {
   if (ep_on) {
     // every rank's MoE inputs (the normalised rows for the tensor-core
     // experts, or their digit tables for the mma.sync ones) and router logits
+    const cudaEvent_t t_ag = ep_timing ? ep_mark(st) : nullptr;
     ep_group_start(ep);
     if (tc) {
       ep_allgather(ep, bb.xmoe, size_t(T) * D * sizeof(float), st);
@@ -1281,6 +1322,7 @@ void Model::enqueue_batch_moe(int l, int T, bool chunked, cudaStream_t st) {
     }
     ep_allgather(ep, bb.rlog, size_t(T) * (E + 1) * sizeof(float), st);
     ep_group_end(ep);
+    if (ep_timing) ep_coll_ev.emplace_back(t_ag, ep_mark(st));
   }
   BRouteArgs r;
   r.logits = bb.rlog; r.T = Ta; r.E = E; r.K = K; r.norm_topk = c.norm_topk;
@@ -1357,7 +1399,9 @@ void Model::enqueue_batch_combine(int T, int Ta, int own, bool ep_on, cudaStream
     ce.h = bb.h; ce.part = ep_part; ce.ydown = bb.ydown; ce.ystride = D; ce.slot_of = bb.slot_of; ce.w = bb.w;
     ce.sh = bb.sh; ce.T = Ta; ce.K = K; ce.D = D; ce.own_lo = own; ce.own_hi = own + T;
     launch_bcombine_ep(ce, st, pdl);
+    const cudaEvent_t t_rs = ep_timing ? ep_mark(st) : nullptr;
     ep_reduce_scatter(ep, ep_part, bb.h, size_t(T) * D, st);
+    if (ep_timing) ep_coll_ev.emplace_back(t_rs, ep_mark(st));
   } else {
     BCombineArgs cb;
     cb.h = bb.h; cb.ydown = bb.ydown; cb.ystride = D; cb.slot_of = bb.slot_of; cb.w = bb.w; cb.sh = bb.sh;
@@ -1412,6 +1456,11 @@ void Model::run_batch(State* const* s, int S, const int* counts, int T) {
     if (it == bb.graphs.end())
       it = bb.graphs.emplace(key, capture(stream, [&] { enqueue_batch(T, S, chunked, stream); })).first;
     SWL_CUDA(cudaGraphLaunch(it->second, stream));
+  } else if (ep_step && ep_timing) {
+    const cudaEvent_t t0 = ep_mark(stream);
+    enqueue_batch(T, S, chunked, stream);
+    ep_step_ev.emplace_back(t0, ep_mark(stream));
+    if (ep_coll_ev.size() > 4096) ep_collect();
   } else {
     enqueue_batch(T, S, chunked, stream);
   }
@@ -1982,6 +2031,7 @@ int swl_ep_init(swl_model* model, int32_t rank, int32_t world, const void* id, i
   }
   m.ep = c;
   m.ep_graph = !env_flag("SWL_EP_NO_GRAPH");
+  m.ep_timing = env_flag("SWL_EP_TIMING") && !m.ep_graph;
   m.ep_rank = rank;
   m.ep_world = world;
   m.ep_tokens = tokens_per_rank;
@@ -2006,6 +2056,24 @@ int swl_ep_info(const swl_model* model, int32_t* rank, int32_t* world, int32_t* 
   if (expert_lo) *expert_lo = m.ep ? m.ep_lo() : 0;
   if (expert_hi) *expert_hi = m.ep ? m.ep_hi() : m.cfg.experts;
   return m.ep ? 1 : 0;
+  API_END
+}
+
+int swl_ep_timing(swl_model* model, int32_t reset, double* out) {
+  API_BEGIN
+  if (!model || !out) throw Error(ERR_INVALID, "null argument");
+  Model& m = model->m;
+  SWL_CUDA(cudaSetDevice(m.device));
+  m.ep_collect();
+  out[0] = double(m.ep_step_n);
+  out[1] = m.ep_step_ms;
+  out[2] = double(m.ep_coll_n);
+  out[3] = m.ep_coll_ms;
+  if (reset) {
+    m.ep_step_n = m.ep_coll_n = 0;
+    m.ep_step_ms = m.ep_coll_ms = 0.0;
+  }
+  return m.ep_timing ? 1 : 0;
   API_END
 }
 

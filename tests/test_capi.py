@@ -47,6 +47,8 @@ def test_null_arguments_are_rejected():
     assert swl.lib().swl_model_open(None, 0.0, 0, None) == swl.SWL_ERR_INVALID
     assert swl.lib().swl_step(None, None, None, 0, None) == swl.SWL_ERR_INVALID
     assert swl.lib().swl_state_position(None) == -1
+    out = (C.c_double * 4)()
+    assert swl.lib().swl_ep_timing(None, 0, out) == swl.SWL_ERR_INVALID
 
 
 def test_python_mirror_raises_without_gpu_or_loads_with_one():
