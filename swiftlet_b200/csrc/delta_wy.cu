@@ -323,6 +323,131 @@ __global__ void __launch_bounds__(256) k_delta_prep(const DeltaArgs a, const WyA
   }
 }
 
+// Decode-step inputs of the delta rule (one token per sequence, token t =
+// sequence t), as k_delta_prep writes them for prompts, with one CTA per
+// (token, block of 128 conv channels) and one channel per thread: the causal
+// conv of the channel over the ring's K - 1 older inputs (read before the
+// dependency wait) and the token's own, SiLU, and the token's input stored in
+// ring slot pos % K (which none of its taps read). A q or k block is one key
+// head: its RMSNorm (sum of squares in k_delta_prep's order) and scale
+// 1/dk or 1/sqrt(dk) are applied in place. A value block also writes its
+// channels' output gate silu(z), and its first thread the head's (log g,
+// beta) (QwenCPUModel.swift:423-458).
+__global__ void __launch_bounds__(128) k_delta_prep_dec(const DeltaArgs a, const WyArgs w) {
+  __shared__ float sq[128];
+  __shared__ float nrm;
+  const int tok = blockIdx.x, c = blockIdx.y * 128 + threadIdx.x, lane = threadIdx.x & 31;
+  const int K = a.conv_k, cd = a.conv_dim, dk = a.dk, keyDim = a.nk * dk;
+  const StateDev* sd = a.sd + tok;
+  const int pos = *sd->pos;
+  float* ring = sd->conv[a.layer];
+  float acc = 0.f;
+  for (int jj = 0; jj < K - 1; ++jj)  // older inputs, oldest first: written by earlier steps
+    acc += a.conv_w[c * K + jj] * ring[int64_t(((pos - (K - 1) + jj) % K + K) % K) * cd + c];
+  pdl_wait();
+  const float* proj = a.proj + int64_t(tok) * a.proj_stride;
+  const float x = proj[delta_src(a, c)];
+  acc += a.conv_w[c * K + K - 1] * x;
+  ring[int64_t(pos % K) * cd + c] = x;
+  const float o = silu_ref(acc);
+  pdl_launch();
+  if (c < 2 * keyDim) {
+    sq[threadIdx.x] = o;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float ss = 0.f;
+      for (int i = lane; i < dk; i += 32) ss += sq[i] * sq[i];
+      ss = warp_sum(ss);
+      if (lane == 0) nrm = 1.f / sqrtf(ss / float(dk) + 1e-6f);
+    }
+    __syncthreads();
+    const float inv = 1.f / sqrtf(float(dk));
+    if (c < keyDim) w.qw[int64_t(tok) * w.q_stride + c] = (o * nrm) * (inv * inv);
+    else w.kw[int64_t(tok) * w.k_stride + c - keyDim] = (o * nrm) * inv;
+  } else {
+    const int i = c - 2 * keyDim, hv = i / a.dv, d = i - hv * a.dv;
+    w.vw[int64_t(tok) * w.v_stride + i] = o;
+    a.z[int64_t(tok) * a.nv * a.dv + i] = silu_ref(proj[delta_z(a, hv, d)]);
+    if (d == 0) {
+      int bi, ai;
+      delta_ba(a, hv, bi, ai);
+      w.lgw[int64_t(tok) * w.gb_stride + 2 * hv] = -expf(a.a_log[hv]) * softplus_ref(proj[ai] + a.dt_bias[hv]);
+      w.lgw[int64_t(tok) * w.gb_stride + 2 * hv + 1] = sigmoid_ref(proj[bi]);
+    }
+  }
+}
+
+void launch_delta_prep_dec(const DeltaArgs& a, const WyArgs& w, int T, cudaStream_t st, bool pdl) {
+  if (a.dk != 128 || a.conv_dim % 128 || a.dv > 128 || 128 % a.dv)
+    throw Error(ERR_UNSUPPORTED, "delta rule decode inputs: head sizes outside the kernel's range");
+  launch(k_delta_prep_dec, dim3(T, a.conv_dim / 128), dim3(128), 0, st, pdl, a, w);
+}
+
+// Decode step of the delta rule from k_delta_prep's per-token inputs (token
+// blockIdx.z is its sequence's only token): RPW state rows of value head
+// blockIdx.x per warp, lane l holding columns 4l..4l+3, loaded before the
+// dependency wait; then S <- g S, S <- S + k beta (v - S k), y = S q
+// (QwenCPUModel.swift:459-488, as k_delta4). With the per-head conv, norms
+// and gates done once per token by the prep, a CTA's work after its wait is
+// two float4 loads, its rows' v, the update and the stores, so the state
+// streams at close to HBM rate.
+template <int RPW, int NW>
+__global__ void __launch_bounds__(NW * 32) k_delta_step(const WyArgs w) {
+  constexpr int RB = RPW * NW, DK = WY_DK;
+  const int hv = blockIdx.x, tok = blockIdx.z, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hk = hv / (w.nv / w.nk), dv = w.dv;
+  const int row0 = blockIdx.y * RB + warp * RPW;
+  float* S = w.sd[tok].dstate[w.layer];
+  float4* S4 = reinterpret_cast<float4*>(S + (int64_t(hv) * dv + row0) * DK) + lane;
+  float4 st[RPW];
+#pragma unroll
+  for (int j = 0; j < RPW; ++j) st[j] = S4[j * (DK / 4)];
+  pdl_wait();
+  const float4 qr = reinterpret_cast<const float4*>(w.q + int64_t(tok) * w.q_stride + hk * DK)[lane];
+  const float4 kr = reinterpret_cast<const float4*>(w.k + int64_t(tok) * w.k_stride + hk * DK)[lane];
+  const float lgv = w.lg[int64_t(tok) * w.gb_stride + 2 * hv], beta = w.lg[int64_t(tok) * w.gb_stride + 2 * hv + 1];
+  const float vl = lane < RPW ? w.v[int64_t(tok) * w.v_stride + hv * dv + row0 + lane] : 0.f;
+  pdl_launch();
+  const float g = expf(lgv);
+  float kv[RPW];
+#pragma unroll
+  for (int j = 0; j < RPW; ++j) {
+    st[j].x *= g; st[j].y *= g; st[j].z *= g; st[j].w *= g;
+    kv[j] = st[j].x * kr.x + st[j].y * kr.y + st[j].z * kr.z + st[j].w * kr.w;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1)
+#pragma unroll
+    for (int j = 0; j < RPW; ++j) kv[j] += __shfl_xor_sync(0xffffffffu, kv[j], o);
+  float y[RPW];
+#pragma unroll
+  for (int j = 0; j < RPW; ++j) {
+    const float delta = (__shfl_sync(0xffffffffu, vl, j) - kv[j]) * beta;
+    st[j].x += kr.x * delta; st[j].y += kr.y * delta; st[j].z += kr.z * delta; st[j].w += kr.w * delta;
+    y[j] = st[j].x * qr.x + st[j].y * qr.y + st[j].z * qr.z + st[j].w * qr.w;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1)
+#pragma unroll
+    for (int j = 0; j < RPW; ++j) y[j] += __shfl_xor_sync(0xffffffffu, y[j], o);
+#pragma unroll
+  for (int j = 0; j < RPW; ++j) S4[j * (DK / 4)] = st[j];
+  if (lane < RPW) {
+    float yl = y[0];
+#pragma unroll
+    for (int j = 1; j < RPW; ++j) if (lane == j) yl = y[j];
+    w.y[int64_t(tok) * w.y_stride + hv * dv + row0 + lane] = yl;
+  }
+}
+
+void launch_delta_step(const WyArgs& a, int T, cudaStream_t st, bool pdl) {
+  constexpr int RPW = 4, NW = 8;
+  if (a.dk != WY_DK || a.dv % (RPW * NW) || a.nv % a.nk)
+    throw Error(ERR_UNSUPPORTED, "delta rule decode step: head sizes outside its range");
+  launch(k_delta_step<RPW, NW>, dim3(a.nv, a.dv / (RPW * NW), T), dim3(NW * 32), 0, st, pdl, a);
+  path_note("delta_step");
+}
+
 bool delta_wy_supported(int dk, int dv, int nk, int nv, int conv_dim) {
   return !std::getenv("SWL_NO_WY") && dk == WY_DK && dv % WY_R == 0 && 2 * nk <= 64 && nv % nk == 0 &&
          size_t(conv_dim) * 4 <= 64 * 1024;

@@ -161,6 +161,10 @@ struct WyArgs {
 bool delta_wy_supported(int dk, int dv, int nk, int nv, int conv_dim);
 void launch_delta_prep(const DeltaArgs& a, const WyArgs& w, int T, cudaStream_t stream, bool pdl);
 void launch_delta_wy(const WyArgs& a, int S, cudaStream_t stream, bool pdl);
+// Decode step of T sequences (one token each): the per-token inputs
+// (k_delta_prep_dec, which also advances the conv ring), then the state.
+void launch_delta_prep_dec(const DeltaArgs& a, const WyArgs& w, int T, cudaStream_t stream, bool pdl);
+void launch_delta_step(const WyArgs& a, int T, cudaStream_t stream, bool pdl);
 
 struct AttnArgs {
   const float* qout;       // [H * 2 * hd] (per head: q | gate)

@@ -300,6 +300,11 @@ struct Model {
   void enqueue_batch(int T, int S, bool chunked, cudaStream_t st);
   void enqueue_batch_moe(int l, int T, bool chunked, cudaStream_t st);
   void enqueue_batch_combine(int T, int Ta, int own, bool ep_on, cudaStream_t st);
+  // DeltaNet decode step of T sequences (one token each) at layer l: from
+  // kDeltaSplitMin sequences on, per-token conv / norms / gates once
+  // (k_delta_prep_dec) and then the state streamed by k_delta_step; below it
+  // the single fused kernel, whose one launch costs less at small batch.
+  void enqueue_delta_decode(const DeltaArgs& d, int T, int l, cudaStream_t st);
   // S sequences consume counts[i] tokens each (T in total, already in
   // bb.tokens, sequence-major)
   void run_batch(State* const* s, int S, const int* counts, int T);
@@ -1241,7 +1246,7 @@ void Model::enqueue_batch(int T, int S, bool chunked, cudaStream_t st) {
         }
         launch_conv_ring(d, S, st, pdl);
       } else {
-        launch_delta_batch(d, T, st, pdl);
+        enqueue_delta_decode(d, T, l, st);
       }
       digit(bb.yv, c.value_dim(), T, c.value_dim(), ld.out_lin.gs, PRO_GATEDNORM, bb.zv, ld.dnorm, c.dv, nullptr,
             bb.bt_a, bb.meta_a);
@@ -1390,6 +1395,24 @@ void Model::enqueue_batch_moe(int l, int T, bool chunked, cudaStream_t st) {
 // Expert outputs back into the residual stream: the weighted routed sums
 // and the gated shared expert (QwenCPUModel.swift:552-566), or with expert
 // parallelism this rank's partial sums and their reduce-scatter.
+constexpr int kDeltaSplitMin = 4;
+
+void Model::enqueue_delta_decode(const DeltaArgs& d, int T, int l, cudaStream_t st) {
+  const ModelConfig& c = cfg;
+  if (T < kDeltaSplitMin || !delta_wy_supported(c.dk, c.dv, c.nk, c.nv, c.conv_dim()) || c.conv_dim() % 128 ||
+      c.dv > 128 || 128 % c.dv) {
+    launch_delta_batch(d, T, st, use_pdl);
+    return;
+  }
+  WyArgs w;
+  w.q = w.qw = bb.wy_q; w.k = w.kw = bb.wy_k; w.v = w.vw = bb.wy_v; w.lg = w.lgw = bb.wy_gb;
+  w.q_stride = w.k_stride = c.key_dim(); w.v_stride = c.value_dim(); w.gb_stride = 2 * c.nv;
+  w.nk = c.nk; w.nv = c.nv; w.dk = c.dk; w.dv = c.dv; w.sd = d.sd; w.layer = l;
+  w.y = d.y; w.y_stride = c.value_dim();
+  launch_delta_prep_dec(d, w, T, st, use_pdl);
+  launch_delta_step(w, T, st, use_pdl);
+}
+
 void Model::enqueue_batch_combine(int T, int Ta, int own, bool ep_on, cudaStream_t st) {
   const ModelConfig& c = cfg;
   const int D = c.hidden, K = c.topk;
@@ -2377,7 +2400,7 @@ int swl_bench_delta_sweep(swl_model* model, int32_t T, int32_t iters, float* ms_
       } else {
         d.proj = m.bb.proj; d.proj_stride = m.bb.projn; d.sd = m.bb.sds; d.rows_per_block = c.dv <= 128 ? c.dv : 32;
         d.y = m.bb.yv; d.z = m.bb.zv;
-        launch_delta_batch(d, T, m.stream, m.use_pdl);
+        m.enqueue_delta_decode(d, T, l, m.stream);
       }
       ++nl;
     }
