@@ -866,9 +866,31 @@ __global__ void __launch_bounds__(1024) k_bargmax(const float* logits, int V, in
   const float* l = logits + int64_t(blockIdx.x) * V;
   float v = -INFINITY;
   int idx = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float x = l[i];
+  auto take = [&](float x, int i) {
     if (x > v || (idx == 0x7fffffff)) { v = x; idx = i; }
+  };
+  if ((V & 3) == 0 && (reinterpret_cast<uintptr_t>(l) & 15) == 0) {
+    // four 16-byte loads in flight per thread; each thread still meets its
+    // indices in increasing order, so the first maximum wins as below
+    const float4* l4 = reinterpret_cast<const float4*>(l);
+    const int n4 = V >> 2, step = int(blockDim.x);
+    for (int b = threadIdx.x; b < n4; b += 4 * step) {
+      float4 q[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) q[u] = b + u * step < n4 ? l4[b + u * step] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i4 = b + u * step;
+        if (i4 < n4) {
+          take(q[u].x, 4 * i4);
+          take(q[u].y, 4 * i4 + 1);
+          take(q[u].z, 4 * i4 + 2);
+          take(q[u].w, 4 * i4 + 3);
+        }
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < V; i += blockDim.x) take(l[i], i);
   }
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
