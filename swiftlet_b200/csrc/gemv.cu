@@ -349,8 +349,15 @@ static bool plan_idense(const QLin* lins, float* const* ys, int nseg, int in, in
   }
   T.total = T.cum[nseg];
   if (T.total <= 0) return false;
-  T.rpc = std::max((T.total + sm_count() - 1) / sm_count(), 16);
+  // Large launches (in_proj of the DeltaNet layers, lm_head) take two CTAs
+  // per SM, each within 112 KB of shared memory so both stay resident: twice
+  // the warps hide the tile loop's dependent latencies (B = 1 decode 501.5 ->
+  // 510.2 tok/s on B200, same inputs).
+  const bool two = T.total >= 4 * 16 * sm_count();
+  const int ctas = two ? 2 * sm_count() : sm_count();
+  T.rpc = std::max((T.total + ctas - 1) / ctas, 16);
   grid = (T.total + T.rpc - 1) / T.rpc;
+  if (two && g_budget > 112 * 1024) g_budget = 112 * 1024;  // restored by the caller's BudgetScope
   for (int sg = 0; sg < nseg; ++sg)
     if (!encode_rows(&M.m[sg], lins[sg].w, lins[sg].out, lins[sg].row_bytes, 16, 0, 0)) return false;
   T.slot = imma_block_bytes(l0, 16);
